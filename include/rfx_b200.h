@@ -1,0 +1,159 @@
+/* rfx_b200 — B200-native forest growth and proximity for RFX-Fuse (C ABI).
+ *
+ * Replaces the reference's GPU seam `gpu_growtree_batch(...)` (include/rf_growtree.hpp:45,
+ * cuda/rf_growtree.cu:3006, called from RandomForest::fit_batch_gpu,
+ * src/rf_random_forest.cpp:2000-2464) and the CPU per-tree loop it stands in for
+ * (RandomForest::grow_tree_single, src/rf_random_forest.cpp:1278-1997).  The results are
+ * those of the reference CPU path: bootstrap (src/rf_bootstrap.cpp:15-84), quantile binning
+ * (src/rf_histogram.cpp:13-160), histogram growth (src/rf_growtree.cpp:616-1161), OOB drop
+ * (src/rf_testreebag.cpp:13-125), permutation importance (src/rf_varimp.cpp:218-597),
+ * proximity (src/rf_proximity.cpp:99-230) and finishprox (src/rf_finishprox.cpp:12-74).
+ *
+ * Conventions: plain pointers and sizes only.  Host pointers unless the name ends in
+ * `_dev`.  Every function returns RFX_OK (0) or a negative RFX_ERR_* code and never
+ * throws; rfx_last_error() gives the message of the calling thread's last failure.  A
+ * context is bound to one CUDA device and is not re-entrant.
+ */
+#ifndef RFX_B200_H
+#define RFX_B200_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RFX_ABI_VERSION 1
+
+enum {
+    RFX_OK = 0,
+    RFX_ERR_ARG = -1,          /* invalid argument */
+    RFX_ERR_CUDA = -2,         /* CUDA runtime failure (message has the CUDA error) */
+    RFX_ERR_OOM = -3,          /* device allocation failed */
+    RFX_ERR_UNSUPPORTED = -4,  /* option outside what the device path implements */
+    RFX_ERR_STATE = -5,        /* call order violated (e.g. grow before load) */
+    RFX_ERR_DEVICE = -6        /* a kernel reported an internal consistency error */
+};
+
+enum { RFX_TASK_CLASSIFICATION = 0, RFX_TASK_REGRESSION = 1, RFX_TASK_UNSUPERVISED = 2 };
+
+/* Effective fit parameters (already resolved the way the estimator wrappers resolve them:
+ * python/randomforest_py.cpp:1270-1320, 1404-1411, 3123-3124, 3232-3234, 4687-4692;
+ * include/rf_config.hpp:15-32). */
+typedef struct {
+    int task;               /* RFX_TASK_* */
+    int n;                  /* rows supplied (real rows for unsupervised) */
+    int p;                  /* features */
+    int mtry;               /* features drawn (with replacement) per searched node */
+    int minndsize;          /* split needs >= minndsize rows (2x for regression) */
+    int maxnode;            /* node cap per tree */
+    int iseed;              /* grower seed base: tree t draws from MT19937(iseed + t) */
+    int boot_seed;          /* bootstrap seed base: MT19937(boot_seed + t); 12345 in the reference */
+    int nbins;              /* histogram bins, <= 256 */
+    int maxcat;             /* the estimator's maxcat (category bound of importance walks) */
+    int compute_importance; /* permutation importance (rf_varimp.cpp) */
+    int compute_proximity;  /* OOB x in-bag leaf co-membership counts */
+    int prox_rows;          /* proximity covers rows [0, prox_rows); 0 = all grown rows */
+    int batch_trees;        /* trees grown concurrently on the device; 0 = automatic */
+    int keep_tree_oob;      /* keep per-tree OOB predictions for rfx_oob_fold (regression) */
+} rfx_fit_params;
+
+typedef struct {
+    const float* X;              /* [n x p] row-major */
+    const int* y_class;          /* [n] class labels (any integers), classification only */
+    const float* y_reg;          /* [n] targets, regression only */
+    const float* sample_weights; /* [n] bootstrap weights or NULL (uniform) */
+    const int* cat;              /* [p] 1 = quantitative, k > 1 = k categories; NULL = all 1 */
+    const float* classwt;        /* [nclass] OOB vote weights or NULL */
+} rfx_inputs;
+
+/* Per-tree arrays of one rfx_grow call, [ntree x maxnode] (treemap [ntree x 2*maxnode]),
+ * laid out like the reference RandomForest members (src/rf_random_forest.cpp:358-452).
+ * Any pointer may be NULL. */
+typedef struct {
+    int* nodestatus; int* bestvar; float* xbestsplit; int* treemap; int* nodeclass;
+    int* nnode; float* nodepred; float* tnodewt;
+    int* nin;        /* [ntree x N] bootstrap multiplicities */
+    int* oob_leaf;   /* [ntree x N] terminal node of OOB rows, in-bag rows -1 */
+    float* tree_rr;  /* [ntree x p] per-tree importance rr (0 where unused) */
+    uint8_t* tree_used; /* [ntree x p] 1 where rr enters avimp */
+} rfx_trees;
+
+/* Forest accumulators after all rfx_grow calls since rfx_load (N = grown rows: n, or 2n
+ * for unsupervised).  Any pointer may be NULL. */
+typedef struct {
+    int nclass;      /* out: classes (1 for regression, 2 for unsupervised) */
+    int N;           /* out: grown rows */
+    int* nout;       /* [N] times each row was out of bag */
+    int* votes;      /* [N x nclass] integer OOB vote counts */
+    float* q;        /* [N x nclass] raw OOB vote sums (classwt-weighted), reference q_ */
+    float* oob_sum;  /* [N] regression: sum of OOB predictions in tree order */
+    float* avimp;    /* [p] summed importance in tree order */
+    float* sqsd;     /* [p] summed squared importance in tree order */
+    int* labels;     /* [N] 0-based labels the trees were grown on (classification) */
+} rfx_accum;
+
+const char* rfx_last_error(void);
+int rfx_abi_version(void);
+int rfx_device_count(void);
+
+/* Context bound to CUDA device `device`; NULL on failure (see rfx_last_error). */
+void* rfx_create(int device);
+void rfx_destroy(void* ctx);
+
+/* Upload inputs, bin features on the device and reset all accumulators. */
+int rfx_load(void* ctx, const rfx_fit_params* prm, const rfx_inputs* in);
+
+/* Grow trees [tree_begin, tree_begin + ntree) on the loaded data and fold their OOB votes,
+ * predictions, importance and proximity into the accumulators.  Successive calls must
+ * cover increasing tree ids for the float folds to follow the reference's tree order.
+ * `out` (may be NULL) receives the per-tree arrays of these trees. */
+int rfx_grow(void* ctx, int tree_begin, int ntree, rfx_trees* out);
+
+/* Copy the accumulators to the host. */
+int rfx_results(void* ctx, rfx_accum* res);
+
+/* rfx_load + rfx_grow(0, ntree) + rfx_results. */
+int rfx_fit(void* ctx, const rfx_fit_params* prm, const rfx_inputs* in, int ntree,
+            rfx_trees* trees, rfx_accum* res);
+
+/* Proximity accumulation target: int32 upper triangle (i < j) of the OOB x in-bag
+ * co-membership counts C_ij = P_ij + P_ji over rows [0, R), packed row by row
+ * (index i*(2R-i-1)/2 + j-i-1), length R(R-1)/2.  The caller owns the device memory (so
+ * that it can reduce it across GPUs with NCCL); NULL makes the context allocate its own.
+ * Must be called after rfx_load. */
+int rfx_set_prox_buffer(void* ctx, int* upper_dev, int64_t len);
+/* Device pointer and length of the current proximity counts. */
+int rfx_get_prox_buffer(void* ctx, int** upper_dev, int64_t* len);
+/* Device pointers of the nout [N] and vote [N x nclass] accumulators (NCCL all-reduce). */
+int rfx_get_vote_buffers(void* ctx, int** nout_dev, int** votes_dev);
+
+/* finishprox of rows [row_begin, row_end) of the R x R matrix from upper-triangle counts
+ * and nout (both device): out_dev[(i-row_begin)*R + j] = float32 of the reference's
+ * double result (diag 1).  Stream-ordered on the context's stream. */
+int rfx_prox_finish(void* ctx, const int* upper_dev, const int* nout_dev, int R,
+                    int row_begin, int row_end, float* out_dev);
+
+/* Same as rfx_prox_finish on the context's own counts and nout, rows [row_begin, row_end)
+ * of the R x R matrix written to host memory out_host[(i-row_begin)*R + j]; processed in
+ * row blocks so the device scratch stays bounded (python/randomforest_py.cpp:2129-2155). */
+int rfx_prox_dense(void* ctx, int row_begin, int row_end, float* out_host);
+
+/* Regression, keep_tree_oob: vec_dev[i] <- fold of the per-tree OOB predictions of the
+ * trees grown so far, in tree order, starting from the incoming value (device, [N]). */
+int rfx_oob_fold(void* ctx, float* vec_dev);
+
+/* q_dev[i] = classwt[c] added votes_dev[i] times (float, sequential), the reference's
+ * vote accumulation (src/rf_random_forest.cpp:1500-1520); classwt NULL = 1.0. */
+int rfx_votes_to_q(void* ctx, const int* votes_dev, const float* classwt, int N, int nclass,
+                   float* q_dev);
+
+/* Stream-ordered device-to-host copy of `bytes` from src_dev (e.g. the proximity counts). */
+int rfx_copy_to_host(void* ctx, void* dst_host, const void* src_dev, size_t bytes);
+
+/* Wait for the context's stream. */
+int rfx_sync(void* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,745 @@
+// Host orchestration and the C ABI of rfx_b200 (declared in include/rfx_b200.h).
+//
+// One context = one CUDA device + one stream.  rfx_load puts the dataset in HBM (raw
+// values column-major, packed bin rows, bin edges, targets, the importance permutation);
+// rfx_grow grows batches of trees level by level (rfx_grow.cu) and folds each batch's OOB
+// votes, predictions, importance and proximity into device accumulators in tree order.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <random>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/rfx_b200.h"
+#include "rfx_device.cuh"
+#include "rfx_kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+struct RfxError : std::runtime_error {
+    int code;
+    RfxError(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define RFX_CUDA(call)                                                                     \
+    do {                                                                                   \
+        cudaError_t e_ = (call);                                                           \
+        if (e_ != cudaSuccess)                                                             \
+            throw RfxError(e_ == cudaErrorMemoryAllocation ? RFX_ERR_OOM : RFX_ERR_CUDA,   \
+                           std::string(#call) + ": " + cudaGetErrorString(e_));            \
+    } while (0)
+
+#define RFX_LAUNCH(name)                                                                   \
+    do {                                                                                   \
+        cudaError_t e_ = cudaGetLastError();                                               \
+        if (e_ != cudaSuccess)                                                             \
+            throw RfxError(RFX_ERR_CUDA, std::string("launch ") + name + ": " +            \
+                                             cudaGetErrorString(e_));                      \
+    } while (0)
+
+void require(bool ok, int code, const std::string& msg) {
+    if (!ok) throw RfxError(code, msg);
+}
+
+template <class F>
+int guarded(F&& f) {
+    try {
+        f();
+        return RFX_OK;
+    } catch (const RfxError& e) {
+        g_last_error = e.what();
+        return e.code;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return RFX_ERR_ARG;
+    }
+}
+
+// Device buffer that only grows.
+struct DBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+    void* get(size_t bytes) {
+        if (bytes == 0) bytes = 16;
+        if (bytes > cap) {
+            if (p) cudaFree(p);
+            p = nullptr;
+            cap = 0;
+            RFX_CUDA(cudaMalloc(&p, bytes));
+            cap = bytes;
+        }
+        return p;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+    }
+};
+
+size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct Ctx {
+    int device = 0;
+    int sm_count = 148;
+    cudaStream_t st = nullptr;
+    int* h_counters = nullptr;  // pinned
+
+    // loaded dataset
+    bool loaded = false;
+    rfx_fit_params prm{};
+    int N = 0, p = 0, nclass = 0, task = 0, M = 0, R = 0;
+    std::vector<int> labels0;   // 0-based labels (classification / unsupervised)
+    std::vector<float> classwt;
+    rfx::Data D{};
+    DBuf xc, rows, edges, nb, kind, cat, lab, yreg, yv, perm, ks, cumw, totw, keys_a, keys_b;
+    int perm_n = -1;
+
+    // accumulators
+    DBuf nout, votes, oob_sum, avimp, sqsd, prox_own, qtmp, cw_dev, tree_oob_all;
+    int* prox = nullptr;
+    int64_t prox_len = 0;
+    int trees_done = 0;
+    int tree_oob_cap = 0, tree_oob_n = 0;
+
+    // batch buffers
+    int Tcap = 0;
+    rfx::Batch B{};
+    DBuf b_nin, b_seg0, b_seg1, b_ninbag, b_oob, b_noob, b_mt, b_mtpos, b_status, b_bestvar,
+        b_xbest, b_treemap, b_nodeclass, b_nodepred, b_tnodewt, b_ndstart, b_ndcnt, b_ndbuf,
+        b_ndflag, b_ndcrit0, b_ndmaj, b_ndsum, b_ndkey, b_feat, b_lvl, b_srch, b_srchcnt,
+        b_srchoff, b_counters, b_oobleaf, b_used, b_right, b_rightimp, b_d2, b_d0, b_rr;
+
+    ~Ctx() {
+        DBuf* all[] = {&xc, &rows, &edges, &nb, &kind, &cat, &lab, &yreg, &yv, &perm, &ks, &cumw,
+                       &totw, &keys_a, &keys_b, &nout, &votes, &oob_sum, &avimp, &sqsd,
+                       &prox_own, &qtmp, &cw_dev, &tree_oob_all, &b_nin, &b_seg0, &b_seg1,
+                       &b_ninbag, &b_oob, &b_noob, &b_mt, &b_mtpos, &b_status, &b_bestvar,
+                       &b_xbest, &b_treemap, &b_nodeclass, &b_nodepred, &b_tnodewt, &b_ndstart,
+                       &b_ndcnt, &b_ndbuf, &b_ndflag, &b_ndcrit0, &b_ndmaj, &b_ndsum, &b_ndkey,
+                       &b_feat, &b_lvl, &b_srch, &b_srchcnt, &b_srchoff, &b_counters,
+                       &b_oobleaf, &b_used, &b_right, &b_rightimp, &b_d2, &b_d0, &b_rr};
+        cudaSetDevice(device);
+        if (st) cudaStreamSynchronize(st);
+        for (DBuf* b : all) b->release();
+        if (h_counters) cudaFreeHost(h_counters);
+        if (st) cudaStreamDestroy(st);
+    }
+};
+
+Ctx* as_ctx(void* c) {
+    require(c != nullptr, RFX_ERR_ARG, "null context");
+    Ctx* x = static_cast<Ctx*>(c);
+    RFX_CUDA(cudaSetDevice(x->device));
+    return x;
+}
+
+int grid_for(long long n, int threads, int cap) {
+    return (int)std::max(1LL, std::min((long long)cap, (n + threads - 1) / threads));
+}
+
+// Synthetic rows of RandomForest::fit_unsupervised (src/rf_random_forest.cpp:1068-1086):
+// column k is shuffled by std::shuffle with std::mt19937(iseed + k * 1000003).  Built on
+// the host with the same C++ standard library algorithm so the rows are bit-identical.
+void synthetic_rows(const float* X, int n, int p, int iseed, std::vector<float>& out) {
+    out.resize((size_t)2 * n * p);
+    std::memcpy(out.data(), X, sizeof(float) * (size_t)n * p);
+    std::vector<float> col(n);
+    for (int k = 0; k < p; ++k) {
+        std::mt19937 g((uint32_t)(iseed + k * 1000003));
+        for (int i = 0; i < n; ++i) col[i] = X[(size_t)i * p + k];
+        std::shuffle(col.begin(), col.end(), g);
+        for (int i = 0; i < n; ++i) out[(size_t)(n + i) * p + k] = col[i];
+    }
+}
+
+void alloc_batch(Ctx& c, int Tcap) {
+    const size_t N = c.N, M = c.M, T = Tcap, p = c.p;
+    rfx::Batch& B = c.B;
+    B.nin = (int*)c.b_nin.get(T * N * 4);
+    B.seg[0] = (int*)c.b_seg0.get(T * N * 4);
+    B.seg[1] = (int*)c.b_seg1.get(T * N * 4);
+    B.ninbag = (int*)c.b_ninbag.get(T * 4);
+    B.oob = (int*)c.b_oob.get(T * N * 4);
+    B.noob = (int*)c.b_noob.get(T * 4);
+    B.mt = (uint32_t*)c.b_mt.get(T * 624 * 4);
+    B.mt_pos = (int*)c.b_mtpos.get(T * 4);
+    B.status = (int*)c.b_status.get(T * M * 4);
+    B.bestvar = (int*)c.b_bestvar.get(T * M * 4);
+    B.xbest = (float*)c.b_xbest.get(T * M * 4);
+    B.treemap = (int*)c.b_treemap.get(T * M * 8);
+    B.nodeclass = (int*)c.b_nodeclass.get(T * M * 4);
+    B.nodepred = (float*)c.b_nodepred.get(T * M * 4);
+    B.tnodewt = (float*)c.b_tnodewt.get(T * M * 4);
+    B.nd_start = (int*)c.b_ndstart.get(T * M * 4);
+    B.nd_cnt = (int*)c.b_ndcnt.get(T * M * 4);
+    B.nd_buf = (uint8_t*)c.b_ndbuf.get(T * M);
+    B.nd_flag = (uint8_t*)c.b_ndflag.get(T * M);
+    B.nd_crit0 = (float*)c.b_ndcrit0.get(T * M * 4);
+    B.nd_maj = (int*)c.b_ndmaj.get(T * M * 4);
+    B.nd_sum = (float*)c.b_ndsum.get(T * M * 4);
+    B.nd_key = (unsigned long long*)c.b_ndkey.get(T * M * 8);
+    B.feat = (uint16_t*)c.b_feat.get(T * M * c.prm.mtry * 2);
+    int* lvl = (int*)c.b_lvl.get(T * 5 * 4 + 16);
+    B.lvl_lo = lvl;
+    B.lvl_hi = lvl + T;
+    B.nxt_lo = lvl + 2 * T;
+    B.nxt_hi = lvl + 3 * T;
+    B.nnode = lvl + 4 * T;
+    B.lvl_off = (int*)c.b_srchoff.get((T + 1) * 8);
+    B.srch_off = B.lvl_off + (T + 1);
+    B.srch = (int*)c.b_srch.get(T * M * 4);
+    B.srch_cnt = (int*)c.b_srchcnt.get(T * 4);
+    B.counters = (int*)c.b_counters.get(64);
+    B.oob_leaf = (int*)c.b_oobleaf.get(T * N * 4);
+    B.used = (uint8_t*)c.b_used.get(T * p);
+    B.right = (int*)c.b_right.get(T * 4);
+    B.rightimp = (int*)c.b_rightimp.get(T * p * 4);
+    B.rr = (float*)c.b_rr.get(T * p * 4);
+    if (c.task == RFX_TASK_REGRESSION && c.prm.compute_importance) {
+        B.d2 = (float*)c.b_d2.get(T * N * p * 4);
+        B.d0 = (float*)c.b_d0.get(T * N * 4);
+    } else {
+        B.d2 = nullptr;
+        B.d0 = nullptr;
+    }
+    B.tree_oob = nullptr;
+    B.M = c.M;
+    B.mtry = c.prm.mtry;
+    B.minsplit = c.task == RFX_TASK_REGRESSION ? 2 * c.prm.minndsize : c.prm.minndsize;
+    B.iseed = c.prm.iseed;
+    B.boot_seed = c.prm.boot_seed;
+    c.Tcap = Tcap;
+}
+
+void load(Ctx& c, const rfx_fit_params* prm, const rfx_inputs* in) {
+    require(prm && in && in->X, RFX_ERR_ARG, "null params / inputs / X");
+    const rfx_fit_params P = *prm;
+    require(P.task >= 0 && P.task <= 2, RFX_ERR_ARG, "task must be 0, 1 or 2");
+    require(P.n >= 1 && P.p >= 1, RFX_ERR_ARG, "n and p must be positive");
+    require(P.mtry >= 1 && P.mtry < (1 << 24), RFX_ERR_ARG, "mtry must be >= 1");
+    require(P.maxnode >= 1, RFX_ERR_ARG, "maxnode must be >= 1");
+    require(P.nbins >= 2 && P.nbins <= 256, RFX_ERR_ARG, "nbins must be in [2, 256]");
+    require(P.minndsize >= 0, RFX_ERR_ARG, "minndsize must be >= 0");
+    require(P.task != RFX_TASK_CLASSIFICATION || in->y_class, RFX_ERR_ARG, "y_class required");
+    require(P.task != RFX_TASK_REGRESSION || in->y_reg, RFX_ERR_ARG, "y_reg required");
+    c.loaded = false;
+    c.prm = P;
+    c.task = P.task;
+    c.p = P.p;
+    c.M = P.maxnode;
+    const int n = P.n, p = P.p;
+    std::vector<float> xs;
+    const float* X = in->X;
+    c.labels0.clear();
+    if (P.task == RFX_TASK_UNSUPERVISED) {
+        synthetic_rows(in->X, n, p, P.iseed, xs);
+        X = xs.data();
+        c.N = 2 * n;
+        c.nclass = 2;
+        c.labels0.assign(c.N, 0);
+        std::fill(c.labels0.begin(), c.labels0.begin() + n, 1);
+    } else if (P.task == RFX_TASK_CLASSIFICATION) {
+        // setup_classification_task (src/rf_random_forest.cpp:3287-3309): labels -> rank
+        // among the sorted distinct labels.
+        c.N = n;
+        std::vector<int> u(in->y_class, in->y_class + n);
+        std::sort(u.begin(), u.end());
+        u.erase(std::unique(u.begin(), u.end()), u.end());
+        c.nclass = (int)u.size();
+        c.labels0.resize(n);
+        for (int i = 0; i < n; ++i)
+            c.labels0[i] = (int)(std::lower_bound(u.begin(), u.end(), in->y_class[i]) - u.begin());
+    } else {
+        c.N = n;
+        c.nclass = 1;
+    }
+    require(c.nclass <= rfx::kMaxClass, RFX_ERR_UNSUPPORTED,
+            "more than 32 classes is not supported by the device histograms");
+    const size_t N = c.N;
+    std::vector<int> catv(p, 1);
+    if (in->cat) catv.assign(in->cat, in->cat + p);
+    bool has_cat = false;
+    for (int f = 0; f < p; ++f) {
+        require(catv[f] >= 1, RFX_ERR_ARG, "cat[f] must be >= 1");
+        has_cat |= catv[f] != 1;
+    }
+    c.R = P.prox_rows > 0 ? std::min<int>(P.prox_rows, (int)N) : (int)N;
+    require(!(P.compute_proximity && has_cat), RFX_ERR_UNSUPPORTED,
+            "proximity with categorical features is not supported yet");
+    c.classwt.clear();
+    if (P.task == RFX_TASK_CLASSIFICATION && in->classwt)
+        c.classwt.assign(in->classwt, in->classwt + c.nclass);
+
+    cudaStream_t st = c.st;
+    rfx::Data& D = c.D;
+    D.N = (int)N;
+    D.p = p;
+    D.nclass = c.nclass;
+    D.task = c.task;
+    D.ro = (int)round_up(p, 8);  // the regression target is read as an 8-byte float2
+    D.rs = (int)round_up(D.ro + 8, 16);
+    D.maxcat = P.maxcat > 0 ? P.maxcat : 10;
+    D.has_cat = has_cat ? 1 : 0;
+    float* xc = (float*)c.xc.get(N * p * 4);
+    uint8_t* rows = (uint8_t*)c.rows.get(N * D.rs);
+    float* edges = (float*)c.edges.get((size_t)p * 257 * 4);
+    int* nb = (int*)c.nb.get(p * 4);
+    int* kind = (int*)c.kind.get(p * 4);
+    int* catd = (int*)c.cat.get(p * 4);
+    int* lab = (int*)c.lab.get(N * 4);
+    uint32_t* ka = (uint32_t*)c.keys_a.get(N * p * 4);
+    uint32_t* kb = (uint32_t*)c.keys_b.get(N * p * 4);
+    RFX_CUDA(cudaMemcpyAsync(ka, X, N * p * 4, cudaMemcpyHostToDevice, st));
+    RFX_CUDA(cudaMemcpyAsync(catd, catv.data(), p * 4, cudaMemcpyHostToDevice, st));
+    RFX_CUDA(cudaMemsetAsync(rows, 0, N * D.rs, st));
+    float* yregp = nullptr;
+    float* yvp = nullptr;
+    if (c.task == RFX_TASK_REGRESSION) {
+        yregp = (float*)c.yreg.get(N * 4);
+        yvp = (float*)c.yv.get(N * 4);
+        RFX_CUDA(cudaMemcpyAsync(yregp, in->y_reg, N * 4, cudaMemcpyHostToDevice, st));
+        rfx::k_regr_targets<<<grid_for(N, 256, 4096), 256, 0, st>>>(yregp, (int)N, lab, yvp);
+        RFX_LAUNCH("k_regr_targets");
+    } else {
+        RFX_CUDA(cudaMemcpyAsync(lab, c.labels0.data(), N * 4, cudaMemcpyHostToDevice, st));
+    }
+    {
+        dim3 grid((unsigned)((N + 31) / 32), (unsigned)((p + 31) / 32));
+        rfx::k_transpose<<<grid, dim3(32, 8), 0, st>>>(reinterpret_cast<const float*>(ka), (int)N, p, xc);
+        RFX_LAUNCH("k_transpose");
+    }
+    rfx::k_sort_columns<<<p, 1024, 0, st>>>(xc, (int)N, catd, ka, kb);
+    RFX_LAUNCH("k_sort_columns");
+    rfx::k_edges<<<p, 1024, 0, st>>>(kb, (int)N, catd, P.nbins, reinterpret_cast<float*>(ka), edges, nb, kind);
+    RFX_LAUNCH("k_edges");
+    D.xc = xc;
+    D.rows = rows;
+    D.edges = edges;
+    D.nb = nb;
+    D.kind = kind;
+    D.cat = catd;
+    D.lab = lab;
+    D.yreg = yregp;
+    D.yv = yvp;
+    rfx::k_pack_rows<<<grid_for(N * p, 256, 8192), 256, 0, st>>>(D);
+    RFX_LAUNCH("k_pack_rows");
+    // bootstrap weights (ignored by the unsupervised fit: src/rf_random_forest.cpp:1043)
+    D.cumw = nullptr;
+    D.totw = 0.0f;
+    if (in->sample_weights && c.task != RFX_TASK_UNSUPERVISED) {
+        float* w = (float*)c.keys_b.get(N * p * 4);  // scratch
+        float* cum = (float*)c.cumw.get(N * 4);
+        float* tot = (float*)c.totw.get(16);
+        RFX_CUDA(cudaMemcpyAsync(w, in->sample_weights, N * 4, cudaMemcpyHostToDevice, st));
+        rfx::k_cumw<<<1, 1, 0, st>>>(w, (int)N, cum, tot);
+        RFX_LAUNCH("k_cumw");
+        float h = 0.0f;
+        RFX_CUDA(cudaMemcpyAsync(&h, tot, 4, cudaMemcpyDeviceToHost, st));
+        RFX_CUDA(cudaStreamSynchronize(st));
+        D.cumw = cum;
+        D.totw = h;
+    }
+    // importance permutation depends on N only
+    if (c.perm_n != (int)N) {
+        int* pm = (int*)c.perm.get(N * 4);
+        int* kss = (int*)c.ks.get(N * 4);
+        rfx::k_permutation<<<1, 256, 0, st>>>((int)N, 42u, kss, pm);
+        RFX_LAUNCH("k_permutation");
+        c.perm_n = (int)N;
+    }
+    D.perm = (const int*)c.perm.p;
+    // accumulators
+    int* no = (int*)c.nout.get(N * 4);
+    RFX_CUDA(cudaMemsetAsync(no, 0, N * 4, st));
+    if (c.nclass > 1) {
+        int* v = (int*)c.votes.get(N * c.nclass * 4);
+        RFX_CUDA(cudaMemsetAsync(v, 0, N * c.nclass * 4, st));
+    } else {
+        float* o = (float*)c.oob_sum.get(N * 4);
+        RFX_CUDA(cudaMemsetAsync(o, 0, N * 4, st));
+    }
+    float* av = (float*)c.avimp.get(p * 4);
+    float* sq = (float*)c.sqsd.get(p * 4);
+    RFX_CUDA(cudaMemsetAsync(av, 0, p * 4, st));
+    RFX_CUDA(cudaMemsetAsync(sq, 0, p * 4, st));
+    c.prox = nullptr;
+    c.prox_len = 0;
+    if (P.compute_proximity) {
+        c.prox_len = (int64_t)c.R * (c.R - 1) / 2;
+        c.prox = (int*)c.prox_own.get((size_t)c.prox_len * 4);
+        RFX_CUDA(cudaMemsetAsync(c.prox, 0, (size_t)c.prox_len * 4, st));
+    }
+    c.trees_done = 0;
+    c.tree_oob_n = 0;
+    c.tree_oob_cap = 0;
+    // batch capacity
+    size_t per_tree = N * 4 * 6 + (size_t)c.M * (4 * 12 + 2 * P.mtry + 16) + (size_t)p * 16;
+    if (c.task == RFX_TASK_REGRESSION && P.compute_importance) per_tree += N * (size_t)(p + 1) * 4;
+    size_t free_b = 0, total_b = 0;
+    RFX_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    const size_t budget = std::min<size_t>(free_b / 2, (size_t)32 << 30);
+    int Tcap = P.batch_trees > 0 ? P.batch_trees : 256;
+    Tcap = (int)std::max<size_t>(1, std::min<size_t>((size_t)Tcap, budget / per_tree));
+    Tcap = std::min(Tcap, 4096);
+    alloc_batch(c, Tcap);
+    RFX_CUDA(cudaStreamSynchronize(st));
+    c.loaded = true;
+}
+
+// Dynamic shared memory layout of k_hist.
+struct HistCfg {
+    int warps, stage_rows, warp_bytes, smem, grid;
+};
+
+HistCfg hist_cfg(Ctx& c) {
+    HistCfg h;
+    h.warps = std::min(c.prm.mtry, 16);
+    h.stage_rows = std::max(32, std::min(256, 16384 / c.D.rs));
+    if (c.nclass == 1) h.warp_bytes = (int)round_up(288 + 5 * 1024, 16);
+    else h.warp_bytes = (int)round_up(288 + 1024 * c.nclass + 128, 16);
+    h.smem = h.stage_rows * c.D.rs + h.warps * h.warp_bytes;
+    static thread_local int configured_dev = -1;
+    static thread_local int configured_smem = -1;
+    if (configured_dev != c.device || configured_smem < h.smem) {
+        RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      std::max(h.smem, 48 * 1024)));
+        configured_dev = c.device;
+        configured_smem = h.smem;
+    }
+    int per_sm = 0;
+    RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist, h.warps * 32, h.smem));
+    h.grid = c.sm_count * std::max(1, per_sm);
+    return h;
+}
+
+void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
+    cudaStream_t st = c.st;
+    rfx::Batch B = c.B;
+    B.T = T;
+    B.tree0 = tree0;
+    const size_t N = c.N, M = c.M, p = c.p;
+    const bool keep = c.prm.keep_tree_oob && c.task == RFX_TASK_REGRESSION;
+    if (keep) {
+        if (c.tree_oob_n + T > c.tree_oob_cap) {
+            // grow the per-tree OOB prediction store, keeping what is there
+            const int ncap = std::max(c.tree_oob_n + T, 2 * c.tree_oob_cap);
+            DBuf nb;
+            float* np = (float*)nb.get((size_t)ncap * N * 4);
+            if (c.tree_oob_n > 0)
+                RFX_CUDA(cudaMemcpyAsync(np, c.tree_oob_all.p, (size_t)c.tree_oob_n * N * 4,
+                                         cudaMemcpyDeviceToDevice, st));
+            RFX_CUDA(cudaStreamSynchronize(st));
+            c.tree_oob_all.release();
+            c.tree_oob_all = nb;
+            nb.p = nullptr;
+            c.tree_oob_cap = ncap;
+        }
+        B.tree_oob = (float*)c.tree_oob_all.p + (size_t)c.tree_oob_n * N;
+    }
+    RFX_CUDA(cudaMemsetAsync(B.nin, 0, T * N * 4, st));
+    RFX_CUDA(cudaMemsetAsync(B.status, 0, T * M * 4, st));
+    RFX_CUDA(cudaMemsetAsync(B.bestvar, 0, T * M * 4, st));
+    RFX_CUDA(cudaMemsetAsync(B.xbest, 0, T * M * 4, st));
+    RFX_CUDA(cudaMemsetAsync(B.treemap, 0, T * M * 8, st));
+    RFX_CUDA(cudaMemsetAsync(B.nodeclass, 0, T * M * 4, st));
+    RFX_CUDA(cudaMemsetAsync(B.nodepred, 0, T * M * 4, st));
+    RFX_CUDA(cudaMemsetAsync(B.tnodewt, 0, T * M * 4, st));
+    RFX_CUDA(cudaMemsetAsync(B.oob_leaf, 0xff, T * N * 4, st));
+    RFX_CUDA(cudaMemsetAsync(B.counters, 0, 64, st));
+    RFX_CUDA(cudaMemsetAsync(B.right, 0, T * 4, st));
+    RFX_CUDA(cudaMemsetAsync(B.rightimp, 0, T * p * 4, st));
+    const rfx::Data D = c.D;
+    rfx::k_bootstrap<<<T, 256, 0, st>>>(D, B);
+    RFX_LAUNCH("k_bootstrap");
+    rfx::k_compact<<<T, 1024, 0, st>>>(D, B);
+    RFX_LAUNCH("k_compact");
+    const HistCfg hc = hist_cfg(c);
+    const int gw = c.sm_count * 8;
+    int cur = 0;
+    for (int level = 0;; ++level) {
+        require(level < 1000000, RFX_ERR_DEVICE, "tree growth did not terminate");
+        rfx::k_level_begin<<<1, 1024, 0, st>>>(B);
+        rfx::k_node_eval<<<gw, 256, 0, st>>>(D, B, cur);
+        rfx::k_draw<<<T, 256, 0, st>>>(D, B);
+        rfx::k_srch_scan<<<1, 1024, 0, st>>>(B);
+        rfx::k_hist<<<hc.grid, hc.warps * 32, hc.smem, st>>>(D, B, cur, hc.warps, hc.stage_rows, hc.warp_bytes);
+        rfx::k_commit<<<T, 1024, 0, st>>>(D, B);
+        rfx::k_partition<<<gw, 256, 0, st>>>(D, B, cur);
+        RFX_LAUNCH("level kernels");
+        RFX_CUDA(cudaMemcpyAsync(c.h_counters, B.counters, 16, cudaMemcpyDeviceToHost, st));
+        RFX_CUDA(cudaStreamSynchronize(st));
+        if (c.h_counters[2] == 0) break;
+        cur ^= 1;
+    }
+    const dim3 rg((unsigned)((N + 255) / 256), (unsigned)T);
+    rfx::k_oob_drop<<<rg, 256, 0, st>>>(D, B);
+    rfx::k_votes<<<(unsigned)((N + 255) / 256), 256, 0, st>>>(
+        D, B, (int*)c.nout.p, c.nclass > 1 ? (int*)c.votes.p : nullptr,
+        c.nclass == 1 ? (float*)c.oob_sum.p : nullptr, B.tree_oob, (int)N);
+    RFX_LAUNCH("oob kernels");
+    if (c.prm.compute_importance) {
+        rfx::k_imp_used<<<T, 256, 0, st>>>(D, B);
+        if (c.nclass > 1) {
+            rfx::k_imp_class<<<rg, 256, 0, st>>>(D, B);
+            rfx::k_imp_class_rr<<<T, 256, 0, st>>>(D, B);
+        } else {
+            rfx::k_imp_regr<<<rg, 256, 0, st>>>(D, B);
+            rfx::k_imp_regr_sum<<<T, (int)std::min<size_t>(1024, round_up(p, 32)), 0, st>>>(D, B);
+        }
+        rfx::k_imp_fold<<<1, 256, 0, st>>>(D, B, (float*)c.avimp.p, (float*)c.sqsd.p);
+        RFX_LAUNCH("importance kernels");
+    }
+    if (c.prm.compute_proximity) {
+        rfx::k_prox<<<rg, 256, 0, st>>>(D, B, c.R, c.prox);
+        RFX_LAUNCH("k_prox");
+    }
+    if (keep) c.tree_oob_n += T;
+    if (out) {
+        auto cp = [&](void* dst, const void* src, size_t elems, size_t esz) {
+            if (dst) RFX_CUDA(cudaMemcpyAsync((char*)dst + (size_t)out_off * elems * esz, src,
+                                              (size_t)T * elems * esz, cudaMemcpyDeviceToHost, st));
+        };
+        cp(out->nodestatus, B.status, M, 4);
+        cp(out->bestvar, B.bestvar, M, 4);
+        cp(out->xbestsplit, B.xbest, M, 4);
+        cp(out->treemap, B.treemap, 2 * M, 4);
+        cp(out->nodeclass, B.nodeclass, M, 4);
+        cp(out->nnode, B.nnode, 1, 4);
+        cp(out->nodepred, B.nodepred, M, 4);
+        cp(out->tnodewt, B.tnodewt, M, 4);
+        cp(out->nin, B.nin, N, 4);
+        cp(out->oob_leaf, B.oob_leaf, N, 4);
+        if (c.prm.compute_importance) {
+            cp(out->tree_rr, B.rr, p, 4);
+            if (out->tree_used) {
+                if (c.nclass > 1) cp(out->tree_used, B.used, p, 1);
+                else std::memset(out->tree_used + (size_t)out_off * p, 1, (size_t)T * p);
+            }
+        }
+    }
+    RFX_CUDA(cudaStreamSynchronize(st));
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* rfx_last_error(void) { return g_last_error.c_str(); }
+int rfx_abi_version(void) { return RFX_ABI_VERSION; }
+
+int rfx_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+void* rfx_create(int device) {
+    Ctx* c = nullptr;
+    const int rc = guarded([&] {
+        int n = 0;
+        RFX_CUDA(cudaGetDeviceCount(&n));
+        require(device >= 0 && device < n, RFX_ERR_ARG, "device index out of range");
+        c = new Ctx();
+        c->device = device;
+        RFX_CUDA(cudaSetDevice(device));
+        RFX_CUDA(cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device));
+        RFX_CUDA(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking));
+        RFX_CUDA(cudaMallocHost(&c->h_counters, 64));
+    });
+    if (rc != RFX_OK) {
+        delete c;
+        return nullptr;
+    }
+    return c;
+}
+
+void rfx_destroy(void* ctx) { delete static_cast<Ctx*>(ctx); }
+
+int rfx_load(void* ctx, const rfx_fit_params* prm, const rfx_inputs* in) {
+    return guarded([&] { load(*as_ctx(ctx), prm, in); });
+}
+
+int rfx_grow(void* ctx, int tree_begin, int ntree, rfx_trees* out) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(c.loaded, RFX_ERR_STATE, "rfx_grow before rfx_load");
+        require(tree_begin >= 0 && ntree >= 0, RFX_ERR_ARG, "bad tree range");
+        for (int b0 = 0; b0 < ntree; b0 += c.Tcap) {
+            const int T = std::min(c.Tcap, ntree - b0);
+            grow_batch(c, tree_begin + b0, T, out, b0);
+        }
+        c.trees_done += ntree;
+    });
+}
+
+int rfx_results(void* ctx, rfx_accum* r) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(c.loaded, RFX_ERR_STATE, "rfx_results before rfx_load");
+        require(r != nullptr, RFX_ERR_ARG, "null results");
+        const size_t N = c.N;
+        r->nclass = c.nclass;
+        r->N = (int)N;
+        cudaStream_t st = c.st;
+        if (r->nout) RFX_CUDA(cudaMemcpyAsync(r->nout, c.nout.p, N * 4, cudaMemcpyDeviceToHost, st));
+        if (c.nclass > 1) {
+            if (r->votes)
+                RFX_CUDA(cudaMemcpyAsync(r->votes, c.votes.p, N * c.nclass * 4, cudaMemcpyDeviceToHost, st));
+            if (r->q) {
+                float* q = (float*)c.qtmp.get(N * c.nclass * 4);
+                float* w = nullptr;
+                if (!c.classwt.empty()) {
+                    w = (float*)c.cw_dev.get(c.nclass * 4);
+                    RFX_CUDA(cudaMemcpyAsync(w, c.classwt.data(), c.nclass * 4, cudaMemcpyHostToDevice, st));
+                }
+                rfx::k_votes_to_q<<<grid_for(N * c.nclass, 256, 8192), 256, 0, st>>>(
+                    (const int*)c.votes.p, w, (int)N, c.nclass, q);
+                RFX_LAUNCH("k_votes_to_q");
+                RFX_CUDA(cudaMemcpyAsync(r->q, q, N * c.nclass * 4, cudaMemcpyDeviceToHost, st));
+            }
+            if (r->labels) std::memcpy(r->labels, c.labels0.data(), N * 4);
+        } else if (r->oob_sum) {
+            RFX_CUDA(cudaMemcpyAsync(r->oob_sum, c.oob_sum.p, N * 4, cudaMemcpyDeviceToHost, st));
+        }
+        if (r->avimp) RFX_CUDA(cudaMemcpyAsync(r->avimp, c.avimp.p, c.p * 4, cudaMemcpyDeviceToHost, st));
+        if (r->sqsd) RFX_CUDA(cudaMemcpyAsync(r->sqsd, c.sqsd.p, c.p * 4, cudaMemcpyDeviceToHost, st));
+        RFX_CUDA(cudaStreamSynchronize(st));
+    });
+}
+
+int rfx_fit(void* ctx, const rfx_fit_params* prm, const rfx_inputs* in, int ntree,
+            rfx_trees* trees, rfx_accum* res) {
+    int rc = rfx_load(ctx, prm, in);
+    if (rc != RFX_OK) return rc;
+    rc = rfx_grow(ctx, 0, ntree, trees);
+    if (rc != RFX_OK) return rc;
+    return res ? rfx_results(ctx, res) : RFX_OK;
+}
+
+int rfx_set_prox_buffer(void* ctx, int* upper_dev, int64_t len) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(c.loaded && c.prm.compute_proximity, RFX_ERR_STATE, "proximity is not enabled");
+        require(len == (int64_t)c.R * (c.R - 1) / 2, RFX_ERR_ARG, "proximity buffer length mismatch");
+        if (upper_dev == nullptr) {
+            c.prox = (int*)c.prox_own.get((size_t)len * 4);
+        } else {
+            c.prox = upper_dev;
+        }
+        RFX_CUDA(cudaMemsetAsync(c.prox, 0, (size_t)len * 4, c.st));
+        RFX_CUDA(cudaStreamSynchronize(c.st));
+    });
+}
+
+int rfx_get_prox_buffer(void* ctx, int** upper_dev, int64_t* len) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(upper_dev && len, RFX_ERR_ARG, "null output");
+        *upper_dev = c.prox;
+        *len = c.prox_len;
+    });
+}
+
+int rfx_get_vote_buffers(void* ctx, int** nout_dev, int** votes_dev) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(c.loaded, RFX_ERR_STATE, "not loaded");
+        if (nout_dev) *nout_dev = (int*)c.nout.p;
+        if (votes_dev) *votes_dev = c.nclass > 1 ? (int*)c.votes.p : nullptr;
+    });
+}
+
+int rfx_prox_finish(void* ctx, const int* upper_dev, const int* nout_dev, int R, int row_begin,
+                    int row_end, float* out_dev) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(upper_dev && nout_dev && out_dev, RFX_ERR_ARG, "null pointer");
+        require(R >= 1 && row_begin >= 0 && row_begin <= row_end && row_end <= R, RFX_ERR_ARG,
+                "bad row range");
+        const long long total = (long long)(row_end - row_begin) * R;
+        rfx::k_prox_finish<<<grid_for(total, 256, c.sm_count * 16), 256, 0, c.st>>>(
+            upper_dev, nout_dev, R, row_begin, row_end, out_dev);
+        RFX_LAUNCH("k_prox_finish");
+        RFX_CUDA(cudaStreamSynchronize(c.st));
+    });
+}
+
+int rfx_prox_dense(void* ctx, int row_begin, int row_end, float* out_host) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(c.loaded && c.prox, RFX_ERR_STATE, "proximity was not computed");
+        require(out_host, RFX_ERR_ARG, "null output");
+        const int R = c.R;
+        require(row_begin >= 0 && row_begin <= row_end && row_end <= R, RFX_ERR_ARG, "bad row range");
+        const int rows_per = (int)std::max<long long>(1, ((long long)256 << 20) / ((long long)R * 4));
+        float* tmp = (float*)c.qtmp.get((size_t)std::min(rows_per, std::max(1, row_end - row_begin)) * R * 4);
+        for (int r0 = row_begin; r0 < row_end; r0 += rows_per) {
+            const int r1 = std::min(row_end, r0 + rows_per);
+            const long long total = (long long)(r1 - r0) * R;
+            rfx::k_prox_finish<<<grid_for(total, 256, c.sm_count * 16), 256, 0, c.st>>>(
+                c.prox, (const int*)c.nout.p, R, r0, r1, tmp);
+            RFX_LAUNCH("k_prox_finish");
+            RFX_CUDA(cudaMemcpyAsync(out_host + (size_t)(r0 - row_begin) * R, tmp, (size_t)total * 4,
+                                     cudaMemcpyDeviceToHost, c.st));
+            RFX_CUDA(cudaStreamSynchronize(c.st));
+        }
+    });
+}
+
+int rfx_oob_fold(void* ctx, float* vec_dev) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(c.loaded && c.prm.keep_tree_oob && c.task == RFX_TASK_REGRESSION, RFX_ERR_STATE,
+                "keep_tree_oob regression fit required");
+        if (c.tree_oob_n > 0) {
+            rfx::k_oob_fold<<<(c.N + 255) / 256, 256, 0, c.st>>>((const float*)c.tree_oob_all.p,
+                                                               c.tree_oob_n, c.N, vec_dev);
+            RFX_LAUNCH("k_oob_fold");
+        }
+        RFX_CUDA(cudaStreamSynchronize(c.st));
+    });
+}
+
+int rfx_votes_to_q(void* ctx, const int* votes_dev, const float* classwt, int N, int nclass,
+                   float* q_dev) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(votes_dev && q_dev && N >= 0 && nclass >= 1, RFX_ERR_ARG, "bad arguments");
+        float* w = nullptr;
+        if (classwt) {
+            w = (float*)c.cw_dev.get(nclass * 4);
+            RFX_CUDA(cudaMemcpyAsync(w, classwt, nclass * 4, cudaMemcpyHostToDevice, c.st));
+        }
+        rfx::k_votes_to_q<<<grid_for((long long)N * nclass, 256, 8192), 256, 0, c.st>>>(
+            votes_dev, w, N, nclass, q_dev);
+        RFX_LAUNCH("k_votes_to_q");
+        RFX_CUDA(cudaStreamSynchronize(c.st));
+    });
+}
+
+int rfx_copy_to_host(void* ctx, void* dst_host, const void* src_dev, size_t bytes) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(dst_host && src_dev, RFX_ERR_ARG, "null pointer");
+        RFX_CUDA(cudaMemcpyAsync(dst_host, src_dev, bytes, cudaMemcpyDeviceToHost, c.st));
+        RFX_CUDA(cudaStreamSynchronize(c.st));
+    });
+}
+
+int rfx_sync(void* ctx) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        RFX_CUDA(cudaStreamSynchronize(c.st));
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,317 @@
+// After growth: OOB leaf drop, OOB votes / predictions, permutation importance, proximity
+// co-membership counts and the finishprox normalisation.
+#include "rfx_device.cuh"
+#include "rfx_kernels.h"
+
+namespace rfx {
+
+// cpu_testreebag walk (src/rf_testreebag.cpp:37-121): quantitative (cat <= 2) splits go
+// left when x <= xbestsplit; categorical ones go right (the histogram grower leaves
+// catgoleft empty); at most 1000 steps; a walk that does not end on a terminal node
+// reports the root.  `feat_mask` collects the split features met on the way (p <= 256).
+__device__ __forceinline__ int walk_oob(const Data& D, const int* st, const int* bv,
+                                        const float* xb, const int* tm, int row,
+                                        uint32_t* feat_mask) {
+    int kt = 0, steps = 0;
+    while (st[kt] == 1 && steps < 1000) {
+        ++steps;
+        const int mv = bv[kt];
+        if (feat_mask && mv < 256) feat_mask[mv >> 5] |= 1u << (mv & 31);
+        if (D.cat[mv] <= 2) kt = D.xc[(size_t)mv * D.N + row] <= xb[kt] ? tm[2 * kt] : tm[2 * kt + 1];
+        else kt = tm[2 * kt + 1];
+        if (st[kt] != 1) break;
+    }
+    return (st[kt] == -1 || st[kt] == 2) ? kt : 0;
+}
+
+// OOB leaf of every out-of-bag row of every tree.  grid (rows, trees).
+__global__ void k_oob_drop(Data D, Batch B) {
+    const int t = blockIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= B.noob[t]) return;
+    const size_t mo = (size_t)t * B.M;
+    const int row = B.oob[(size_t)t * D.N + j];
+    B.oob_leaf[(size_t)t * D.N + row] =
+        walk_oob(D, B.status + mo, B.bestvar + mo, B.xbest + mo, B.treemap + 2 * mo, row, nullptr);
+}
+
+// Vote / prediction accumulation in tree order (src/rf_random_forest.cpp:1500-1535):
+// one thread per row walks the batch's trees in order, so the regression float sum is the
+// reference's sequential sum.  Classification keeps integer vote counts.
+__global__ void k_votes(Data D, Batch B, int* nout, int* votes, float* oob_sum,
+                        float* tree_oob, int tree_oob_stride) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= D.N) return;
+    int no = 0;
+    float acc = oob_sum ? oob_sum[i] : 0.0f;
+    for (int t = 0; t < B.T; ++t) {
+        const int leaf = B.oob_leaf[(size_t)t * D.N + i];
+        float v = __int_as_float(0x7fc00000);
+        if (leaf >= 0) {
+            ++no;
+            const size_t m = (size_t)t * B.M + leaf;
+            if (D.nclass == 1) {
+                v = B.nodepred[m];
+                acc += v;
+            } else {
+                const int c = B.nodeclass[m];
+                if (c >= 0 && c < D.nclass) votes[(size_t)i * D.nclass + c] += 1;
+            }
+        }
+        if (tree_oob) tree_oob[(size_t)t * tree_oob_stride + i] = v;
+    }
+    nout[i] += no;
+    if (oob_sum) oob_sum[i] = acc;
+}
+
+// Features used by the splits of each tree (src/rf_varimp.cpp:265-270).  grid (trees).
+__global__ void k_imp_used(Data D, Batch B) {
+    const int t = blockIdx.x;
+    uint8_t* u = B.used + (size_t)t * D.p;
+    for (int k = threadIdx.x; k < D.p; k += blockDim.x) u[k] = 0;
+    __syncthreads();
+    const size_t mo = (size_t)t * B.M;
+    const int nn = B.nnode[t];
+    for (int k = threadIdx.x; k < nn; k += blockDim.x)
+        if (B.status[mo + k] != -1) u[B.bestvar[mo + k]] = 1;
+}
+
+// Permuted walk of cpu_testreeimp_batched (src/rf_varimp.cpp:74-143): feature `mr` is
+// read from row prow, the others from row `row`; returns the terminal's class (or -1).
+__device__ __forceinline__ int walk_perm_class(const Data& D, const int* st, const int* bv,
+                                               const float* xb, const int* tm, const int* ncls,
+                                               int nnode, int row, int prow, int mr) {
+    int kt = 0;
+    for (int k = 0; k < nnode; ++k) {
+        if (st[kt] == -1) return ncls[kt];
+        const int m = bv[kt];
+        if (m < 0 || m >= D.p) break;
+        const float v = D.xc[(size_t)m * D.N + (m == mr ? prow : row)];
+        if (D.cat[m] <= 2) kt = v <= xb[kt] ? tm[2 * kt] : tm[2 * kt + 1];
+        else {
+            const int j = (int)(v + 0.5f);
+            kt = (j >= 0 && j < D.maxcat) ? tm[2 * kt + 1] : tm[2 * kt];
+        }
+        if (kt <= 0) return ncls[0];
+    }
+    return -1;
+}
+
+// Permuted walk of cpu_predict_regression (src/rf_varimp.cpp:427-475).
+__device__ __forceinline__ float walk_perm_regr(const Data& D, const int* st, const int* bv,
+                                                const float* xb, const int* tm, const float* np,
+                                                int nnode, int row, int prow, int mr) {
+    int kt = 0;
+    for (int k = 0; k < nnode; ++k) {
+        if (st[kt] == -1) return np[kt];
+        const int m = bv[kt];
+        if (m < 0 || m >= D.p) break;
+        const float v = D.xc[(size_t)m * D.N + (m == mr ? prow : row)];
+        if (D.cat[m] <= 2) kt = v <= xb[kt] ? tm[2 * kt] : tm[2 * kt + 1];
+        else {
+            const int j = (int)(v + 0.5f);
+            if (j >= 0 && j < D.maxcat) kt = tm[2 * kt + 1];
+            else break;
+        }
+        if (kt < 0 || kt >= nnode) break;
+    }
+    return 0.0f;
+}
+
+// Classification importance counts (cpu_varimp, src/rf_varimp.cpp:218-427): correct OOB
+// votes unpermuted (right) and with each used feature permuted (rightimp).  A feature that
+// the row's own path never tests cannot change its terminal node, so only path features
+// are re-walked.  grid (rows, trees), 256 threads.
+__global__ void __launch_bounds__(256) k_imp_class(Data D, Batch B) {
+    const int t = blockIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    const int noob = B.noob[t];
+    const size_t mo = (size_t)t * B.M;
+    const int *st = B.status + mo, *bv = B.bestvar + mo, *tm = B.treemap + 2 * mo, *nc = B.nodeclass + mo;
+    const float* xb = B.xbest + mo;
+    const bool valid = j < noob;
+    uint32_t mask[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int row = 0, lab = 0, cls0 = -1;
+    if (valid) {
+        row = B.oob[(size_t)t * D.N + j];
+        lab = D.lab[row];
+        walk_oob(D, st, bv, xb, tm, row, mask);
+        cls0 = nc[B.oob_leaf[(size_t)t * D.N + row]];
+    }
+    const bool wide = D.p > 256 || D.has_cat;
+    const int ok0 = valid && cls0 == lab;
+    const int s0 = __reduce_add_sync(kFull, ok0);
+    if (lane == 0 && s0) atomicAdd(&B.right[t], s0);
+    const uint8_t* used = B.used + (size_t)t * D.p;
+    const int nn = B.nnode[t];
+    const int prow = valid ? D.perm[row] : 0;
+    for (int k = 0; k < D.p; ++k) {
+        if (!used[k]) continue;
+        int ok = ok0;
+        if (valid && (wide || ((mask[k >> 5] >> (k & 31)) & 1u)))
+            ok = walk_perm_class(D, st, bv, xb, tm, nc, nn, row, prow, k) == lab;
+        const int s = __reduce_add_sync(kFull, ok);
+        if (lane == 0 && s) atomicAdd(&B.rightimp[(size_t)t * D.p + k], s);
+    }
+}
+
+// rr = (right - rightimp) / noob per used feature (src/rf_varimp.cpp:345-348).
+__global__ void k_imp_class_rr(Data D, Batch B) {
+    const int t = blockIdx.x;
+    const float noob = (float)B.noob[t];
+    for (int k = threadIdx.x; k < D.p; k += blockDim.x) {
+        const size_t q = (size_t)t * D.p + k;
+        B.rr[q] = B.used[q] ? ((float)B.right[t] - (float)B.rightimp[q]) / noob : 0.0f;
+    }
+}
+
+// Regression importance, squared errors (cpu_varimp_regression, src/rf_varimp.cpp:477-597):
+// d0[j] for the unpermuted prediction, d2[j][k] with feature k permuted, per OOB rank j.
+__global__ void __launch_bounds__(256) k_imp_regr(Data D, Batch B) {
+    const int t = blockIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= B.noob[t]) return;
+    const size_t mo = (size_t)t * B.M;
+    const int *st = B.status + mo, *bv = B.bestvar + mo, *tm = B.treemap + 2 * mo;
+    const float *xb = B.xbest + mo, *np = B.nodepred + mo;
+    const int row = B.oob[(size_t)t * D.N + j];
+    uint32_t mask[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    walk_oob(D, st, bv, xb, tm, row, mask);
+    const float pred = np[B.oob_leaf[(size_t)t * D.N + row]];
+    const float y = D.yreg[row];
+    const float d = pred - y;
+    B.d0[(size_t)t * D.N + j] = 1.0f * d * d;
+    const int prow = D.perm[row];
+    const int nn = B.nnode[t];
+    const bool wide = D.p > 256 || D.has_cat;
+    float* out = B.d2 + ((size_t)t * D.N + j) * D.p;
+    for (int k = 0; k < D.p; ++k) {
+        float pk = pred;
+        if (wide || ((mask[k >> 5] >> (k & 31)) & 1u))
+            pk = walk_perm_regr(D, st, bv, xb, tm, np, nn, row, prow, k);
+        const float dk = pk - y;
+        out[k] = 1.0f * dk * dk;
+    }
+}
+
+// Serial sums over the OOB rows in row order (the reference's loop order), then
+// rr = mse_perm - mse_orig.  One block per tree: thread k sums feature k, thread p the
+// unpermuted errors.
+__global__ void k_imp_regr_sum(Data D, Batch B) {
+    __shared__ float mse0;
+    const int t = blockIdx.x;
+    const int noob = B.noob[t];
+    if (noob == 0) {
+        for (int k = threadIdx.x; k < D.p; k += blockDim.x) B.rr[(size_t)t * D.p + k] = 0.0f;
+        return;
+    }
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        const float* d0 = B.d0 + (size_t)t * D.N;
+        for (int j = 0; j < noob; ++j) s += d0[j];
+        mse0 = s / (float)noob;
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < D.p; k += blockDim.x) {
+        float s = 0.0f;
+        const float* d2 = B.d2 + (size_t)t * D.N * D.p + k;
+        for (int j = 0; j < noob; ++j) s += d2[(size_t)j * D.p];
+        B.rr[(size_t)t * D.p + k] = s / (float)noob - mse0;
+    }
+}
+
+// avimp += rr, sqsd += rr*rr over the batch's trees in order (src/rf_random_forest.cpp:1903-1906).
+__global__ void k_imp_fold(Data D, Batch B, float* avimp, float* sqsd) {
+    for (int k = blockIdx.x * blockDim.x + threadIdx.x; k < D.p; k += gridDim.x * blockDim.x) {
+        float a = avimp[k], s = sqsd[k];
+        for (int t = 0; t < B.T; ++t) {
+            const float r = B.rr[(size_t)t * D.p + k];
+            a += r;
+            s += r * r;
+        }
+        avimp[k] = a;
+        sqsd[k] = s;
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Proximity counts (cpu_proximity dense branch, src/rf_proximity.cpp:99-230, integer
+// weights): every OOB row i in terminal node k meets every distinct in-bag row j of k,
+// C[min(i,j), max(i,j)] += 1 in the packed upper triangle over rows [0, R).  The in-bag
+// rows of a terminal node are its segment from growth.  grid (rows, trees).
+// ---------------------------------------------------------------------------------------
+__global__ void k_prox(Data D, Batch B, int R, int* __restrict__ C) {
+    const int t = blockIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= B.noob[t]) return;
+    const int row = B.oob[(size_t)t * D.N + j];
+    if (row >= R) return;
+    const int leaf = B.oob_leaf[(size_t)t * D.N + row];
+    const size_t m = (size_t)t * B.M + leaf;
+    if (B.status[m] != -1) return;
+    const int st = B.nd_start[m], c = B.nd_cnt[m];
+    const int* seg = B.seg[B.nd_buf[m]] + (size_t)t * D.N + st;
+    const long long R2 = 2LL * R;
+    for (int q = 0; q < c; ++q) {
+        const int col = seg[q];
+        if (col >= R) continue;
+        const long long a = min(row, col), b = max(row, col);
+        atomicAdd(&C[a * (R2 - a - 1) / 2 + (b - a - 1)], 1);
+    }
+}
+
+// finishprox (src/rf_finishprox.cpp:12-74) of rows [r0, r1): with C the symmetric count,
+// S_ij = 0.5 * (C/2 * (1/nout_i) + C/2 * (1/nout_j)) in double (a row with nout 0 is left
+// unscaled), diagonal 1, returned as float32 like get_proximity_matrix
+// (python/randomforest_py.cpp:2129-2155).
+__global__ void k_prox_finish(const int* __restrict__ C, const int* __restrict__ nout, int R,
+                              int r0, int r1, float* __restrict__ out) {
+    const long long total = (long long)(r1 - r0) * R;
+    const long long R2 = 2LL * R;
+    for (long long k = blockIdx.x * (long long)blockDim.x + threadIdx.x; k < total;
+         k += (long long)gridDim.x * blockDim.x) {
+        const int i = r0 + (int)(k / R), j = (int)(k % R);
+        float v;
+        if (i == j) {
+            v = 1.0f;
+        } else {
+            const long long a = min(i, j), b = max(i, j);
+            const double h = (double)C[a * (R2 - a - 1) / 2 + (b - a - 1)] / 2.0;
+            const int ni = nout[i], nj = nout[j];
+            const double si = ni > 0 ? h * (1.0 / (double)ni) : h;
+            const double sj = nj > 0 ? h * (1.0 / (double)nj) : h;
+            v = (float)(0.5 * (si + sj));
+        }
+        out[k] = v;
+    }
+}
+
+// q[i][c] = classwt[c] added votes[i][c] times, sequentially (src/rf_random_forest.cpp:1506-1520).
+__global__ void k_votes_to_q(const int* __restrict__ votes, const float* __restrict__ w, int N,
+                             int nclass, float* __restrict__ q) {
+    const long long total = (long long)N * nclass;
+    for (long long k = blockIdx.x * (long long)blockDim.x + threadIdx.x; k < total;
+         k += (long long)gridDim.x * blockDim.x) {
+        const int c = (int)(k % nclass);
+        const float wc = w ? 1.0f * w[c] : 1.0f;
+        float a = 0.0f;
+        for (int r = votes[k]; r > 0; --r) a += wc;
+        q[k] = a;
+    }
+}
+
+// vec[i] += per-tree OOB predictions in tree order (NaN marks in-bag).
+__global__ void k_oob_fold(const float* __restrict__ tree_oob, int ntrees, int N,
+                           float* __restrict__ vec) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= N) return;
+    float a = vec[i];
+    for (int t = 0; t < ntrees; ++t) {
+        const float v = tree_oob[(size_t)t * N + i];
+        if (!isnan(v)) a += v;
+    }
+    vec[i] = a;
+}
+
+}  // namespace rfx

@@ -1,0 +1,180 @@
+"""ctypes binding of the C ABI in include/rfx_b200.h (librfx_b200.so, built in-tree).
+
+The library is the only compute path: importing this module without the built library
+raises, and there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "librfx_b200.so")
+
+RFX_OK = 0
+ERRORS = {-1: "RFX_ERR_ARG", -2: "RFX_ERR_CUDA", -3: "RFX_ERR_OOM", -4: "RFX_ERR_UNSUPPORTED",
+          -5: "RFX_ERR_STATE", -6: "RFX_ERR_DEVICE"}
+TASK_CLASSIFICATION, TASK_REGRESSION, TASK_UNSUPERVISED = 0, 1, 2
+
+_pi = C.POINTER(C.c_int)
+_pf = C.POINTER(C.c_float)
+_pu8 = C.POINTER(C.c_uint8)
+
+
+class FitParams(C.Structure):
+    _fields_ = [(k, C.c_int) for k in (
+        "task", "n", "p", "mtry", "minndsize", "maxnode", "iseed", "boot_seed", "nbins",
+        "maxcat", "compute_importance", "compute_proximity", "prox_rows", "batch_trees",
+        "keep_tree_oob")]
+
+
+class Inputs(C.Structure):
+    _fields_ = [("X", _pf), ("y_class", _pi), ("y_reg", _pf), ("sample_weights", _pf),
+                ("cat", _pi), ("classwt", _pf)]
+
+
+class Trees(C.Structure):
+    _fields_ = [("nodestatus", _pi), ("bestvar", _pi), ("xbestsplit", _pf), ("treemap", _pi),
+                ("nodeclass", _pi), ("nnode", _pi), ("nodepred", _pf), ("tnodewt", _pf),
+                ("nin", _pi), ("oob_leaf", _pi), ("tree_rr", _pf), ("tree_used", _pu8)]
+
+
+class Accum(C.Structure):
+    _fields_ = [("nclass", C.c_int), ("N", C.c_int), ("nout", _pi), ("votes", _pi),
+                ("q", _pf), ("oob_sum", _pf), ("avimp", _pf), ("sqsd", _pf), ("labels", _pi)]
+
+
+SYMBOLS = (
+    "rfx_last_error", "rfx_abi_version", "rfx_device_count", "rfx_create", "rfx_destroy",
+    "rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
+    "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish", "rfx_prox_dense",
+    "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host", "rfx_sync",
+)
+
+_LIB = None
+
+
+def load_library(path: str = LIB_PATH):
+    """Load librfx_b200.so and declare its signatures.  Raises if it is not built."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(path):
+        raise ImportError(f"{path} is not built; run `make -C rfx-fuse_b200` (sm_100a)")
+    L = C.CDLL(path)
+    vp = C.c_void_p
+    L.rfx_last_error.restype = C.c_char_p
+    L.rfx_abi_version.restype = C.c_int
+    L.rfx_device_count.restype = C.c_int
+    L.rfx_create.restype = vp
+    L.rfx_create.argtypes = [C.c_int]
+    L.rfx_destroy.argtypes = [vp]
+    L.rfx_load.argtypes = [vp, C.POINTER(FitParams), C.POINTER(Inputs)]
+    L.rfx_grow.argtypes = [vp, C.c_int, C.c_int, C.POINTER(Trees)]
+    L.rfx_results.argtypes = [vp, C.POINTER(Accum)]
+    L.rfx_fit.argtypes = [vp, C.POINTER(FitParams), C.POINTER(Inputs), C.c_int,
+                          C.POINTER(Trees), C.POINTER(Accum)]
+    L.rfx_set_prox_buffer.argtypes = [vp, vp, C.c_int64]
+    L.rfx_get_prox_buffer.argtypes = [vp, C.POINTER(vp), C.POINTER(C.c_int64)]
+    L.rfx_get_vote_buffers.argtypes = [vp, C.POINTER(vp), C.POINTER(vp)]
+    L.rfx_prox_finish.argtypes = [vp, vp, vp, C.c_int, C.c_int, C.c_int, vp]
+    L.rfx_prox_dense.argtypes = [vp, C.c_int, C.c_int, _pf]
+    L.rfx_oob_fold.argtypes = [vp, vp]
+    L.rfx_votes_to_q.argtypes = [vp, vp, _pf, C.c_int, C.c_int, vp]
+    L.rfx_copy_to_host.argtypes = [vp, vp, vp, C.c_size_t]
+    L.rfx_sync.argtypes = [vp]
+    for name in ("rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
+                 "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish",
+                 "rfx_prox_dense", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host",
+                 "rfx_sync"):
+        getattr(L, name).restype = C.c_int
+    _LIB = L
+    return L
+
+
+class RfxError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{ERRORS.get(code, code)}: {msg}")
+        self.code = code
+
+
+def check(rc: int) -> None:
+    if rc != RFX_OK:
+        raise RfxError(rc, (load_library().rfx_last_error() or b"").decode(errors="replace"))
+
+
+def ptr(a, t):
+    return None if a is None else a.ctypes.data_as(t)
+
+
+class Context:
+    """One CUDA device.  Owns the device copy of a loaded dataset and its accumulators."""
+
+    def __init__(self, device: int = 0):
+        L = load_library()
+        self._lib = L
+        h = L.rfx_create(int(device))
+        if not h:
+            raise RfxError(-2, (L.rfx_last_error() or b"").decode(errors="replace"))
+        self.handle = C.c_void_p(h)
+        self.device = device
+
+    def close(self):
+        if getattr(self, "handle", None):
+            self._lib.rfx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def load(self, prm: FitParams, inputs: Inputs):
+        check(self._lib.rfx_load(self.handle, C.byref(prm), C.byref(inputs)))
+
+    def grow(self, tree_begin: int, ntree: int, trees: Trees | None = None):
+        check(self._lib.rfx_grow(self.handle, tree_begin, ntree,
+                                 C.byref(trees) if trees is not None else None))
+
+    def results(self, acc: Accum):
+        check(self._lib.rfx_results(self.handle, C.byref(acc)))
+
+    def prox_dense(self, r0: int, r1: int, out: np.ndarray):
+        check(self._lib.rfx_prox_dense(self.handle, r0, r1, ptr(out, _pf)))
+
+    def prox_buffer(self):
+        p = C.c_void_p()
+        n = C.c_int64()
+        check(self._lib.rfx_get_prox_buffer(self.handle, C.byref(p), C.byref(n)))
+        return p.value, n.value
+
+    def set_prox_buffer(self, dev_ptr: int | None, length: int):
+        check(self._lib.rfx_set_prox_buffer(self.handle, C.c_void_p(dev_ptr) if dev_ptr else None,
+                                            C.c_int64(length)))
+
+    def vote_buffers(self):
+        a, b = C.c_void_p(), C.c_void_p()
+        check(self._lib.rfx_get_vote_buffers(self.handle, C.byref(a), C.byref(b)))
+        return a.value, b.value
+
+    def prox_finish(self, upper_dev: int, nout_dev: int, R: int, r0: int, r1: int, out_dev: int):
+        check(self._lib.rfx_prox_finish(self.handle, C.c_void_p(upper_dev), C.c_void_p(nout_dev),
+                                        R, r0, r1, C.c_void_p(out_dev)))
+
+    def oob_fold(self, vec_dev: int):
+        check(self._lib.rfx_oob_fold(self.handle, C.c_void_p(vec_dev)))
+
+    def votes_to_q(self, votes_dev: int, classwt, N: int, nclass: int, q_dev: int):
+        cw = None if classwt is None else np.ascontiguousarray(classwt, np.float32)
+        check(self._lib.rfx_votes_to_q(self.handle, C.c_void_p(votes_dev), ptr(cw, _pf), N, nclass,
+                                       C.c_void_p(q_dev)))
+
+    def copy_to_host(self, dst: np.ndarray, src_dev: int):
+        check(self._lib.rfx_copy_to_host(self.handle, dst.ctypes.data_as(C.c_void_p),
+                                         C.c_void_p(src_dev), dst.nbytes))
+
+    def sync(self):
+        check(self._lib.rfx_sync(self.handle))

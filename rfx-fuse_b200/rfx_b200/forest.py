@@ -1,0 +1,351 @@
+"""Drop-in estimators with the RFXFuse Python surface (python/randomforest_py.cpp).
+
+RandomForestClassifier / RandomForestRegressor / RandomForestUnsupervised keep the
+reference constructor arguments and defaults, and resolve them the same way
+(python/randomforest_py.cpp:1270-1320, 1367-1500, 3066-3240, 4628-5040).  ``fit`` runs the
+whole forest on the GPU through librfx_b200.so; the getters return what the reference's
+getters return.  Arguments that only select among the reference's own implementations
+(use_gpu, use_sparse, gpu_loss_function, show_progress, ...) are accepted and ignored:
+there is one implementation here, the device one.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from . import _abi as A
+
+MAX_NODE_CAP = 32001
+
+
+def calculate_maxnode(nsample: int, minndsize: int, user_maxnode: int = 0) -> int:
+    """include/rf_config.hpp:15-32."""
+    if user_maxnode > 0:
+        return int(user_maxnode)
+    m = max(int(minndsize), 1)
+    leaves = (int(nsample) + m - 1) // m
+    return min(2 * leaves + 1, MAX_NODE_CAP)
+
+
+def _isqrt_f32(x: int) -> int:
+    # static_cast<integer_t>(std::sqrt(static_cast<real_t>(x)))
+    return int(np.sqrt(np.float32(x), dtype=np.float32))
+
+
+def detect_categorical(X: np.ndarray, maxcat: int, categorical_features=None) -> np.ndarray:
+    """cat[] exactly as RandomForestClassifier::fit builds it (python/randomforest_py.cpp:1413-1460)."""
+    n, p = X.shape
+    cat = np.ones(p, np.int32)
+    if categorical_features is not None:
+        for c in list(categorical_features):
+            c = int(c)
+            if 0 <= c < p:
+                cat[c] = len(np.unique(X[:, c]))
+        return cat
+    for m in range(p):
+        col = X[:, m]
+        u = np.unique(col)
+        all_int = not np.any(np.abs(col - np.round(col)) > np.float32(1e-5))
+        mn = min(np.float32(1e10), col.min()) if n else np.float32(1e10)
+        mx = max(np.float32(-1e10), col.max()) if n else np.float32(-1e10)
+        if all_int and 2 < len(u) <= maxcat and mn >= 0.0 and mx < np.float32(maxcat):
+            cat[m] = len(u)
+    return cat
+
+
+class _Forest:
+    _task = None
+
+    def __init__(self, nsample=1000, ntree=100, mdim=10, nclass=2, maxcat=10, mtry=0,
+                 maxnode=0, minndsize=1, ncsplit=25, ncmax=25, iseed=12345,
+                 compute_proximity=False, compute_importance=True,
+                 compute_local_importance=False, use_gpu=True, use_qlora=False,
+                 quant_mode="nf4", use_sparse=False, sparsity_threshold=1e-6, batch_size=0,
+                 nodesize=5, cutoff=0.01, show_progress=True, progress_desc="",
+                 gpu_loss_function="gini", rank=32, power_iterations=30, n_threads_cpu=0,
+                 use_rfgap=False, importance_method="local_imp", clique_M=-1,
+                 use_casewise=False, compute_proximity_importance=False,
+                 compute_leaf_assignments=False, categorical_features=None,
+                 use_histogram=True, n_bins=256, class_weight="", classwt=None,
+                 device=0, prox_rows=0, batch_trees=0):
+        if use_casewise:
+            raise NotImplementedError("use_casewise=True is not implemented on the device path")
+        if use_rfgap:
+            raise NotImplementedError("RF-GAP proximity is not implemented on the device path")
+        if compute_local_importance:
+            raise NotImplementedError("local importance is not implemented on the device path")
+        if not use_histogram:
+            raise NotImplementedError("only the histogram grower exists on the device path")
+        self.nsample = int(nsample)
+        self.ntree = int(ntree)
+        self.mdim = int(mdim)
+        self.maxcat = int(maxcat)
+        self.minndsize = int(minndsize)
+        self.iseed = int(iseed)
+        self.compute_proximity = bool(compute_proximity)
+        self.compute_importance = bool(compute_importance)
+        self.use_qlora = bool(use_qlora)
+        self.n_bins = min(int(n_bins), 256)
+        self.categorical_features = categorical_features
+        self.class_weight = class_weight
+        self.classwt = classwt
+        self.device = int(device)
+        self.prox_rows = int(prox_rows)
+        self.batch_trees = int(batch_trees)
+        self.nodesize = int(nodesize)  # stored, never read by the growers (as in the reference)
+        self._mtry_arg = int(mtry)
+        self._maxnode = calculate_maxnode(self.nsample, self.minndsize, int(maxnode))
+        self._mtry = self._resolve_mtry_ctor(int(mtry))
+        self._ctx = None
+        self._fitted = False
+
+    # ---- resolution rules of the reference wrappers
+    def _resolve_mtry_ctor(self, mtry):
+        return mtry if mtry > 0 else _isqrt_f32(self.mdim)
+
+    def _context(self):
+        if self._ctx is None:
+            self._ctx = A.Context(self.device)
+        return self._ctx
+
+    def _fit(self, X, y, sample_weights, task, mtry, maxnode, classwt):
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        if X.ndim != 2:
+            raise RuntimeError("X must be 2-dimensional (samples, features)")
+        n, p = X.shape
+        self.n_features_ = p
+        cat = detect_categorical(X, self.maxcat, self.categorical_features)
+        self._cat = cat
+        prm = A.FitParams(task, n, p, mtry, self.minndsize, maxnode, self.iseed, 12345,
+                          self.n_bins, self.maxcat, int(self.compute_importance),
+                          int(self.compute_proximity), self.prox_rows, self.batch_trees, 0)
+        ycls = yreg = sw = cw = None
+        if task == A.TASK_CLASSIFICATION:
+            ycls = np.ascontiguousarray(y, dtype=np.int32)
+        elif task == A.TASK_REGRESSION:
+            yreg = np.ascontiguousarray(y, dtype=np.float32)
+        if sample_weights is not None and len(sample_weights) > 0:
+            sw = np.ascontiguousarray(sample_weights, dtype=np.float32)
+        if classwt is not None:
+            cw = np.ascontiguousarray(classwt, dtype=np.float32)
+        inp = A.Inputs(A.ptr(X, A._pf), A.ptr(ycls, A._pi), A.ptr(yreg, A._pf), A.ptr(sw, A._pf),
+                       A.ptr(cat, A._pi), A.ptr(cw, A._pf))
+        N = 2 * n if task == A.TASK_UNSUPERVISED else n
+        T, M = self.ntree, maxnode
+        tr = {
+            "nodestatus": np.zeros((T, M), np.int32), "bestvar": np.zeros((T, M), np.int32),
+            "xbestsplit": np.zeros((T, M), np.float32), "treemap": np.zeros((T, 2 * M), np.int32),
+            "nodeclass": np.zeros((T, M), np.int32), "nnode": np.zeros(T, np.int32),
+            "nodepred": np.zeros((T, M), np.float32), "tnodewt": np.zeros((T, M), np.float32),
+            "tree_rr": np.zeros((T, p), np.float32), "tree_used": np.zeros((T, p), np.uint8),
+        }
+        trees = A.Trees(*[A.ptr(tr[k], t) for k, t in (
+            ("nodestatus", A._pi), ("bestvar", A._pi), ("xbestsplit", A._pf), ("treemap", A._pi),
+            ("nodeclass", A._pi), ("nnode", A._pi), ("nodepred", A._pf), ("tnodewt", A._pf))],
+            None, None, A.ptr(tr["tree_rr"], A._pf), A.ptr(tr["tree_used"], A._pu8))
+        ctx = self._context()
+        ctx.load(prm, inp)
+        ctx.grow(0, T, trees)
+        ncl = {A.TASK_REGRESSION: 1, A.TASK_UNSUPERVISED: 2}.get(task)
+        if ncl is None:
+            ncl = len(np.unique(ycls))
+        acc = {"nout": np.zeros(N, np.int32), "votes": np.zeros((N, ncl), np.int32),
+               "q": np.zeros((N, ncl), np.float32), "oob_sum": np.zeros(N, np.float32),
+               "avimp": np.zeros(p, np.float32), "sqsd": np.zeros(p, np.float32),
+               "labels": np.zeros(N, np.int32)}
+        ac = A.Accum(0, 0, *[A.ptr(acc[k], t) for k, t in (
+            ("nout", A._pi), ("votes", A._pi), ("q", A._pf), ("oob_sum", A._pf), ("avimp", A._pf),
+            ("sqsd", A._pf), ("labels", A._pi))])
+        if ncl == 1:
+            ac.votes = None
+            ac.q = None
+            ac.labels = None
+        ctx.results(ac)
+        self.trees_ = tr
+        self.acc_ = acc
+        self.n_rows_ = N
+        self.nclass_ = ncl
+        self._task_id = task
+        self._maxnode_eff = M
+        self._mtry_eff = mtry
+        self._fitted = True
+        self._finalize(y)
+        return None
+
+    def _finalize(self, y):
+        acc = self.acc_
+        nout = acc["nout"]
+        # feature importance: finalize_training (src/rf_random_forest.cpp:2690-2698)
+        av = acc["avimp"]
+        s = np.add.accumulate(np.abs(av), dtype=np.float32)[-1] if len(av) else np.float32(0)
+        self._importances = av.copy() if s > 0 else np.zeros_like(av)
+
+    def _check(self):
+        if not self._fitted:
+            raise RuntimeError("Model must be fitted first")
+
+    # ---- reference getters
+    def feature_importances_(self):
+        self._check()
+        return self._importances.copy()
+
+    def get_oob_error(self):
+        self._check()
+        return float(self._oob_error)
+
+    def get_oob_counts(self):
+        self._check()
+        return self.acc_["nout"].copy()
+
+    def get_n_samples(self):
+        return self.n_rows_
+
+    def get_n_features(self):
+        return self.n_features_
+
+    def get_n_classes(self):
+        return self.nclass_
+
+    def get_proximity_matrix(self):
+        """Dense float32 finishprox'd proximity (python/randomforest_py.cpp:2129-2181)."""
+        self._check()
+        if not self.compute_proximity:
+            raise RuntimeError("Proximity was not computed (compute_proximity=False)")
+        ctx = self._context()
+        _, length = ctx.prox_buffer()
+        R = int(round((1 + math.sqrt(1 + 8 * length)) / 2)) if length else (
+            self.prox_rows or self.n_rows_)
+        out = np.empty((R, R), np.float32)
+        ctx.prox_dense(0, R, out)
+        return out
+
+    def get_proximity_counts(self):
+        """Packed upper triangle (i < j) of the integer OOB x in-bag co-membership counts."""
+        self._check()
+        ctx = self._context()
+        dev, length = ctx.prox_buffer()
+        out = np.empty(length, np.int32)
+        if length:
+            ctx.copy_to_host(out, dev)
+        return out
+
+
+def _argmax_last(q: np.ndarray) -> np.ndarray:
+    """argmax with the reference's `>=` scan: ties go to the highest class index."""
+    k = q.shape[1]
+    return (k - 1 - np.argmax(q[:, ::-1], axis=1)).astype(np.int32)
+
+
+class _Classifying(_Forest):
+    def _class_error_and_preds(self, labels0):
+        acc = self.acc_
+        q = acc["q"]
+        nout = acc["nout"]
+        oob = nout > 0
+        pred = _argmax_last(q)
+        # compute_classification_error (src/rf_random_forest.cpp:3947-4012)
+        tot = int(oob.sum())
+        correct = int((pred[oob] == labels0[oob]).sum())
+        self._oob_error = (np.float32(1.0) - np.float32(correct) / np.float32(tot)) if tot else np.float32(0)
+        # compute_oob_predictions (src/rf_random_forest.cpp:3776-3840)
+        self._oob_class = np.where(oob, pred, 0).astype(np.int32)
+        tv = np.add.accumulate(q, axis=1, dtype=np.float32)[:, -1] if q.shape[1] else np.zeros(len(q), np.float32)
+        probs = np.full(q.shape, np.float32(1.0) / np.float32(q.shape[1]), np.float32)
+        ok = oob & (tv > 0)
+        probs[ok] = q[ok] / tv[ok, None]
+        self._oob_proba = probs
+
+    def get_oob_predictions(self):
+        self._check()
+        return self._oob_class.astype(np.float32)
+
+
+class RandomForestClassifier(_Classifying):
+    _task = A.TASK_CLASSIFICATION
+
+    def fit(self, X, y, sample_weights=None):
+        y = np.ascontiguousarray(y, dtype=np.int32)
+        ncl = len(np.unique(y))
+        classwt = None
+        if self.classwt is not None:
+            classwt = np.ascontiguousarray(self.classwt, dtype=np.float32)
+            if classwt.shape[0] != ncl:
+                raise RuntimeError(f"classwt length ({classwt.shape[0]}) must match number of classes ({ncl})")
+        elif self.class_weight == "balanced":
+            counts = np.zeros(ncl, np.int64)
+            for c in y:
+                if 0 <= c < ncl:
+                    counts[c] += 1
+            n = np.float32(len(y))
+            classwt = np.array([n / (np.float32(ncl) * np.float32(k)) if k > 0 else np.float32(1.0)
+                                for k in counts], np.float32)
+        self.classwt_ = classwt
+        self._fit(X, y, sample_weights, A.TASK_CLASSIFICATION, self._mtry, self._maxnode, classwt)
+
+    def _finalize(self, y):
+        super()._finalize(y)
+        self._class_error_and_preds(self.acc_["labels"])
+
+
+class RandomForestRegressor(_Forest):
+    _task = A.TASK_REGRESSION
+
+    def __init__(self, *args, **kw):
+        kw.setdefault("compute_proximity", False)
+        super().__init__(*args, **kw)
+
+    def fit(self, X, y, sample_weights=None):
+        self._y = np.ascontiguousarray(y, dtype=np.float32)
+        self._fit(X, self._y, sample_weights, A.TASK_REGRESSION, self._mtry, self._maxnode, None)
+
+    def _finalize(self, y):
+        super()._finalize(y)
+        # compute_regression_mse (src/rf_random_forest.cpp:4014-4058)
+        s = self.acc_["oob_sum"]
+        nout = self.acc_["nout"]
+        oob = nout > 0
+        pred = s.copy()
+        pred[oob] = s[oob] / nout[oob].astype(np.float32)
+        err = (self._y[oob] - pred[oob]).astype(np.float32)
+        sq = (err * err).astype(np.float32)
+        sse = np.add.accumulate(sq, dtype=np.float32)[-1] if len(sq) else np.float32(0)
+        tot = int(oob.sum())
+        self._oob_error = np.float32(sse / np.float32(tot)) if tot else np.float32(0)
+        self._oob_pred = pred
+
+    def get_oob_predictions(self):
+        self._check()
+        return self._oob_pred.copy()
+
+    def get_oob_mse(self):
+        return self.get_oob_error()
+
+
+class RandomForestUnsupervised(_Classifying):
+    _task = A.TASK_UNSUPERVISED
+
+    def __init__(self, nsample=1000, ntree=100, mdim=10, maxcat=10, mtry=0, maxnode=0,
+                 minndsize=1, ncsplit=25, ncmax=25, iseed=12345, compute_proximity=True,
+                 compute_importance=True, **kw):
+        super().__init__(nsample=nsample, ntree=ntree, mdim=mdim, maxcat=maxcat, mtry=mtry,
+                         maxnode=maxnode, minndsize=minndsize, ncsplit=ncsplit, ncmax=ncmax,
+                         iseed=iseed, compute_proximity=compute_proximity,
+                         compute_importance=compute_importance, **kw)
+
+    def _resolve_mtry_ctor(self, mtry):
+        return mtry  # 0 is resolved at fit time (setup_unsupervised_task)
+
+    def fit(self, X, sample_weights=None):
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        n, p = X.shape
+        mtry = self._mtry if self._mtry > 0 else max(1, _isqrt_f32(p))
+        maxnode = calculate_maxnode(2 * n, self.minndsize)  # src/rf_random_forest.cpp:1106
+        self._fit(X, None, None, A.TASK_UNSUPERVISED, mtry, maxnode, None)
+
+    def _finalize(self, y):
+        super()._finalize(y)
+        n2 = self.n_rows_
+        labels = np.zeros(n2, np.int32)
+        labels[: n2 // 2] = 1
+        self._class_error_and_preds(labels)
