@@ -150,6 +150,23 @@ int rfx_votes_to_q(void* ctx, const int* votes_dev, const float* classwt, int N,
 /* Stream-ordered device-to-host copy of `bytes` from src_dev (e.g. the proximity counts). */
 int rfx_copy_to_host(void* ctx, void* dst_host, const void* src_dev, size_t bytes);
 
+/* Measurement.  Counters since the last rfx_reset_stats: kernels launched by the library,
+ * and, while profiling is on, the CUDA-event time of the histogram kernels of every level
+ * together with the algorithmic bytes they read (sum over searched nodes of
+ * rows * (mtry + target bytes)). */
+typedef struct {
+    int64_t kernel_launches;
+    int64_t hist_launches;
+    double hist_ms;
+    double hist_bytes;
+    int64_t levels;
+    int64_t trees;
+} rfx_stats;
+int rfx_get_stream(void* ctx, void** stream);   /* the context's cudaStream_t */
+int rfx_set_profiling(void* ctx, int on);
+int rfx_get_stats(void* ctx, rfx_stats* out);
+int rfx_reset_stats(void* ctx);
+
 /* Wait for the context's stream. */
 int rfx_sync(void* ctx);
 

@@ -12,6 +12,8 @@ constexpr int kMaxClass = 32;     // classes supported by the device histograms
 constexpr int kBins = 256;        // histogram bins (uint8 codes)
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr unsigned long long kNoKey = ~0ull;
+constexpr int kBigSegment = 2048;  // segments above this are partitioned by a whole block
+constexpr int kSmallNode = 64;     // nodes up to this size are searched by one warp
 
 // ------------------------------------------------------------------------------------
 // MT19937, the generator of include/rf_utils.hpp:74-141: init_genrand seeding, standard
@@ -153,7 +155,12 @@ struct Batch {
     int* srch;        // [T][M] searched nodes of the level, in node order
     int* srch_cnt;    // [T]
     int* srch_off;    // [T+1]
-    int* counters;    // [8]: 0 level total, 1 searched total, 2 next-level total, 3 error
+    int* counters;    // [8]: 0 level total, 1 searched total, 2 next-level total, 4 big searched
+    unsigned long long* hist_bytes;  // algorithmic bytes read by k_hist (sum of c_v*(mtry+L))
+    int* srch_big;    // [T][M] searched nodes with more than kSmallNode rows, in node order
+    int* srch_big_cnt;  // [T]
+    int* srch_big_off;  // [T+1]
+    long long* part_big;  // split nodes (t*M + node) with segments above kBigSegment; count in counters[5]
     // post-growth
     int* oob_leaf;    // [T][N] terminal node of OOB rows (-1 in-bag)
     uint8_t* used;    // [T][p]
@@ -163,6 +170,15 @@ struct Batch {
     float* d0;        // [T][N]
     float* rr;        // [T][p]
     float* tree_oob;  // [T][N] per-tree OOB predictions (NaN in-bag), optional
+};
+
+// Launch shape of k_hist (rfx_hist.cu).
+struct HistArgs {
+    int warps;       // warps per block = drawn features per work unit
+    int groups;      // work units per searched node = ceil(mtry / warps)
+    int stage_rows;  // rows staged per chunk (multiple of 32)
+    int cstride;     // bytes per staged feature column (stage_rows + 4)
+    int warp_bytes;  // per-warp scratch
 };
 
 // Locate the tree of a flattened task index given an exclusive prefix `off` of length T+1.

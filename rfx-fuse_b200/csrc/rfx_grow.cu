@@ -66,6 +66,7 @@ __global__ void __launch_bounds__(1024) k_level_begin(Batch B) {
         B.lvl_off[B.T] = carry;
         B.counters[0] = carry;
         B.counters[2] = 0;
+        B.counters[5] = 0;
     }
 }
 
@@ -90,14 +91,24 @@ __global__ void __launch_bounds__(256) k_node_eval(Data D, Batch B, int cur) {
         float ts = 0.0f, ts2 = 0.0f;
         int maj = 0, nz = 0;
         if (regr) {
-            for (int b0 = 0; b0 < c; b0 += 32) {
-                const int i = b0 + lane;
-                const float v = i < c ? D.yv[seg[i]] : 0.0f;
-                const int k = min(32, c - b0);
-                for (int j = 0; j < k; ++j) {
-                    const float x = __shfl_sync(kFull, v, j);
-                    ts += x * 1.0f;
-                    ts2 += x * x * 1.0f;
+            // serial sums in row order (lane 0's copy is the one kept); 8 x 32 values are
+            // gathered per step so their loads are in flight together
+            constexpr int U = 8;
+            for (int b0 = 0; b0 < c; b0 += 32 * U) {
+                float v[U];
+#pragma unroll
+                for (int q = 0; q < U; ++q) {
+                    const int i = b0 + q * 32 + lane;
+                    v[q] = i < c ? D.yv[seg[i]] : 0.0f;
+                }
+#pragma unroll
+                for (int q = 0; q < U; ++q) {
+                    const int k = min(32, c - (b0 + q * 32));
+                    for (int j = 0; j < k; ++j) {
+                        const float x = __shfl_sync(kFull, v[q], j);
+                        ts += x * 1.0f;
+                        ts2 += x * x * 1.0f;
+                    }
                 }
             }
         } else {
@@ -160,17 +171,22 @@ __global__ void __launch_bounds__(256) k_draw(Data D, Batch B) {
     const int t = blockIdx.x;
     const int lo = B.lvl_lo[t], hi = B.lvl_hi[t];
     int* srch = B.srch + (size_t)t * B.M;
-    int carry = 0;
+    int* big = B.srch_big + (size_t)t * B.M;
+    int carry = 0, bcarry = 0;
     for (int k0 = lo; k0 < hi; k0 += blockDim.x) {
         const int node = k0 + threadIdx.x;
         const bool f = node < hi && B.nd_flag[(size_t)t * B.M + node];
-        int tot;
+        const bool fb = f && B.nd_cnt[(size_t)t * B.M + node] > kSmallNode;
+        int tot, btot;
         const int ex = block_excl_scan(f ? 1 : 0, ws, tot);
+        const int bex = block_excl_scan(fb ? 1 : 0, ws, btot);
         if (f) {
             srch[carry + ex] = node;
             B.nd_key[(size_t)t * B.M + node] = kNoKey;
         }
+        if (fb) big[bcarry + bex] = node;
         carry += tot;
+        bcarry += btot;
     }
     __syncthreads();
     const int S = carry;
@@ -189,7 +205,11 @@ __global__ void __launch_bounds__(256) k_draw(Data D, Batch B) {
         for (int k = threadIdx.x; k < 624; k += blockDim.x) g[k] = s[k];
         if (threadIdx.x == 0) B.mt_pos[t] = pos;
     }
-    if (threadIdx.x == 0) B.srch_cnt[t] = (B.nnode[t] + 2 <= B.M) ? S : 0;
+    if (threadIdx.x == 0) {
+        const bool open = B.nnode[t] + 2 <= B.M;
+        B.srch_cnt[t] = open ? S : 0;
+        B.srch_big_cnt[t] = open ? bcarry : 0;
+    }
 }
 
 __global__ void __launch_bounds__(1024) k_srch_scan(Batch B) {
@@ -203,257 +223,20 @@ __global__ void __launch_bounds__(1024) k_srch_scan(Batch B) {
         if (t < B.T) B.srch_off[t] = carry + ex;
         carry += tot;
     }
+    int bcarry = 0;
+    for (int t0 = 0; t0 < B.T; t0 += blockDim.x) {
+        const int t = t0 + threadIdx.x;
+        const int w = t < B.T ? B.srch_big_cnt[t] : 0;
+        int tot;
+        const int ex = block_excl_scan(w, ws, tot);
+        if (t < B.T) B.srch_big_off[t] = bcarry + ex;
+        bcarry += tot;
+    }
     if (threadIdx.x == 0) {
         B.srch_off[B.T] = carry;
+        B.srch_big_off[B.T] = bcarry;
         B.counters[1] = carry;
-    }
-}
-
-// ---------------------------------------------------------------------------------------
-// Histogram split search (one block per searched node, one warp per drawn feature):
-// histogram_find_best_split_classification / _regression (src/rf_growtree.cpp:22-184)
-// and the per-node comparison across the mtry draws (:820-836, :929-955).
-//
-// The node's packed rows (bins + target) are staged through shared memory in chunks, so
-// each row crosses L2 once per level however many features are drawn.  Each warp builds
-// its feature's histogram: classification as integer class counts (the reference's float
-// counts are small integers, so exact); regression as float sums that must equal the
-// reference's row-order serial sums bin by bin -- rows that hit the same bin within a
-// 32-row step are added one rank at a time, in row order.
-//
-// Only non-empty bins can win (an empty bin repeats the previous bin's criterion, and
-// the reference keeps the first of equal values), so the scan runs over the compacted
-// list of non-empty bins.  The running left/right sums of the scan are serial float
-// chains in the reference; lanes 0..2 compute them in bin order, then all lanes evaluate
-// the criterion of every candidate bin in parallel and the first minimum wins.
-//
-// Per-node winner: key = (order-preserving bits of the criterion, draw index, bin); the
-// smallest key is the reference's choice (regression: lowest MSE, first draw wins ties;
-// classification: highest 2 - gini, i.e. lowest -(2 - gini), first draw wins ties).
-// ---------------------------------------------------------------------------------------
-struct HistLayout {
-    int warp_bytes;   // per-warp scratch
-    int stage_rows;   // rows staged per chunk
-};
-
-__device__ __forceinline__ void warp_compact_bins(uint32_t* mask, uint8_t* bl, int lane, int& m) {
-    // bl[0..m) = ascending list of set bits of mask[0..8).
-    uint32_t w = lane < 8 ? mask[lane] : 0u;
-    int cnt = __popc(w), x = cnt;
-    for (int o = 1; o < 8; o <<= 1) {
-        const int y = __shfl_up_sync(kFull, x, o);
-        if (lane >= o) x += y;
-    }
-    int off = x - cnt;
-    m = __shfl_sync(kFull, x, 7);
-    if (lane < 8) {
-        while (w) {
-            const int b = __ffs(w) - 1;
-            w &= w - 1;
-            bl[off++] = (uint8_t)(lane * 32 + b);
-        }
-        mask[lane] = 0u;
-    }
-    __syncwarp();
-}
-
-__global__ void __launch_bounds__(512) k_hist(Data D, Batch B, int cur, int nwarp_blk,
-                                              int stage_rows, int warp_bytes) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ unsigned long long wkey[16];
-    __shared__ int snode[4];
-    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const int nthr = blockDim.x;
-    const bool regr = D.nclass == 1;
-    const int nc = D.nclass;
-    const int rs = D.rs, ro = D.ro;
-    uint8_t* stage = smem;
-    uint8_t* wbase = smem + (size_t)stage_rows * rs + (size_t)wib * warp_bytes;
-    // per-warp scratch
-    uint32_t* mask = reinterpret_cast<uint32_t*>(wbase);                // [8]
-    uint8_t* bl = wbase + 32;                                           // [256]
-    float* sy = reinterpret_cast<float*>(wbase + 288);                  // [256] / class hist
-    float* sy2 = sy + kBins;
-    int* cn = reinterpret_cast<int*>(sy2 + kBins);
-    float* r1 = reinterpret_cast<float*>(cn + kBins);
-    float* r2 = r1 + kBins;
-    int* h = reinterpret_cast<int*>(wbase + 288);                       // [256][nc] + tc[32]
-    int* tc = h + kBins * nc;
-    // scratch starts zeroed
-    for (int k = lane; k < warp_bytes / 4; k += 32) reinterpret_cast<uint32_t*>(wbase)[k] = 0u;
-    __syncwarp();
-    const int total = B.counters[1];
-    const uint32_t lt = (1u << lane) - 1u;
-    for (int si = blockIdx.x; si < total; si += gridDim.x) {
-        if (threadIdx.x == 0) {
-            const int t = tree_of(B.srch_off, B.T, si);
-            snode[0] = t;
-            snode[1] = B.srch[(size_t)t * B.M + (si - B.srch_off[t])];
-        }
-        __syncthreads();
-        const int t = snode[0], node = snode[1];
-        const size_t m = (size_t)t * B.M + node;
-        const int start = B.nd_start[m], c = B.nd_cnt[m];
-        const int* seg = B.seg[cur] + (size_t)t * D.N + start;
-        const uint16_t* featp = B.feat + (size_t)t * B.M * B.mtry + (size_t)node * B.mtry;
-        unsigned long long best_key = kNoKey;
-        for (int r0 = 0; r0 < B.mtry; r0 += nwarp_blk) {
-            const int mv = r0 + wib;
-            const bool active = mv < B.mtry;
-            const int f = active ? featp[mv] : 0;
-            // ---- histogram over the node's rows, staged chunk by chunk
-            for (int c0 = 0; c0 < c; c0 += stage_rows) {
-                const int ch = min(stage_rows, c - c0);
-                const int pieces = rs >> 4;
-                for (int k = threadIdx.x; k < ch * pieces; k += nthr) {
-                    const int rr = k / pieces, pc = k - rr * pieces;
-                    const uint4* src = reinterpret_cast<const uint4*>(D.rows + (size_t)seg[c0 + rr] * rs) + pc;
-                    reinterpret_cast<uint4*>(stage + (size_t)rr * rs)[pc] = __ldg(src);
-                }
-                __syncthreads();
-                if (active) {
-                    for (int s0 = 0; s0 < ch; s0 += 32) {
-                        const int i = s0 + lane;
-                        const bool valid = i < ch;
-                        const uint8_t* row = stage + (size_t)i * rs;
-                        const int b = valid ? row[f] : kBins;
-                        const uint32_t peers = __match_any_sync(kFull, b);
-                        const int rank = __popc(peers & lt);
-                        if (valid && rank == 0) atomicOr(&mask[b >> 5], 1u << (b & 31));
-                        if (regr) {
-                            float v = 0.0f, v2 = 0.0f;
-                            if (valid) {
-                                const float2 yy = *reinterpret_cast<const float2*>(row + ro);
-                                v = yy.x;
-                                v2 = yy.y;
-                            }
-                            const int maxr = __reduce_max_sync(kFull, valid ? __popc(peers) - 1 : 0);
-                            for (int q = 0; q <= maxr; ++q) {
-                                if (valid && rank == q) {
-                                    sy[b] += v * 1.0f;
-                                    sy2[b] += v2 * 1.0f;
-                                    cn[b] += 1;
-                                }
-                                __syncwarp();
-                            }
-                        } else if (valid) {
-                            atomicAdd(&h[b * nc + *reinterpret_cast<const int*>(row + ro)], 1);
-                        }
-                    }
-                }
-                __syncthreads();
-            }
-            // ---- scan of the non-empty bins
-            unsigned long long key = kNoKey;
-            if (active) {
-                __syncwarp();
-                int nm;
-                warp_compact_bins(mask, bl, lane, nm);
-                const int nbf = D.nb[f];
-                (void)nbf;
-                float bestv = 1e20f;
-                int bestj = 0x7fffffff;
-                if (regr) {
-                    if (lane == 0) {
-                        float tot = 0.0f;
-                        for (int j = 0; j < nm; ++j) tot += sy[bl[j]];
-                        float l = 0.0f, r = tot;
-                        for (int j = 0; j < nm; ++j) {
-                            const float s = sy[bl[j]];
-                            l += s;
-                            r -= s;
-                            sy[j] = l;
-                            r1[j] = r;
-                        }
-                    } else if (lane == 1) {
-                        float tot = 0.0f;
-                        for (int j = 0; j < nm; ++j) tot += sy2[bl[j]];
-                        float l = 0.0f, r = tot;
-                        for (int j = 0; j < nm; ++j) {
-                            const float s = sy2[bl[j]];
-                            l += s;
-                            r -= s;
-                            sy2[j] = l;
-                            r2[j] = r;
-                        }
-                    } else if (lane == 2) {
-                        int l = 0;
-                        for (int j = 0; j < nm; ++j) {
-                            l += cn[bl[j]];
-                            cn[j] = l;
-                        }
-                    }
-                    __syncwarp();
-                    for (int j = lane; j < nm - 1; j += 32) {
-                        const float cl = (float)cn[j], cr = (float)(c - cn[j]);
-                        const float sl = sy[j], sr = r1[j], s2l = sy2[j], s2r = r2[j];
-                        const float ml = sl / cl, mr = sr / cr;
-                        const float vl = s2l / cl - ml * ml, vr = s2r / cr - mr * mr;
-                        const float tot = cl + cr;
-                        const float mse = (cl * vl + cr * vr) / tot;
-                        if (mse < bestv) { bestv = mse; bestj = j; }
-                    }
-                } else {
-                    if (lane < nc) {
-                        int l = 0;
-                        for (int j = 0; j < nm; ++j) {
-                            l += h[bl[j] * nc + lane];
-                            h[j * nc + lane] = l;
-                        }
-                        tc[lane] = l;
-                    }
-                    __syncwarp();
-                    for (int j = lane; j < nm - 1; j += 32) {
-                        int tl = 0;
-                        for (int k = 0; k < nc; ++k) tl += h[j * nc + k];
-                        const float tlf = (float)tl, trf = (float)(c - tl);
-                        float gl = 1.0f, gr = 1.0f;
-                        for (int k = 0; k < nc; ++k) {
-                            const int lk = h[j * nc + k];
-                            const float pl = (float)lk / tlf;
-                            const float pr = (float)(tc[k] - lk) / trf;
-                            gl -= pl * pl;
-                            gr -= pr * pr;
-                        }
-                        const float tot = tlf + trf;
-                        const float g = (tlf * gl + trf * gr) / tot;
-                        if (g < bestv) { bestv = g; bestj = j; }
-                    }
-                }
-                // first minimum across lanes
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float ov = __shfl_xor_sync(kFull, bestv, o);
-                    const int oj = __shfl_xor_sync(kFull, bestj, o);
-                    if (ov < bestv || (ov == bestv && oj < bestj)) { bestv = ov; bestj = oj; }
-                }
-                if (bestj != 0x7fffffff) {
-                    const float crit = regr ? bestv : -(2.0f - bestv);
-                    key = ((unsigned long long)ord_of(crit) << 32) |
-                          ((unsigned long long)mv << 8) | (unsigned long long)bl[bestj];
-                }
-                __syncwarp();
-                // restore zeroed scratch
-                if (regr) {
-                    for (int j = lane; j < nm; j += 32) {
-                        const int b = bl[j];
-                        sy[j] = 0.0f; sy2[j] = 0.0f; cn[j] = 0;
-                        sy[b] = 0.0f; sy2[b] = 0.0f; cn[b] = 0;
-                    }
-                } else {
-                    for (int j = lane; j < nm; j += 32) {
-                        const int b = bl[j];
-                        for (int k = 0; k < nc; ++k) { h[j * nc + k] = 0; h[b * nc + k] = 0; }
-                    }
-                }
-                __syncwarp();
-            }
-            if (lane == 0) wkey[wib] = key;
-            __syncthreads();
-            if (threadIdx.x == 0)
-                for (int w = 0; w < nwarp_blk; ++w) best_key = min(best_key, wkey[w]);
-            __syncthreads();
-        }
-        if (threadIdx.x == 0) B.nd_key[m] = best_key;
+        B.counters[4] = bcarry;
     }
 }
 
@@ -505,6 +288,7 @@ __global__ void __launch_bounds__(1024) k_commit(Data D, Batch B) {
                 B.xbest[m] = split;
                 B.treemap[2 * m] = child;
                 B.treemap[2 * m + 1] = child + 1;
+                if (B.nd_cnt[m] > kBigSegment) B.part_big[atomicAdd(&B.counters[5], 1)] = (long long)m;
                 B.status[(size_t)t * M + child] = 2;
                 B.status[(size_t)t * M + child + 1] = 2;
             } else {
@@ -551,6 +335,7 @@ __global__ void __launch_bounds__(256) k_partition(Data D, Batch B, int cur) {
         const float* x = D.xc + (size_t)f * D.N;
         const int* src = B.seg[cur] + (size_t)t * D.N + start;
         int* dst = B.seg[cur ^ 1] + (size_t)t * D.N + start;
+        if (c > kBigSegment) continue;  // k_partition_big
         const bool cache = c <= 32 * 64;
         int nl = 0;
         for (int b0 = 0, q = 0; b0 < c; b0 += 32, ++q) {
@@ -587,6 +372,91 @@ __global__ void __launch_bounds__(256) k_partition(Data D, Batch B, int cur) {
             B.nd_start[mr] = start + nl;
             B.nd_cnt[mr] = c - nl;
         }
+    }
+}
+
+// Stable partition of the large split segments (c > kBigSegment), one block per node.
+// Pass 1 evaluates x <= split for every row (8 consecutive rows per thread, gathers in
+// flight together) and keeps the outcome as a bitmask in shared memory; pass 2 scatters
+// with a block-wide scan per 2048-row tile.  Segments longer than the bitmask (384,000
+// rows) re-evaluate the comparison in pass 2.
+constexpr int kPartItems = 8;
+constexpr int kPartBitWords = 12000;  // ~47 KiB of flags (static shared memory limit)
+
+__global__ void __launch_bounds__(256) k_partition_big(Data D, Batch B, int cur) {
+    __shared__ uint32_t flags[kPartBitWords];
+    __shared__ int ws[32];
+    __shared__ int red;
+    const int total = B.counters[5];
+    const int tile = kPartItems * blockDim.x;
+    for (int w = blockIdx.x; w < total; w += gridDim.x) {
+        const size_t m = (size_t)B.part_big[w];
+        const int t = (int)(m / B.M);
+        const int c = B.nd_cnt[m];
+        const int start = B.nd_start[m];
+        const int f = B.bestvar[m];
+        const float split = B.xbest[m];
+        const float* x = D.xc + (size_t)f * D.N;
+        const int* src = B.seg[cur] + (size_t)t * D.N + start;
+        int* dst = B.seg[cur ^ 1] + (size_t)t * D.N + start;
+        const bool cached = c <= kPartBitWords * 32;
+        if (threadIdx.x == 0) red = 0;
+        __syncthreads();
+        int mine = 0;
+        for (int b0 = 0; b0 < c; b0 += tile) {
+            const int i0 = b0 + threadIdx.x * kPartItems;
+            uint32_t bitsv = 0;
+#pragma unroll
+            for (int k = 0; k < kPartItems; ++k) {
+                const int i = i0 + k;
+                if (i < c && x[src[i]] <= split) bitsv |= 1u << k;
+            }
+            mine += __popc(bitsv);
+            if (cached && i0 < c) reinterpret_cast<uint8_t*>(flags)[i0 >> 3] = (uint8_t)bitsv;
+        }
+        atomicAdd(&red, mine);
+        __syncthreads();
+        const int nl = red;
+        int lcarry = 0, rcarry = 0;
+        for (int b0 = 0; b0 < c; b0 += tile) {
+            const int i0 = b0 + threadIdx.x * kPartItems;
+            uint32_t bitsv = 0;
+            if (cached) {
+                bitsv = i0 < c ? reinterpret_cast<const uint8_t*>(flags)[i0 >> 3] : 0u;
+            } else {
+#pragma unroll
+                for (int k = 0; k < kPartItems; ++k) {
+                    const int i = i0 + k;
+                    if (i < c && x[src[i]] <= split) bitsv |= 1u << k;
+                }
+            }
+            const int nvalid = max(0, min(kPartItems, c - i0));
+            const int lcnt = __popc(bitsv);
+            int ltot, rtot;
+            const int lex = block_excl_scan(lcnt, ws, ltot);
+            const int rex = block_excl_scan(nvalid - lcnt, ws, rtot);
+            int lp = lcarry + lex, rp = nl + rcarry + rex;
+#pragma unroll
+            for (int k = 0; k < kPartItems; ++k) {
+                const int i = i0 + k;
+                if (i < c) {
+                    const int sid = src[i];
+                    if ((bitsv >> k) & 1u) dst[lp++] = sid;
+                    else dst[rp++] = sid;
+                }
+            }
+            lcarry += ltot;
+            rcarry += rtot;
+        }
+        if (threadIdx.x == 0) {
+            const int l = B.treemap[2 * m], r = B.treemap[2 * m + 1];
+            const size_t ml = (size_t)t * B.M + l, mr = (size_t)t * B.M + r;
+            B.nd_start[ml] = start;
+            B.nd_cnt[ml] = nl;
+            B.nd_start[mr] = start + nl;
+            B.nd_cnt[mr] = c - nl;
+        }
+        __syncthreads();
     }
 }
 

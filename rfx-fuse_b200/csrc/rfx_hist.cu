@@ -1,0 +1,397 @@
+// Histogram split search: histogram_find_best_split_classification / _regression
+// (src/rf_growtree.cpp:22-184) and the per-node comparison across the mtry draws
+// (src/rf_growtree.cpp:820-836, :929-955), for every searched node of a level at once.
+//
+// Two kernels share the work by node size:
+//   k_hist        nodes with more than kSmallNode rows: one block per (node, group of up to
+//                 8 draws), one warp per drawn feature, the node's rows streamed through
+//                 shared memory in chunks;
+//   k_hist_small  nodes with at most kSmallNode rows (the great majority at deep levels):
+//                 one warp per node does all mtry draws from rows staged once.
+//
+// Each warp builds its feature's histogram: classification as integer class counts (the
+// reference's float counts are small integers, so exact); regression as float sums that
+// equal the reference's row-order serial sums bin by bin -- rows that hit the same bin
+// within a 32-row step are added one rank at a time, in row order.
+//
+// Only non-empty bins can win (an empty bin repeats the previous bin's criterion and the
+// reference keeps the first of equal values), so the scan runs over the ascending list of
+// non-empty bins.  The scan's running left/right sums are serial float chains in the
+// reference and are computed in bin order; the criterion of every candidate bin is then
+// evaluated in parallel and the first minimum wins.
+//
+// Winner key = (order-preserving bits of the criterion, draw index, bin); the smallest key
+// over all draws of the node is the reference's choice (regression: lowest MSE, first draw
+// wins ties; classification: highest 2 - gini, i.e. lowest -(2 - gini), first draw wins).
+#include "rfx_device.cuh"
+#include "rfx_kernels.h"
+
+namespace rfx {
+
+// bl[0..m) = ascending list of the non-empty bins (cnt[b] > 0).
+__device__ __forceinline__ int warp_nonempty_bins(const int* cnt, uint8_t* bl, int lane) {
+    int k = 0;
+    uint32_t bits = 0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+        if (cnt[lane * 8 + q] > 0) { bits |= 1u << q; ++k; }
+    int x = k;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFull, x, o);
+        if (lane >= o) x += y;
+    }
+    int off = x - k;
+    while (bits) {
+        const int q = __ffs(bits) - 1;
+        bits &= bits - 1;
+        bl[off++] = (uint8_t)(lane * 8 + q);
+    }
+    const int m = __shfl_sync(kFull, x, 31);
+    __syncwarp();
+    return m;
+}
+
+// Byte q of each of four words -> one word (row r in byte r).
+__device__ __forceinline__ uint32_t gather_byte(uint32_t a, uint32_t b, uint32_t c, uint32_t d, int q) {
+    const uint32_t lo = __byte_perm(a, b, (uint32_t)(q | ((q + 4) << 4)));
+    const uint32_t hi = __byte_perm(c, d, (uint32_t)(q | ((q + 4) << 4)));
+    return __byte_perm(lo, hi, 0x5410);
+}
+
+// Fold one draw's histogram (sy/sy2/cn or h/cn) into its best key; restores the zeroed
+// scratch.  `c` = node rows, `mv` = draw index.  All lanes call it.
+__device__ __forceinline__ unsigned long long scan_bins(bool regr, int nc, int c, int mv, int lane,
+                                                        uint8_t* bl, float* sy, float* sy2,
+                                                        int* cn, int* h) {
+    const int nm = warp_nonempty_bins(cn, bl, lane);
+    float bestv = 1e20f;
+    int bestj = 0x7fffffff;
+    if (regr) {
+        // bins in 32-wide slices; the serial chains run redundantly on every lane from
+        // shuffled per-bin totals (one add per non-empty bin, no shared-memory round trips)
+        float tot = 0.0f, tot2 = 0.0f;
+        for (int s0 = 0; s0 < nm; s0 += 32) {
+            const int j = s0 + lane;
+            const int b = j < nm ? bl[j] : 0;
+            const float sa = j < nm ? sy[b] : 0.0f, qa = j < nm ? sy2[b] : 0.0f;
+            const int kmax = min(32, nm - s0);
+            for (int k = 0; k < kmax; ++k) {
+                tot += __shfl_sync(kFull, sa, k);
+                tot2 += __shfl_sync(kFull, qa, k);
+            }
+        }
+        float L = 0.0f, R = tot, L2 = 0.0f, R2 = tot2;
+        int kc = 0;
+        for (int s0 = 0; s0 < nm; s0 += 32) {
+            const int j = s0 + lane;
+            const int b = j < nm ? bl[j] : 0;
+            const float sa = j < nm ? sy[b] : 0.0f, qa = j < nm ? sy2[b] : 0.0f;
+            const int ka = j < nm ? cn[b] : 0;
+            float mL = 0.0f, mR = 0.0f, mL2 = 0.0f, mR2 = 0.0f;
+            int mC = 0;
+            const int kmax = min(32, nm - s0);
+            for (int k = 0; k < kmax; ++k) {
+                const float a = __shfl_sync(kFull, sa, k);
+                const float a2 = __shfl_sync(kFull, qa, k);
+                kc += __shfl_sync(kFull, ka, k);
+                L += a;
+                R -= a;
+                L2 += a2;
+                R2 -= a2;
+                if (k == lane) { mL = L; mR = R; mL2 = L2; mR2 = R2; mC = kc; }
+            }
+            if (j < nm - 1) {
+                const float cl = (float)mC, cr = (float)(c - mC);
+                const float ml = mL / cl, mr = mR / cr;
+                const float vl = mL2 / cl - ml * ml, vr = mR2 / cr - mr * mr;
+                const float tt = cl + cr;
+                const float mse = (cl * vl + cr * vr) / tt;
+                if (mse < bestv) { bestv = mse; bestj = j; }
+            }
+        }
+    } else {
+        // integer class prefix over the non-empty bins (lane k owns class k), in place
+        __syncwarp();
+        if (lane < nc) {
+            int l = 0;
+            for (int j = 0; j < nm; ++j) {
+                l += h[bl[j] * nc + lane];
+                h[j * nc + lane] = l;
+            }
+            h[256 * nc + lane] = l;  // class totals
+        }
+        __syncwarp();
+        const int* tc = h + 256 * nc;
+        for (int j = lane; j < nm - 1; j += 32) {
+            int tl = 0;
+            for (int k = 0; k < nc; ++k) tl += h[j * nc + k];
+            const float tlf = (float)tl, trf = (float)(c - tl);
+            float gl = 1.0f, gr = 1.0f;
+            for (int k = 0; k < nc; ++k) {
+                const int lk = h[j * nc + k];
+                const float pl = (float)lk / tlf;
+                const float pr = (float)(tc[k] - lk) / trf;
+                gl -= pl * pl;
+                gr -= pr * pr;
+            }
+            const float tt = tlf + trf;
+            const float g = (tlf * gl + trf * gr) / tt;
+            if (g < bestv) { bestv = g; bestj = j; }
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, bestv, o);
+        const int oj = __shfl_xor_sync(kFull, bestj, o);
+        if (ov < bestv || (ov == bestv && oj < bestj)) { bestv = ov; bestj = oj; }
+    }
+    unsigned long long key = kNoKey;
+    if (bestj != 0x7fffffff) {
+        const float crit = regr ? bestv : -(2.0f - bestv);
+        key = ((unsigned long long)ord_of(crit) << 32) | ((unsigned long long)mv << 8) |
+              (unsigned long long)bl[bestj];
+    }
+    __syncwarp();
+    for (int j = lane; j < nm; j += 32) {
+        const int b = bl[j];
+        if (regr) {
+            sy[b] = 0.0f;
+            sy2[b] = 0.0f;
+        } else {
+            for (int k = 0; k < nc; ++k) { h[j * nc + k] = 0; h[b * nc + k] = 0; }
+        }
+        cn[b] = 0;
+    }
+    __syncwarp();
+    return key;
+}
+
+// Per-warp scratch layout shared by both kernels (after any staging area):
+//   bl[256] uint8 | sy[256] f32 | sy2[256] f32 | cn[256] i32 | h[(256+1) * nclass] i32
+__device__ __forceinline__ void warp_scratch(uint8_t* w, uint8_t*& bl, float*& sy, float*& sy2,
+                                             int*& cn, int*& h) {
+    bl = w;
+    sy = reinterpret_cast<float*>(w + 256);
+    sy2 = sy + kBins;
+    cn = reinterpret_cast<int*>(sy2 + kBins);
+    h = cn + kBins;
+}
+
+// Histogram of one feature over the 32-row step starting at row s0 (bins `b`, targets v/v2
+// or label), rows in order.  All lanes call it.
+__device__ __forceinline__ void hist_step(bool regr, int nc, bool valid, int b, float v, float v2,
+                                          int label, int lane, float* sy, float* sy2, int* cn,
+                                          int* h) {
+    const uint32_t peers = __match_any_sync(kFull, b);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (regr) {
+        const int maxr = __reduce_max_sync(kFull, valid ? __popc(peers) - 1 : 0);
+        for (int qq = 0; qq <= maxr; ++qq) {
+            if (valid && rank == qq) {
+                sy[b] += v * 1.0f;
+                sy2[b] += v2 * 1.0f;
+                cn[b] += 1;
+            }
+            __syncwarp();
+        }
+    } else {
+        if (valid) {
+            atomicAdd(&h[b * nc + label], 1);
+            if (rank == 0) atomicAdd(&cn[b], __popc(peers));
+        }
+        __syncwarp();
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Large nodes.  The block streams the node's packed rows (uint8 bins of every feature +
+// the target) from L2 through shared memory: each thread loads 4 consecutive rows x 16
+// bytes into registers, the next chunk's loads in flight while the warps work on the
+// current one, and stores them transposed (feature-major, padded stride) so that the 32
+// lanes of a warp read 32 consecutive bytes of their feature without bank conflicts.
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_hist(Data D, Batch B, int cur, HistArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ int snode[2];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int nthr = blockDim.x;
+    const bool regr = D.nclass == 1;
+    const int nc = D.nclass;
+    const int rs = D.rs, ro = D.ro;
+    const int pieces = rs >> 4;
+    const int CH = a.stage_rows;
+    const int CS = a.cstride;
+    uint8_t* col = smem;                                                    // [rs][CS]
+    uint32_t* ytgt = reinterpret_cast<uint32_t*>(smem + (size_t)rs * CS);   // [CH][2]
+    uint8_t* wbase = smem + (size_t)rs * CS + (size_t)CH * 8 + (size_t)wib * a.warp_bytes;
+    uint8_t* bl;
+    float *sy, *sy2;
+    int *cn, *h;
+    warp_scratch(wbase, bl, sy, sy2, cn, h);
+    for (int k = lane; k < a.warp_bytes / 4; k += 32) reinterpret_cast<uint32_t*>(wbase)[k] = 0u;
+    __syncwarp();
+    const int total = B.counters[4] * a.groups;
+    const int units = (CH >> 2) * pieces;
+    for (int task = blockIdx.x; task < total; task += gridDim.x) {
+        const int si = task / a.groups, grp = task - si * a.groups;
+        if (threadIdx.x == 0) {
+            const int t = tree_of(B.srch_big_off, B.T, si);
+            snode[0] = t;
+            snode[1] = B.srch_big[(size_t)t * B.M + (si - B.srch_big_off[t])];
+        }
+        __syncthreads();
+        const int t = snode[0], node = snode[1];
+        const size_t m = (size_t)t * B.M + node;
+        const int start = B.nd_start[m], c = B.nd_cnt[m];
+        const int* seg = B.seg[cur] + (size_t)t * D.N + start;
+        const uint16_t* featp = B.feat + (size_t)t * B.M * B.mtry + (size_t)node * B.mtry;
+        if (threadIdx.x == 0 && grp == 0 && B.hist_bytes)
+            atomicAdd(B.hist_bytes, (unsigned long long)c * (unsigned long long)(B.mtry + (regr ? 4 : 1)));
+        const int mv = grp * a.warps + wib;
+        const bool active = mv < B.mtry;
+        const int f = active ? featp[mv] : 0;
+        uint4 reg[2][4];
+        auto load_chunk = [&](int c0) {
+            const int ch = min(CH, c - c0);
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int unit = threadIdx.x + u * nthr;
+                if (unit < units) {
+                    const int rg = unit / pieces, pc = unit - rg * pieces;
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const int i = rg * 4 + r;
+                        reg[u][r] = i < ch ? __ldg(reinterpret_cast<const uint4*>(D.rows + (size_t)seg[c0 + i] * rs) + pc)
+                                           : make_uint4(0, 0, 0, 0);
+                    }
+                }
+            }
+        };
+        auto store_chunk = [&]() {
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int unit = threadIdx.x + u * nthr;
+                if (unit < units) {
+                    const int rg = unit / pieces, pc = unit - rg * pieces;
+                    const uint32_t* w0 = reinterpret_cast<const uint32_t*>(&reg[u][0]);
+                    const uint32_t* w1 = reinterpret_cast<const uint32_t*>(&reg[u][1]);
+                    const uint32_t* w2 = reinterpret_cast<const uint32_t*>(&reg[u][2]);
+                    const uint32_t* w3 = reinterpret_cast<const uint32_t*>(&reg[u][3]);
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const int w = j >> 2, q = j & 3;
+                        *reinterpret_cast<uint32_t*>(col + (size_t)(pc * 16 + j) * CS + rg * 4) =
+                            gather_byte(w0[w], w1[w], w2[w], w3[w], q);
+                    }
+                    if (pc == (ro >> 4)) {
+                        const bool hi = (ro & 15) != 0;  // target in words 2,3 of the piece
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) {
+                            const uint4 v = reg[u][r];
+                            reinterpret_cast<uint2*>(ytgt)[rg * 4 + r] =
+                                hi ? make_uint2(v.z, v.w) : make_uint2(v.x, v.y);
+                        }
+                    }
+                }
+            }
+        };
+        if (c > 0) load_chunk(0);
+        for (int c0 = 0; c0 < c; c0 += CH) {
+            const int ch = min(CH, c - c0);
+            __syncthreads();
+            store_chunk();
+            __syncthreads();
+            if (c0 + CH < c) load_chunk(c0 + CH);  // in flight during the histogram work
+            if (active) {
+                const uint8_t* fcol = col + (size_t)f * CS;
+                for (int s0 = 0; s0 < ch; s0 += 32) {
+                    const int i = s0 + lane;
+                    const bool valid = i < ch;
+                    const int b = valid ? fcol[i] : kBins;
+                    const uint2 yy = reinterpret_cast<const uint2*>(ytgt)[i];
+                    hist_step(regr, nc, valid, b, __uint_as_float(yy.x), __uint_as_float(yy.y),
+                              (int)yy.x, lane, sy, sy2, cn, h);
+                }
+            }
+        }
+        if (active) {
+            __syncwarp();
+            const unsigned long long key = scan_bins(regr, nc, c, mv, lane, bl, sy, sy2, cn, h);
+            if (lane == 0 && key != kNoKey) atomicMin(&B.nd_key[m], key);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Small nodes (c <= kSmallNode rows): one warp per searched node does all mtry draws.
+// The node's rows are staged once in the warp's own shared memory (row-major with a
+// 4-byte pad, so each lane reading its own row's byte f is conflict free); the targets
+// stay in registers.
+// ---------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, int warp_bytes) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const bool regr = D.nclass == 1;
+    const int nc = D.nclass;
+    const int rs = D.rs, ro = D.ro;
+    const int RS = rs + 4;
+    uint8_t* wbase = smem + (size_t)wib * warp_bytes;
+    uint8_t* stage = wbase;  // [kSmallNode][RS]
+    uint8_t* bl;
+    float *sy, *sy2;
+    int *cn, *h;
+    warp_scratch(stage + kSmallNode * RS, bl, sy, sy2, cn, h);
+    for (int k = lane; k < (warp_bytes - kSmallNode * RS) / 4; k += 32)
+        reinterpret_cast<uint32_t*>(bl)[k] = 0u;
+    __syncwarp();
+    const int total = B.counters[1];
+    const int nwarps = gridDim.x * (blockDim.x >> 5);
+    const int words = rs >> 2;
+    for (int si = blockIdx.x * (blockDim.x >> 5) + wib; si < total; si += nwarps) {
+        const int t = tree_of(B.srch_off, B.T, si);
+        const int node = B.srch[(size_t)t * B.M + (si - B.srch_off[t])];
+        const size_t m = (size_t)t * B.M + node;
+        const int c = B.nd_cnt[m];
+        if (c > kSmallNode) continue;  // k_hist
+        if (lane == 0 && B.hist_bytes)
+            atomicAdd(B.hist_bytes, (unsigned long long)c * (unsigned long long)(B.mtry + (regr ? 4 : 1)));
+        const int* seg = B.seg[cur] + (size_t)t * D.N + B.nd_start[m];
+        const uint16_t* featp = B.feat + (size_t)t * B.M * B.mtry + (size_t)node * B.mtry;
+        float v[2] = {0.0f, 0.0f}, v2[2] = {0.0f, 0.0f};
+        int lab[2] = {0, 0};
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+            const int i = hh * 32 + lane;
+            if (i < c) {
+                const uint4* src = reinterpret_cast<const uint4*>(D.rows + (size_t)seg[i] * rs);
+                uint32_t* dst = reinterpret_cast<uint32_t*>(stage + (size_t)i * RS);
+                for (int w = 0; w < words; w += 4) {
+                    const uint4 q = __ldg(src + (w >> 2));
+                    dst[w] = q.x; dst[w + 1] = q.y; dst[w + 2] = q.z; dst[w + 3] = q.w;
+                }
+                v[hh] = __uint_as_float(dst[ro >> 2]);
+                v2[hh] = __uint_as_float(dst[(ro >> 2) + 1]);
+                lab[hh] = (int)dst[ro >> 2];
+            }
+        }
+        __syncwarp();
+        unsigned long long best = kNoKey;
+        for (int mv = 0; mv < B.mtry; ++mv) {
+            const int f = featp[mv];
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+                if (hh * 32 < c) {
+                    const int i = hh * 32 + lane;
+                    const bool valid = i < c;
+                    const int b = valid ? stage[(size_t)i * RS + f] : kBins;
+                    hist_step(regr, nc, valid, b, v[hh], v2[hh], lab[hh], lane, sy, sy2, cn, h);
+                }
+            }
+            best = min(best, scan_bins(regr, nc, c, mv, lane, bl, sy, sy2, cn, h));
+        }
+        if (lane == 0) B.nd_key[m] = best;
+        __syncwarp();
+    }
+}
+
+}  // namespace rfx

@@ -7,7 +7,10 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <random>
 #include <stdexcept>
 #include <string>
@@ -98,7 +101,7 @@ struct Ctx {
     std::vector<float> classwt;
     rfx::Data D{};
     DBuf xc, rows, edges, nb, kind, cat, lab, yreg, yv, perm, ks, cumw, totw, keys_a, keys_b;
-    int perm_n = -1;
+    cudaEvent_t perm_event = nullptr;  // owned by the process-wide permutation cache
 
     // accumulators
     DBuf nout, votes, oob_sum, avimp, sqsd, prox_own, qtmp, cw_dev, tree_oob_all;
@@ -107,13 +110,20 @@ struct Ctx {
     int trees_done = 0;
     int tree_oob_cap = 0, tree_oob_n = 0;
 
+    // measurement
+    bool profiling = false;
+    bool level_log = std::getenv("RFX_LEVEL_LOG") != nullptr;  // per-level trace on stderr
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    long long launches = 0, hist_launches = 0, levels = 0, trees = 0;
+    double hist_ms = 0.0;
+
     // batch buffers
     int Tcap = 0;
     rfx::Batch B{};
     DBuf b_nin, b_seg0, b_seg1, b_ninbag, b_oob, b_noob, b_mt, b_mtpos, b_status, b_bestvar,
         b_xbest, b_treemap, b_nodeclass, b_nodepred, b_tnodewt, b_ndstart, b_ndcnt, b_ndbuf,
         b_ndflag, b_ndcrit0, b_ndmaj, b_ndsum, b_ndkey, b_feat, b_lvl, b_srch, b_srchcnt,
-        b_srchoff, b_counters, b_oobleaf, b_used, b_right, b_rightimp, b_d2, b_d0, b_rr;
+        b_srchoff, b_counters, b_oobleaf, b_used, b_right, b_rightimp, b_d2, b_d0, b_rr, b_srchbig, b_partbig;
 
     ~Ctx() {
         DBuf* all[] = {&xc, &rows, &edges, &nb, &kind, &cat, &lab, &yreg, &yv, &perm, &ks, &cumw,
@@ -123,14 +133,44 @@ struct Ctx {
                        &b_xbest, &b_treemap, &b_nodeclass, &b_nodepred, &b_tnodewt, &b_ndstart,
                        &b_ndcnt, &b_ndbuf, &b_ndflag, &b_ndcrit0, &b_ndmaj, &b_ndsum, &b_ndkey,
                        &b_feat, &b_lvl, &b_srch, &b_srchcnt, &b_srchoff, &b_counters,
-                       &b_oobleaf, &b_used, &b_right, &b_rightimp, &b_d2, &b_d0, &b_rr};
+                       &b_oobleaf, &b_used, &b_right, &b_rightimp, &b_d2, &b_d0, &b_rr, &b_srchbig, &b_partbig};
         cudaSetDevice(device);
         if (st) cudaStreamSynchronize(st);
         for (DBuf* b : all) b->release();
         if (h_counters) cudaFreeHost(h_counters);
+        if (ev0) cudaEventDestroy(ev0);
+        if (ev1) cudaEventDestroy(ev1);
         if (st) cudaStreamDestroy(st);
     }
 };
+
+// Importance permutation cache, one per (device, N), never freed (process lifetime).  It
+// is computed on a side stream; only the importance kernels wait for its event.
+struct PermEntry {
+    int* perm = nullptr;
+    cudaEvent_t done = nullptr;
+};
+
+const PermEntry& permutation_for(int device, int N) {
+    static std::mutex mu;
+    static std::map<std::pair<int, int>, PermEntry> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find({device, N});
+    if (it != cache.end()) return it->second;
+    PermEntry e;
+    int* ks = nullptr;
+    cudaStream_t side = nullptr;
+    RFX_CUDA(cudaMalloc(&e.perm, (size_t)N * 4));
+    RFX_CUDA(cudaMalloc(&ks, (size_t)std::max(N, 1) * 4));
+    RFX_CUDA(cudaStreamCreateWithFlags(&side, cudaStreamNonBlocking));
+    RFX_CUDA(cudaEventCreateWithFlags(&e.done, cudaEventDisableTiming));
+    rfx::k_permutation<<<1, 256, 0, side>>>(N, 42u, ks, e.perm);
+    RFX_LAUNCH("k_permutation");
+    RFX_CUDA(cudaEventRecord(e.done, side));
+    RFX_CUDA(cudaFreeAsync(ks, side));
+    RFX_CUDA(cudaStreamDestroy(side));  // returns at once; queued work still completes
+    return cache.emplace(std::make_pair(device, N), e).first->second;
+}
 
 Ctx* as_ctx(void* c) {
     require(c != nullptr, RFX_ERR_ARG, "null context");
@@ -191,11 +231,16 @@ void alloc_batch(Ctx& c, int Tcap) {
     B.nxt_lo = lvl + 2 * T;
     B.nxt_hi = lvl + 3 * T;
     B.nnode = lvl + 4 * T;
-    B.lvl_off = (int*)c.b_srchoff.get((T + 1) * 8);
+    B.lvl_off = (int*)c.b_srchoff.get((T + 1) * 12);
     B.srch_off = B.lvl_off + (T + 1);
+    B.srch_big_off = B.srch_off + (T + 1);
+    B.srch_big = (int*)c.b_srchbig.get(T * M * 4);
+    B.part_big = (long long*)c.b_partbig.get(T * (N / rfx::kBigSegment + 2) * 8);
     B.srch = (int*)c.b_srch.get(T * M * 4);
-    B.srch_cnt = (int*)c.b_srchcnt.get(T * 4);
+    B.srch_cnt = (int*)c.b_srchcnt.get(T * 8);
+    B.srch_big_cnt = B.srch_cnt + T;
     B.counters = (int*)c.b_counters.get(64);
+    B.hist_bytes = reinterpret_cast<unsigned long long*>(B.counters + 8);
     B.oob_leaf = (int*)c.b_oobleaf.get(T * N * 4);
     B.used = (uint8_t*)c.b_used.get(T * p);
     B.right = (int*)c.b_right.get(T * 4);
@@ -222,6 +267,7 @@ void load(Ctx& c, const rfx_fit_params* prm, const rfx_inputs* in) {
     const rfx_fit_params P = *prm;
     require(P.task >= 0 && P.task <= 2, RFX_ERR_ARG, "task must be 0, 1 or 2");
     require(P.n >= 1 && P.p >= 1, RFX_ERR_ARG, "n and p must be positive");
+    require(P.p <= 1000, RFX_ERR_UNSUPPORTED, "more than 1000 features is not supported");
     require(P.mtry >= 1 && P.mtry < (1 << 24), RFX_ERR_ARG, "mtry must be >= 1");
     require(P.maxnode >= 1, RFX_ERR_ARG, "maxnode must be >= 1");
     require(P.nbins >= 2 && P.nbins <= 256, RFX_ERR_ARG, "nbins must be in [2, 256]");
@@ -345,15 +391,11 @@ void load(Ctx& c, const rfx_fit_params* prm, const rfx_inputs* in) {
         D.cumw = cum;
         D.totw = h;
     }
-    // importance permutation depends on N only
-    if (c.perm_n != (int)N) {
-        int* pm = (int*)c.perm.get(N * 4);
-        int* kss = (int*)c.ks.get(N * 4);
-        rfx::k_permutation<<<1, 256, 0, st>>>((int)N, 42u, kss, pm);
-        RFX_LAUNCH("k_permutation");
-        c.perm_n = (int)N;
+    {
+        const PermEntry& pe = permutation_for(c.device, (int)N);
+        D.perm = pe.perm;
+        c.perm_event = pe.done;
     }
-    D.perm = (const int*)c.perm.p;
     // accumulators
     int* no = (int*)c.nout.get(N * 4);
     RFX_CUDA(cudaMemsetAsync(no, 0, N * 4, st));
@@ -388,33 +430,41 @@ void load(Ctx& c, const rfx_fit_params* prm, const rfx_inputs* in) {
     Tcap = (int)std::max<size_t>(1, std::min<size_t>((size_t)Tcap, budget / per_tree));
     Tcap = std::min(Tcap, 4096);
     alloc_batch(c, Tcap);
+    RFX_CUDA(cudaMemsetAsync(c.B.counters, 0, 64, st));
     RFX_CUDA(cudaStreamSynchronize(st));
     c.loaded = true;
 }
 
-// Dynamic shared memory layout of k_hist.
+// Launch shapes of the histogram kernels (rfx_hist.cu).
 struct HistCfg {
-    int warps, stage_rows, warp_bytes, smem, grid;
+    rfx::HistArgs a;
+    int threads, smem, grid;
+    int small_warp_bytes, small_smem, small_grid;
 };
 
 HistCfg hist_cfg(Ctx& c) {
     HistCfg h;
-    h.warps = std::min(c.prm.mtry, 16);
-    h.stage_rows = std::max(32, std::min(256, 16384 / c.D.rs));
-    if (c.nclass == 1) h.warp_bytes = (int)round_up(288 + 5 * 1024, 16);
-    else h.warp_bytes = (int)round_up(288 + 1024 * c.nclass + 128, 16);
-    h.smem = h.stage_rows * c.D.rs + h.warps * h.warp_bytes;
-    static thread_local int configured_dev = -1;
-    static thread_local int configured_smem = -1;
-    if (configured_dev != c.device || configured_smem < h.smem) {
-        RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      std::max(h.smem, 48 * 1024)));
-        configured_dev = c.device;
-        configured_smem = h.smem;
-    }
+    const int pieces = c.D.rs / 16;
+    const int scratch = (int)round_up(256 + 3 * 1024 + (c.nclass > 1 ? (257 * c.nclass + 32) * 4 : 0), 16);
+    h.a.warps = 8;
+    h.a.groups = (c.prm.mtry + h.a.warps - 1) / h.a.warps;
+    // rows per staged chunk: a multiple of 32 with at most 2 load units per thread
+    h.a.stage_rows = std::min(256, (2 * 256 * 4 / pieces) / 32 * 32);
+    h.a.cstride = h.a.stage_rows + 4;
+    h.a.warp_bytes = scratch;
+    h.threads = 32 * h.a.warps;
+    h.smem = c.D.rs * h.a.cstride + h.a.stage_rows * 8 + h.a.warps * h.a.warp_bytes;
+    RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  std::max(h.smem, 48 * 1024)));
     int per_sm = 0;
-    RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist, h.warps * 32, h.smem));
+    RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist, h.threads, h.smem));
     h.grid = c.sm_count * std::max(1, per_sm);
+    h.small_warp_bytes = (int)round_up(rfx::kSmallNode * (c.D.rs + 4), 16) + scratch;
+    h.small_smem = 8 * h.small_warp_bytes;
+    RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  std::max(h.small_smem, 48 * 1024)));
+    RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist_small, 256, h.small_smem));
+    h.small_grid = c.sm_count * std::max(1, per_sm);
     return h;
 }
 
@@ -451,7 +501,7 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
     RFX_CUDA(cudaMemsetAsync(B.nodepred, 0, T * M * 4, st));
     RFX_CUDA(cudaMemsetAsync(B.tnodewt, 0, T * M * 4, st));
     RFX_CUDA(cudaMemsetAsync(B.oob_leaf, 0xff, T * N * 4, st));
-    RFX_CUDA(cudaMemsetAsync(B.counters, 0, 64, st));
+    RFX_CUDA(cudaMemsetAsync(B.counters, 0, 32, st));  // level counters; hist_bytes persists
     RFX_CUDA(cudaMemsetAsync(B.right, 0, T * 4, st));
     RFX_CUDA(cudaMemsetAsync(B.rightimp, 0, T * p * 4, st));
     const rfx::Data D = c.D;
@@ -459,6 +509,8 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
     RFX_LAUNCH("k_bootstrap");
     rfx::k_compact<<<T, 1024, 0, st>>>(D, B);
     RFX_LAUNCH("k_compact");
+    c.launches += 2;
+    c.trees += T;
     const HistCfg hc = hist_cfg(c);
     const int gw = c.sm_count * 8;
     int cur = 0;
@@ -468,12 +520,27 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
         rfx::k_node_eval<<<gw, 256, 0, st>>>(D, B, cur);
         rfx::k_draw<<<T, 256, 0, st>>>(D, B);
         rfx::k_srch_scan<<<1, 1024, 0, st>>>(B);
-        rfx::k_hist<<<hc.grid, hc.warps * 32, hc.smem, st>>>(D, B, cur, hc.warps, hc.stage_rows, hc.warp_bytes);
+        if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev0, st));
+        rfx::k_hist<<<hc.grid, hc.threads, hc.smem, st>>>(D, B, cur, hc.a);
+        rfx::k_hist_small<<<hc.small_grid, 256, hc.small_smem, st>>>(D, B, cur, hc.small_warp_bytes);
+        if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev1, st));
         rfx::k_commit<<<T, 1024, 0, st>>>(D, B);
         rfx::k_partition<<<gw, 256, 0, st>>>(D, B, cur);
+        rfx::k_partition_big<<<c.sm_count * 2, 256, 0, st>>>(D, B, cur);
         RFX_LAUNCH("level kernels");
         RFX_CUDA(cudaMemcpyAsync(c.h_counters, B.counters, 16, cudaMemcpyDeviceToHost, st));
         RFX_CUDA(cudaStreamSynchronize(st));
+        c.launches += 9;
+        c.levels += 1;
+        if (c.profiling) {
+            float ms = 0.0f;
+            RFX_CUDA(cudaEventElapsedTime(&ms, c.ev0, c.ev1));
+            c.hist_ms += ms;
+            c.hist_launches += 1;
+            if (c.level_log)
+                std::fprintf(stderr, "[rfx] tree0=%d level=%d nodes=%d searched=%d next=%d hist_ms=%.3f\n",
+                             tree0, level, c.h_counters[0], c.h_counters[1], c.h_counters[2], ms);
+        }
         if (c.h_counters[2] == 0) break;
         cur ^= 1;
     }
@@ -483,7 +550,9 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
         D, B, (int*)c.nout.p, c.nclass > 1 ? (int*)c.votes.p : nullptr,
         c.nclass == 1 ? (float*)c.oob_sum.p : nullptr, B.tree_oob, (int)N);
     RFX_LAUNCH("oob kernels");
+    c.launches += 2;
     if (c.prm.compute_importance) {
+        RFX_CUDA(cudaStreamWaitEvent(st, c.perm_event, 0));
         rfx::k_imp_used<<<T, 256, 0, st>>>(D, B);
         if (c.nclass > 1) {
             rfx::k_imp_class<<<rg, 256, 0, st>>>(D, B);
@@ -494,10 +563,12 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
         }
         rfx::k_imp_fold<<<1, 256, 0, st>>>(D, B, (float*)c.avimp.p, (float*)c.sqsd.p);
         RFX_LAUNCH("importance kernels");
+        c.launches += 4;
     }
     if (c.prm.compute_proximity) {
         rfx::k_prox<<<rg, 256, 0, st>>>(D, B, c.R, c.prox);
         RFX_LAUNCH("k_prox");
+        c.launches += 1;
     }
     if (keep) c.tree_oob_n += T;
     if (out) {
@@ -731,6 +802,53 @@ int rfx_copy_to_host(void* ctx, void* dst_host, const void* src_dev, size_t byte
         Ctx& c = *as_ctx(ctx);
         require(dst_host && src_dev, RFX_ERR_ARG, "null pointer");
         RFX_CUDA(cudaMemcpyAsync(dst_host, src_dev, bytes, cudaMemcpyDeviceToHost, c.st));
+        RFX_CUDA(cudaStreamSynchronize(c.st));
+    });
+}
+
+int rfx_get_stream(void* ctx, void** stream) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(stream != nullptr, RFX_ERR_ARG, "null output");
+        *stream = (void*)c.st;
+    });
+}
+
+int rfx_set_profiling(void* ctx, int on) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        if (on && !c.ev0) {
+            RFX_CUDA(cudaEventCreate(&c.ev0));
+            RFX_CUDA(cudaEventCreate(&c.ev1));
+        }
+        c.profiling = on != 0;
+    });
+}
+
+int rfx_get_stats(void* ctx, rfx_stats* s) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(s != nullptr, RFX_ERR_ARG, "null output");
+        unsigned long long hb = 0;
+        if (c.B.hist_bytes) {
+            RFX_CUDA(cudaMemcpyAsync(&hb, c.B.hist_bytes, 8, cudaMemcpyDeviceToHost, c.st));
+            RFX_CUDA(cudaStreamSynchronize(c.st));
+        }
+        s->kernel_launches = c.launches;
+        s->hist_launches = c.hist_launches;
+        s->hist_ms = c.hist_ms;
+        s->hist_bytes = (double)hb;
+        s->levels = c.levels;
+        s->trees = c.trees;
+    });
+}
+
+int rfx_reset_stats(void* ctx) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        c.launches = c.hist_launches = c.levels = c.trees = 0;
+        c.hist_ms = 0.0;
+        if (c.B.hist_bytes) RFX_CUDA(cudaMemsetAsync(c.B.hist_bytes, 0, 8, c.st));
         RFX_CUDA(cudaStreamSynchronize(c.st));
     });
 }

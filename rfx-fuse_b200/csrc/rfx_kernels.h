@@ -21,9 +21,13 @@ __global__ void k_level_begin(Batch B);
 __global__ void k_node_eval(Data D, Batch B, int cur);
 __global__ void k_draw(Data D, Batch B);
 __global__ void k_srch_scan(Batch B);
-__global__ void k_hist(Data D, Batch B, int cur, int nwarp_blk, int stage_rows, int warp_bytes);
 __global__ void k_commit(Data D, Batch B);
 __global__ void k_partition(Data D, Batch B, int cur);
+__global__ void k_partition_big(Data D, Batch B, int cur);
+
+// rfx_hist.cu
+__global__ void k_hist(Data D, Batch B, int cur, HistArgs a);
+__global__ void k_hist_small(Data D, Batch B, int cur, int warp_bytes);
 
 // rfx_post.cu
 __global__ void k_oob_drop(Data D, Batch B);

@@ -46,11 +46,18 @@ class Accum(C.Structure):
                 ("q", _pf), ("oob_sum", _pf), ("avimp", _pf), ("sqsd", _pf), ("labels", _pi)]
 
 
+class Stats(C.Structure):
+    _fields_ = [("kernel_launches", C.c_int64), ("hist_launches", C.c_int64),
+                ("hist_ms", C.c_double), ("hist_bytes", C.c_double), ("levels", C.c_int64),
+                ("trees", C.c_int64)]
+
+
 SYMBOLS = (
     "rfx_last_error", "rfx_abi_version", "rfx_device_count", "rfx_create", "rfx_destroy",
     "rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
     "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish", "rfx_prox_dense",
-    "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host", "rfx_sync",
+    "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host", "rfx_get_stream",
+    "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats", "rfx_sync",
 )
 
 _LIB = None
@@ -84,10 +91,15 @@ def load_library(path: str = LIB_PATH):
     L.rfx_oob_fold.argtypes = [vp, vp]
     L.rfx_votes_to_q.argtypes = [vp, vp, _pf, C.c_int, C.c_int, vp]
     L.rfx_copy_to_host.argtypes = [vp, vp, vp, C.c_size_t]
+    L.rfx_get_stream.argtypes = [vp, C.POINTER(vp)]
+    L.rfx_set_profiling.argtypes = [vp, C.c_int]
+    L.rfx_get_stats.argtypes = [vp, C.POINTER(Stats)]
+    L.rfx_reset_stats.argtypes = [vp]
     L.rfx_sync.argtypes = [vp]
     for name in ("rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
                  "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish",
                  "rfx_prox_dense", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host",
+                 "rfx_get_stream", "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats",
                  "rfx_sync"):
         getattr(L, name).restype = C.c_int
     _LIB = L
@@ -175,6 +187,22 @@ class Context:
     def copy_to_host(self, dst: np.ndarray, src_dev: int):
         check(self._lib.rfx_copy_to_host(self.handle, dst.ctypes.data_as(C.c_void_p),
                                          C.c_void_p(src_dev), dst.nbytes))
+
+    def stream(self) -> int:
+        s = C.c_void_p()
+        check(self._lib.rfx_get_stream(self.handle, C.byref(s)))
+        return s.value or 0
+
+    def set_profiling(self, on: bool):
+        check(self._lib.rfx_set_profiling(self.handle, int(bool(on))))
+
+    def stats(self) -> dict:
+        s = Stats()
+        check(self._lib.rfx_get_stats(self.handle, C.byref(s)))
+        return {k: getattr(s, k) for k, _ in Stats._fields_}
+
+    def reset_stats(self):
+        check(self._lib.rfx_reset_stats(self.handle))
 
     def sync(self):
         check(self._lib.rfx_sync(self.handle))
