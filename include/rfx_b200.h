@@ -138,6 +138,25 @@ int rfx_prox_finish(void* ctx, const int* upper_dev, const int* nout_dev, int R,
  * row blocks so the device scratch stays bounded (python/randomforest_py.cpp:2129-2155). */
 int rfx_prox_dense(void* ctx, int row_begin, int row_end, float* out_host);
 
+/* Allocation-free variant of rfx_prox_dense (no counterpart in the reference).
+ * For callers that must not allocate device memory -- e.g. a serving process or a host
+ * application whose memory pool owns the whole device budget, where a cudaMalloc would
+ * fail or stall the device.  It needs no context: the caller passes the upper-triangle
+ * counts and nout (device pointers, e.g. from rfx_get_prox_buffer / rfx_get_vote_buffers or
+ * its own NCCL-reduced copies), the row range, the host destination and a CUDA stream
+ * (NULL = legacy default stream); the current device is used.  Finished rows are staged in
+ * one fixed device array of RFX_STATIC_SCRATCH_FLOATS floats (16 MiB) that every GPU which
+ * loads the library keeps until the process exits; R must not exceed that size (one row
+ * has to fit), otherwise RFX_ERR_ARG.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * No cudaMalloc / cudaFree is called.  All calls share the array, which keeps the last
+ * call's rows; it is fully rewritten before each use, so nothing needs clearing, but calls
+ * that overlap on the GPU (other threads or streams) race on it.  Returns after the rows
+ * are on the host. */
+#define RFX_STATIC_SCRATCH_FLOATS (4 * 1024 * 1024)
+int rfx_prox_dense_static(const int* upper_dev, const int* nout_dev, int R, int row_begin,
+                          int row_end, float* out_host, void* stream);
+
 /* Regression, keep_tree_oob: vec_dev[i] <- fold of the per-tree OOB predictions of the
  * trees grown so far, in tree order, starting from the incoming value (device, [N]). */
 int rfx_oob_fold(void* ctx, float* vec_dev);

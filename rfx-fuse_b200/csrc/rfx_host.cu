@@ -599,6 +599,8 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
 
 }  // namespace
 
+void rfx_record_error(const std::string& msg) { g_last_error = msg; }
+
 extern "C" {
 
 const char* rfx_last_error(void) { return g_last_error.c_str(); }
