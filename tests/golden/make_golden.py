@@ -1,0 +1,92 @@
+"""Generate the golden fixtures of tests/golden/ from the reference itself.
+
+The reference's CPU implementation is compiled from its own sources into oracle/_ref
+(`make -C oracle ref`); oracle/ref_harness.cpp drives it and dumps the per-tree arrays
+that its Python API does not expose.  The reference has no golden vectors of its own, so
+these fixtures are the pin of the CPU oracle (tests/test_oracle_golden.py) and, through
+it, of the device path.
+
+    python tests/golden/make_golden.py        # rewrites tests/golden/*.npz
+"""
+import os
+import sys
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.dirname(HERE))
+sys.path.insert(0, os.path.join(ROOT, "rfx-fuse_b200"))
+
+import oracle  # noqa: E402
+from _helpers import synth  # noqa: E402
+
+KEYS = ("nodestatus", "bestvar", "xbestsplit", "treemap", "nodeclass", "nnode", "nodepred",
+        "tnodewt", "nin", "nodextr", "nout", "q", "oob_pred", "avimp", "sqsd", "oob_error")
+
+
+def binning_data():
+    rng = np.random.default_rng(99)
+    n = 700
+    X = np.empty((n, 7), np.float32)
+    X[:, 0] = rng.normal(size=n)
+    X[:, 1] = np.round(rng.normal(size=n), 1)          # heavy ties
+    X[:, 2] = rng.integers(0, 2, n)                    # binary 0/1
+    X[:, 3] = rng.integers(0, 5, n)                    # categorical (cat=5)
+    X[:, 4] = 2.5                                      # constant
+    X[:, 5] = rng.integers(0, 40, n) * 0.25            # 40 distinct values
+    X[:, 6] = rng.exponential(size=n) * 1e-3           # tiny spread
+    cat = np.array([1, 1, 1, 5, 1, 1, 1], np.int32)
+    return X, cat
+
+
+CASES = {
+    # name: (task, data kind, n, p, seed, fit kwargs)
+    "class_prox": (0, "class", 600, 8, 1, dict(ntree=4, mtry=3, minndsize=1, proximity=True)),
+    "multiclass_classwt": (0, "multiclass", 800, 6, 2,
+                           dict(ntree=3, mtry=2, minndsize=2, classwt=[0.1, 0.4, 0.7, 1.0])),
+    "regr": (1, "regr", 1500, 12, 3, dict(ntree=3, mtry=4, minndsize=5)),
+    "regr_bins16_cap": (1, "regr", 1200, 8, 4, dict(ntree=3, mtry=3, minndsize=2, nbins=16, maxnode=151)),
+    "unsup_prox": (2, "gmm", 300, 6, 5, dict(ntree=3, mtry=2, minndsize=1, proximity=True)),
+}
+
+
+def main():
+    if not oracle.ref_available():
+        raise SystemExit("oracle/_ref is not built: run `make -C oracle ref`")
+    out = {}
+    for name, (task, kind, n, p, seed, kw) in CASES.items():
+        X, y = synth(kind, n, p, seed)
+        r = oracle.ref_fit(task, X, y, **kw)
+        d = {"X": X}
+        if y is not None:
+            d["y"] = y
+        for k in KEYS:
+            if r.get(k) is not None:
+                d[k] = np.asarray(r[k])
+        if kw.get("proximity"):
+            N = r["nout"].shape[0]
+            d["prox_pairs"] = r["prox_raw"].reshape(N, N).T.astype(np.int32)  # P[i][j]
+            d["prox"] = r["prox"]
+        d["maxnode"] = np.int32(r["maxnode"])
+        out[name] = d
+    # weighted bootstrap and binning vectors
+    rng = np.random.default_rng(7)
+    sw = rng.uniform(0.1, 3.0, size=900).astype(np.float32)
+    boot = {"nin_w": np.stack([oracle.ref_bootstrap(900, t, sw) for t in range(3)]),
+            "nin": np.stack([oracle.ref_bootstrap(900, t) for t in range(3)]), "sw": sw}
+    Xb, cat = binning_data()
+    e, nb, kind, xb = oracle.ref_binning(Xb, cat, 256)
+    e16, nb16, kind16, xb16 = oracle.ref_binning(Xb, cat, 16)
+    binning = {"X": Xb, "cat": cat, "edges": e, "nb": nb, "kind": kind, "xb": xb,
+               "edges16": e16, "nb16": nb16, "kind16": kind16, "xb16": xb16}
+    for name, d in out.items():
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **d)
+    np.savez_compressed(os.path.join(HERE, "bootstrap.npz"), **boot)
+    np.savez_compressed(os.path.join(HERE, "binning.npz"), **binning)
+    print("wrote", sorted(os.listdir(HERE)))
+
+
+if __name__ == "__main__":
+    main()
