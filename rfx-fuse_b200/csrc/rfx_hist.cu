@@ -324,9 +324,9 @@ __global__ void __launch_bounds__(256) k_hist(Data D, Batch B, int cur, HistArgs
 
 // ---------------------------------------------------------------------------------------
 // Small nodes (c <= kSmallNode rows): one warp per searched node does all mtry draws.
-// The node's rows are staged once in the warp's own shared memory (row-major with a
-// 4-byte pad, so each lane reading its own row's byte f is conflict free); the targets
-// stay in registers.
+// Each lane holds up to two of the node's rows (address and target in registers) and
+// reads the drawn feature's bin directly from the packed row; per-warp shared memory holds
+// only the histogram, which keeps many warps resident to hide the latency.
 // ---------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, int warp_bytes) {
     extern __shared__ __align__(16) uint8_t smem[];
@@ -334,19 +334,16 @@ __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, in
     const bool regr = D.nclass == 1;
     const int nc = D.nclass;
     const int rs = D.rs, ro = D.ro;
-    const int RS = rs + 4;
     uint8_t* wbase = smem + (size_t)wib * warp_bytes;
-    uint8_t* stage = wbase;  // [kSmallNode][RS]
     uint8_t* bl;
     float *sy, *sy2;
     int *cn, *h;
-    warp_scratch(stage + kSmallNode * RS, bl, sy, sy2, cn, h);
-    for (int k = lane; k < (warp_bytes - kSmallNode * RS) / 4; k += 32)
+    warp_scratch(wbase, bl, sy, sy2, cn, h);
+    for (int k = lane; k < warp_bytes / 4; k += 32)
         reinterpret_cast<uint32_t*>(bl)[k] = 0u;
     __syncwarp();
     const int total = B.counters[1];
     const int nwarps = gridDim.x * (blockDim.x >> 5);
-    const int words = rs >> 2;
     for (int si = blockIdx.x * (blockDim.x >> 5) + wib; si < total; si += nwarps) {
         const int t = tree_of(B.srch_off, B.T, si);
         const int node = B.srch[(size_t)t * B.M + (si - B.srch_off[t])];
@@ -357,24 +354,22 @@ __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, in
             atomicAdd(B.hist_bytes, (unsigned long long)c * (unsigned long long)(B.mtry + (regr ? 4 : 1)));
         const int* seg = B.seg[cur] + (size_t)t * D.N + B.nd_start[m];
         const uint16_t* featp = B.feat + (size_t)t * B.M * B.mtry + (size_t)node * B.mtry;
+        // each lane keeps its rows' address and target in registers; the bins are read
+        // straight from the packed rows (L1-resident after the first draw)
+        const uint8_t* rowp[2] = {D.rows, D.rows};
         float v[2] = {0.0f, 0.0f}, v2[2] = {0.0f, 0.0f};
         int lab[2] = {0, 0};
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
             const int i = hh * 32 + lane;
             if (i < c) {
-                const uint4* src = reinterpret_cast<const uint4*>(D.rows + (size_t)seg[i] * rs);
-                uint32_t* dst = reinterpret_cast<uint32_t*>(stage + (size_t)i * RS);
-                for (int w = 0; w < words; w += 4) {
-                    const uint4 q = __ldg(src + (w >> 2));
-                    dst[w] = q.x; dst[w + 1] = q.y; dst[w + 2] = q.z; dst[w + 3] = q.w;
-                }
-                v[hh] = __uint_as_float(dst[ro >> 2]);
-                v2[hh] = __uint_as_float(dst[(ro >> 2) + 1]);
-                lab[hh] = (int)dst[ro >> 2];
+                rowp[hh] = D.rows + (size_t)seg[i] * rs;
+                const uint2 tg = __ldg(reinterpret_cast<const uint2*>(rowp[hh] + ro));
+                v[hh] = __uint_as_float(tg.x);
+                v2[hh] = __uint_as_float(tg.y);
+                lab[hh] = (int)tg.x;
             }
         }
-        __syncwarp();
         unsigned long long best = kNoKey;
         for (int mv = 0; mv < B.mtry; ++mv) {
             const int f = featp[mv];
@@ -383,7 +378,7 @@ __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, in
                 if (hh * 32 < c) {
                     const int i = hh * 32 + lane;
                     const bool valid = i < c;
-                    const int b = valid ? stage[(size_t)i * RS + f] : kBins;
+                    const int b = valid ? (int)__ldg(rowp[hh] + f) : kBins;
                     hist_step(regr, nc, valid, b, v[hh], v2[hh], lab[hh], lane, sy, sy2, cn, h);
                 }
             }

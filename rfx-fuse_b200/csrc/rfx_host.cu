@@ -459,7 +459,7 @@ HistCfg hist_cfg(Ctx& c) {
     int per_sm = 0;
     RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist, h.threads, h.smem));
     h.grid = c.sm_count * std::max(1, per_sm);
-    h.small_warp_bytes = (int)round_up(rfx::kSmallNode * (c.D.rs + 4), 16) + scratch;
+    h.small_warp_bytes = scratch;
     h.small_smem = 8 * h.small_warp_bytes;
     RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   std::max(h.small_smem, 48 * 1024)));
