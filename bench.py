@@ -315,7 +315,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="rfx", choices=["rfx", "reference"])
-    ap.add_argument("--step-trees", type=int, default=100)
+    ap.add_argument("--step-trees", type=int, default=250)
     ap.add_argument("--batch-trees", type=int, default=0)
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--cpu-trees", type=int, default=8)

@@ -176,22 +176,56 @@ __global__ void __launch_bounds__(256) k_imp_regr(Data D, Batch B) {
     const int *st = B.status + mo, *bv = B.bestvar + mo, *tm = B.treemap + 2 * mo;
     const float *xb = B.xbest + mo, *np = B.nodepred + mo;
     const int row = B.oob[(size_t)t * D.N + j];
-    uint32_t mask[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    walk_oob(D, st, bv, xb, tm, row, mask);
     const float pred = np[B.oob_leaf[(size_t)t * D.N + row]];
     const float y = D.yreg[row];
     const float d = pred - y;
-    B.d0[(size_t)t * D.N + j] = 1.0f * d * d;
+    const float dd = 1.0f * d * d;
+    B.d0[(size_t)t * D.N + j] = dd;
     const int prow = D.perm[row];
     const int nn = B.nnode[t];
-    const bool wide = D.p > 256 || D.has_cat;
     float* out = B.d2 + ((size_t)t * D.N + j) * D.p;
-    for (int k = 0; k < D.p; ++k) {
-        float pk = pred;
-        if (wide || ((mask[k >> 5] >> (k & 31)) & 1u))
-            pk = walk_perm_regr(D, st, bv, xb, tm, np, nn, row, prow, k);
+    // The permuted walk for feature k follows the row's own path up to the first node that
+    // tests k; features never tested on the path keep the unpermuted error.
+    constexpr int kMaxPath = 48;
+    int path[kMaxPath];
+    int depth = 0;
+    bool deep = D.has_cat != 0;
+    if (!deep) {
+        int kt = 0, steps = 0;
+        while (st[kt] == 1 && steps < 1000) {
+            ++steps;
+            if (depth == kMaxPath) { deep = true; break; }
+            path[depth++] = kt;
+            const int mv = bv[kt];
+            kt = D.xc[(size_t)mv * D.N + row] <= xb[kt] ? tm[2 * kt] : tm[2 * kt + 1];
+            if (st[kt] != 1) break;
+        }
+    }
+    if (deep) {
+        for (int k = 0; k < D.p; ++k) {
+            const float dk = walk_perm_regr(D, st, bv, xb, tm, np, nn, row, prow, k) - y;
+            out[k] = 1.0f * dk * dk;
+        }
+        return;
+    }
+    for (int k = 0; k < D.p; ++k) out[k] = dd;
+    for (int i = 0; i < depth; ++i) {
+        const int f = bv[path[i]];
+        bool first = true;
+        for (int q = 0; q < i; ++q) first &= bv[path[q]] != f;
+        if (!first) continue;
+        // resume the walk at path[i] with feature f read from the permuted row
+        int kt = path[i];
+        float pk = 0.0f;
+        for (int k = i; k < nn; ++k) {
+            if (st[kt] == -1) { pk = np[kt]; break; }
+            const int m = bv[kt];
+            const float v = D.xc[(size_t)m * D.N + (m == f ? prow : row)];
+            kt = v <= xb[kt] ? tm[2 * kt] : tm[2 * kt + 1];
+            if (kt < 0 || kt >= nn) break;
+        }
         const float dk = pk - y;
-        out[k] = 1.0f * dk * dk;
+        out[f] = 1.0f * dk * dk;
     }
 }
 
@@ -206,17 +240,32 @@ __global__ void k_imp_regr_sum(Data D, Batch B) {
         for (int k = threadIdx.x; k < D.p; k += blockDim.x) B.rr[(size_t)t * D.p + k] = 0.0f;
         return;
     }
+    // serial chains; 16 loads are issued before each group of dependent adds
     if (threadIdx.x == 0) {
         float s = 0.0f;
         const float* d0 = B.d0 + (size_t)t * D.N;
-        for (int j = 0; j < noob; ++j) s += d0[j];
+        for (int j0 = 0; j0 < noob; j0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) v[q] = j0 + q < noob ? d0[j0 + q] : 0.0f;
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+                if (j0 + q < noob) s += v[q];
+        }
         mse0 = s / (float)noob;
     }
     __syncthreads();
     for (int k = threadIdx.x; k < D.p; k += blockDim.x) {
         float s = 0.0f;
         const float* d2 = B.d2 + (size_t)t * D.N * D.p + k;
-        for (int j = 0; j < noob; ++j) s += d2[(size_t)j * D.p];
+        for (int j0 = 0; j0 < noob; j0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) v[q] = j0 + q < noob ? d2[(size_t)(j0 + q) * D.p] : 0.0f;
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+                if (j0 + q < noob) s += v[q];
+        }
         B.rr[(size_t)t * D.p + k] = s / (float)noob - mse0;
     }
 }
