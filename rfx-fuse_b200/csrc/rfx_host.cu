@@ -559,7 +559,8 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
             rfx::k_imp_class_rr<<<T, 256, 0, st>>>(D, B);
         } else {
             rfx::k_imp_regr<<<rg, 256, 0, st>>>(D, B);
-            rfx::k_imp_regr_sum<<<T, (int)std::min<size_t>(1024, round_up(p, 32)), 0, st>>>(D, B);
+            const int tr = (int)std::max<size_t>(1, std::min<size_t>(64, (48 * 1024) / ((p + 1) * 4)));
+            rfx::k_imp_regr_sum<<<T, 256, (size_t)tr * (p + 1) * 4, st>>>(D, B, tr);
         }
         rfx::k_imp_fold<<<1, 256, 0, st>>>(D, B, (float*)c.avimp.p, (float*)c.sqsd.p);
         RFX_LAUNCH("importance kernels");

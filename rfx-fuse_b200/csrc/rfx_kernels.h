@@ -37,7 +37,7 @@ __global__ void k_imp_used(Data D, Batch B);
 __global__ void k_imp_class(Data D, Batch B);
 __global__ void k_imp_class_rr(Data D, Batch B);
 __global__ void k_imp_regr(Data D, Batch B);
-__global__ void k_imp_regr_sum(Data D, Batch B);
+__global__ void k_imp_regr_sum(Data D, Batch B, int tile_rows);
 __global__ void k_imp_fold(Data D, Batch B, float* avimp, float* sqsd);
 __global__ void k_prox(Data D, Batch B, int R, int* C);
 __global__ void k_prox_finish(const int* C, const int* nout, int R, int r0, int r1, float* out);

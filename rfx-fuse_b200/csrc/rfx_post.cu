@@ -230,43 +230,51 @@ __global__ void __launch_bounds__(256) k_imp_regr(Data D, Batch B) {
 }
 
 // Serial sums over the OOB rows in row order (the reference's loop order), then
-// rr = mse_perm - mse_orig.  One block per tree: thread k sums feature k, thread p the
-// unpermuted errors.
-__global__ void k_imp_regr_sum(Data D, Batch B) {
+// rr = mse_perm - mse_orig.  One block per tree: the block streams tiles of the row-major
+// [noob][p] squared errors through shared memory with coalesced loads; thread k then adds
+// feature k's column of the tile in row order, thread p the unpermuted errors.
+__global__ void __launch_bounds__(256) k_imp_regr_sum(Data D, Batch B, int kSumTile) {
+    extern __shared__ float tile[];  // [kSumTile][p + 1]
     __shared__ float mse0;
     const int t = blockIdx.x;
     const int noob = B.noob[t];
+    const int p = D.p, P1 = D.p + 1;
     if (noob == 0) {
-        for (int k = threadIdx.x; k < D.p; k += blockDim.x) B.rr[(size_t)t * D.p + k] = 0.0f;
+        for (int k = threadIdx.x; k < p; k += blockDim.x) B.rr[(size_t)t * p + k] = 0.0f;
         return;
     }
-    // serial chains; 16 loads are issued before each group of dependent adds
-    if (threadIdx.x == 0) {
-        float s = 0.0f;
-        const float* d0 = B.d0 + (size_t)t * D.N;
-        for (int j0 = 0; j0 < noob; j0 += 16) {
-            float v[16];
-#pragma unroll
-            for (int q = 0; q < 16; ++q) v[q] = j0 + q < noob ? d0[j0 + q] : 0.0f;
-#pragma unroll
-            for (int q = 0; q < 16; ++q)
-                if (j0 + q < noob) s += v[q];
+    const float* d2 = B.d2 + (size_t)t * D.N * p;
+    const float* d0 = B.d0 + (size_t)t * D.N;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // columns threadIdx.x + 256*q (q < 4: p+1 <= 1024)
+    for (int j0 = 0; j0 < noob; j0 += kSumTile) {
+        const int rows = min(kSumTile, noob - j0);
+        __syncthreads();
+        for (int e = threadIdx.x; e < rows * p; e += blockDim.x) {
+            const int r = e / p, k = e - r * p;
+            tile[r * P1 + k] = d2[(size_t)(j0 + r) * p + k];
         }
-        mse0 = s / (float)noob;
+        for (int r = threadIdx.x; r < rows; r += blockDim.x) tile[r * P1 + p] = d0[j0 + r];
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int k = threadIdx.x + q * blockDim.x;
+            if (k <= p) {
+                float s = acc[q];
+                for (int r = 0; r < rows; ++r) s += tile[r * P1 + k];
+                acc[q] = s;
+            }
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int k = threadIdx.x + q * blockDim.x;
+        if (k == p) mse0 = acc[q] / (float)noob;
     }
     __syncthreads();
-    for (int k = threadIdx.x; k < D.p; k += blockDim.x) {
-        float s = 0.0f;
-        const float* d2 = B.d2 + (size_t)t * D.N * D.p + k;
-        for (int j0 = 0; j0 < noob; j0 += 16) {
-            float v[16];
 #pragma unroll
-            for (int q = 0; q < 16; ++q) v[q] = j0 + q < noob ? d2[(size_t)(j0 + q) * D.p] : 0.0f;
-#pragma unroll
-            for (int q = 0; q < 16; ++q)
-                if (j0 + q < noob) s += v[q];
-        }
-        B.rr[(size_t)t * D.p + k] = s / (float)noob - mse0;
+    for (int q = 0; q < 4; ++q) {
+        const int k = threadIdx.x + q * blockDim.x;
+        if (k < p) B.rr[(size_t)t * p + k] = acc[q] / (float)noob - mse0;
     }
 }
 
