@@ -1,0 +1,181 @@
+"""Tree-sharded fits over several GPUs (one process per GPU, torch.distributed).
+
+Every tree's randomness depends only on its id (bootstrap MT19937(12345 + t), grower
+MT19937(iseed + t)), so rank r grows the contiguous id block [r*T/W, (r+1)*T/W) and its
+trees are identical to the single-GPU forest's.  Combining the ranks keeps the reference's
+results exact:
+
+* nout and the integer vote counts are summed (all-reduce); the classwt-weighted vote sums
+  q are then rebuilt from the counts exactly as the reference accumulates them;
+* regression OOB prediction sums are float sums in tree order, so they are folded rank by
+  rank (rank r continues from rank r-1's vector) -- a chain of point-to-point transfers of
+  one [N] vector, not a reduction;
+* importance: per-tree rr rows are gathered and summed in tree order;
+* proximity: integer counts in a caller-owned device buffer, summed with one all-reduce.
+
+The collectives are plain torch.distributed calls (NCCL over NVLink on GPUs, gloo on CPU
+for the tests); they run once per fit, outside the per-level work.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def tree_block(ntree: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous tree-id block of a rank: [begin, end)."""
+    return ntree * rank // world, ntree * (rank + 1) // world
+
+
+def ordered_fold(vec, fold_local, dist):
+    """Fold a [N] float vector through the ranks in rank (= tree) order.
+
+    ``vec`` starts at zero on every rank; ``fold_local(vec)`` adds this rank's trees in
+    tree order, in place.  Returns the final vector on every rank.
+    """
+    rank, world = dist.get_rank(), dist.get_world_size()
+    if rank > 0:
+        dist.recv(vec, src=rank - 1)
+    fold_local(vec)
+    if rank < world - 1:
+        dist.send(vec, dst=rank + 1)
+    dist.broadcast(vec, src=world - 1)
+    return vec
+
+
+def ordered_importance(tree_rr: np.ndarray, tree_used: np.ndarray, dist):
+    """avimp, sqsd = float32 sums over all ranks' trees in tree order (reference:
+    src/rf_random_forest.cpp:1903-1906, avimp_[i] += avimp_temp[i] per tree)."""
+    parts = [None] * dist.get_world_size()
+    dist.all_gather_object(parts, (np.asarray(tree_rr, np.float32), np.asarray(tree_used, np.uint8)))
+    rr = np.concatenate([p[0] for p in parts])
+    used = np.concatenate([p[1] for p in parts])
+    p = rr.shape[1]
+    av = np.zeros(p, np.float32)
+    sq = np.zeros(p, np.float32)
+    for t in range(rr.shape[0]):
+        r = np.where(used[t] != 0, rr[t], np.float32(0)).astype(np.float32)
+        av = (av + r).astype(np.float32)
+        sq = (sq + (r * r).astype(np.float32)).astype(np.float32)
+    return av, sq
+
+
+def votes_to_q(votes: np.ndarray, classwt) -> np.ndarray:
+    """q[i][c] = classwt[c] added votes[i][c] times (float32, sequential).  Host version for
+    the combine of a sharded fit; the device version is rfx_votes_to_q."""
+    nclass = votes.shape[1]
+    w = np.ones(nclass, np.float32) if classwt is None else np.asarray(classwt, np.float32)
+    q = np.zeros(votes.shape, np.float32)
+    kmax = int(votes.max()) if votes.size else 0
+    for k in range(kmax):
+        live = votes > k
+        q = np.where(live, (q + w[None, :]).astype(np.float32), q)
+    return q
+
+
+def fit_sharded(est, X, y=None, dist=None, device=None):
+    """Fit ``est`` (an rfx_b200 estimator) with its trees sharded over the process group.
+
+    Every rank must call it with the same data.  Returns this rank's tree block; the
+    estimator ends with the combined forest-level results (nout, votes/q or OOB sums,
+    importance, proximity counts) on every rank.
+    """
+    import torch
+
+    from . import _abi as A
+    from .forest import (RandomForestClassifier, RandomForestRegressor, RandomForestUnsupervised,
+                         _isqrt_f32, calculate_maxnode, detect_categorical)
+
+    if dist is None:
+        import torch.distributed as dist
+    rank, world = dist.get_rank(), dist.get_world_size()
+    dev = torch.device("cuda", device if device is not None else torch.cuda.current_device())
+    X = np.ascontiguousarray(X, np.float32)
+    n, p = X.shape
+    if isinstance(est, RandomForestRegressor):
+        task = A.TASK_REGRESSION
+    elif isinstance(est, RandomForestUnsupervised):
+        task = A.TASK_UNSUPERVISED
+    elif isinstance(est, RandomForestClassifier):
+        task = A.TASK_CLASSIFICATION
+    else:
+        raise TypeError("unsupported estimator")
+    t0, t1 = tree_block(est.ntree, rank, world)
+    # same preparation as est.fit, but grow only this rank's block
+    if task == A.TASK_UNSUPERVISED:
+        mtry = est._mtry if est._mtry > 0 else max(1, _isqrt_f32(p))
+        maxnode = calculate_maxnode(2 * n, est.minndsize)
+    else:
+        mtry, maxnode = est._mtry, est._maxnode
+    est.device = dev.index
+    est._ctx = A.Context(dev.index)
+    ctx = est._ctx
+    cat = detect_categorical(X, est.maxcat, est.categorical_features)
+    prm = A.FitParams(task, n, p, mtry, est.minndsize, maxnode, est.iseed, 12345, est.n_bins,
+                      est.maxcat, int(est.compute_importance), int(est.compute_proximity),
+                      est.prox_rows, est.batch_trees, int(task == A.TASK_REGRESSION))
+    ycls = np.ascontiguousarray(y, np.int32) if task == A.TASK_CLASSIFICATION else None
+    yreg = np.ascontiguousarray(y, np.float32) if task == A.TASK_REGRESSION else None
+    cw = None if getattr(est, "classwt", None) is None else np.ascontiguousarray(est.classwt, np.float32)
+    inp = A.Inputs(A.ptr(X, A._pf), A.ptr(ycls, A._pi), A.ptr(yreg, A._pf), None,
+                   A.ptr(cat, A._pi), A.ptr(cw, A._pf))
+    ctx.load(prm, inp)
+    N = 2 * n if task == A.TASK_UNSUPERVISED else n
+    prox = None
+    if est.compute_proximity:
+        _, length = ctx.prox_buffer()
+        prox = torch.zeros(length, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)  # the library's stream does not order after torch's
+        ctx.set_prox_buffer(prox.data_ptr(), length)
+    k = t1 - t0
+    rr = np.zeros((k, p), np.float32)
+    used = np.zeros((k, p), np.uint8)
+    trees = A.Trees(None, None, None, None, None, None, None, None, None, None,
+                    A.ptr(rr, A._pf), A.ptr(used, A._pu8))
+    ctx.grow(t0, k, trees)
+    ncl = 1 if task == A.TASK_REGRESSION else (2 if task == A.TASK_UNSUPERVISED else len(np.unique(ycls)))
+    nout = np.zeros(N, np.int32)
+    votes = np.zeros((N, ncl), np.int32)
+    labels = np.zeros(N, np.int32)
+    ac = A.Accum(0, 0, A.ptr(nout, A._pi), A.ptr(votes, A._pi) if ncl > 1 else None, None, None,
+                 None, None, A.ptr(labels, A._pi) if ncl > 1 else None)
+    ctx.results(ac)
+    t_nout = torch.from_numpy(nout).to(dev)
+    dist.all_reduce(t_nout)
+    acc = {"nout": t_nout.cpu().numpy(), "labels": labels}
+    if ncl > 1:
+        t_votes = torch.from_numpy(votes).to(dev)
+        dist.all_reduce(t_votes)
+        acc["votes"] = t_votes.cpu().numpy()
+        q = torch.zeros((N, ncl), dtype=torch.float32, device=dev)
+        torch.cuda.synchronize(dev)
+        ctx.votes_to_q(t_votes.data_ptr(), cw if task == A.TASK_CLASSIFICATION else None, N, ncl,
+                       q.data_ptr())
+        acc["q"] = q.cpu().numpy()
+    else:
+        vec = torch.zeros(N, dtype=torch.float32, device=dev)
+        torch.cuda.synchronize(dev)
+
+        def fold_local(v):
+            torch.cuda.synchronize(dev)
+            ctx.oob_fold(v.data_ptr())
+
+        ordered_fold(vec, fold_local, dist)
+        acc["oob_sum"] = vec.cpu().numpy()
+    if est.compute_importance:
+        acc["avimp"], acc["sqsd"] = ordered_importance(rr, used if ncl > 1 else np.ones_like(used), dist)
+    else:
+        acc["avimp"] = acc["sqsd"] = np.zeros(p, np.float32)
+    if prox is not None:
+        ctx.sync()
+        dist.all_reduce(prox)
+        torch.cuda.synchronize(dev)
+        est._sharded_prox = (prox, t_nout)
+    est.acc_ = acc
+    est.n_rows_ = N
+    est.nclass_ = ncl
+    est.n_features_ = p
+    est._fitted = True
+    if task == A.TASK_REGRESSION:
+        est._y = yreg
+    est._finalize(y)
+    return t0, t1
