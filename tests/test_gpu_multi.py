@@ -70,6 +70,6 @@ def test_two_gpu_sharded_fit_equals_single_gpu():
     want_c = (c.acc_["nout"], c.acc_["q"], c.acc_["avimp"], np.float32(c.get_oob_error()), c.get_proximity_matrix())
     for rank in range(2):
         for got, want in zip(out[rank]["regr"], want_r):
-            assert np.array_equal(np.asarray(got).view(np.uint8), np.asarray(want).view(np.uint8))
+            assert np.array_equal(np.atleast_1d(got).view(np.uint8), np.atleast_1d(want).view(np.uint8))
         for got, want in zip(out[rank]["class"], want_c):
-            assert np.array_equal(np.asarray(got).view(np.uint8), np.asarray(want).view(np.uint8))
+            assert np.array_equal(np.atleast_1d(got).view(np.uint8), np.atleast_1d(want).view(np.uint8))
