@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define RFX_ABI_VERSION 1
+#define RFX_ABI_VERSION 2
 
 enum {
     RFX_OK = 0,
@@ -55,6 +55,10 @@ typedef struct {
     int prox_rows;          /* proximity covers rows [0, prox_rows); 0 = all grown rows */
     int batch_trees;        /* trees grown concurrently on the device; 0 = automatic */
     int keep_tree_oob;      /* keep per-tree OOB predictions for rfx_oob_fold (regression) */
+    int lowrank_rank;       /* > 0 with compute_proximity: low-rank mode (use_qlora=True,
+                               include/rf_proximity_lowrank.hpp:27-439).  No dense counts are
+                               kept; every tree's leaf groups are stored instead for
+                               rfx_lowrank_build.  Rank <= 64. */
 } rfx_fit_params;
 
 typedef struct {
@@ -185,6 +189,51 @@ int rfx_get_stream(void* ctx, void** stream);   /* the context's cudaStream_t */
 int rfx_set_profiling(void* ctx, int on);
 int rfx_get_stats(void* ctx, rfx_stats* out);
 int rfx_reset_stats(void* ctx);
+
+/* ---- Low-rank proximity (use_qlora=True, quant_mode="int8") --------------------------
+ * Replaces LowRankProximityMatrix (include/rf_proximity_lowrank.hpp:27-439,
+ * cuda/rf_proximity_lowrank.cu:414-1340) and get_lowrank_factors
+ * (src/rf_random_forest.cpp:4562-4603, python/randomforest_py.cpp:2183-2223).  S is the
+ * finishprox'd proximity of rows [0, R) (S_ij = C_ij (1/nout_i + 1/nout_j) / 4, S_ii = 1,
+ * C the OOB x in-bag co-membership counts of the trees grown so far).  The factors A
+ * ([R][rank]) give S ~ A A^T: a randomized range finder on S applied through per-leaf sums
+ * (C is never formed), Cholesky-QR, a Jacobi eigensolve of the projected matrix and the
+ * top-`rank` non-negative eigenpairs, then per-row symmetric int8 quantisation
+ * (A_i = scale_i * q_i). */
+
+/* Sum `count` floats of buf_dev over all processes in place (e.g. an NCCL all-reduce);
+ * return 0 on success.  Called on the caller's thread with the context's stream idle. */
+typedef int (*rfx_reduce_fn)(void* user, float* buf_dev, int64_t count);
+
+/* Build the factors from the stored trees.  oversample extra sketch columns (rank +
+ * oversample <= 96), power_iters extra passes, seed of the random test matrix.  nout_dev
+ * (device, [R]) overrides the context's OOB counts (the all-reduced counts of a sharded
+ * fit); reduce (may be NULL) sums every sketch pass over the processes that hold the other
+ * trees.  Costs (power_iters + 2) passes over the stored trees. */
+int rfx_lowrank_build(void* ctx, int rank, int oversample, int power_iters, uint64_t seed,
+                      const int* nout_dev, rfx_reduce_fn reduce, void* reduce_user);
+
+/* The factors: A_host [R][rank] dequantised float (may be NULL), q_host [R][rank] int8
+ * (may be NULL), scale_host [R] (may be NULL); *rank_out = rank, *rows_out = R. */
+int rfx_lowrank_factors(void* ctx, float* A_host, int8_t* q_host, float* scale_host,
+                        int* rank_out, int* rows_out);
+
+/* Top-k neighbours of rows [row_begin, row_end) under the quantised product
+ * P_ij = (dot(q_i, q_j) * scale_i) * scale_j, j != i, ordered by value descending then
+ * index ascending; k <= 64.  idx_host / val_host are [rows][k]; slots beyond R - 1
+ * neighbours hold -1 / -inf.  The product runs on the tensor cores (tcgen05, bf16 operands
+ * holding the int8 values exactly, fp32 accumulation) with the selection fused into the
+ * accumulator read-out, so P is never written. */
+int rfx_lowrank_topk(void* ctx, int k, int row_begin, int row_end, int* idx_host,
+                     float* val_host);
+
+/* Rows [row_begin, row_end) of P (same kernel, every value written; diagonal included):
+ * the reconstructed approximate proximity, out_host [rows][R]. */
+int rfx_lowrank_product(void* ctx, int row_begin, int row_end, float* out_host);
+
+/* Y_dev = S X_dev for the trees stored in low-rank mode (this context's trees only), X and
+ * Y device [R][ncols] row-major, ncols <= 128; nout_dev as in rfx_lowrank_build. */
+int rfx_prox_apply(void* ctx, const float* X_dev, int ncols, const int* nout_dev, float* Y_dev);
 
 /* Wait for the context's stream. */
 int rfx_sync(void* ctx);

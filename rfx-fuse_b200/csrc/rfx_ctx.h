@@ -1,0 +1,169 @@
+// Host-side context of rfx_b200: error plumbing, growing device buffers and the per-device
+// context shared by the host translation units (rfx_host.cu, rfx_lowrank_host.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstdlib>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/rfx_b200.h"
+#include "rfx_device.cuh"
+
+namespace rfxh {
+extern thread_local std::string g_last_error;
+
+struct RfxError : std::runtime_error {
+    int code;
+    RfxError(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define RFX_CUDA(call)                                                                     \
+    do {                                                                                   \
+        cudaError_t e_ = (call);                                                           \
+        if (e_ != cudaSuccess)                                                             \
+            throw RfxError(e_ == cudaErrorMemoryAllocation ? RFX_ERR_OOM : RFX_ERR_CUDA,   \
+                           std::string(#call) + ": " + cudaGetErrorString(e_));            \
+    } while (0)
+
+#define RFX_LAUNCH(name)                                                                   \
+    do {                                                                                   \
+        cudaError_t e_ = cudaGetLastError();                                               \
+        if (e_ != cudaSuccess)                                                             \
+            throw RfxError(RFX_ERR_CUDA, std::string("launch ") + name + ": " +            \
+                                             cudaGetErrorString(e_));                      \
+    } while (0)
+
+inline void require(bool ok, int code, const std::string& msg) {
+    if (!ok) throw RfxError(code, msg);
+}
+
+template <class F>
+int guarded(F&& f) {
+    try {
+        f();
+        return RFX_OK;
+    } catch (const RfxError& e) {
+        g_last_error = e.what();
+        return e.code;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return RFX_ERR_ARG;
+    }
+}
+
+// Device buffer that only grows.
+struct DBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+    void* get(size_t bytes) {
+        if (bytes == 0) bytes = 16;
+        if (bytes > cap) {
+            if (p) cudaFree(p);
+            p = nullptr;
+            cap = 0;
+            RFX_CUDA(cudaMalloc(&p, bytes));
+            cap = bytes;
+        }
+        return p;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+    }
+};
+
+inline size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+struct Ctx {
+    int device = 0;
+    int sm_count = 148;
+    cudaStream_t st = nullptr;
+    int* h_counters = nullptr;  // pinned
+
+    // loaded dataset
+    bool loaded = false;
+    rfx_fit_params prm{};
+    int N = 0, p = 0, nclass = 0, task = 0, M = 0, R = 0;
+    std::vector<int> labels0;   // 0-based labels (classification / unsupervised)
+    std::vector<float> classwt;
+    rfx::Data D{};
+    DBuf xc, rows, edges, nb, kind, cat, lab, yreg, yv, perm, ks, cumw, totw, keys_a, keys_b;
+    cudaEvent_t perm_event = nullptr;  // owned by the process-wide permutation cache
+
+    // accumulators
+    DBuf nout, votes, oob_sum, avimp, sqsd, prox_own, qtmp, cw_dev, tree_oob_all;
+    int* prox = nullptr;
+    int64_t prox_len = 0;
+    int trees_done = 0;
+    int tree_oob_cap = 0, tree_oob_n = 0;
+
+    // measurement
+    bool profiling = false;
+    bool level_log = std::getenv("RFX_LEVEL_LOG") != nullptr;  // per-level trace on stderr
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    long long launches = 0, hist_launches = 0, levels = 0, trees = 0;
+    double hist_ms = 0.0;
+
+    // low-rank proximity (rfx_lowrank_host.cu): per-tree leaf groups, then the factors
+    int lr_rank = 0;            // requested rank, 0 = off
+    int lr_n = 0, lr_cap = 0;   // trees stored / capacity
+    int lr_G = 0;               // group-offset stride per tree (maxnode + 2)
+    int lr_k = 0, lr_Rpad = 0;  // factor rank and rows padded to the product tile
+    bool lr_ready = false;
+    DBuf lr_code, lr_order, lr_goff, lr_ngroups, lr_tmp;
+    DBuf lr_X, lr_Z, lr_CZ, lr_Y, lr_ls, lr_part, lr_small, lr_A, lr_q, lr_qb, lr_s, lr_smax,
+        lr_err, lr_out_i, lr_out_v;
+
+    // batch buffers
+    int Tcap = 0;
+    rfx::Batch B{};
+    DBuf b_nin, b_seg0, b_seg1, b_ninbag, b_oob, b_noob, b_mt, b_mtpos, b_status, b_bestvar,
+        b_xbest, b_treemap, b_nodeclass, b_nodepred, b_tnodewt, b_ndstart, b_ndcnt, b_ndbuf,
+        b_ndflag, b_ndcrit0, b_ndmaj, b_ndsum, b_ndkey, b_feat, b_lvl, b_srch, b_srchcnt,
+        b_srchoff, b_counters, b_oobleaf, b_used, b_right, b_rightimp, b_d2, b_d0, b_rr, b_srchbig, b_partbig;
+
+    ~Ctx() {
+        DBuf* all[] = {&xc, &rows, &edges, &nb, &kind, &cat, &lab, &yreg, &yv, &perm, &ks, &cumw,
+                       &totw, &keys_a, &keys_b, &nout, &votes, &oob_sum, &avimp, &sqsd,
+                       &prox_own, &qtmp, &cw_dev, &tree_oob_all, &b_nin, &b_seg0, &b_seg1,
+                       &b_ninbag, &b_oob, &b_noob, &b_mt, &b_mtpos, &b_status, &b_bestvar,
+                       &b_xbest, &b_treemap, &b_nodeclass, &b_nodepred, &b_tnodewt, &b_ndstart,
+                       &b_ndcnt, &b_ndbuf, &b_ndflag, &b_ndcrit0, &b_ndmaj, &b_ndsum, &b_ndkey,
+                       &b_feat, &b_lvl, &b_srch, &b_srchcnt, &b_srchoff, &b_counters,
+                       &b_oobleaf, &b_used, &b_right, &b_rightimp, &b_d2, &b_d0, &b_rr, &b_srchbig, &b_partbig,
+                       &lr_code, &lr_order, &lr_goff, &lr_ngroups, &lr_tmp, &lr_X, &lr_Z,
+                       &lr_CZ, &lr_Y, &lr_ls, &lr_part, &lr_small, &lr_A, &lr_q, &lr_qb, &lr_s,
+                       &lr_smax, &lr_err, &lr_out_i, &lr_out_v};
+        cudaSetDevice(device);
+        if (st) cudaStreamSynchronize(st);
+        for (DBuf* b : all) b->release();
+        if (h_counters) cudaFreeHost(h_counters);
+        if (ev0) cudaEventDestroy(ev0);
+        if (ev1) cudaEventDestroy(ev1);
+        if (st) cudaStreamDestroy(st);
+    }
+};
+
+inline Ctx* as_ctx(void* c) {
+    require(c != nullptr, RFX_ERR_ARG, "null context");
+    Ctx* x = static_cast<Ctx*>(c);
+    RFX_CUDA(cudaSetDevice(x->device));
+    return x;
+}
+
+inline int grid_for(long long n, int threads, int cap) {
+    return (int)std::max(1LL, std::min((long long)cap, (n + threads - 1) / threads));
+}
+
+
+// Low-rank proximity store (rfx_lowrank_host.cu): make room for `extra` more trees, and
+// store the leaf groups of the T trees of a grown batch.
+void lr_reserve(Ctx& c, int extra);
+void lr_store_batch(Ctx& c, const rfx::Batch& B, int T);
+
+}  // namespace rfxh

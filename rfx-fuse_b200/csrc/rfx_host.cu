@@ -20,129 +20,13 @@
 #include "rfx_device.cuh"
 #include "rfx_kernels.h"
 
+#include "rfx_ctx.h"
+
+thread_local std::string rfxh::g_last_error;
+
 namespace {
 
-thread_local std::string g_last_error;
-
-struct RfxError : std::runtime_error {
-    int code;
-    RfxError(int c, const std::string& m) : std::runtime_error(m), code(c) {}
-};
-
-#define RFX_CUDA(call)                                                                     \
-    do {                                                                                   \
-        cudaError_t e_ = (call);                                                           \
-        if (e_ != cudaSuccess)                                                             \
-            throw RfxError(e_ == cudaErrorMemoryAllocation ? RFX_ERR_OOM : RFX_ERR_CUDA,   \
-                           std::string(#call) + ": " + cudaGetErrorString(e_));            \
-    } while (0)
-
-#define RFX_LAUNCH(name)                                                                   \
-    do {                                                                                   \
-        cudaError_t e_ = cudaGetLastError();                                               \
-        if (e_ != cudaSuccess)                                                             \
-            throw RfxError(RFX_ERR_CUDA, std::string("launch ") + name + ": " +            \
-                                             cudaGetErrorString(e_));                      \
-    } while (0)
-
-void require(bool ok, int code, const std::string& msg) {
-    if (!ok) throw RfxError(code, msg);
-}
-
-template <class F>
-int guarded(F&& f) {
-    try {
-        f();
-        return RFX_OK;
-    } catch (const RfxError& e) {
-        g_last_error = e.what();
-        return e.code;
-    } catch (const std::exception& e) {
-        g_last_error = e.what();
-        return RFX_ERR_ARG;
-    }
-}
-
-// Device buffer that only grows.
-struct DBuf {
-    void* p = nullptr;
-    size_t cap = 0;
-    void* get(size_t bytes) {
-        if (bytes == 0) bytes = 16;
-        if (bytes > cap) {
-            if (p) cudaFree(p);
-            p = nullptr;
-            cap = 0;
-            RFX_CUDA(cudaMalloc(&p, bytes));
-            cap = bytes;
-        }
-        return p;
-    }
-    void release() {
-        if (p) cudaFree(p);
-        p = nullptr;
-        cap = 0;
-    }
-};
-
-size_t round_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
-
-struct Ctx {
-    int device = 0;
-    int sm_count = 148;
-    cudaStream_t st = nullptr;
-    int* h_counters = nullptr;  // pinned
-
-    // loaded dataset
-    bool loaded = false;
-    rfx_fit_params prm{};
-    int N = 0, p = 0, nclass = 0, task = 0, M = 0, R = 0;
-    std::vector<int> labels0;   // 0-based labels (classification / unsupervised)
-    std::vector<float> classwt;
-    rfx::Data D{};
-    DBuf xc, rows, edges, nb, kind, cat, lab, yreg, yv, perm, ks, cumw, totw, keys_a, keys_b;
-    cudaEvent_t perm_event = nullptr;  // owned by the process-wide permutation cache
-
-    // accumulators
-    DBuf nout, votes, oob_sum, avimp, sqsd, prox_own, qtmp, cw_dev, tree_oob_all;
-    int* prox = nullptr;
-    int64_t prox_len = 0;
-    int trees_done = 0;
-    int tree_oob_cap = 0, tree_oob_n = 0;
-
-    // measurement
-    bool profiling = false;
-    bool level_log = std::getenv("RFX_LEVEL_LOG") != nullptr;  // per-level trace on stderr
-    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
-    long long launches = 0, hist_launches = 0, levels = 0, trees = 0;
-    double hist_ms = 0.0;
-
-    // batch buffers
-    int Tcap = 0;
-    rfx::Batch B{};
-    DBuf b_nin, b_seg0, b_seg1, b_ninbag, b_oob, b_noob, b_mt, b_mtpos, b_status, b_bestvar,
-        b_xbest, b_treemap, b_nodeclass, b_nodepred, b_tnodewt, b_ndstart, b_ndcnt, b_ndbuf,
-        b_ndflag, b_ndcrit0, b_ndmaj, b_ndsum, b_ndkey, b_feat, b_lvl, b_srch, b_srchcnt,
-        b_srchoff, b_counters, b_oobleaf, b_used, b_right, b_rightimp, b_d2, b_d0, b_rr, b_srchbig, b_partbig;
-
-    ~Ctx() {
-        DBuf* all[] = {&xc, &rows, &edges, &nb, &kind, &cat, &lab, &yreg, &yv, &perm, &ks, &cumw,
-                       &totw, &keys_a, &keys_b, &nout, &votes, &oob_sum, &avimp, &sqsd,
-                       &prox_own, &qtmp, &cw_dev, &tree_oob_all, &b_nin, &b_seg0, &b_seg1,
-                       &b_ninbag, &b_oob, &b_noob, &b_mt, &b_mtpos, &b_status, &b_bestvar,
-                       &b_xbest, &b_treemap, &b_nodeclass, &b_nodepred, &b_tnodewt, &b_ndstart,
-                       &b_ndcnt, &b_ndbuf, &b_ndflag, &b_ndcrit0, &b_ndmaj, &b_ndsum, &b_ndkey,
-                       &b_feat, &b_lvl, &b_srch, &b_srchcnt, &b_srchoff, &b_counters,
-                       &b_oobleaf, &b_used, &b_right, &b_rightimp, &b_d2, &b_d0, &b_rr, &b_srchbig, &b_partbig};
-        cudaSetDevice(device);
-        if (st) cudaStreamSynchronize(st);
-        for (DBuf* b : all) b->release();
-        if (h_counters) cudaFreeHost(h_counters);
-        if (ev0) cudaEventDestroy(ev0);
-        if (ev1) cudaEventDestroy(ev1);
-        if (st) cudaStreamDestroy(st);
-    }
-};
+using namespace rfxh;
 
 // Importance permutation cache, one per (device, N), never freed (process lifetime).  It
 // is computed on a side stream; only the importance kernels wait for its event.
@@ -170,17 +54,6 @@ const PermEntry& permutation_for(int device, int N) {
     RFX_CUDA(cudaFreeAsync(ks, side));
     RFX_CUDA(cudaStreamDestroy(side));  // returns at once; queued work still completes
     return cache.emplace(std::make_pair(device, N), e).first->second;
-}
-
-Ctx* as_ctx(void* c) {
-    require(c != nullptr, RFX_ERR_ARG, "null context");
-    Ctx* x = static_cast<Ctx*>(c);
-    RFX_CUDA(cudaSetDevice(x->device));
-    return x;
-}
-
-int grid_for(long long n, int threads, int cap) {
-    return (int)std::max(1LL, std::min((long long)cap, (n + threads - 1) / threads));
 }
 
 // Synthetic rows of RandomForest::fit_unsupervised (src/rf_random_forest.cpp:1068-1086):
@@ -318,6 +191,10 @@ void load(Ctx& c, const rfx_fit_params* prm, const rfx_inputs* in) {
     c.R = P.prox_rows > 0 ? std::min<int>(P.prox_rows, (int)N) : (int)N;
     require(!(P.compute_proximity && has_cat), RFX_ERR_UNSUPPORTED,
             "proximity with categorical features is not supported yet");
+    require(P.lowrank_rank >= 0 && P.lowrank_rank <= 64, RFX_ERR_UNSUPPORTED,
+            "low-rank proximity rank must be in [0, 64]");
+    require(P.lowrank_rank == 0 || P.maxnode + 1 < 65535, RFX_ERR_UNSUPPORTED,
+            "low-rank proximity needs maxnode < 65534");
     c.classwt.clear();
     if (P.task == RFX_TASK_CLASSIFICATION && in->classwt)
         c.classwt.assign(in->classwt, in->classwt + c.nclass);
@@ -412,7 +289,11 @@ void load(Ctx& c, const rfx_fit_params* prm, const rfx_inputs* in) {
     RFX_CUDA(cudaMemsetAsync(sq, 0, p * 4, st));
     c.prox = nullptr;
     c.prox_len = 0;
-    if (P.compute_proximity) {
+    c.lr_rank = P.compute_proximity && P.lowrank_rank > 0 ? P.lowrank_rank : 0;
+    c.lr_n = 0;
+    c.lr_G = c.M + 2;
+    c.lr_ready = false;
+    if (P.compute_proximity && c.lr_rank == 0) {
         c.prox_len = (int64_t)c.R * (c.R - 1) / 2;
         c.prox = (int*)c.prox_own.get((size_t)c.prox_len * 4);
         RFX_CUDA(cudaMemsetAsync(c.prox, 0, (size_t)c.prox_len * 4, st));
@@ -566,11 +447,12 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
         RFX_LAUNCH("importance kernels");
         c.launches += 4;
     }
-    if (c.prm.compute_proximity) {
+    if (c.prm.compute_proximity && c.prox) {
         rfx::k_prox<<<rg, 256, 0, st>>>(D, B, c.R, c.prox);
         RFX_LAUNCH("k_prox");
         c.launches += 1;
     }
+    if (c.lr_rank > 0) lr_store_batch(c, B, T);
     if (keep) c.tree_oob_n += T;
     if (out) {
         auto cp = [&](void* dst, const void* src, size_t elems, size_t esz) {
@@ -647,6 +529,7 @@ int rfx_grow(void* ctx, int tree_begin, int ntree, rfx_trees* out) {
         Ctx& c = *as_ctx(ctx);
         require(c.loaded, RFX_ERR_STATE, "rfx_grow before rfx_load");
         require(tree_begin >= 0 && ntree >= 0, RFX_ERR_ARG, "bad tree range");
+        lr_reserve(c, ntree);
         for (int b0 = 0; b0 < ntree; b0 += c.Tcap) {
             const int T = std::min(c.Tcap, ntree - b0);
             grow_batch(c, tree_begin + b0, T, out, b0);

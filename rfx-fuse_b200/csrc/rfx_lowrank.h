@@ -1,0 +1,60 @@
+// Kernels of the low-rank proximity path (rfx_lowrank.cu, rfx_topk.cu).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+
+#include "rfx_device.cuh"
+
+namespace rfx {
+
+constexpr uint16_t kNoGroup = 0xFFFF;  // row outside the proximity rows
+constexpr int kLrMaxR = 96;            // sketch columns (rank + oversampling) at most
+constexpr int kLrK = 64;               // stored factor width (rank <= 64, zero padded)
+
+// product / top-k kernel geometry
+constexpr int kTkRows = 128;    // rows of a CTA (MMA M)
+constexpr int kTkCols = 256;    // columns of a tile (MMA N)
+constexpr int kTkStages = 3;    // column-tile ring
+constexpr int kTkSlots = 96;    // candidate slots per row (>= k + 32)
+constexpr int kTkThreads = 192; // warp 0 loads, warp 1 issues MMAs, warps 2-5 read out
+constexpr int kTkSmem = 16384 + kTkStages * 32768 + kTkSlots * kTkRows * 8 + 128 + 1024;
+
+struct TopkArgs {
+    int R;              // valid rows (= valid columns)
+    int r0, r1;         // rows of this launch
+    int ntiles;         // column tiles (Rpad / 256)
+    int k;              // neighbours kept; 0 = write the product densely
+    const float* scale; // [Rpad]
+    const float* smax;  // [Rpad / 32] chunk maxima of scale
+    int* out_idx;       // [r1 - r0][k]
+    float* out_val;     // [r1 - r0][k]
+    float* dense;       // [r1 - r0][dense_ld] when k == 0
+    long long dense_ld;
+    int* err;           // [0]: nonzero after a wait timed out
+};
+
+__global__ void k_lr_groups(Batch B, int N, int R, int G, uint16_t* code, int* order, int* goff,
+                            int* ngroups, int* tmp);
+// k_lr_leafsum / k_lr_scatter for a sketch width of 32 * nq columns (1 <= nq <= 8);
+// false for another width.
+bool lr_launch_leafsum(int nq, dim3 grid, cudaStream_t st, const int* order, const int* goff,
+                       const int* ngroups, int N, int G, const float* Z, float* LS);
+bool lr_launch_scatter(int nq, int grid, cudaStream_t st, const uint16_t* code, int N, int R, int T,
+                       int G, const float* LS, float* Y);
+__global__ void k_lr_prep(const float* X, int R, int r, const int* nout, int W, float* Z);
+__global__ void k_lr_combine(const float* CZ, int W, const float* X, int R, int r, const int* nout,
+                             float* Y);
+__global__ void k_lr_omega(float* X, int R, int r, unsigned long long seed);
+__global__ void k_lr_gram(const float* A, int ra, const float* Bm, int rb, int R, int rows_per_block,
+                          double* part);
+__global__ void k_lr_gram_reduce(const double* part, int nblk, int ra, int rb, int sym, double* G);
+__global__ void k_lr_chol_inv(const double* Gm, int r, double* Uinv);
+__global__ void k_lr_rowmat(const float* Y, int R, int rin, const double* Mat, int rout, float* Out);
+__global__ void k_lr_eig_select(const double* Tm, int r, int k, double* Mk, double* lam_out);
+__global__ void k_lr_quantize(const float* A, int R, int k, int Rpad, int8_t* q, uint16_t* qb,
+                              float* scale);
+__global__ void k_lr_smax(const float* scale, int Rpad, float* smax);
+__global__ void k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a);
+
+}  // namespace rfx

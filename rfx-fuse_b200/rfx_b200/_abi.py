@@ -27,7 +27,7 @@ class FitParams(C.Structure):
     _fields_ = [(k, C.c_int) for k in (
         "task", "n", "p", "mtry", "minndsize", "maxnode", "iseed", "boot_seed", "nbins",
         "maxcat", "compute_importance", "compute_proximity", "prox_rows", "batch_trees",
-        "keep_tree_oob")]
+        "keep_tree_oob", "lowrank_rank")]
 
 
 class Inputs(C.Structure):
@@ -58,7 +58,12 @@ SYMBOLS = (
     "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish", "rfx_prox_dense",
     "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host", "rfx_get_stream",
     "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats", "rfx_sync",
+    "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk", "rfx_lowrank_product",
+    "rfx_prox_apply",
 )
+
+# int (*)(void* user, float* buf_dev, int64_t count): in-place sum over processes
+REDUCE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_int64)
 
 _LIB = None
 
@@ -96,11 +101,18 @@ def load_library(path: str = LIB_PATH):
     L.rfx_get_stats.argtypes = [vp, C.POINTER(Stats)]
     L.rfx_reset_stats.argtypes = [vp]
     L.rfx_sync.argtypes = [vp]
+    L.rfx_lowrank_build.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_uint64, vp, REDUCE_FN, vp]
+    L.rfx_lowrank_factors.argtypes = [vp, _pf, C.POINTER(C.c_int8), _pf, C.POINTER(C.c_int),
+                                      C.POINTER(C.c_int)]
+    L.rfx_lowrank_topk.argtypes = [vp, C.c_int, C.c_int, C.c_int, _pi, _pf]
+    L.rfx_lowrank_product.argtypes = [vp, C.c_int, C.c_int, _pf]
+    L.rfx_prox_apply.argtypes = [vp, vp, C.c_int, vp, vp]
     for name in ("rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
                  "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish",
                  "rfx_prox_dense", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host",
                  "rfx_get_stream", "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats",
-                 "rfx_sync"):
+                 "rfx_sync", "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk",
+                 "rfx_lowrank_product", "rfx_prox_apply"):
         getattr(L, name).restype = C.c_int
     _LIB = L
     return L
@@ -206,3 +218,49 @@ class Context:
 
     def sync(self):
         check(self._lib.rfx_sync(self.handle))
+
+    # ---- low-rank proximity ----
+    def lowrank_build(self, rank: int, oversample: int = 16, power_iters: int = 1, seed: int = 0,
+                      nout_dev: int | None = None, reduce=None):
+        """Build the int8 factors.  ``reduce(dev_ptr, count)`` (optional) sums a device float
+        buffer over the processes in place; it runs once per sketch pass."""
+        cb = REDUCE_FN(0)
+        if reduce is not None:
+            def _cb(_user, buf, count):
+                try:
+                    reduce(int(buf), int(count))
+                    return 0
+                except Exception:  # reported as RFX_ERR_DEVICE by the library
+                    return 1
+            cb = REDUCE_FN(_cb)
+        check(self._lib.rfx_lowrank_build(self.handle, int(rank), int(oversample),
+                                          int(power_iters), C.c_uint64(seed & (2**64 - 1)),
+                                          C.c_void_p(nout_dev) if nout_dev else None, cb, None))
+
+    def lowrank_factors(self):
+        """(A float32 [R, k] dequantised, q int8 [R, k], scale float32 [R])."""
+        k, R = C.c_int(), C.c_int()
+        check(self._lib.rfx_lowrank_factors(self.handle, None, None, None, C.byref(k), C.byref(R)))
+        A = np.zeros((R.value, k.value), np.float32)
+        q = np.zeros((R.value, k.value), np.int8)
+        s = np.zeros(R.value, np.float32)
+        check(self._lib.rfx_lowrank_factors(self.handle, ptr(A, _pf), q.ctypes.data_as(C.POINTER(C.c_int8)),
+                                            ptr(s, _pf), C.byref(k), C.byref(R)))
+        return A, q, s
+
+    def lowrank_topk(self, k: int, r0: int, r1: int):
+        idx = np.zeros((r1 - r0, k), np.int32)
+        val = np.zeros((r1 - r0, k), np.float32)
+        check(self._lib.rfx_lowrank_topk(self.handle, int(k), int(r0), int(r1), ptr(idx, _pi),
+                                         ptr(val, _pf)))
+        return idx, val
+
+    def lowrank_product(self, r0: int, r1: int, R: int):
+        out = np.zeros((r1 - r0, R), np.float32)
+        check(self._lib.rfx_lowrank_product(self.handle, int(r0), int(r1), ptr(out, _pf)))
+        return out
+
+    def prox_apply(self, X_dev: int, ncols: int, Y_dev: int, nout_dev: int | None = None):
+        check(self._lib.rfx_prox_apply(self.handle, C.c_void_p(X_dev), int(ncols),
+                                       C.c_void_p(nout_dev) if nout_dev else None,
+                                       C.c_void_p(Y_dev)))

@@ -68,7 +68,8 @@ class _Forest:
                  use_casewise=False, compute_proximity_importance=False,
                  compute_leaf_assignments=False, categorical_features=None,
                  use_histogram=True, n_bins=256, class_weight="", classwt=None,
-                 device=0, prox_rows=0, batch_trees=0):
+                 device=0, prox_rows=0, batch_trees=0, lowrank_oversample=16,
+                 lowrank_power_iters=1):
         if use_casewise:
             raise NotImplementedError("use_casewise=True is not implemented on the device path")
         if use_rfgap:
@@ -86,6 +87,16 @@ class _Forest:
         self.compute_proximity = bool(compute_proximity)
         self.compute_importance = bool(compute_importance)
         self.use_qlora = bool(use_qlora)
+        self.quant_mode = str(quant_mode)
+        self.rank = int(rank)
+        self.lowrank_oversample = int(lowrank_oversample)
+        self.lowrank_power_iters = int(lowrank_power_iters)
+        if self.use_qlora and self.compute_proximity:
+            if self.quant_mode.lower() != "int8":
+                raise NotImplementedError("low-rank proximity is stored as int8 factors: "
+                                          "use quant_mode='int8'")
+            if not 1 <= self.rank <= 64:
+                raise NotImplementedError("low-rank proximity rank must be in [1, 64]")
         self.n_bins = min(int(n_bins), 256)
         self.categorical_features = categorical_features
         self.class_weight = class_weight
@@ -104,6 +115,9 @@ class _Forest:
     def _resolve_mtry_ctor(self, mtry):
         return mtry if mtry > 0 else _isqrt_f32(self.mdim)
 
+    def _lowrank_rank(self):
+        return self.rank if (self.use_qlora and self.compute_proximity) else 0
+
     def _context(self):
         if self._ctx is None:
             self._ctx = A.Context(self.device)
@@ -119,7 +133,8 @@ class _Forest:
         self._cat = cat
         prm = A.FitParams(task, n, p, mtry, self.minndsize, maxnode, self.iseed, 12345,
                           self.n_bins, self.maxcat, int(self.compute_importance),
-                          int(self.compute_proximity), self.prox_rows, self.batch_trees, 0)
+                          int(self.compute_proximity), self.prox_rows, self.batch_trees, 0,
+                          self._lowrank_rank())
         ycls = yreg = sw = cw = None
         if task == A.TASK_CLASSIFICATION:
             ycls = np.ascontiguousarray(y, dtype=np.int32)
@@ -162,6 +177,9 @@ class _Forest:
             ac.q = None
             ac.labels = None
         ctx.results(ac)
+        if self._lowrank_rank():
+            ctx.lowrank_build(self.rank, self.lowrank_oversample, self.lowrank_power_iters,
+                              seed=self.iseed)
         self.trees_ = tr
         self.acc_ = acc
         self.n_rows_ = N
@@ -212,6 +230,12 @@ class _Forest:
         self._check()
         if not self.compute_proximity:
             raise RuntimeError("Proximity was not computed (compute_proximity=False)")
+        if self._lowrank_rank():
+            raise RuntimeError(
+                "Proximity matrix not available in full form. Low-rank mode is active "
+                "(use_qlora=True). Proximity is stored in low-rank factors (A and B). Use "
+                "get_lowrank_factors() instead, or disable use_qlora for datasets whose full "
+                "matrix fits.")
         ctx = self._context()
         _, length = ctx.prox_buffer()
         R = int(round((1 + math.sqrt(1 + 8 * length)) / 2)) if length else (
@@ -228,6 +252,46 @@ class _Forest:
         out = np.empty((R, R), np.float32)
         ctx.prox_dense(0, R, out)
         return out
+
+    # ---- low-rank proximity (use_qlora=True, quant_mode="int8")
+    def _check_lowrank(self):
+        self._check()
+        if not self._lowrank_rank():
+            raise RuntimeError(
+                "Low-rank factors not available. Either low-rank mode is not active "
+                "(use_qlora=True required), or factors have not been computed yet.")
+
+    def get_lowrank_factors(self):
+        """(A float64 [n, r], B float64 [n, r], r) with proximity ~ A B^T and B = A, the
+        dequantised int8 factors (python/randomforest_py.cpp:2183-2223)."""
+        self._check_lowrank()
+        Af, _, _ = self._context().lowrank_factors()
+        A64 = Af.astype(np.float64)
+        return A64, A64.copy(), int(Af.shape[1])
+
+    def get_lowrank_quantized(self):
+        """(q int8 [n, r], scale float32 [n]): A_i = scale_i * q_i."""
+        self._check_lowrank()
+        _, q, s = self._context().lowrank_factors()
+        return q, s
+
+    def get_lowrank_topk(self, k=50, row_begin=0, row_end=None):
+        """Top-k neighbours of every row under the quantised low-rank proximity, j != i:
+        (indices int32 [rows, k], values float32 [rows, k]), value descending."""
+        self._check_lowrank()
+        R = self._lowrank_rows()
+        row_end = R if row_end is None else int(row_end)
+        return self._context().lowrank_topk(int(k), int(row_begin), row_end)
+
+    def get_lowrank_product(self, row_begin=0, row_end=None):
+        """Rows of the reconstructed low-rank proximity (scale_i scale_j q_i . q_j)."""
+        self._check_lowrank()
+        R = self._lowrank_rows()
+        row_end = R if row_end is None else int(row_end)
+        return self._context().lowrank_product(int(row_begin), row_end, R)
+
+    def _lowrank_rows(self):
+        return self.prox_rows if self.prox_rows else self.n_rows_
 
     def get_proximity_counts(self):
         """Packed upper triangle (i < j) of the integer OOB x in-bag co-membership counts."""
