@@ -213,6 +213,13 @@ typedef int (*rfx_reduce_fn)(void* user, float* buf_dev, int64_t count);
 int rfx_lowrank_build(void* ctx, int rank, int oversample, int power_iters, uint64_t seed,
                       const int* nout_dev, rfx_reduce_fn reduce, void* reduce_user);
 
+/* Use caller-supplied factors (no reference counterpart; e.g. factors saved from an earlier
+ * fit, or built by another process): q_host [rows][rank] int8 in [-127, 127], scale_host
+ * [rows] finite, >= 0.  No fit is needed; rfx_lowrank_topk / _product / _factors then
+ * work on these rows. */
+int rfx_lowrank_set_factors(void* ctx, const int8_t* q_host, const float* scale_host, int rows,
+                            int rank);
+
 /* The factors: A_host [R][rank] dequantised float (may be NULL), q_host [R][rank] int8
  * (may be NULL), scale_host [R] (may be NULL); *rank_out = rank, *rows_out = R. */
 int rfx_lowrank_factors(void* ctx, float* A_host, int8_t* q_host, float* scale_host,

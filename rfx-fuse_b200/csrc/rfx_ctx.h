@@ -114,9 +114,11 @@ struct Ctx {
     int lr_n = 0, lr_cap = 0;   // trees stored / capacity
     int lr_G = 0;               // group-offset stride per tree (maxnode + 2)
     int lr_k = 0, lr_Rpad = 0;  // factor rank and rows padded to the product tile
+    int lr_R = 0;               // factor rows
     bool lr_ready = false;
+    std::vector<int> lr_pos;    // stored position of every original row (product order)
     DBuf lr_code, lr_order, lr_goff, lr_ngroups, lr_tmp;
-    DBuf lr_X, lr_Z, lr_CZ, lr_Y, lr_ls, lr_part, lr_small, lr_A, lr_q, lr_qb, lr_s, lr_smax,
+    DBuf lr_X, lr_Z, lr_CZ, lr_Y, lr_ls, lr_part, lr_small, lr_A, lr_q, lr_qb, lr_s, lr_qbp, lr_sp, lr_perm, lr_blocks, lr_np, lr_norm, lr_ids, lr_keys, lr_order_s, lr_cub,
         lr_err, lr_out_i, lr_out_v;
 
     // batch buffers
@@ -137,8 +139,8 @@ struct Ctx {
                        &b_feat, &b_lvl, &b_srch, &b_srchcnt, &b_srchoff, &b_counters,
                        &b_oobleaf, &b_used, &b_right, &b_rightimp, &b_d2, &b_d0, &b_rr, &b_srchbig, &b_partbig,
                        &lr_code, &lr_order, &lr_goff, &lr_ngroups, &lr_tmp, &lr_X, &lr_Z,
-                       &lr_CZ, &lr_Y, &lr_ls, &lr_part, &lr_small, &lr_A, &lr_q, &lr_qb, &lr_s,
-                       &lr_smax, &lr_err, &lr_out_i, &lr_out_v};
+                       &lr_CZ, &lr_Y, &lr_ls, &lr_part, &lr_small, &lr_A, &lr_q, &lr_qb, &lr_s, &lr_qbp, &lr_sp, &lr_perm, &lr_blocks, &lr_np, &lr_norm, &lr_ids, &lr_keys, &lr_order_s, &lr_cub,
+                       &lr_err, &lr_out_i, &lr_out_v};
         cudaSetDevice(device);
         if (st) cudaStreamSynchronize(st);
         for (DBuf* b : all) b->release();

@@ -571,13 +571,54 @@ __global__ void k_lr_quantize(const float* __restrict__ A, int R, int k, int Rpa
     }
 }
 
-// Maximum scale of every 32-row chunk (the bound of the product kernel's chunk filter).
-__global__ void k_lr_smax(const float* __restrict__ scale, int Rpad, float* __restrict__ smax) {
-    const int c = blockIdx.x * blockDim.x + threadIdx.x;
-    if (c >= Rpad / 32) return;
-    float m = 0.0f;
-    for (int i = 0; i < 32; ++i) m = fmaxf(m, scale[32 * c + i]);
-    smax[c] = m;
+// Caller-supplied factors q [R][rank] / scale [R] into the padded [Rpad][kLrK] layouts.
+__global__ void k_lr_load_factors(const int8_t* __restrict__ qin, const float* __restrict__ sin,
+                                  int R, int rank, int Rpad, int8_t* __restrict__ q,
+                                  uint16_t* __restrict__ qb, float* __restrict__ scale) {
+    const long long total = (long long)Rpad * kLrK;
+    for (long long k = blockIdx.x * (long long)blockDim.x + threadIdx.x; k < total;
+         k += (long long)gridDim.x * blockDim.x) {
+        const int i = (int)(k / kLrK), c = (int)(k % kLrK);
+        const int v = (i < R && c < rank) ? (int)qin[(size_t)i * rank + c] : 0;
+        q[k] = (int8_t)v;
+        qb[k] = (uint16_t)(__float_as_uint((float)v) >> 16);
+        if (c == 0) scale[i] = i < R ? sin[i] : 0.0f;
+    }
+}
+
+// n_i = scale_i * |q_i|_2 (the Cauchy-Schwarz bound factor of row i) and ids[i] = i.
+__global__ void k_lr_norms(const int8_t* __restrict__ q, const float* __restrict__ scale, int R,
+                           float* __restrict__ norm, int* __restrict__ ids) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= R) return;
+    const int8_t* r = q + (size_t)i * kLrK;
+    int ss = 0;
+    for (int c = 0; c < kLrK; ++c) ss += (int)r[c] * (int)r[c];
+    norm[i] = scale[i] * sqrtf((float)ss);
+    ids[i] = i;
+}
+
+// Factor rows in the product's stored order: position p holds original row order[p] (rows
+// by descending n, so the strongest candidates are met first); positions >= R are zero with
+// id INT_MAX.  order == null: identity.
+__global__ void k_lr_permute(const uint16_t* __restrict__ qb, const float* __restrict__ scale,
+                             const float* __restrict__ norm, const int* __restrict__ order, int R,
+                             int Rpad, uint16_t* __restrict__ qbp, float* __restrict__ sp,
+                             float* __restrict__ np, int* __restrict__ perm) {
+    const long long total = (long long)Rpad * (kLrK / 8);  // 16-byte pieces
+    for (long long k = blockIdx.x * (long long)blockDim.x + threadIdx.x; k < total;
+         k += (long long)gridDim.x * blockDim.x) {
+        const int pos = (int)(k / (kLrK / 8)), piece = (int)(k % (kLrK / 8));
+        const int src = pos < R ? (order ? order[pos] : pos) : -1;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (src >= 0) v = reinterpret_cast<const uint4*>(qb + (size_t)src * kLrK)[piece];
+        reinterpret_cast<uint4*>(qbp + (size_t)pos * kLrK)[piece] = v;
+        if (piece == 0) {
+            sp[pos] = src >= 0 ? scale[src] : 0.0f;
+            np[pos] = src >= 0 ? norm[src] : 0.0f;
+            perm[pos] = src >= 0 ? src : 0x7fffffff;
+        }
+    }
 }
 
 }  // namespace rfx

@@ -16,22 +16,30 @@ constexpr int kLrK = 64;               // stored factor width (rank <= 64, zero 
 constexpr int kTkRows = 128;    // rows of a CTA (MMA M)
 constexpr int kTkCols = 256;    // columns of a tile (MMA N)
 constexpr int kTkStages = 3;    // column-tile ring
-constexpr int kTkSlots = 96;    // candidate slots per row (>= k + 32)
+constexpr int kTkSlots = 64;    // heap entries per row (k <= 64)
 constexpr int kTkThreads = 192; // warp 0 loads, warp 1 issues MMAs, warps 2-5 read out
-constexpr int kTkSmem = 16384 + kTkStages * 32768 + kTkSlots * kTkRows * 8 + 128 + 1024;
+constexpr int kTkSmem = 16384 + kTkStages * 32768 + kTkSlots * kTkRows * 8 + 128 + 4096 + 1024;
 
 struct TopkArgs {
     int R;              // valid rows (= valid columns)
-    int r0, r1;         // rows of this launch
+    int r0, r1;         // original rows whose results are written
+    const int* blocks;  // [grid] 128-row blocks (of the stored order) of the CTAs, or null:
+                        // CTA b takes positions r0 + 128 b (identity order)
+    const int* perm;    // [Rpad] original id of every stored position (>= R for padding),
+                        // or null (identity order)
     int ntiles;         // column tiles (Rpad / 256)
     int k;              // neighbours kept; 0 = write the product densely
-    const float* scale; // [Rpad]
-    const float* smax;  // [Rpad / 32] chunk maxima of scale
+    const float* scale; // [Rpad] by stored position
+    const float* norm;  // [Rpad] s_j * |q_j| by stored position, descending (with perm), or
+                        // null: no early stop
     int* out_idx;       // [r1 - r0][k]
     float* out_val;     // [r1 - r0][k]
-    float* dense;       // [r1 - r0][dense_ld] when k == 0
+    float* dense;       // [r1 - r0][dense_ld] by original column, when k == 0
     long long dense_ld;
     int* err;           // [0]: nonzero after a wait timed out
+    unsigned long long* prof;  // optional counters (null: off): chunks tested, chunks
+                               // scanned, candidates pushed, -, read-out wait
+                               // polls, MMA wait polls, load wait polls
 };
 
 __global__ void k_lr_groups(Batch B, int N, int R, int G, uint16_t* code, int* order, int* goff,
@@ -54,7 +62,12 @@ __global__ void k_lr_rowmat(const float* Y, int R, int rin, const double* Mat, i
 __global__ void k_lr_eig_select(const double* Tm, int r, int k, double* Mk, double* lam_out);
 __global__ void k_lr_quantize(const float* A, int R, int k, int Rpad, int8_t* q, uint16_t* qb,
                               float* scale);
-__global__ void k_lr_smax(const float* scale, int Rpad, float* smax);
+__global__ void k_lr_load_factors(const int8_t* qin, const float* sin, int R, int rank, int Rpad,
+                                  int8_t* q, uint16_t* qb, float* scale);
+__global__ void k_lr_norms(const int8_t* q, const float* scale, int R, float* norm, int* ids);
+__global__ void k_lr_permute(const uint16_t* qb, const float* scale, const float* norm,
+                             const int* order, int R, int Rpad, uint16_t* qbp, float* sp,
+                             float* np, int* perm);
 __global__ void k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a);
 
 }  // namespace rfx

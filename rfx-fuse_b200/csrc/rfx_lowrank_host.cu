@@ -2,13 +2,16 @@
 // rfx_topk.cu; ABI in include/rfx_b200.h).
 //
 // Fit: with lowrank_rank > 0 every grown batch stores its trees' leaf groups (row -> group
-// code, rows grouped by leaf and in-bag/OOB, group offsets) instead of dense counts.
+// code, rows ordered by leaf and in-bag/OOB, group offsets) instead of dense counts.
 // Build: randomized range finder on S (Halko, Martinsson & Tropp, SIAM Review 53(2), 2011,
 // algorithms 4.3/4.4 with Cholesky-QR twice as the orthonormaliser), then the eigenpairs of
 // the r x r projection Q^T S Q; A = Q V_k sqrt(max(lambda_k, 0)) is the best rank-k
 // positive semidefinite approximation of S within range(Q); A is stored int8 per row.
+#include <cub/cub.cuh>
 #include <cudaTypedefs.h>
 
+#include <cmath>
+#include <cstdio>
 #include <cstring>
 #include <mutex>
 
@@ -124,41 +127,71 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // Tensor map of the bf16 factor rows [Rpad][64]: boxes of 128 rows x 64 columns, 128-byte
 // swizzle (one box row is exactly one 128-byte swizzle span).
-CUtensorMap factor_map(Ctx& c) {
+CUtensorMap factor_map(Ctx& c, void* rows) {
     CUtensorMap tm;
     std::memset(&tm, 0, sizeof(tm));
     const cuuint64_t dims[2] = {(cuuint64_t)rfx::kLrK, (cuuint64_t)c.lr_Rpad};
     const cuuint64_t strides[1] = {(cuuint64_t)rfx::kLrK * 2};
     const cuuint32_t box[2] = {(cuuint32_t)rfx::kLrK, 128};
     const cuuint32_t es[2] = {1, 1};
-    const CUresult r = encode_fn()(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, c.lr_qb.p, dims, strides,
+    const CUresult r = encode_fn()(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, dims, strides,
                                    box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     require(r == CUDA_SUCCESS, RFX_ERR_CUDA, "cuTensorMapEncodeTiled failed");
     return tm;
 }
 
-// One launch of the product kernel over rows [r0, r1).
+// One launch of the product kernel for original rows [r0, r1).  Top-k (k > 0) runs on the
+// rows stored by descending bound factor n (early stop); the dense product (k == 0) on the
+// identity order.
 void run_product(Ctx& c, int r0, int r1, int k, int* oi, float* ov, float* dense, long long ld) {
     cudaStream_t st = c.st;
-    const CUtensorMap tm = factor_map(c);
+    const bool ordered = k > 0;
+    const CUtensorMap tm = factor_map(c, ordered ? c.lr_qbp.p : c.lr_qb.p);
     int* err = (int*)c.lr_err.get(16);
     RFX_CUDA(cudaMemsetAsync(err, 0, 16, st));
     rfx::TopkArgs a;
-    a.R = c.R;
+    a.R = c.lr_R;
     a.r0 = r0;
     a.r1 = r1;
     a.ntiles = c.lr_Rpad / rfx::kTkCols;
     a.k = k;
-    a.scale = (const float*)c.lr_s.p;
-    a.smax = (const float*)c.lr_smax.p;
+    a.scale = (const float*)(ordered ? c.lr_sp.p : c.lr_s.p);
+    a.perm = ordered ? (const int*)c.lr_perm.p : nullptr;
+    a.norm = ordered ? (const float*)c.lr_np.p : nullptr;
+    a.blocks = nullptr;
+    int grid = (r1 - r0 + rfx::kTkRows - 1) / rfx::kTkRows;
+    if (ordered) {
+        // the 128-row blocks of the stored order that hold any requested row
+        std::vector<int> blk;
+        if (r0 == 0 && r1 == c.lr_R) {
+            for (int b = 0; b < (c.lr_R + rfx::kTkRows - 1) / rfx::kTkRows; ++b) blk.push_back(b);
+        } else {
+            std::vector<char> mark((c.lr_R + rfx::kTkRows - 1) / rfx::kTkRows, 0);
+            for (int i = r0; i < r1; ++i) mark[c.lr_pos[i] / rfx::kTkRows] = 1;
+            for (int b = 0; b < (int)mark.size(); ++b)
+                if (mark[b]) blk.push_back(b);
+        }
+        int* db = (int*)c.lr_blocks.get(blk.size() * 4);
+        RFX_CUDA(cudaMemcpyAsync(db, blk.data(), blk.size() * 4, cudaMemcpyHostToDevice, st));
+        RFX_CUDA(cudaStreamSynchronize(st));  // blk is a local vector
+        a.blocks = db;
+        grid = (int)blk.size();
+    }
     a.out_idx = oi;
     a.out_val = ov;
     a.dense = dense;
     a.dense_ld = ld;
     a.err = err;
+    a.prof = nullptr;
+    unsigned long long* prof = nullptr;
+    static const bool want_prof = std::getenv("RFX_TOPK_PROF") != nullptr;
+    if (want_prof) {
+        prof = (unsigned long long*)c.lr_part.get(64 * 8);
+        RFX_CUDA(cudaMemsetAsync(prof, 0, 128, st));
+        a.prof = prof;
+    }
     set_smem((const void*)rfx::k_topk_tc, rfx::kTkSmem);
-    const int grid = (r1 - r0 + rfx::kTkRows - 1) / rfx::kTkRows;
     rfx::k_topk_tc<<<grid, rfx::kTkThreads, rfx::kTkSmem, st>>>(tm, a);
     RFX_LAUNCH("k_topk_tc");
     c.launches += 1;
@@ -166,6 +199,55 @@ void run_product(Ctx& c, int r0, int r1, int k, int* oi, float* ov, float* dense
     RFX_CUDA(cudaMemcpyAsync(&h, err, 4, cudaMemcpyDeviceToHost, st));
     RFX_CUDA(cudaStreamSynchronize(st));
     require(h == 0, RFX_ERR_DEVICE, "product kernel: a pipeline wait timed out (code " + std::to_string(h) + ")");
+    if (prof) {
+        unsigned long long hp[16] = {};
+        RFX_CUDA(cudaMemcpy(hp, prof, 128, cudaMemcpyDeviceToHost));
+        std::fprintf(stderr,
+                     "[rfx topk] rows=%d chunks=%llu scanned=%llu pushes=%llu compactions=%llu "
+                     "polls: readout=%llu mma=%llu load=%llu  cycles: readout wait=%llu "
+                     "readout total=%llu mma wait-acc=%llu mma wait-load=%llu load wait-free=%llu\n",
+                     r1 - r0, hp[0], hp[1], hp[2], hp[3], hp[4], hp[5], hp[6], hp[7], hp[8], hp[9],
+                     hp[10], hp[11]);
+    }
+}
+
+// The product's stored order of the factors (rows by descending n_i = scale_i |q_i|,
+// stable: ties by row id) from lr_q / lr_qb / lr_s of R rows.
+void order_factors(Ctx& c, int R, int rank) {
+    cudaStream_t st = c.st;
+    const int Rpad = (int)round_up(R, rfx::kTkCols);
+    const int8_t* q = (const int8_t*)c.lr_q.p;
+    const uint16_t* qb = (const uint16_t*)c.lr_qb.p;
+    const float* s = (const float*)c.lr_s.p;
+    float* nrm = (float*)c.lr_norm.get((size_t)R * 4);
+    int* ids = (int*)c.lr_ids.get((size_t)R * 4);
+    float* keys = (float*)c.lr_keys.get((size_t)R * 4);
+    int* order = (int*)c.lr_order_s.get((size_t)R * 4);
+    rfx::k_lr_norms<<<(R + 255) / 256, 256, 0, st>>>(q, s, R, nrm, ids);
+    RFX_LAUNCH("k_lr_norms");
+    size_t tmp_bytes = 0;
+    RFX_CUDA(cub::DeviceRadixSort::SortPairsDescending(nullptr, tmp_bytes, nrm, keys, ids, order,
+                                                       R, 0, 32, st));
+    void* tmp = c.lr_cub.get(tmp_bytes);
+    RFX_CUDA(cub::DeviceRadixSort::SortPairsDescending(tmp, tmp_bytes, nrm, keys, ids, order, R, 0,
+                                                       32, st));
+    uint16_t* qbp = (uint16_t*)c.lr_qbp.get((size_t)Rpad * rfx::kLrK * 2);
+    float* sp = (float*)c.lr_sp.get((size_t)Rpad * 4);
+    float* np_ = (float*)c.lr_np.get((size_t)Rpad * 4);
+    int* perm = (int*)c.lr_perm.get((size_t)Rpad * 4);
+    rfx::k_lr_permute<<<grid_for((long long)Rpad * 8, 256, c.sm_count * 16), 256, 0, st>>>(
+        qb, s, nrm, order, R, Rpad, qbp, sp, np_, perm);
+    RFX_LAUNCH("k_lr_permute");
+    std::vector<int> hp(R);
+    RFX_CUDA(cudaMemcpyAsync(hp.data(), perm, (size_t)R * 4, cudaMemcpyDeviceToHost, st));
+    c.launches += 2;
+    RFX_CUDA(cudaStreamSynchronize(st));
+    c.lr_pos.assign(R, 0);
+    for (int p = 0; p < R; ++p) c.lr_pos[hp[p]] = p;
+    c.lr_k = rank;
+    c.lr_Rpad = Rpad;
+    c.lr_R = R;
+    c.lr_ready = true;
 }
 
 }  // namespace
@@ -274,16 +356,38 @@ int rfx_lowrank_build(void* ctx, int rank, int oversample, int power_iters, uint
         int8_t* q = (int8_t*)c.lr_q.get((size_t)Rpad * rfx::kLrK);
         uint16_t* qb = (uint16_t*)c.lr_qb.get((size_t)Rpad * rfx::kLrK * 2);
         float* s = (float*)c.lr_s.get((size_t)Rpad * 4);
-        float* smax = (float*)c.lr_smax.get((size_t)(Rpad / 32) * 4);
         rfx::k_lr_quantize<<<c.sm_count * 8, 256, 0, st>>>(A, R, rank, Rpad, q, qb, s);
         RFX_LAUNCH("k_lr_quantize");
-        rfx::k_lr_smax<<<(Rpad / 32 + 255) / 256, 256, 0, st>>>(s, Rpad, smax);
-        RFX_LAUNCH("k_lr_smax");
-        c.launches += 5;
-        RFX_CUDA(cudaStreamSynchronize(st));
-        c.lr_k = rank;
-        c.lr_Rpad = Rpad;
-        c.lr_ready = true;
+        c.launches += 4;
+        order_factors(c, R, rank);
+    });
+}
+
+int rfx_lowrank_set_factors(void* ctx, const int8_t* q_host, const float* scale_host, int rows,
+                            int rank) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(q_host && scale_host, RFX_ERR_ARG, "null factors");
+        require(rows >= 1 && rank >= 1 && rank <= rfx::kLrK, RFX_ERR_ARG, "bad factor shape");
+        for (size_t i = 0; i < (size_t)rows * rank; ++i)
+            require(q_host[i] >= -127, RFX_ERR_ARG, "factor values must be in [-127, 127]");
+        for (int i = 0; i < rows; ++i)
+            require(scale_host[i] >= 0.0f && std::isfinite(scale_host[i]), RFX_ERR_ARG,
+                    "scales must be finite and non-negative");
+        cudaStream_t st = c.st;
+        const int Rpad = (int)round_up(rows, rfx::kTkCols);
+        int8_t* qin = (int8_t*)c.lr_X.get((size_t)rows * rank);
+        float* sin = (float*)c.lr_Y.get((size_t)rows * 4);
+        RFX_CUDA(cudaMemcpyAsync(qin, q_host, (size_t)rows * rank, cudaMemcpyHostToDevice, st));
+        RFX_CUDA(cudaMemcpyAsync(sin, scale_host, (size_t)rows * 4, cudaMemcpyHostToDevice, st));
+        int8_t* q = (int8_t*)c.lr_q.get((size_t)Rpad * rfx::kLrK);
+        uint16_t* qb = (uint16_t*)c.lr_qb.get((size_t)Rpad * rfx::kLrK * 2);
+        float* s = (float*)c.lr_s.get((size_t)Rpad * 4);
+        rfx::k_lr_load_factors<<<grid_for((long long)Rpad * rfx::kLrK, 256, c.sm_count * 16), 256, 0, st>>>(
+            qin, sin, rows, rank, Rpad, q, qb, s);
+        RFX_LAUNCH("k_lr_load_factors");
+        c.launches += 1;
+        order_factors(c, rows, rank);
     });
 }
 
@@ -292,7 +396,7 @@ int rfx_lowrank_factors(void* ctx, float* A_host, int8_t* q_host, float* scale_h
     return guarded([&] {
         Ctx& c = *as_ctx(ctx);
         require(c.lr_ready, RFX_ERR_STATE, "low-rank factors have not been built");
-        const int R = c.R, k = c.lr_k;
+        const int R = c.lr_R, k = c.lr_k;
         std::vector<int8_t> qh((size_t)R * rfx::kLrK);
         std::vector<float> sh(R);
         RFX_CUDA(cudaMemcpyAsync(qh.data(), c.lr_q.p, qh.size(), cudaMemcpyDeviceToHost, c.st));
@@ -316,7 +420,7 @@ int rfx_lowrank_topk(void* ctx, int k, int row_begin, int row_end, int* idx_host
         Ctx& c = *as_ctx(ctx);
         require(c.lr_ready, RFX_ERR_STATE, "low-rank factors have not been built");
         require(k >= 1 && k <= 64, RFX_ERR_ARG, "k must be in [1, 64]");
-        require(row_begin >= 0 && row_begin <= row_end && row_end <= c.R, RFX_ERR_ARG, "bad row range");
+        require(row_begin >= 0 && row_begin <= row_end && row_end <= c.lr_R, RFX_ERR_ARG, "bad row range");
         require(idx_host && val_host, RFX_ERR_ARG, "null output");
         const int rows = row_end - row_begin;
         if (rows == 0) return;
@@ -333,9 +437,9 @@ int rfx_lowrank_product(void* ctx, int row_begin, int row_end, float* out_host) 
     return guarded([&] {
         Ctx& c = *as_ctx(ctx);
         require(c.lr_ready, RFX_ERR_STATE, "low-rank factors have not been built");
-        require(row_begin >= 0 && row_begin <= row_end && row_end <= c.R, RFX_ERR_ARG, "bad row range");
+        require(row_begin >= 0 && row_begin <= row_end && row_end <= c.lr_R, RFX_ERR_ARG, "bad row range");
         require(out_host, RFX_ERR_ARG, "null output");
-        const int R = c.R;
+        const int R = c.lr_R;
         const long long ld = c.lr_Rpad;
         const int chunk = (int)std::max<long long>(rfx::kTkRows,
             (((long long)256 << 20) / (ld * 4)) / rfx::kTkRows * rfx::kTkRows);

@@ -5,20 +5,26 @@
 // accumulate in fp32, exactly as integers (64 * 127^2 < 2^24), so the bf16 MMA equals the
 // int8 dot product.  P_ij = (acc_ij * s_i) * s_j in fp32.
 //
-// CTA = 128 rows (the MMA's M), sweeping all column tiles of 256 (N) in ascending order:
+// The factor rows are stored by descending n_j = s_j |q_j| (Cauchy-Schwarz: P_ij <= n_i n_j),
+// so the strongest candidates come first and each row's k-th value rises at once.
+// CTA = 128 rows (the MMA's M), sweeping the column tiles of 256 (N) in stored order:
 //   warp 0      one thread issues TMA loads: the CTA's 128x64 row tile once, then the
 //               256x64 column tiles through a 3-stage ring (128-byte swizzle, K-major);
 //   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators) and one thread
 //               issues 4 x tcgen05.mma (K = 16 each) per tile, committing to the ring's
 //               "empty" barrier and to the accumulator's "full" barrier;
-//   warps 2-5   read the accumulator (tcgen05.ld 32x32b, thread = row), release it, and
-//               keep each row's best k under (value desc, column asc): a chunk of 32 columns
-//               is skipped when an upper bound of its values (chunk max * s_i * max s_j) does
-//               not beat the row's current k-th value; survivors go to the row's candidate
-//               slots in shared memory (slot-major, conflict-free), compacted by quickselect
-//               when full.
-// Columns arrive in ascending order, so a new candidate with a value equal to the k-th
-// never displaces it, and the result is the exact top-k under the total order.
+//   warps 2-5   read the accumulator (tcgen05.ld 32x32b, thread = row, 128 columns per
+//               wait), release it, and keep each row's best k under (value desc, original
+//               column asc).  The tile's 256 column scales and ids are staged in shared
+//               memory (each thread loads two for the next tile while it works on this one).
+//               A chunk of 32 columns is scanned only when max_j(acc_ij * s_j) * s_i reaches
+//               the row's current k-th value less a 1e-6 relative margin (the exact value
+//               rounds the same three factors in another order); survivors that beat the
+//               bar enter the row's heap of the best k in shared memory.  A row is final once n_i * n_(next tile's first
+//               column) is below its k-th value; when all 128 rows are final the CTA lowers
+//               its stop limit and the three roles end their sweeps.
+// The bar carries the k-th entry's column id, so ties are broken by the original index
+// whatever the sweep order, and the result is the exact top-k under the total order.
 //
 // Every wait is bounded (about one second); on expiry the CTA records the failure in
 // a.err, drains its own copies in flight, frees its TMEM and returns.
@@ -56,17 +62,34 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Wait for the phase of `parity` to complete; false on timeout or when another role of the
-// CTA has aborted (abort may be null: wait regardless).
-__device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+// Wait for the phase of `parity` to complete.  Returns kWaitOk, or kWaitFail on timeout or
+// when another role of the CTA has aborted (abort may be null: wait regardless), or
+// kWaitStop once step `it` is at or beyond the CTA's stop limit (limit may be null).
+constexpr int kWaitFail = 0, kWaitOk = 1, kWaitStop = 2;
+
+__device__ int mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                         unsigned long long* polls = nullptr, volatile int* limit = nullptr,
+                         int it = 0) {
     const unsigned long long t0 = now_ns();
     for (uint32_t spin = 1;; ++spin) {
-        if (mbar_try(bar, parity)) return true;
+        if (polls) ++*polls;
+        if (mbar_try(bar, parity)) return kWaitOk;
         if ((spin & 63u) == 0) {
-            if (abort && *abort) return false;
-            if (now_ns() - t0 > kWaitNs) return false;
+            if (limit && it >= *limit) return kWaitStop;
+            if (abort && *abort) return kWaitFail;
+            if (now_ns() - t0 > kWaitNs) return kWaitFail;
         }
     }
+}
+
+// mbar_wait that also adds the cycles it spent to *cyc.
+__device__ __forceinline__ int mbar_wait_t(uint32_t bar, uint32_t parity, volatile int* abort,
+                                           unsigned long long* polls, unsigned long long* cyc,
+                                           volatile int* limit = nullptr, int it = 0) {
+    const long long t0 = clock64();
+    const int r = mbar_wait(bar, parity, abort, polls, limit, it);
+    *cyc += (unsigned long long)(clock64() - t0);
+    return r;
 }
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -130,9 +153,9 @@ __device__ __forceinline__ void tc_fence_after() {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 }
 
-// 32 consecutive fp32 accumulator columns of this thread's TMEM lane.
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
+// Issue a load of 32 consecutive fp32 accumulator columns of this thread's TMEM lane; the
+// registers are valid after tmem_wait().
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t* r) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -143,69 +166,65 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
           "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
           "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int e = 0; e < 32; ++e) v[e] = __uint_as_float(r[e]);
 }
 
-// Candidate slots of one row: slot s of the row at v[s * kTkRows], j[s * kTkRows].
+__device__ __forceinline__ void tmem_wait() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Ties 32 loaded registers to a point after tmem_wait() so no use moves above the wait.
+__device__ __forceinline__ void tmem_pin32(uint32_t* r) {
+    asm volatile(""
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                   "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                   "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                   "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                   "+r"(r[30]), "+r"(r[31]));
+}
+
+// The best k of one row are kept as a binary heap in shared memory whose root is the
+// worst kept entry (the bar a new column must beat).  Entry s of the row sits at
+// v[s * kTkRows], j[s * kTkRows] (slot-major: lanes never share a bank).  Sift-up and
+// sift-down run a fixed number of predicated steps, so lanes of a warp stay converged.
 __device__ __forceinline__ bool better(float va, int ja, float vb, int jb) {
     return va > vb || (va == vb && ja < jb);
 }
 
-__device__ __forceinline__ void swap_slots(float* v, int* j, int a, int b) {
-    const float tv = v[a * kTkRows];
-    const int tj = j[a * kTkRows];
-    v[a * kTkRows] = v[b * kTkRows];
-    j[a * kTkRows] = j[b * kTkRows];
-    v[b * kTkRows] = tv;
-    j[b * kTkRows] = tj;
-}
+constexpr int kHeapDepth = 6;  // levels below the root of a heap of <= 64 entries
 
-// Reorder slots [0, n) so that [0, k) hold the k best (Hoare quickselect on slot k-1).
-__device__ void select_best(float* v, int* j, int n, int k) {
-    int lo = 0, hi = n - 1;
-    const int kth = k - 1;
-    while (lo < hi) {
-        const int mid = (lo + hi) >> 1;
-        const float pv = v[mid * kTkRows];
-        const int pj = j[mid * kTkRows];
-        int a = lo, b = hi;
-        while (a <= b) {
-            while (better(v[a * kTkRows], j[a * kTkRows], pv, pj)) ++a;
-            while (better(pv, pj, v[b * kTkRows], j[b * kTkRows])) --b;
-            if (a <= b) {
-                swap_slots(v, j, a, b);
-                ++a;
-                --b;
-            }
+// Insert (val, col) into a heap of n < k entries.
+__device__ __forceinline__ void heap_insert(float* v, int* j, int n, float val, int col) {
+    int i = n;
+#pragma unroll
+    for (int l = 0; l < kHeapDepth; ++l) {
+        const int p = (i - 1) >> 1;
+        if (i > 0 && better(v[p * kTkRows], j[p * kTkRows], val, col)) {  // parent is better:
+            v[i * kTkRows] = v[p * kTkRows];                               // the new entry rises
+            j[i * kTkRows] = j[p * kTkRows];
+            i = p;
         }
-        if (kth <= b) hi = b;
-        else if (kth >= a) lo = a;
-        else break;
     }
+    v[i * kTkRows] = val;
+    j[i * kTkRows] = col;
 }
 
-struct PushResult {
-    int cnt;
-    float theta;
-};
-
-// Append a candidate; when the slots are full keep the best k and return the new bar
-// (the k-th value).
-__device__ __noinline__ PushResult push_candidate(float* v, int* j, int cnt, int k, float val,
-                                                  int col, float theta) {
-    v[cnt * kTkRows] = val;
-    j[cnt * kTkRows] = col;
-    ++cnt;
-    if (cnt == kTkSlots) {
-        select_best(v, j, cnt, k);
-        cnt = k;
-        float worst = v[0];
-        for (int s = 1; s < k; ++s) worst = fminf(worst, v[s * kTkRows]);
-        theta = worst;
+// Replace the root (worst) of a full heap of n entries by (val, col) and restore the order.
+__device__ __forceinline__ void heap_replace_root(float* v, int* j, int n, float val, int col) {
+    int i = 0;
+#pragma unroll
+    for (int l = 0; l < kHeapDepth; ++l) {
+        const int c0 = 2 * i + 1, c1 = c0 + 1;
+        int c = c0;
+        if (c1 < n && better(v[c0 * kTkRows], j[c0 * kTkRows], v[c1 * kTkRows], j[c1 * kTkRows])) c = c1;
+        if (c0 < n && better(val, col, v[c * kTkRows], j[c * kTkRows])) {  // worse child rises
+            v[i * kTkRows] = v[c * kTkRows];
+            j[i * kTkRows] = j[c * kTkRows];
+            i = c;
+        }
     }
-    return {cnt, theta};
+    v[i * kTkRows] = val;
+    j[i * kTkRows] = col;
 }
 
 }  // namespace
@@ -219,18 +238,26 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
     float* cand_v = (float*)(sm + 16384 + kTkStages * 32768);
     int* cand_j = (int*)(sm + 16384 + kTkStages * 32768 + kTkSlots * kTkRows * 4);
     uint64_t* bars = (uint64_t*)(sm + 16384 + kTkStages * 32768 + kTkSlots * kTkRows * 8);
-    // bars: full[0..2], empty[3..5], acc_full[6..7], acc_empty[8..9], a_full[10]
-    uint32_t* tmem_slot = (uint32_t*)(bars + 11);
+    // bars: full[0..2], empty[3..5], acc_full[6..7], acc_empty[8..9], a_full[10],
+    // sready[11..12] (the tile's column scales and row ids are in sc[b] / sid[b])
+    uint32_t* tmem_slot = (uint32_t*)(bars + 13);
     volatile int* abort = (volatile int*)(tmem_slot + 1);
+    volatile int* limit = (volatile int*)(tmem_slot + 2);  // column tiles the CTA still needs
+    int* ndone = (int*)(tmem_slot + 3);                     // read-out warps whose rows are final
+    float* sc = (float*)((uint8_t*)bars + 128);   // [2][256] column scales of a tile
+    int* sid = (int*)((uint8_t*)bars + 128 + 2048);  // [2][256] original ids of its columns
     const uint32_t bar0 = smem_u32(bars);
     auto full = [&](int s) { return bar0 + 8u * s; };
     auto empty = [&](int s) { return bar0 + 8u * (3 + s); };
     auto accf = [&](int b) { return bar0 + 8u * (6 + b); };
     auto acce = [&](int b) { return bar0 + 8u * (8 + b); };
     const uint32_t afull = bar0 + 80u;
+    auto sready = [&](int b) { return bar0 + 8u * (11 + b); };
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row_base = a.r0 + blockIdx.x * kTkRows;
+    // first position (row of the stored factor order) of this CTA's 128 rows
+    const int pos_base = a.blocks ? a.blocks[blockIdx.x] * kTkRows : a.r0 + blockIdx.x * kTkRows;
+    const int ntiles = a.ntiles;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTkStages; ++s) {
@@ -242,7 +269,11 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
             mbar_init(acce(b), 128);
         }
         mbar_init(afull, 1);
+        mbar_init(sready(0), 128);
+        mbar_init(sready(1), 128);
         *abort = 0;
+        *limit = ntiles;
+        *ndone = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 1) {
@@ -256,18 +287,20 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int ntiles = a.ntiles;
 
     if (warp == 0) {
         if (lane == 0) {
             // ---------------- TMA producer ----------------
             int issued = 0;
+            unsigned long long polls = 0, cyc_empty = 0;
             mbar_expect_tx(afull, 16384);
-            tma_load(smem_u32(sA), &tm, 0, row_base, afull);
-            for (int it = 0; it < ntiles; ++it) {
+            tma_load(smem_u32(sA), &tm, 0, pos_base, afull);
+            for (int it = 0; it < ntiles && it < *limit; ++it) {
                 const int s = it % kTkStages;
                 const uint32_t ph = (uint32_t)(it / kTkStages) & 1u;
-                if (!mbar_wait(empty(s), ph ^ 1u, abort)) {
+                const int w = mbar_wait_t(empty(s), ph ^ 1u, abort, &polls, &cyc_empty, limit, it);
+                if (w == kWaitStop) break;
+                if (w == kWaitFail) {
                     if (!*abort) atomicExch(a.err, 1);
                     *abort = 1;
                     break;
@@ -278,6 +311,10 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
                 tma_load(dst + 16384, &tm, 0, it * kTkCols + 128, full(s));
                 issued = it + 1;
             }
+            if (a.prof) {
+                atomicAdd(a.prof + 6, polls);
+                atomicAdd(a.prof + 11, cyc_empty);
+            }
             // drain this thread's copies still in flight
             mbar_wait(afull, 0, nullptr);
             for (int it = issued > kTkStages ? issued - kTkStages : 0; it < issued; ++it)
@@ -287,14 +324,18 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------- MMA issuer ----------------
-            bool ok = mbar_wait(afull, 0, abort);
+            bool ok = mbar_wait(afull, 0, abort) == kWaitOk;
             int last = -1;
+            unsigned long long polls = 0, cyc_acce = 0, cyc_full = 0;
             const uint64_t da = sw128_desc(smem_u32(sA));
-            for (int it = 0; ok && it < ntiles; ++it) {
+            for (int it = 0; ok && it < ntiles && it < *limit; ++it) {
                 const int s = it % kTkStages, b = it & 1;
                 const uint32_t ph = (uint32_t)(it / kTkStages) & 1u;
                 const uint32_t bph = (uint32_t)(it >> 1) & 1u;
-                if (!mbar_wait(acce(b), bph ^ 1u, abort) || !mbar_wait(full(s), ph, abort)) {
+                int w = mbar_wait_t(acce(b), bph ^ 1u, abort, &polls, &cyc_acce, limit, it);
+                if (w == kWaitOk) w = mbar_wait_t(full(s), ph, abort, &polls, &cyc_full, limit, it);
+                if (w == kWaitStop) break;
+                if (w == kWaitFail) {
                     ok = false;
                     break;
                 }
@@ -312,6 +353,11 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
                 if (!*abort) atomicExch(a.err, 2);
                 *abort = 1;
             }
+            if (a.prof) {
+                atomicAdd(a.prof + 5, polls);
+                atomicAdd(a.prof + 9, cyc_acce);
+                atomicAdd(a.prof + 10, cyc_full);
+            }
             // the last MMAs must finish before the accumulators are freed
             if (last >= 0) mbar_wait(accf(last & 1), (uint32_t)(last >> 1) & 1u, nullptr);
         }
@@ -319,80 +365,174 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
     } else {
         // ---------------- read-out and selection ----------------
         const int rl = 32 * (warp & 3) + lane;  // TMEM lane = row of the tile
-        const int row = row_base + rl;
-        const bool valid = row < a.r1;
-        const float si = valid ? __ldg(a.scale + row) : 0.0f;
+        const int pos = pos_base + rl;
+        const int row = pos < a.R ? (a.perm ? __ldg(a.perm + pos) : pos) : -1;  // original id
+        const bool valid = row >= a.r0 && row < a.r1;
+        const float si = pos < a.R ? __ldg(a.scale + pos) : 0.0f;
+        // Cauchy-Schwarz bound of the row against later columns: P_ij <= n_i n_j, with the
+        // columns stored by n_j descending; 1e-5 covers the roundings of P and of n
+        const float ni = a.norm && pos < a.R ? __ldg(a.norm + pos) * 1.00001f : 0.0f;
+        bool warp_final = false;
         const int k = a.k;
         float* cv = cand_v + rl;
         int* cj = cand_j + rl;
-        int cnt = 0;
-        float theta = -__int_as_float(0x7f800000);
+        int cnt = 0;                                  // heap entries
+        float theta = -__int_as_float(0x7f800000);    // bar: the root once the heap is full
+        int theta_j = 0x7fffffff;
         const uint32_t lane_addr = (uint32_t)(32 * (warp & 3)) << 16;
         bool ok = true;
+        unsigned long long n_test = 0, n_scan = 0, n_push = 0, polls = 0;
+        unsigned long long cyc_wait = 0;
+        const long long cyc0 = clock64();
+        // column scales and ids of a tile: each thread stages two of the 256 (loaded one tile
+        // ahead, stored once the tile's reads of the other buffer are done)
+        auto fetch = [&](int it, float2& s2, int2& i2) {
+            const int p0 = it * kTkCols + 2 * rl;
+            s2 = __ldg(reinterpret_cast<const float2*>(a.scale + p0));
+            i2 = a.perm ? __ldg(reinterpret_cast<const int2*>(a.perm + p0)) : make_int2(p0, p0 + 1);
+        };
+        auto stage = [&](int b, float2 s2, int2 i2) {
+            reinterpret_cast<float2*>(sc + b * kTkCols)[rl] = s2;
+            reinterpret_cast<int2*>(sid + b * kTkCols)[rl] = i2;
+            mbar_arrive(sready(b));
+        };
+        float2 nxt_s;
+        int2 nxt_i;
+        fetch(0, nxt_s, nxt_i);
+        stage(0, nxt_s, nxt_i);
         for (int it = 0; it < ntiles; ++it) {
             const int b = it & 1;
-            if (!mbar_wait(accf(b), (uint32_t)(it >> 1) & 1u, abort)) {
+            if (it + 1 < ntiles) fetch(it + 1, nxt_s, nxt_i);
+            // (a stop limit at or below this tile means every row of the CTA is final)
+            int w = mbar_wait_t(sready(b), (uint32_t)(it >> 1) & 1u, abort, &polls, &cyc_wait, limit, it);
+            if (w == kWaitOk && *(volatile int*)ndone == 4) {  // every row is final: stop the sweep
+                atomicMin((int*)limit, it);
+                break;
+            }
+            if (w == kWaitOk)
+                w = mbar_wait_t(accf(b), (uint32_t)(it >> 1) & 1u, abort, &polls, &cyc_wait, limit, it);
+            if (w == kWaitStop) break;
+            if (w == kWaitFail) {
                 ok = false;
                 break;
             }
             __syncwarp();
             tc_fence_after();
-            const int jt = it * kTkCols;
-#pragma unroll 1
-            for (int c = 0; c < kTkCols / 32; ++c) {
-                float v[32];
+            const float* scb = sc + b * kTkCols;
+            const int* idb = sid + b * kTkCols;
+            // a column can only beat the bar if its product with the row scale, taken in the
+            // other order (two roundings either way), reaches the bar less a 1e-6 margin
+            const float theta_lo = theta - fabsf(theta) * 1e-6f;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {  // 128 columns per TMEM wait
+                uint32_t r[4][32];
                 __syncwarp();
-                tmem_ld32(tmem + lane_addr + (uint32_t)(b * kTkCols + 32 * c), v);
-                if (c == kTkCols / 32 - 1) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    tmem_ld32_issue(tmem + lane_addr + (uint32_t)(b * kTkCols + 128 * h + 32 * c), r[c]);
+                tmem_wait();
+#pragma unroll
+                for (int c = 0; c < 4; ++c) tmem_pin32(r[c]);
+                if (h == 1) {
                     tc_fence_before();
                     mbar_arrive(acce(b));
                 }
-                const int j0 = jt + 32 * c;
                 if (k == 0) {
                     if (valid) {
-                        float* o = a.dense + (size_t)(row - a.r0) * a.dense_ld + j0;
+                        float* o = a.dense + (size_t)(row - a.r0) * a.dense_ld;
 #pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            if (j0 + e < a.R) o[e] = (v[e] * si) * __ldg(a.scale + j0 + e);
+                        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) {
+                                const int j = idb[128 * h + 32 * c + e];
+                                if (j < a.R)
+                                    o[j] = (__uint_as_float(r[c][e]) * si) * scb[128 * h + 32 * c + e];
+                            }
+                        }
                     }
                     continue;
                 }
-                float mx = v[0];
 #pragma unroll
-                for (int e = 1; e < 32; ++e) mx = fmaxf(mx, v[e]);
-                const float bound = mx >= 0.0f ? (mx * si) * __ldg(a.smax + (j0 >> 5)) : 0.0f;
-                if (!(valid && bound > theta)) continue;
+                for (int c = 0; c < 4; ++c) {
+                    const float4* s4 = reinterpret_cast<const float4*>(scb + 128 * h + 32 * c);
+                    float m[16];
 #pragma unroll
-                for (int e = 0; e < 32; ++e) {
-                    const int col = j0 + e;
-                    const float val = (v[e] * si) * __ldg(a.scale + col);
-                    if (val > theta && col != row && col < a.R) {
-                        const PushResult pr = push_candidate(cv, cj, cnt, k, val, col, theta);
-                        cnt = pr.cnt;
-                        theta = pr.theta;
+                    for (int e4 = 0; e4 < 4; ++e4) {
+                        const float4 lo = s4[e4], hi = s4[e4 + 4];
+                        const float sl[4] = {lo.x, lo.y, lo.z, lo.w};
+                        const float sh[4] = {hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            m[4 * e4 + u] = fmaxf(__uint_as_float(r[c][4 * e4 + u]) * sl[u],
+                                                  __uint_as_float(r[c][16 + 4 * e4 + u]) * sh[u]);
+                    }
+#pragma unroll
+                    for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+                        for (int e = 0; e < w; ++e) m[e] = fmaxf(m[e], m[e + w]);
+                    ++n_test;
+                    if (!(valid && m[0] * si >= theta_lo)) continue;
+                    ++n_scan;
+                    const int4* i4 = reinterpret_cast<const int4*>(idb + 128 * h + 32 * c);
+#pragma unroll
+                    for (int e4 = 0; e4 < 8; ++e4) {
+                        const float4 sj = s4[e4];
+                        const int4 jj = i4[e4];
+                        const float sjv[4] = {sj.x, sj.y, sj.z, sj.w};
+                        const int jv[4] = {jj.x, jj.y, jj.z, jj.w};
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int e = 4 * e4 + u;
+                            const int col = jv[u];
+                            const float val = (__uint_as_float(r[c][e]) * si) * sjv[u];
+                            if (better(val, col, theta, theta_j) && col != row && col < a.R) {
+                                ++n_push;
+                                if (cnt < k) {
+                                    heap_insert(cv, cj, cnt, val, col);
+                                    ++cnt;
+                                } else {
+                                    heap_replace_root(cv, cj, cnt, val, col);
+                                }
+                                if (cnt == k) {
+                                    theta = cv[0];
+                                    theta_j = cj[0];
+                                }
+                            }
+                        }
                     }
                 }
             }
+            // a row is final once no later column can beat its k-th value
+            if (k > 0 && a.norm && !warp_final && it + 1 < ntiles) {
+                const float nb = __ldg(a.norm + (it + 1) * kTkCols);
+                const bool fin = !valid || ni * nb < theta;
+                __syncwarp();
+                if (__all_sync(0xffffffffu, fin)) {
+                    warp_final = true;
+                    if (lane == 0) atomicAdd(ndone, 1);
+                }
+            }
+            if (it + 1 < ntiles) stage(b ^ 1, nxt_s, nxt_i);
+        }
+        if (a.prof) {
+            atomicAdd(a.prof + 0, n_test);
+            atomicAdd(a.prof + 1, n_scan);
+            atomicAdd(a.prof + 2, n_push);
+            atomicAdd(a.prof + 4, polls);
+            atomicAdd(a.prof + 7, cyc_wait);
+            atomicAdd(a.prof + 8, (unsigned long long)(clock64() - cyc0));
         }
         if (!ok) {
             if (!*abort) atomicExch(a.err, 3);
             *abort = 1;
         } else if (valid && k > 0) {
-            if (cnt > k) {
-                select_best(cv, cj, cnt, k);
-                cnt = k;
-            }
-            for (int s = 1; s < cnt; ++s) {  // insertion sort of the kept slots
-                const float tv = cv[s * kTkRows];
-                const int tj = cj[s * kTkRows];
-                int u = s - 1;
-                while (u >= 0 && better(tv, tj, cv[u * kTkRows], cj[u * kTkRows])) {
-                    cv[(u + 1) * kTkRows] = cv[u * kTkRows];
-                    cj[(u + 1) * kTkRows] = cj[u * kTkRows];
-                    --u;
-                }
-                cv[(u + 1) * kTkRows] = tv;
-                cj[(u + 1) * kTkRows] = tj;
+            // heap sort: the worst entry goes to the back, best first at the end
+            for (int n = cnt; n > 1; --n) {
+                const float wv = cv[0];
+                const int wj = cj[0];
+                heap_replace_root(cv, cj, n - 1, cv[(n - 1) * kTkRows], cj[(n - 1) * kTkRows]);
+                cv[(n - 1) * kTkRows] = wv;
+                cj[(n - 1) * kTkRows] = wj;
             }
             int* oi = a.out_idx + (size_t)(row - a.r0) * k;
             float* ov = a.out_val + (size_t)(row - a.r0) * k;

@@ -59,7 +59,7 @@ SYMBOLS = (
     "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host", "rfx_get_stream",
     "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats", "rfx_sync",
     "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk", "rfx_lowrank_product",
-    "rfx_prox_apply",
+    "rfx_prox_apply", "rfx_lowrank_set_factors",
 )
 
 # int (*)(void* user, float* buf_dev, int64_t count): in-place sum over processes
@@ -107,12 +107,13 @@ def load_library(path: str = LIB_PATH):
     L.rfx_lowrank_topk.argtypes = [vp, C.c_int, C.c_int, C.c_int, _pi, _pf]
     L.rfx_lowrank_product.argtypes = [vp, C.c_int, C.c_int, _pf]
     L.rfx_prox_apply.argtypes = [vp, vp, C.c_int, vp, vp]
+    L.rfx_lowrank_set_factors.argtypes = [vp, C.POINTER(C.c_int8), _pf, C.c_int, C.c_int]
     for name in ("rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
                  "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish",
                  "rfx_prox_dense", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host",
                  "rfx_get_stream", "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats",
                  "rfx_sync", "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk",
-                 "rfx_lowrank_product", "rfx_prox_apply"):
+                 "rfx_lowrank_product", "rfx_prox_apply", "rfx_lowrank_set_factors"):
         getattr(L, name).restype = C.c_int
     _LIB = L
     return L
@@ -236,6 +237,12 @@ class Context:
         check(self._lib.rfx_lowrank_build(self.handle, int(rank), int(oversample),
                                           int(power_iters), C.c_uint64(seed & (2**64 - 1)),
                                           C.c_void_p(nout_dev) if nout_dev else None, cb, None))
+
+    def lowrank_set_factors(self, q: np.ndarray, scale: np.ndarray):
+        q = np.ascontiguousarray(q, np.int8)
+        scale = np.ascontiguousarray(scale, np.float32)
+        check(self._lib.rfx_lowrank_set_factors(self.handle, q.ctypes.data_as(C.POINTER(C.c_int8)),
+                                                ptr(scale, _pf), q.shape[0], q.shape[1]))
 
     def lowrank_factors(self):
         """(A float32 [R, k] dequantised, q int8 [R, k], scale float32 [R])."""

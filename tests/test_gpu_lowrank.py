@@ -119,3 +119,44 @@ def test_factor_quality_vs_exact_proximity():
     recall = np.mean([len(np.intersect1d(idx[i], exact[i])) / 50 for i in range(S.shape[0])])
     print(f"low-rank rank={rank}: rmse={rmse:.4g} best={rmse_best:.4g} top50 recall={recall:.3f}")
     assert recall > 0.3, recall
+
+
+def _topk_ref(q, s, k):
+    """Exact top-k of the quantised product for every row (numpy, float32 like the kernel)."""
+    acc = (q.astype(np.int64) @ q.astype(np.int64).T).astype(np.float32)
+    P = (acc * s[:, None]) * s[None, :]
+    R = P.shape[0]
+    Pm = P.copy()
+    np.fill_diagonal(Pm, -np.inf)
+    order = np.argsort(-Pm, axis=1, kind="stable")[:, :k]  # value desc, index asc
+    val = np.take_along_axis(Pm, order, axis=1)
+    idx = order.astype(np.int32)
+    idx[np.isneginf(val)] = -1
+    return P, idx, val.astype(np.float32)
+
+
+@pytest.mark.parametrize("k", [1, 50, 64])
+def test_topk_kernel_adversarial_factors(k):
+    """Caller-supplied factors with duplicated rows (ties broken by index), zero rows, zero
+    scales and negative products, over 20 column tiles (the early stop engages)."""
+    import rfx_b200
+    rng = np.random.default_rng(21)
+    R, rank = 5000, 37
+    q = rng.integers(-127, 128, size=(R, rank)).astype(np.int8)
+    q[rng.integers(0, R, 600)] = q[rng.integers(0, R, 600)]  # duplicate rows -> equal values
+    q[10:20] = 0                                              # zero rows
+    s = rng.uniform(0.001, 0.02, size=R).astype(np.float32)
+    s[rng.integers(0, R, 200)] = np.float32(0.01)            # shared scales -> more ties
+    s[30:35] = 0.0                                            # zero scales
+    ctx = rfx_b200.Context(0)
+    ctx.lowrank_set_factors(q, s)
+    P, idx_np, val_np = _topk_ref(q, s, k)
+    idx, val = ctx.lowrank_topk(k, 0, R)
+    assert np.array_equal(idx, idx_np)
+    assert np.array_equal(val.view(np.uint32), val_np.view(np.uint32))
+    # an interleaved row range
+    idx2, val2 = ctx.lowrank_topk(k, 1234, 3456)
+    assert np.array_equal(idx2, idx_np[1234:3456])
+    assert np.array_equal(val2.view(np.uint32), val_np[1234:3456].view(np.uint32))
+    dense = ctx.lowrank_product(100, 300, R)
+    assert np.array_equal(dense.view(np.uint32), P[100:300].view(np.uint32))
