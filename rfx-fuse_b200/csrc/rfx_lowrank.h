@@ -18,7 +18,7 @@ constexpr int kTkCols = 256;    // columns of a tile (MMA N)
 constexpr int kTkStages = 3;    // column-tile ring
 constexpr int kTkSlots = 64;    // heap entries per row (k <= 64)
 constexpr int kTkThreads = 192; // warp 0 loads, warp 1 issues MMAs, warps 2-5 read out
-constexpr int kTkSmem = 16384 + kTkStages * 32768 + kTkSlots * kTkRows * 8 + 128 + 4096 + 1024;
+constexpr int kTkSmem = 16384 + kTkStages * 32768 + kTkSlots * kTkRows * 8 + 128 + 4096 + 16384 + 1024;
 
 struct TopkArgs {
     int R;              // valid rows (= valid columns)

@@ -193,8 +193,10 @@ __device__ __forceinline__ bool better(float va, int ja, float vb, int jb) {
 
 constexpr int kHeapDepth = 6;  // levels below the root of a heap of <= 64 entries
 
-// Insert (val, col) into a heap of n < k entries.
-__device__ __forceinline__ void heap_insert(float* v, int* j, int n, float val, int col) {
+// Insert (val, col) into a heap of n < k entries.  (Out of line, like heap_replace_root: the
+// read-out calls them from many unrolled sites, and inlined copies overflow the
+// instruction cache.)
+__device__ __noinline__ void heap_insert(float* v, int* j, int n, float val, int col) {
     int i = n;
 #pragma unroll
     for (int l = 0; l < kHeapDepth; ++l) {
@@ -210,7 +212,7 @@ __device__ __forceinline__ void heap_insert(float* v, int* j, int n, float val, 
 }
 
 // Replace the root (worst) of a full heap of n entries by (val, col) and restore the order.
-__device__ __forceinline__ void heap_replace_root(float* v, int* j, int n, float val, int col) {
+__device__ __noinline__ void heap_replace_root(float* v, int* j, int n, float val, int col) {
     int i = 0;
 #pragma unroll
     for (int l = 0; l < kHeapDepth; ++l) {
@@ -245,6 +247,7 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
     volatile int* limit = (volatile int*)(tmem_slot + 2);  // column tiles the CTA still needs
     int* ndone = (int*)(tmem_slot + 3);                     // read-out warps whose rows are final
     float* sc = (float*)((uint8_t*)bars + 128);   // [2][256] column scales of a tile
+    float* scratch = (float*)((uint8_t*)bars + 128 + 4096);  // [32][128] values of a chunk
     int* sid = (int*)((uint8_t*)bars + 128 + 2048);  // [2][256] original ids of its columns
     const uint32_t bar0 = smem_u32(bars);
     auto full = [&](int s) { return bar0 + 8u * s; };
@@ -376,6 +379,7 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
         const int k = a.k;
         float* cv = cand_v + rl;
         int* cj = cand_j + rl;
+        float* scr = scratch + rl;
         int cnt = 0;                                  // heap entries
         float theta = -__int_as_float(0x7f800000);    // bar: the root once the heap is full
         int theta_j = 0x7fffffff;
@@ -423,7 +427,7 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
             // a column can only beat the bar if its product with the row scale, taken in the
             // other order (two roundings either way), reaches the bar less a 1e-6 margin
             const float theta_lo = theta - fabsf(theta) * 1e-6f;
-#pragma unroll
+#pragma unroll 1
             for (int h = 0; h < 2; ++h) {  // 128 columns per TMEM wait
                 uint32_t r[4][32];
                 __syncwarp();
@@ -473,7 +477,11 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
                     ++n_test;
                     if (!(valid && m[0] * si >= theta_lo)) continue;
                     ++n_scan;
-                    const int4* i4 = reinterpret_cast<const int4*>(idb + 128 * h + 32 * c);
+                    // exact values of the chunk into this thread's scratch column, and the
+                    // mask of those that beat the bar; then one push site walks the mask
+                    const int* idc = idb + 128 * h + 32 * c;
+                    const int4* i4 = reinterpret_cast<const int4*>(idc);
+                    uint32_t mask = 0;
 #pragma unroll
                     for (int e4 = 0; e4 < 8; ++e4) {
                         const float4 sj = s4[e4];
@@ -483,21 +491,29 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
 #pragma unroll
                         for (int u = 0; u < 4; ++u) {
                             const int e = 4 * e4 + u;
-                            const int col = jv[u];
                             const float val = (__uint_as_float(r[c][e]) * si) * sjv[u];
-                            if (better(val, col, theta, theta_j) && col != row && col < a.R) {
-                                ++n_push;
-                                if (cnt < k) {
-                                    heap_insert(cv, cj, cnt, val, col);
-                                    ++cnt;
-                                } else {
-                                    heap_replace_root(cv, cj, cnt, val, col);
-                                }
-                                if (cnt == k) {
-                                    theta = cv[0];
-                                    theta_j = cj[0];
-                                }
-                            }
+                            scr[e * kTkRows] = val;
+                            const bool pass = better(val, jv[u], theta, theta_j) && jv[u] != row &&
+                                              jv[u] < a.R;
+                            mask |= (pass ? 1u : 0u) << e;
+                        }
+                    }
+                    while (mask) {
+                        const int e = __ffs(mask) - 1;
+                        mask &= mask - 1;
+                        const float val = scr[e * kTkRows];
+                        const int col = idc[e];
+                        if (!better(val, col, theta, theta_j)) continue;  // the bar rose meanwhile
+                        ++n_push;
+                        if (cnt < k) {
+                            heap_insert(cv, cj, cnt, val, col);
+                            ++cnt;
+                        } else {
+                            heap_replace_root(cv, cj, cnt, val, col);
+                        }
+                        if (cnt == k) {
+                            theta = cv[0];
+                            theta_j = cj[0];
                         }
                     }
                 }
