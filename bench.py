@@ -17,6 +17,15 @@ OOB prediction fold, permutation importance).  Metric: fit trees/s for the whole
 
 --impl reference times the reference's own CPU implementation (oracle/_ref, compiled from
 the reference sources; else the CPU port) on the same workload with all host threads.
+
+Other workloads (--workload; each prints its own line, the default is config1):
+  config0  classification n=10000 p=20, 100 trees, mtry 4, nodesize 1, OOB x in-bag proximity
+           counts + finishprox'd dense matrix; adds "proximity" (pair updates/s, finish GB/s).
+  config2  unsupervised n=50000 real rows (+50000 synthetic) p=100 GMM, 300 trees, mtry 10,
+           nodesize 1, proximity counts over the 50000 real rows (5 GB upper triangle).
+  config3  classification n=1,000,000 p=200 10-class GMM, classwt [1..10]/10, mtry 14,
+           nodesize 1, low-rank proximity rank 64 (int8 factors) + top-50 per row; adds
+           "lowrank" (sketch GB/s, product TFLOP/s on the tensor cores, top-50 time).
 """
 from __future__ import annotations
 
@@ -189,6 +198,13 @@ def run_reference(args):
 
 
 def run_rfx(args):
+    if args.workload == "config1":
+        return run_config1(args)
+    from bench_workloads import run_workload
+    return run_workload(args)
+
+
+def run_config1(args):
     import torch
 
     import rfx_b200
@@ -315,13 +331,20 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="rfx", choices=["rfx", "reference"])
-    ap.add_argument("--step-trees", type=int, default=250)
+    ap.add_argument("--step-trees", type=int, default=None)
     ap.add_argument("--batch-trees", type=int, default=0)
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--cpu-trees", type=int, default=8)
     ap.add_argument("--ref-step-trees", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="config1", choices=["config1", "config0", "config2", "config3"])
     args = ap.parse_args()
+    args.step_trees_set = args.step_trees is not None
+    if args.step_trees is None:
+        args.step_trees = 250
+    if args.impl == "reference" and args.workload != "config1":
+        from bench_workloads import run_workload_reference
+        return run_workload_reference(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_rfx(args)

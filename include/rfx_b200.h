@@ -176,7 +176,7 @@ int rfx_copy_to_host(void* ctx, void* dst_host, const void* src_dev, size_t byte
 /* Measurement.  Counters since the last rfx_reset_stats: kernels launched by the library,
  * and, while profiling is on, the CUDA-event time of the histogram kernels of every level
  * together with the algorithmic bytes they read (sum over searched nodes of
- * rows * (mtry + target bytes)). */
+ * rows * (mtry + target bytes)), and of the proximity kernel with the pairs it added. */
 typedef struct {
     int64_t kernel_launches;
     int64_t hist_launches;
@@ -184,6 +184,12 @@ typedef struct {
     double hist_bytes;
     int64_t levels;
     int64_t trees;
+    double prox_pair_updates;  /* OOB x in-bag pairs added to the proximity counts */
+    double prox_ms;            /* CUDA-event time of the proximity kernel (profiling on) */
+    double topk_ms;            /* CUDA-event time of the low-rank product kernel (profiling on) */
+    int64_t topk_tiles;        /* 128 x 256 x 64 product tiles it multiplied */
+    double sketch_ms;          /* CUDA-event time of the low-rank sketch passes (profiling on) */
+    double sketch_bytes;       /* their algorithmic bytes: per tree 2 R W 4 + 6 R */
 } rfx_stats;
 int rfx_get_stream(void* ctx, void** stream);   /* the context's cudaStream_t */
 int rfx_set_profiling(void* ctx, int on);

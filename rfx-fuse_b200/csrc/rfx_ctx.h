@@ -108,6 +108,10 @@ struct Ctx {
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
     long long launches = 0, hist_launches = 0, levels = 0, trees = 0;
     double hist_ms = 0.0;
+    double prox_ms = 0.0;
+    double topk_ms = 0.0;
+    double sketch_ms = 0.0, sketch_bytes = 0.0;
+    long long topk_tiles = 0;
 
     // low-rank proximity (rfx_lowrank_host.cu): per-tree leaf groups, then the factors
     int lr_rank = 0;            // requested rank, 0 = off

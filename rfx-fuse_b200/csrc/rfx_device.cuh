@@ -157,6 +157,7 @@ struct Batch {
     int* srch_off;    // [T+1]
     int* counters;    // [8]: 0 level total, 1 searched total, 2 next-level total, 4 big searched
     unsigned long long* hist_bytes;  // algorithmic bytes read by k_hist (sum of c_v*(mtry+L))
+    unsigned long long* prox_pairs;  // proximity pair updates counted by k_prox
     int* srch_big;    // [T][M] searched nodes with more than kSmallNode rows, in node order
     int* srch_big_cnt;  // [T]
     int* srch_big_off;  // [T+1]

@@ -114,6 +114,7 @@ void alloc_batch(Ctx& c, int Tcap) {
     B.srch_big_cnt = B.srch_cnt + T;
     B.counters = (int*)c.b_counters.get(64);
     B.hist_bytes = reinterpret_cast<unsigned long long*>(B.counters + 8);
+    B.prox_pairs = reinterpret_cast<unsigned long long*>(B.counters + 10);
     B.oob_leaf = (int*)c.b_oobleaf.get(T * N * 4);
     B.used = (uint8_t*)c.b_used.get(T * p);
     B.right = (int*)c.b_right.get(T * 4);
@@ -448,9 +449,17 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
         c.launches += 4;
     }
     if (c.prm.compute_proximity && c.prox) {
+        if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev0, st));
         rfx::k_prox<<<rg, 256, 0, st>>>(D, B, c.R, c.prox);
         RFX_LAUNCH("k_prox");
         c.launches += 1;
+        if (c.profiling) {
+            RFX_CUDA(cudaEventRecord(c.ev1, st));
+            RFX_CUDA(cudaEventSynchronize(c.ev1));
+            float ms = 0.0f;
+            RFX_CUDA(cudaEventElapsedTime(&ms, c.ev0, c.ev1));
+            c.prox_ms += ms;
+        }
     }
     if (c.lr_rank > 0) lr_store_batch(c, B, T);
     if (keep) c.tree_oob_n += T;
@@ -715,15 +724,21 @@ int rfx_get_stats(void* ctx, rfx_stats* s) {
     return guarded([&] {
         Ctx& c = *as_ctx(ctx);
         require(s != nullptr, RFX_ERR_ARG, "null output");
-        unsigned long long hb = 0;
+        unsigned long long hb[2] = {0, 0};
         if (c.B.hist_bytes) {
-            RFX_CUDA(cudaMemcpyAsync(&hb, c.B.hist_bytes, 8, cudaMemcpyDeviceToHost, c.st));
+            RFX_CUDA(cudaMemcpyAsync(hb, c.B.hist_bytes, 16, cudaMemcpyDeviceToHost, c.st));
             RFX_CUDA(cudaStreamSynchronize(c.st));
         }
         s->kernel_launches = c.launches;
         s->hist_launches = c.hist_launches;
         s->hist_ms = c.hist_ms;
-        s->hist_bytes = (double)hb;
+        s->hist_bytes = (double)hb[0];
+        s->prox_pair_updates = (double)hb[1];
+        s->prox_ms = c.prox_ms;
+        s->topk_ms = c.topk_ms;
+        s->topk_tiles = c.topk_tiles;
+        s->sketch_ms = c.sketch_ms;
+        s->sketch_bytes = c.sketch_bytes;
         s->levels = c.levels;
         s->trees = c.trees;
     });
@@ -734,7 +749,11 @@ int rfx_reset_stats(void* ctx) {
         Ctx& c = *as_ctx(ctx);
         c.launches = c.hist_launches = c.levels = c.trees = 0;
         c.hist_ms = 0.0;
-        if (c.B.hist_bytes) RFX_CUDA(cudaMemsetAsync(c.B.hist_bytes, 0, 8, c.st));
+        c.prox_ms = 0.0;
+        c.topk_ms = 0.0;
+        c.topk_tiles = 0;
+        c.sketch_ms = c.sketch_bytes = 0.0;
+        if (c.B.hist_bytes) RFX_CUDA(cudaMemsetAsync(c.B.hist_bytes, 0, 16, c.st));
         RFX_CUDA(cudaStreamSynchronize(c.st));
     });
 }

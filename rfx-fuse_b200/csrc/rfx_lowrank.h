@@ -36,7 +36,7 @@ struct TopkArgs {
     float* out_val;     // [r1 - r0][k]
     float* dense;       // [r1 - r0][dense_ld] by original column, when k == 0
     long long dense_ld;
-    int* err;           // [0]: nonzero after a wait timed out
+    int* err;           // [0]: nonzero after a wait timed out; [1] += column tiles multiplied
     unsigned long long* prof;  // optional counters (null: off): chunks tested, chunks
                                // scanned, candidates pushed, -, read-out wait
                                // polls, MMA wait polls, load wait polls

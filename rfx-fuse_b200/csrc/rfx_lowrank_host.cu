@@ -38,6 +38,7 @@ void apply_counts(Ctx& c, const float* Z, int W, float* CZ) {
     const int* goff = (const int*)c.lr_goff.p;
     const int* ng = (const int*)c.lr_ngroups.p;
     const int nq = nq_of(W);
+    if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev0, st));
     for (int t0 = 0; t0 < c.lr_n; t0 += Tc) {
         const int T = std::min(Tc, c.lr_n - t0);
         const dim3 g((unsigned)((G - 1 + 7) / 8), (unsigned)T);
@@ -48,6 +49,16 @@ void apply_counts(Ctx& c, const float* Z, int W, float* CZ) {
         rfx::lr_launch_scatter(nq, (R + 7) / 8, st, code + (size_t)t0 * N, N, R, T, G, LS, CZ);
         RFX_LAUNCH("k_lr_scatter");
         c.launches += 2;
+    }
+    if (c.profiling) {
+        RFX_CUDA(cudaEventRecord(c.ev1, st));
+        RFX_CUDA(cudaEventSynchronize(c.ev1));
+        float ms = 0.0f;
+        RFX_CUDA(cudaEventElapsedTime(&ms, c.ev0, c.ev1));
+        c.sketch_ms += ms;
+        // per tree: gather of the R rows of Z into leaf sums, gather of a leaf sum per row
+        // (W floats each), plus the row order (4 B) and group code (2 B) of every row
+        c.sketch_bytes += (double)c.lr_n * ((double)R * W * 4.0 * 2.0 + (double)R * 6.0);
     }
 }
 
@@ -192,12 +203,21 @@ void run_product(Ctx& c, int r0, int r1, int k, int* oi, float* ov, float* dense
         a.prof = prof;
     }
     set_smem((const void*)rfx::k_topk_tc, rfx::kTkSmem);
+    if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev0, st));
     rfx::k_topk_tc<<<grid, rfx::kTkThreads, rfx::kTkSmem, st>>>(tm, a);
     RFX_LAUNCH("k_topk_tc");
+    if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev1, st));
     c.launches += 1;
-    int h = 0;
-    RFX_CUDA(cudaMemcpyAsync(&h, err, 4, cudaMemcpyDeviceToHost, st));
+    int hv[2] = {0, 0};
+    RFX_CUDA(cudaMemcpyAsync(hv, err, 8, cudaMemcpyDeviceToHost, st));
     RFX_CUDA(cudaStreamSynchronize(st));
+    const int h = hv[0];
+    c.topk_tiles += hv[1];
+    if (c.profiling) {
+        float ms = 0.0f;
+        RFX_CUDA(cudaEventElapsedTime(&ms, c.ev0, c.ev1));
+        c.topk_ms += ms;
+    }
     require(h == 0, RFX_ERR_DEVICE, "product kernel: a pipeline wait timed out (code " + std::to_string(h) + ")");
     if (prof) {
         unsigned long long hp[16] = {};

@@ -310,12 +310,15 @@ __global__ void k_prox(Data D, Batch B, int R, int* __restrict__ C) {
     const int st = B.nd_start[m], c = B.nd_cnt[m];
     const int* seg = B.seg[B.nd_buf[m]] + (size_t)t * D.N + st;
     const long long R2 = 2LL * R;
+    unsigned long long done = 0;
     for (int q = 0; q < c; ++q) {
         const int col = seg[q];
         if (col >= R) continue;
         const long long a = min(row, col), b = max(row, col);
         atomicAdd(&C[a * (R2 - a - 1) / 2 + (b - a - 1)], 1);
+        ++done;
     }
+    if (B.prox_pairs && done) atomicAdd(B.prox_pairs, done);
 }
 
 // finishprox (src/rf_finishprox.cpp:12-74) of rows [r0, r1): with C the symmetric count,

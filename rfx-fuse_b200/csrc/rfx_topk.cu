@@ -356,6 +356,7 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
                 if (!*abort) atomicExch(a.err, 2);
                 *abort = 1;
             }
+            atomicAdd(a.err + 1, last + 1);  // column tiles multiplied by this CTA
             if (a.prof) {
                 atomicAdd(a.prof + 5, polls);
                 atomicAdd(a.prof + 9, cyc_acce);

@@ -49,7 +49,9 @@ class Accum(C.Structure):
 class Stats(C.Structure):
     _fields_ = [("kernel_launches", C.c_int64), ("hist_launches", C.c_int64),
                 ("hist_ms", C.c_double), ("hist_bytes", C.c_double), ("levels", C.c_int64),
-                ("trees", C.c_int64)]
+                ("trees", C.c_int64), ("prox_pair_updates", C.c_double), ("prox_ms", C.c_double),
+                ("topk_ms", C.c_double), ("topk_tiles", C.c_int64), ("sketch_ms", C.c_double),
+                ("sketch_bytes", C.c_double)]
 
 
 SYMBOLS = (
