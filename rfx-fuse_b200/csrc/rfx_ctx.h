@@ -109,6 +109,13 @@ struct Ctx {
     long long launches = 0, hist_launches = 0, levels = 0, trees = 0;
     double hist_ms = 0.0;
     double prox_ms = 0.0;
+    double prox_pull_pairs = 0.0;  // pairs added by the pull kernel (the push kernel counts its own)
+    // proximity counting: 0 automatic, 1 push, 2 pull (RFX_PROX_MODE=push|pull)
+    int prox_mode = std::getenv("RFX_PROX_MODE") == nullptr
+                        ? 0
+                        : (std::string(std::getenv("RFX_PROX_MODE")) == "push"
+                               ? 1
+                               : (std::string(std::getenv("RFX_PROX_MODE")) == "pull" ? 2 : 0));
     double topk_ms = 0.0;
     double sketch_ms = 0.0, sketch_bytes = 0.0;
     long long topk_tiles = 0;
@@ -131,7 +138,7 @@ struct Ctx {
     DBuf b_nin, b_seg0, b_seg1, b_ninbag, b_oob, b_noob, b_mt, b_mtpos, b_status, b_bestvar,
         b_xbest, b_treemap, b_nodeclass, b_nodepred, b_tnodewt, b_ndstart, b_ndcnt, b_ndbuf,
         b_ndflag, b_ndcrit0, b_ndmaj, b_ndsum, b_ndkey, b_feat, b_lvl, b_srch, b_srchcnt,
-        b_srchoff, b_counters, b_oobleaf, b_used, b_right, b_rightimp, b_d2, b_d0, b_rr, b_srchbig, b_partbig;
+        b_srchoff, b_counters, b_oobleaf, b_used, b_right, b_rightimp, b_d2, b_d0, b_rr, b_srchbig, b_partbig, b_pcode, b_pocnt, b_ppairs;
 
     ~Ctx() {
         DBuf* all[] = {&xc, &rows, &edges, &nb, &kind, &cat, &lab, &yreg, &yv, &perm, &ks, &cumw,
@@ -141,7 +148,7 @@ struct Ctx {
                        &b_xbest, &b_treemap, &b_nodeclass, &b_nodepred, &b_tnodewt, &b_ndstart,
                        &b_ndcnt, &b_ndbuf, &b_ndflag, &b_ndcrit0, &b_ndmaj, &b_ndsum, &b_ndkey,
                        &b_feat, &b_lvl, &b_srch, &b_srchcnt, &b_srchoff, &b_counters,
-                       &b_oobleaf, &b_used, &b_right, &b_rightimp, &b_d2, &b_d0, &b_rr, &b_srchbig, &b_partbig,
+                       &b_oobleaf, &b_used, &b_right, &b_rightimp, &b_d2, &b_d0, &b_rr, &b_srchbig, &b_partbig, &b_pcode, &b_pocnt, &b_ppairs,
                        &lr_code, &lr_order, &lr_goff, &lr_ngroups, &lr_tmp, &lr_X, &lr_Z,
                        &lr_CZ, &lr_Y, &lr_ls, &lr_part, &lr_small, &lr_A, &lr_q, &lr_qb, &lr_s, &lr_qbp, &lr_sp, &lr_perm, &lr_blocks, &lr_np, &lr_norm, &lr_ids, &lr_keys, &lr_order_s, &lr_cub,
                        &lr_err, &lr_out_i, &lr_out_v};

@@ -450,9 +450,42 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
     }
     if (c.prm.compute_proximity && c.prox) {
         if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev0, st));
-        rfx::k_prox<<<rg, 256, 0, st>>>(D, B, c.R, c.prox);
-        RFX_LAUNCH("k_prox");
-        c.launches += 1;
+        // push (k_prox: one atomic per pair) or pull (k_prox_pull: every tile of the
+        // triangle compares the batch's leaf codes), whichever the batch's exact pair count
+        // makes cheaper: push ~ pairs / 2e10 s, pull ~ tiles * 128^2 * T/2 * 3 / 3e13 s
+        bool pull = c.prox_mode == 2;
+        if (c.prox_mode != 1) {
+            const int R = c.R, Tp = T + (T & 1);
+            uint16_t* code = (uint16_t*)c.b_pcode.get((size_t)Tp * R * 2);
+            int* ocnt = (int*)c.b_pocnt.get((size_t)T * M * 4);
+            unsigned long long* pairs_d = (unsigned long long*)c.b_ppairs.get(16);
+            if (T & 1) RFX_CUDA(cudaMemsetAsync(code + (size_t)T * R, 0xFF, (size_t)R * 2, st));
+            RFX_CUDA(cudaMemsetAsync(pairs_d, 0, 8, st));
+            rfx::k_prox_codes<<<T, 1024, 0, st>>>(B, (int)N, R, code, ocnt, pairs_d);
+            RFX_LAUNCH("k_prox_codes");
+            c.launches += 1;
+            unsigned long long pairs = 0;
+            RFX_CUDA(cudaMemcpyAsync(&pairs, pairs_d, 8, cudaMemcpyDeviceToHost, st));
+            RFX_CUDA(cudaStreamSynchronize(st));
+            const long long nb = (R + 127) / 128;
+            const long long tiles = nb * (nb + 1) / 2;
+            if (c.prox_mode == 0) {
+                const double push_s = (double)pairs / 2e10;
+                const double pull_s = (double)tiles * 16384.0 * (Tp / 2) * 3.0 / 3e13;
+                pull = pull_s < push_s;
+            }
+            if (pull) {
+                rfx::k_prox_pull<<<(unsigned)tiles, 256, 0, st>>>(code, Tp, R, (int)nb, c.prox);
+                RFX_LAUNCH("k_prox_pull");
+                c.launches += 1;
+                c.prox_pull_pairs += (double)pairs;
+            }
+        }
+        if (!pull) {
+            rfx::k_prox<<<rg, 256, 0, st>>>(D, B, c.R, c.prox);
+            RFX_LAUNCH("k_prox");
+            c.launches += 1;
+        }
         if (c.profiling) {
             RFX_CUDA(cudaEventRecord(c.ev1, st));
             RFX_CUDA(cudaEventSynchronize(c.ev1));
@@ -631,10 +664,7 @@ int rfx_prox_finish(void* ctx, const int* upper_dev, const int* nout_dev, int R,
         require(upper_dev && nout_dev && out_dev, RFX_ERR_ARG, "null pointer");
         require(R >= 1 && row_begin >= 0 && row_begin <= row_end && row_end <= R, RFX_ERR_ARG,
                 "bad row range");
-        const long long total = (long long)(row_end - row_begin) * R;
-        rfx::k_prox_finish<<<grid_for(total, 256, c.sm_count * 16), 256, 0, c.st>>>(
-            upper_dev, nout_dev, R, row_begin, row_end, out_dev);
-        RFX_LAUNCH("k_prox_finish");
+        RFX_CUDA(rfx::launch_prox_finish(upper_dev, nout_dev, R, row_begin, row_end, out_dev, c.st));
         RFX_CUDA(cudaStreamSynchronize(c.st));
     });
 }
@@ -651,9 +681,7 @@ int rfx_prox_dense(void* ctx, int row_begin, int row_end, float* out_host) {
         for (int r0 = row_begin; r0 < row_end; r0 += rows_per) {
             const int r1 = std::min(row_end, r0 + rows_per);
             const long long total = (long long)(r1 - r0) * R;
-            rfx::k_prox_finish<<<grid_for(total, 256, c.sm_count * 16), 256, 0, c.st>>>(
-                c.prox, (const int*)c.nout.p, R, r0, r1, tmp);
-            RFX_LAUNCH("k_prox_finish");
+            RFX_CUDA(rfx::launch_prox_finish(c.prox, (const int*)c.nout.p, R, r0, r1, tmp, c.st));
             RFX_CUDA(cudaMemcpyAsync(out_host + (size_t)(r0 - row_begin) * R, tmp, (size_t)total * 4,
                                      cudaMemcpyDeviceToHost, c.st));
             RFX_CUDA(cudaStreamSynchronize(c.st));
@@ -733,7 +761,7 @@ int rfx_get_stats(void* ctx, rfx_stats* s) {
         s->hist_launches = c.hist_launches;
         s->hist_ms = c.hist_ms;
         s->hist_bytes = (double)hb[0];
-        s->prox_pair_updates = (double)hb[1];
+        s->prox_pair_updates = (double)hb[1] + c.prox_pull_pairs;
         s->prox_ms = c.prox_ms;
         s->topk_ms = c.topk_ms;
         s->topk_tiles = c.topk_tiles;
@@ -750,6 +778,7 @@ int rfx_reset_stats(void* ctx) {
         c.launches = c.hist_launches = c.levels = c.trees = 0;
         c.hist_ms = 0.0;
         c.prox_ms = 0.0;
+        c.prox_pull_pairs = 0.0;
         c.topk_ms = 0.0;
         c.topk_tiles = 0;
         c.sketch_ms = c.sketch_bytes = 0.0;

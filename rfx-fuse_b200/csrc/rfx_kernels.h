@@ -40,7 +40,13 @@ __global__ void k_imp_regr(Data D, Batch B);
 __global__ void k_imp_regr_sum(Data D, Batch B, int tile_rows);
 __global__ void k_imp_fold(Data D, Batch B, float* avimp, float* sqsd);
 __global__ void k_prox(Data D, Batch B, int R, int* C);
+__global__ void k_prox_codes(Batch B, int N, int R, uint16_t* code, int* ocnt,
+                             unsigned long long* pairs);
+__global__ void k_prox_pull(const uint16_t* code, int Tp, int R, int nb, int* C);
 __global__ void k_prox_finish(const int* C, const int* nout, int R, int r0, int r1, float* out);
+// k_prox_finish over rows [r0, r1) with its tile grid.
+cudaError_t launch_prox_finish(const int* C, const int* nout, int R, int r0, int r1, float* out,
+                               cudaStream_t st);
 __global__ void k_votes_to_q(const int* votes, const float* w, int N, int nclass, float* q);
 __global__ void k_oob_fold(const float* tree_oob, int ntrees, int N, float* vec);
 

@@ -64,9 +64,7 @@ extern "C" int rfx_prox_dense_static(const int* upper_dev, const int* nout_dev, 
     for (int r0 = row_begin; r0 < row_end; r0 += rows_per) {
         const int r1 = std::min(row_end, r0 + rows_per);
         const long long total = (long long)(r1 - r0) * R;
-        const int grid = (int)std::max(1LL, std::min(4096LL, (total + 255) / 256));
-        rfx::k_prox_finish<<<grid, 256, 0, st>>>(upper_dev, nout_dev, R, r0, r1, scratch);
-        e = cudaGetLastError();
+        e = rfx::launch_prox_finish(upper_dev, nout_dev, R, r0, r1, scratch, st);
         if (e != cudaSuccess) return fail(RFX_ERR_CUDA, std::string("launch: ") + cudaGetErrorString(e));
         e = cudaMemcpyAsync(out_host + (size_t)(r0 - row_begin) * R, scratch, (size_t)total * 4,
                             cudaMemcpyDeviceToHost, st);

@@ -321,30 +321,213 @@ __global__ void k_prox(Data D, Batch B, int R, int* __restrict__ C) {
     if (B.prox_pairs && done) atomicAdd(B.prox_pairs, done);
 }
 
+// ---------------------------------------------------------------------------------------
+// The same counts pulled tile by tile.  Give every row of tree t the 16-bit code
+// 2 * (terminal node) + (1 if OOB): rows i and j add one pair in tree t exactly when their
+// codes differ in the last bit only.  k_prox_codes writes the codes of a batch ([T][R],
+// rows >= R and padding trees 0xFFFF, which never pair) and counts the pairs the batch
+// adds (sum over terminal nodes of OOB rows x in-bag rows, both below R), which decides
+// between pushing (k_prox) and pulling (k_prox_pull).  Block per tree; ocnt: [T][M] ints.
+// ---------------------------------------------------------------------------------------
+__global__ void k_prox_codes(Batch B, int N, int R, uint16_t* __restrict__ code,
+                             int* __restrict__ ocnt, unsigned long long* __restrict__ pairs) {
+    __shared__ unsigned long long red[32];
+    const int t = blockIdx.x, M = B.M;
+    const int nn = B.nnode[t];
+    const int* status = B.status + (size_t)t * M;
+    uint16_t* ct = code + (size_t)t * R;
+    int* oc = ocnt + (size_t)t * M;
+    for (int m = threadIdx.x; m < nn; m += blockDim.x) oc[m] = 0;
+    __syncthreads();
+    const int noob = B.noob[t];
+    const int* oob = B.oob + (size_t)t * N;
+    const int* oleaf = B.oob_leaf + (size_t)t * N;
+    for (int i = threadIdx.x; i < noob; i += blockDim.x) {
+        const int row = oob[i];
+        if (row >= R) continue;
+        const int leaf = oleaf[row];
+        atomicAdd(&oc[leaf], 1);
+        ct[row] = (uint16_t)(2 * leaf + 1);
+    }
+    __syncthreads();
+    unsigned long long mine = 0;
+    for (int m = threadIdx.x; m < nn; m += blockDim.x) {
+        if (status[m] != -1) continue;
+        const size_t nm = (size_t)t * M + m;
+        const int* seg = B.seg[B.nd_buf[nm]] + (size_t)t * N + B.nd_start[nm];
+        const int c = B.nd_cnt[nm];
+        int k = 0;
+        for (int q = 0; q < c; ++q) {
+            const int row = seg[q];
+            if (row >= R) continue;
+            ct[row] = (uint16_t)(2 * m);
+            ++k;
+        }
+        mine += (unsigned long long)k * (unsigned long long)oc[m];
+    }
+    for (int o = 16; o > 0; o >>= 1) mine += __shfl_xor_sync(0xffffffffu, mine, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mine;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long tot = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) tot += red[w];
+        atomicAdd(pairs, tot);
+    }
+}
+
+// C[i][j] (i < j < R) += #{trees t of the batch : code_t(i) ^ code_t(j) == 1}.  Block per
+// 128 x 128 tile of the upper triangle (tile id k enumerates block pairs bi <= bj row by
+// row); thread (tx, ty) owns rows i0 + 8 ty .. +7 and columns j0 + 8 tx .. +7.  Codes of two
+// trees travel packed in one word; the column codes are staged with the OOB bit flipped, so
+// a pair is a 16-bit half-word equality (__vcmpeq2: 0xFFFF per equal half).  Tp is even.
+constexpr int kPullTile = 128;
+constexpr int kPullChunk = 32;  // tree pairs staged per pass
+
+__global__ void __launch_bounds__(256) k_prox_pull(const uint16_t* __restrict__ code, int Tp,
+                                                   int R, int nb, int* __restrict__ C) {
+    __shared__ __align__(16) uint32_t si[kPullChunk][kPullTile];
+    __shared__ __align__(16) uint32_t sj[kPullChunk][kPullTile];
+    // tile id -> (bi, bj), bi <= bj; row bi holds nb - bi tiles
+    long long k = blockIdx.x;
+    int bi = 0;
+    {
+        // first tile of row b is b*nb - b*(b-1)/2; invert with a square root and fix up
+        const double nbd = nb + 0.5;
+        int g = (int)(nbd - sqrt(nbd * nbd - 2.0 * (double)k));
+        g = max(0, min(nb - 1, g));
+        while (g > 0 && (long long)g * nb - (long long)g * (g - 1) / 2 > k) --g;
+        while (g + 1 < nb && (long long)(g + 1) * nb - (long long)(g + 1) * g / 2 <= k) ++g;
+        bi = g;
+    }
+    const int bj = bi + (int)(k - ((long long)bi * nb - (long long)bi * (bi - 1) / 2));
+    const int i0 = bi * kPullTile, j0 = bj * kPullTile;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    int acc[8][8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int v = 0; v < 8; ++v) acc[u][v] = 0;
+    for (int tp0 = 0; tp0 < Tp / 2; tp0 += kPullChunk) {
+        const int ntp = min(kPullChunk, Tp / 2 - tp0);
+        for (int e = threadIdx.x; e < kPullChunk * kPullTile; e += blockDim.x) {
+            const int tp = e / kPullTile, r = e % kPullTile;
+            uint32_t wi = 0xFFFFFFFFu, wj = 0xFFFFFFFFu;
+            if (tp < ntp) {
+                const size_t t0 = (size_t)(2 * (tp0 + tp));
+                const int ri = i0 + r, rj = j0 + r;
+                if (ri < R) wi = (uint32_t)code[t0 * R + ri] | ((uint32_t)code[(t0 + 1) * R + ri] << 16);
+                if (rj < R) wj = (uint32_t)code[t0 * R + rj] | ((uint32_t)code[(t0 + 1) * R + rj] << 16);
+            }
+            si[tp][r] = wi;
+            sj[tp][r] = wj ^ 0x00010001u;
+        }
+        __syncthreads();
+        for (int tp = 0; tp < ntp; ++tp) {
+            const uint4 a0 = *reinterpret_cast<const uint4*>(&si[tp][8 * ty]);
+            const uint4 a1 = *reinterpret_cast<const uint4*>(&si[tp][8 * ty + 4]);
+            const uint4 b0 = *reinterpret_cast<const uint4*>(&sj[tp][8 * tx]);
+            const uint4 b1 = *reinterpret_cast<const uint4*>(&sj[tp][8 * tx + 4]);
+            const uint32_t a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const uint32_t b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+#pragma unroll
+                for (int v = 0; v < 8; ++v) acc[u][v] += __popc(__vcmpeq2(a[u], b[v]));
+        }
+        __syncthreads();
+    }
+    const long long R2 = 2LL * R;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        const int i = i0 + 8 * ty + u;
+        if (i >= R) continue;
+        int* row = C + (long long)i * (R2 - i - 1) / 2 - i - 1;  // row[j] for j > i
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+            const int j = j0 + 8 * tx + v;
+            if (j > i && j < R) row[j] += acc[u][v] >> 4;
+        }
+    }
+}
+
 // finishprox (src/rf_finishprox.cpp:12-74) of rows [r0, r1): with C the symmetric count,
 // S_ij = 0.5 * (C/2 * (1/nout_i) + C/2 * (1/nout_j)) in double (a row with nout 0 is left
 // unscaled), diagonal 1, returned as float32 like get_proximity_matrix
-// (python/randomforest_py.cpp:2129-2155).
-__global__ void k_prox_finish(const int* __restrict__ C, const int* __restrict__ nout, int R,
-                              int r0, int r1, float* __restrict__ out) {
-    const long long total = (long long)(r1 - r0) * R;
+// (python/randomforest_py.cpp:2129-2155).  Block per 64 x 64 output tile: a tile above the
+// diagonal reads its counts row by row from the packed upper triangle, a tile below it reads
+// the mirrored tile (again row by row) and transposes it through shared memory, so every
+// global access is contiguous; tiles crossing the diagonal read entry by entry.
+constexpr int kFinTile = 64;
+
+__device__ __forceinline__ long long upper_index(long long a, long long b, long long R2) {
+    return a * (R2 - a - 1) / 2 + (b - a - 1);  // a < b
+}
+
+__global__ void __launch_bounds__(256) k_prox_finish(const int* __restrict__ C,
+                                                     const int* __restrict__ nout, int R,
+                                                     int r0, int r1, float* __restrict__ out) {
+    __shared__ int tile[kFinTile][kFinTile + 1];  // tile[ii][jj] = C of (i0 + ii, j0 + jj)
+    __shared__ double sc_i[kFinTile], sc_j[kFinTile];
+    const int i0 = r0 + blockIdx.y * kFinTile, j0 = blockIdx.x * kFinTile;
     const long long R2 = 2LL * R;
-    for (long long k = blockIdx.x * (long long)blockDim.x + threadIdx.x; k < total;
-         k += (long long)gridDim.x * blockDim.x) {
-        const int i = r0 + (int)(k / R), j = (int)(k % R);
+    const int tid = threadIdx.x;
+    if (tid < kFinTile) {
+        const int i = i0 + tid;
+        const int ni = i < r1 ? nout[i] : 0;
+        sc_i[tid] = ni > 0 ? 1.0 / (double)ni : 1.0;
+    } else if (tid < 2 * kFinTile) {
+        const int j = j0 + tid - kFinTile;
+        const int nj = j < R ? nout[j] : 0;
+        sc_j[tid - kFinTile] = nj > 0 ? 1.0 / (double)nj : 1.0;
+    }
+    const bool upper = i0 + kFinTile <= j0;  // every i < every j
+    const bool lower = j0 + kFinTile <= i0;  // every j < every i
+    if (upper) {
+        for (int e = tid; e < kFinTile * kFinTile; e += blockDim.x) {
+            const int ii = e / kFinTile, jj = e % kFinTile;
+            const int i = i0 + ii, j = j0 + jj;
+            tile[ii][jj] = (i < r1 && j < R) ? C[upper_index(i, j, R2)] : 0;
+        }
+    } else if (lower) {
+        for (int e = tid; e < kFinTile * kFinTile; e += blockDim.x) {
+            const int jj = e / kFinTile, ii = e % kFinTile;  // consecutive threads: row j, ascending i
+            const int i = i0 + ii, j = j0 + jj;
+            tile[ii][jj] = (i < r1 && j < R) ? C[upper_index(j, i, R2)] : 0;
+        }
+    } else {
+        for (int e = tid; e < kFinTile * kFinTile; e += blockDim.x) {
+            const int ii = e / kFinTile, jj = e % kFinTile;
+            const int i = i0 + ii, j = j0 + jj;
+            int v = 0;
+            if (i < r1 && j < R && i != j) v = C[upper_index(min(i, j), max(i, j), R2)];
+            tile[ii][jj] = v;
+        }
+    }
+    __syncthreads();
+    for (int e = tid; e < kFinTile * kFinTile; e += blockDim.x) {
+        const int ii = e / kFinTile, jj = e % kFinTile;
+        const int i = i0 + ii, j = j0 + jj;
+        if (i >= r1 || j >= R) continue;
         float v;
         if (i == j) {
             v = 1.0f;
         } else {
-            const long long a = min(i, j), b = max(i, j);
-            const double h = (double)C[a * (R2 - a - 1) / 2 + (b - a - 1)] / 2.0;
-            const int ni = nout[i], nj = nout[j];
-            const double si = ni > 0 ? h * (1.0 / (double)ni) : h;
-            const double sj = nj > 0 ? h * (1.0 / (double)nj) : h;
+            const double h = (double)tile[ii][jj] / 2.0;
+            const double si = h * sc_i[ii];
+            const double sj = h * sc_j[jj];
             v = (float)(0.5 * (si + sj));
         }
-        out[k] = v;
+        out[(size_t)(i - r0) * R + j] = v;
     }
+}
+
+cudaError_t launch_prox_finish(const int* C, const int* nout, int R, int r0, int r1, float* out,
+                               cudaStream_t st) {
+    if (r1 <= r0) return cudaSuccess;
+    const dim3 grid((unsigned)((R + kFinTile - 1) / kFinTile),
+                    (unsigned)((r1 - r0 + kFinTile - 1) / kFinTile));
+    k_prox_finish<<<grid, 256, 0, st>>>(C, nout, R, r0, r1, out);
+    return cudaGetLastError();
 }
 
 // q[i][c] = classwt[c] added votes[i][c] times, sequentially (src/rf_random_forest.cpp:1506-1520).

@@ -33,7 +33,9 @@ def test_config1_full_size_two_trees():
     compare_fit(g, o, 1)
 
 
-def test_config0_full_size_with_proximity():
+@pytest.mark.parametrize("mode", ["push", "pull"])
+def test_config0_full_size_with_proximity(mode, monkeypatch):
+    monkeypatch.setenv("RFX_PROX_MODE", mode)
     X, y = config0_data()
     M = oracle.maxnode(len(y), 1, 0)
     g = gpu_fit(0, X, y, ntree=6, mtry=4, minndsize=1, maxnode=M, proximity=True)

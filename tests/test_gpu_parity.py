@@ -26,9 +26,12 @@ def both(task, X, y, **kw):
     return g, o
 
 
-def test_classification_proximity():
+@pytest.mark.parametrize("mode", ["push", "pull", "auto"])
+def test_classification_proximity(mode, monkeypatch):
+    # counts pushed per pair (atomics) or pulled per 128x128 tile (leaf-code compares)
+    monkeypatch.setenv("RFX_PROX_MODE", mode)
     X, y = synth("class", 1500, 12, 1)
-    g, o = both(0, X, y, ntree=6, mtry=3, minndsize=1, proximity=True)
+    g, o = both(0, X, y, ntree=7, mtry=3, minndsize=1, proximity=True)
     compare_fit(g, o, 0, proximity=True)
 
 
@@ -50,7 +53,9 @@ def test_regression_few_bins_and_node_cap():
     compare_fit(g, o, 1)
 
 
-def test_unsupervised_proximity():
+@pytest.mark.parametrize("mode", ["push", "pull"])
+def test_unsupervised_proximity(mode, monkeypatch):
+    monkeypatch.setenv("RFX_PROX_MODE", mode)
     X, _ = synth("gmm", 600, 8, 5)
     g, o = both(2, X, None, ntree=4, mtry=3, minndsize=1, proximity=True)
     compare_fit(g, o, 2, proximity=True)
