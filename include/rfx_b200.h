@@ -59,6 +59,7 @@ typedef struct {
                                include/rf_proximity_lowrank.hpp:27-439).  No dense counts are
                                kept; every tree's leaf groups are stored instead for
                                rfx_lowrank_build.  Rank <= 64. */
+    int keep_forest;        /* keep the grown trees on the device (packed) for rfx_predict */
 } rfx_fit_params;
 
 typedef struct {
@@ -195,6 +196,35 @@ int rfx_get_stream(void* ctx, void** stream);   /* the context's cudaStream_t */
 int rfx_set_profiling(void* ctx, int on);
 int rfx_get_stats(void* ctx, rfx_stats* out);
 int rfx_reset_stats(void* ctx);
+
+/* ---- Prediction of new rows -----------------------------------------------------------
+ * Replaces RandomForest::predict_classification / predict_proba (new-data branch) and
+ * predict_regression (src/rf_random_forest.cpp:3403-3590, 3863-3945).  A fit with
+ * keep_forest leaves its trees on the device; rfx_load_forest puts any forest there (e.g. the
+ * arrays of a saved model).  Walks follow the reference exactly: at most maxnode steps per
+ * tree; cat == 1 features go left when x <= xbestsplit; any other feature takes the
+ * categorical branch, jcat = (int)(x + 0.5) in [0, cat) going right (catgoleft is empty for
+ * histogram-grown trees) and any other jcat voting class 0 (regression: the root's value).
+ * Classification folds classwt-weighted float votes in tree order (first maximum wins;
+ * probabilities are votes / their sum); regression averages the values in tree order. */
+typedef struct {
+    int task;                 /* RFX_TASK_CLASSIFICATION or RFX_TASK_REGRESSION */
+    int ntree, maxnode, nclass, p;
+    const int* nodestatus;    /* [ntree][maxnode] */
+    const int* bestvar;
+    const float* xbestsplit;
+    const int* treemap;       /* [ntree][2 * maxnode] */
+    const int* nodeclass;     /* classification */
+    const float* nodepred;    /* regression */
+    const int* cat;           /* [p] */
+    const float* classwt;     /* [nclass] or NULL (votes of 1) */
+} rfx_forest;
+int rfx_load_forest(void* ctx, const rfx_forest* forest);
+
+/* X_host [n][p] row-major float; outputs may be NULL: class_out [n] (0-based class),
+ * proba_out [n][nclass], value_out [n] (regression). */
+int rfx_predict(void* ctx, const float* X_host, int n, int p, int* class_out, float* proba_out,
+                float* value_out);
 
 /* ---- Low-rank proximity (use_qlora=True, quant_mode="int8") --------------------------
  * Replaces LowRankProximityMatrix (include/rf_proximity_lowrank.hpp:27-439,

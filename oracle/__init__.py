@@ -113,6 +113,28 @@ def finishprox(nout, pairs):
     return out
 
 
+def predict(task, trees, X, nclass, cat, classwt=None):
+    """orc_predict on the tree arrays of a fit (dict with nodestatus, bestvar, xbestsplit,
+    treemap, nodeclass, nodepred).  Returns (cls, proba) for classification, pred for
+    regression."""
+    X = np.ascontiguousarray(X, np.float32)
+    n, p = X.shape
+    T, M = trees["nodestatus"].shape
+    cat = np.ascontiguousarray(cat, np.int32)
+    cw = None if classwt is None else np.ascontiguousarray(classwt, np.float32)
+    arr = {k: np.ascontiguousarray(trees[k]) for k in
+           ("nodestatus", "bestvar", "xbestsplit", "treemap", "nodeclass", "nodepred")}
+    cls = np.zeros(n, np.int32)
+    proba = np.zeros((n, max(nclass, 1)), np.float32)
+    reg = np.zeros(n, np.float32)
+    lib().orc_predict(task, T, M, nclass, p, _p(cat, _pi), _p(cw, _pf),
+                      _p(arr["nodestatus"], _pi), _p(arr["bestvar"], _pi),
+                      _p(arr["xbestsplit"], _pf), _p(arr["treemap"], _pi),
+                      _p(arr["nodeclass"], _pi), _p(arr["nodepred"], _pf), _p(X, _pf), n,
+                      _p(cls, _pi), _p(proba, _pf), _p(reg, _pf))
+    return reg if task == 1 else (cls, proba)
+
+
 def fit(task, X, y=None, *, ntree, mtry, minndsize, maxnode, iseed=12345, nbins=256,
         sample_weights=None, cat=None, classwt=None, importance=True, proximity=False,
         dump_trees=True):

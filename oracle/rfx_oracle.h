@@ -58,6 +58,14 @@ int orc_maxnode(int n, int minndsize, int user_maxnode);
 int orc_fit(const orc_params* prm, const float* X, const int* ycls, const float* yreg,
             const float* sample_weights, const int* cat, const float* classwt, orc_out* out);
 int orc_finishprox(int N, const int* nout, const int* prox_pairs, double* out);
+/* Prediction of new rows by tree traversal (X row-major [n][p]).  Classification: classwt-
+ * weighted float votes -> cls_out [n] (0-based class) and proba_out [n][nclass]; regression:
+ * reg_out [n].  catgoleft is empty for histogram-grown trees (all zero). */
+int orc_predict(int task, int ntree, int maxnode, int nclass, int p, const int* cat,
+                const float* classwt, const int* nodestatus, const int* bestvar,
+                const float* xbestsplit, const int* treemap, const int* nodeclass,
+                const float* nodepred, const float* X, int n, int* cls_out, float* proba_out,
+                float* reg_out);
 
 #ifdef __cplusplus
 }

@@ -132,6 +132,11 @@ struct Ctx {
     DBuf lr_X, lr_Z, lr_CZ, lr_Y, lr_ls, lr_part, lr_small, lr_A, lr_q, lr_qb, lr_s, lr_qbp, lr_sp, lr_perm, lr_blocks, lr_np, lr_norm, lr_ids, lr_keys, lr_order_s, lr_cub,
         lr_err, lr_out_i, lr_out_v;
 
+    // stored forest for prediction (rfx_predict.cu)
+    int f_T = 0, f_cap = 0, f_M = 0, f_p = 0, f_nclass = 0, f_task = 0;
+    bool f_classwt = false;
+    DBuf f_nodes, f_root, f_cat, f_cw, p_X, p_xc, p_vote, p_val, p_cls, p_proba, p_pred;
+
     // batch buffers
     int Tcap = 0;
     rfx::Batch B{};
@@ -150,7 +155,8 @@ struct Ctx {
                        &b_feat, &b_lvl, &b_srch, &b_srchcnt, &b_srchoff, &b_counters,
                        &b_oobleaf, &b_used, &b_right, &b_rightimp, &b_d2, &b_d0, &b_rr, &b_srchbig, &b_partbig, &b_pcode, &b_pocnt, &b_ppairs,
                        &lr_code, &lr_order, &lr_goff, &lr_ngroups, &lr_tmp, &lr_X, &lr_Z,
-                       &lr_CZ, &lr_Y, &lr_ls, &lr_part, &lr_small, &lr_A, &lr_q, &lr_qb, &lr_s, &lr_qbp, &lr_sp, &lr_perm, &lr_blocks, &lr_np, &lr_norm, &lr_ids, &lr_keys, &lr_order_s, &lr_cub,
+                       &lr_CZ, &lr_Y, &lr_ls, &lr_part, &lr_small, &lr_A, &lr_q, &lr_qb, &lr_s, &lr_qbp, &lr_sp, &lr_perm, &lr_blocks, &lr_np, &lr_norm, &lr_ids, &lr_keys, &lr_order_s, &lr_cub, &f_nodes, &f_root, &f_cat, &f_cw, &p_X,
+                       &p_xc, &p_vote, &p_val, &p_cls, &p_proba, &p_pred,
                        &lr_err, &lr_out_i, &lr_out_v};
         cudaSetDevice(device);
         if (st) cudaStreamSynchronize(st);
@@ -178,5 +184,10 @@ inline int grid_for(long long n, int threads, int cap) {
 // store the leaf groups of the T trees of a grown batch.
 void lr_reserve(Ctx& c, int extra);
 void lr_store_batch(Ctx& c, const rfx::Batch& B, int T);
+
+// Prediction forest (rfx_predict_host.cu): room for `extra` more trees; pack a grown batch.
+void forest_reserve(Ctx& c, int extra);
+void forest_store_batch(Ctx& c, const rfx::Batch& B, int T);
+void forest_reset(Ctx& c);
 
 }  // namespace rfxh

@@ -290,6 +290,7 @@ void load(Ctx& c, const rfx_fit_params* prm, const rfx_inputs* in) {
     RFX_CUDA(cudaMemsetAsync(sq, 0, p * 4, st));
     c.prox = nullptr;
     c.prox_len = 0;
+    forest_reset(c);
     c.lr_rank = P.compute_proximity && P.lowrank_rank > 0 ? P.lowrank_rank : 0;
     c.lr_n = 0;
     c.lr_G = c.M + 2;
@@ -495,6 +496,7 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
         }
     }
     if (c.lr_rank > 0) lr_store_batch(c, B, T);
+    if (c.prm.keep_forest) forest_store_batch(c, B, T);
     if (keep) c.tree_oob_n += T;
     if (out) {
         auto cp = [&](void* dst, const void* src, size_t elems, size_t esz) {
@@ -572,6 +574,7 @@ int rfx_grow(void* ctx, int tree_begin, int ntree, rfx_trees* out) {
         require(c.loaded, RFX_ERR_STATE, "rfx_grow before rfx_load");
         require(tree_begin >= 0 && ntree >= 0, RFX_ERR_ARG, "bad tree range");
         lr_reserve(c, ntree);
+        if (c.prm.keep_forest) forest_reserve(c, ntree);
         for (int b0 = 0; b0 < ntree; b0 += c.Tcap) {
             const int T = std::min(c.Tcap, ntree - b0);
             grow_batch(c, tree_begin + b0, T, out, b0);

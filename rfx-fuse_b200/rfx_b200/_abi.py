@@ -27,7 +27,7 @@ class FitParams(C.Structure):
     _fields_ = [(k, C.c_int) for k in (
         "task", "n", "p", "mtry", "minndsize", "maxnode", "iseed", "boot_seed", "nbins",
         "maxcat", "compute_importance", "compute_proximity", "prox_rows", "batch_trees",
-        "keep_tree_oob", "lowrank_rank")]
+        "keep_tree_oob", "lowrank_rank", "keep_forest")]
 
 
 class Inputs(C.Structure):
@@ -46,6 +46,13 @@ class Accum(C.Structure):
                 ("q", _pf), ("oob_sum", _pf), ("avimp", _pf), ("sqsd", _pf), ("labels", _pi)]
 
 
+class Forest(C.Structure):
+    _fields_ = [("task", C.c_int), ("ntree", C.c_int), ("maxnode", C.c_int), ("nclass", C.c_int),
+                ("p", C.c_int), ("nodestatus", _pi), ("bestvar", _pi), ("xbestsplit", _pf),
+                ("treemap", _pi), ("nodeclass", _pi), ("nodepred", _pf), ("cat", _pi),
+                ("classwt", _pf)]
+
+
 class Stats(C.Structure):
     _fields_ = [("kernel_launches", C.c_int64), ("hist_launches", C.c_int64),
                 ("hist_ms", C.c_double), ("hist_bytes", C.c_double), ("levels", C.c_int64),
@@ -61,7 +68,7 @@ SYMBOLS = (
     "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host", "rfx_get_stream",
     "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats", "rfx_sync",
     "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk", "rfx_lowrank_product",
-    "rfx_prox_apply", "rfx_lowrank_set_factors",
+    "rfx_prox_apply", "rfx_lowrank_set_factors", "rfx_load_forest", "rfx_predict",
 )
 
 # int (*)(void* user, float* buf_dev, int64_t count): in-place sum over processes
@@ -110,12 +117,15 @@ def load_library(path: str = LIB_PATH):
     L.rfx_lowrank_product.argtypes = [vp, C.c_int, C.c_int, _pf]
     L.rfx_prox_apply.argtypes = [vp, vp, C.c_int, vp, vp]
     L.rfx_lowrank_set_factors.argtypes = [vp, C.POINTER(C.c_int8), _pf, C.c_int, C.c_int]
+    L.rfx_load_forest.argtypes = [vp, C.POINTER(Forest)]
+    L.rfx_predict.argtypes = [vp, _pf, C.c_int, C.c_int, _pi, _pf, _pf]
     for name in ("rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
                  "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish",
                  "rfx_prox_dense", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host",
                  "rfx_get_stream", "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats",
                  "rfx_sync", "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk",
-                 "rfx_lowrank_product", "rfx_prox_apply", "rfx_lowrank_set_factors"):
+                 "rfx_lowrank_product", "rfx_prox_apply", "rfx_lowrank_set_factors",
+                 "rfx_load_forest", "rfx_predict"):
         getattr(L, name).restype = C.c_int
     _LIB = L
     return L
@@ -221,6 +231,37 @@ class Context:
 
     def sync(self):
         check(self._lib.rfx_sync(self.handle))
+
+    # ---- prediction ----
+    def load_forest(self, task: int, trees: dict, cat, nclass: int = 1, classwt=None):
+        """Put host tree arrays ([ntree][maxnode]: nodestatus, bestvar, xbestsplit, treemap
+        (x2), nodeclass / nodepred) on the device for predict()."""
+        arr = {k: np.ascontiguousarray(trees[k]) for k in
+               ("nodestatus", "bestvar", "xbestsplit", "treemap", "nodeclass", "nodepred")
+               if trees.get(k) is not None}
+        T, M = arr["nodestatus"].shape
+        cat = np.ascontiguousarray(cat, np.int32)
+        cw = None if classwt is None else np.ascontiguousarray(classwt, np.float32)
+        f = Forest(task, T, M, nclass, cat.shape[0], ptr(arr["nodestatus"], _pi),
+                   ptr(arr["bestvar"], _pi), ptr(arr["xbestsplit"], _pf), ptr(arr["treemap"], _pi),
+                   ptr(arr.get("nodeclass"), _pi), ptr(arr.get("nodepred"), _pf), ptr(cat, _pi),
+                   ptr(cw, _pf))
+        check(self._lib.rfx_load_forest(self.handle, C.byref(f)))
+
+    def predict(self, X: np.ndarray, nclass: int = 0):
+        """(classes int32 [n], proba float32 [n][nclass]) for a classification forest, or
+        values float32 [n] for regression (nclass == 0)."""
+        X = np.ascontiguousarray(X, np.float32)
+        n, p = X.shape
+        if nclass > 0:
+            cls = np.zeros(n, np.int32)
+            proba = np.zeros((n, nclass), np.float32)
+            check(self._lib.rfx_predict(self.handle, ptr(X, _pf), n, p, ptr(cls, _pi),
+                                        ptr(proba, _pf), None))
+            return cls, proba
+        val = np.zeros(n, np.float32)
+        check(self._lib.rfx_predict(self.handle, ptr(X, _pf), n, p, None, None, ptr(val, _pf)))
+        return val
 
     # ---- low-rank proximity ----
     def lowrank_build(self, rank: int, oversample: int = 16, power_iters: int = 1, seed: int = 0,

@@ -33,6 +33,16 @@ def _isqrt_f32(x: int) -> int:
     return int(np.sqrt(np.float32(x), dtype=np.float32))
 
 
+def feature_kinds(task: int, X: np.ndarray, maxcat: int, categorical_features=None) -> np.ndarray:
+    """cat[] of a fit: only the classifier's fit detects categorical columns
+    (python/randomforest_py.cpp:1415-1499); the regressor and the unsupervised forest never
+    call set_categorical_features, so every feature stays quantitative (cat = 1,
+    src/rf_random_forest.cpp:461)."""
+    if task != A.TASK_CLASSIFICATION:
+        return np.ones(X.shape[1], np.int32)
+    return detect_categorical(X, maxcat, categorical_features)
+
+
 def detect_categorical(X: np.ndarray, maxcat: int, categorical_features=None) -> np.ndarray:
     """cat[] exactly as RandomForestClassifier::fit builds it (python/randomforest_py.cpp:1413-1460)."""
     n, p = X.shape
@@ -129,12 +139,12 @@ class _Forest:
             raise RuntimeError("X must be 2-dimensional (samples, features)")
         n, p = X.shape
         self.n_features_ = p
-        cat = detect_categorical(X, self.maxcat, self.categorical_features)
+        cat = feature_kinds(task, X, self.maxcat, self.categorical_features)
         self._cat = cat
         prm = A.FitParams(task, n, p, mtry, self.minndsize, maxnode, self.iseed, 12345,
                           self.n_bins, self.maxcat, int(self.compute_importance),
                           int(self.compute_proximity), self.prox_rows, self.batch_trees, 0,
-                          self._lowrank_rank())
+                          self._lowrank_rank(), int(task != A.TASK_UNSUPERVISED))
         ycls = yreg = sw = cw = None
         if task == A.TASK_CLASSIFICATION:
             ycls = np.ascontiguousarray(y, dtype=np.int32)
@@ -337,6 +347,27 @@ class _Classifying(_Forest):
 class RandomForestClassifier(_Classifying):
     _task = A.TASK_CLASSIFICATION
 
+    def _is_training_size(self, X):
+        # predict_classification / predict_proba treat any input with nsample rows as the
+        # training data and return the stored OOB results (src/rf_random_forest.cpp:3384-3401)
+        return np.asarray(X).shape[0] == self.nsample
+
+    def predict(self, X):
+        """Class labels (python/randomforest_py.cpp:1860-1869)."""
+        self._check()
+        if self._is_training_size(X):
+            return self.classes_[self._oob_class].astype(np.int32)
+        cls, _ = self._context().predict(np.ascontiguousarray(X, np.float32), self.nclass_)
+        return self.classes_[cls].astype(np.int32)
+
+    def predict_proba(self, X):
+        """Class probabilities [n, nclass] (python/randomforest_py.cpp:1871-1880)."""
+        self._check()
+        if self._is_training_size(X):
+            return self._oob_proba.copy()
+        _, proba = self._context().predict(np.ascontiguousarray(X, np.float32), self.nclass_)
+        return proba
+
     def fit(self, X, y, sample_weights=None):
         y = np.ascontiguousarray(y, dtype=np.int32)
         ncl = len(np.unique(y))
@@ -354,6 +385,7 @@ class RandomForestClassifier(_Classifying):
             classwt = np.array([n / (np.float32(ncl) * np.float32(k)) if k > 0 else np.float32(1.0)
                                 for k in counts], np.float32)
         self.classwt_ = classwt
+        self.classes_ = np.unique(y).astype(np.int32)
         self._fit(X, y, sample_weights, A.TASK_CLASSIFICATION, self._mtry, self._maxnode, classwt)
 
     def _finalize(self, y):
@@ -393,6 +425,12 @@ class RandomForestRegressor(_Forest):
 
     def get_oob_mse(self):
         return self.get_oob_error()
+
+    def predict(self, X):
+        """Mean of the trees' values (python/randomforest_py.cpp:1860-1869,
+        src/rf_random_forest.cpp:3494-3590); training-size inputs are walked too."""
+        self._check()
+        return self._context().predict(np.ascontiguousarray(X, np.float32), 0)
 
 
 class RandomForestUnsupervised(_Classifying):

@@ -83,7 +83,7 @@ def fit_sharded(est, X, y=None, dist=None, device=None):
 
     from . import _abi as A
     from .forest import (RandomForestClassifier, RandomForestRegressor, RandomForestUnsupervised,
-                         _isqrt_f32, calculate_maxnode, detect_categorical)
+                         _isqrt_f32, calculate_maxnode, feature_kinds)
 
     if dist is None:
         import torch.distributed as dist
@@ -109,7 +109,7 @@ def fit_sharded(est, X, y=None, dist=None, device=None):
     est.device = dev.index
     est._ctx = A.Context(dev.index)
     ctx = est._ctx
-    cat = detect_categorical(X, est.maxcat, est.categorical_features)
+    cat = feature_kinds(task, X, est.maxcat, est.categorical_features)
     prm = A.FitParams(task, n, p, mtry, est.minndsize, maxnode, est.iseed, 12345, est.n_bins,
                       est.maxcat, int(est.compute_importance), int(est.compute_proximity),
                       est.prox_rows, est.batch_trees, int(task == A.TASK_REGRESSION))

@@ -52,6 +52,53 @@ CASES = {
 }
 
 
+def predict_data(kind, n, p, seed, n_new):
+    """Training data plus new rows for predict(): column p is a 5-level categorical; the new
+    rows carry out-of-range categories and NaNs (the reference's edge branches)."""
+    X, y = synth(kind, n + n_new, p, seed)
+    rng = np.random.default_rng(seed + 100)
+    c = rng.integers(0, 5, n + n_new).astype(np.float32)
+    X = np.concatenate([X, c[:, None]], axis=1)
+    if y is not None and kind != "regr":
+        y = np.where(c == 3, (y + 1) % (y.max() + 1), y).astype(np.int32)  # the column matters
+    Xn = X[n:].copy()
+    Xn[:20, p] = 7.0        # category out of range -> class 0 / root value
+    Xn[20:30, p] = -1.0
+    Xn[30:40, p] = np.nan
+    Xn[40:50, 0] = np.nan   # continuous NaN: goes right
+    return X[:n], (y[:n] if y is not None else None), Xn
+
+
+PREDICT_CASES = {
+    "predict_class": (0, "multiclass", 900, 6, 31, dict(ntree=5, mtry=3, minndsize=1,
+                                                         classwt=[0.3, 1.0, 0.6, 0.9])),
+    "predict_regr": (1, "regr", 900, 6, 32, dict(ntree=5, mtry=3, minndsize=3)),
+}
+
+
+def predict_golden():
+    """Reference predictions of new rows (python/randomforest_py.cpp:1860-1883)."""
+    import rfx_b200.forest as F
+    R = oracle.ref_module()
+    out = {}
+    for name, (task, kind, n, p, seed, kw) in PREDICT_CASES.items():
+        X, y, Xn = predict_data(kind, n, p, seed, 300)
+        cat = F.feature_kinds(task, X, 10, None)
+        common = dict(nsample=n, ntree=kw["ntree"], mtry=kw["mtry"], minndsize=kw["minndsize"],
+                      compute_importance=False, compute_proximity=False, show_progress=False)
+        if task == 0:
+            m = R.RandomForestClassifier(classwt=kw["classwt"], **common)
+            m.fit(X, y)
+            d = {"pred": np.asarray(m.predict(Xn)), "proba": np.asarray(m.predict_proba(Xn))}
+        else:
+            m = R.RandomForestRegressor(**common)
+            m.fit(X, y)
+            d = {"pred": np.asarray(m.predict(Xn))}
+        d.update(X=X, y=y, Xn=Xn, cat=cat, maxnode=np.int32(oracle.maxnode(n, kw["minndsize"], 0)))
+        out[name] = d
+    return out
+
+
 def main():
     if not oracle.ref_available():
         raise SystemExit("oracle/_ref is not built: run `make -C oracle ref`")
@@ -81,6 +128,7 @@ def main():
     e16, nb16, kind16, xb16 = oracle.ref_binning(Xb, cat, 16)
     binning = {"X": Xb, "cat": cat, "edges": e, "nb": nb, "kind": kind, "xb": xb,
                "edges16": e16, "nb16": nb16, "kind16": kind16, "xb16": xb16}
+    out.update(predict_golden())
     for name, d in out.items():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **d)
     np.savez_compressed(os.path.join(HERE, "bootstrap.npz"), **boot)

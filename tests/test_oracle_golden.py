@@ -77,3 +77,26 @@ def test_oracle_matches_reference_on_fresh_case():
     o = oracle.fit(1, X, y, ntree=2, mtry=3, minndsize=3, maxnode=r["maxnode"])
     for k in ("nodestatus", "bestvar", "xbestsplit", "treemap", "nodepred", "nin", "avimp"):
         assert_same(k, o[k], r[k])
+
+
+@pytest.mark.parametrize("name", ["predict_class", "predict_regr"])
+def test_oracle_predict_matches_reference(name):
+    """orc_predict on the oracle's trees equals the reference's predict()/predict_proba() of
+    new rows, including out-of-range categories and NaNs."""
+    g = dict(np.load(os.path.join(GOLD, f"{name}.npz"), allow_pickle=False))
+    task = 0 if name == "predict_class" else 1
+    X, y, Xn, cat = g["X"], g.get("y"), g["Xn"], g["cat"]
+    M = int(g["maxnode"])
+    kw = dict(ntree=5, mtry=3, minndsize=1 if task == 0 else 3, maxnode=M, cat=cat,
+              importance=False)
+    if task == 0:
+        kw["classwt"] = [0.3, 1.0, 0.6, 0.9]
+    o = oracle.fit(task, X, y, **kw)
+    if task == 0:
+        labels = np.unique(y)
+        cls, proba = oracle.predict(0, o, Xn, o["nclass"], cat, kw["classwt"])
+        assert np.array_equal(labels[cls], g["pred"])
+        assert np.array_equal(proba.view(np.uint32), g["proba"].astype(np.float32).view(np.uint32))
+    else:
+        pred = oracle.predict(1, o, Xn, 1, cat)
+        assert np.array_equal(pred.view(np.uint32), g["pred"].astype(np.float32).view(np.uint32))
