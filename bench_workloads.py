@@ -38,6 +38,14 @@ WL = {
 }
 
 
+class _IntView:
+    """Zero-copy view of `count` device int32 values for torch (CUDA array interface)."""
+
+    def __init__(self, ptr, count):
+        self.__cuda_array_interface__ = {"shape": (int(count),), "typestr": "<i4",
+                                         "data": (int(ptr), False), "version": 3}
+
+
 def make(cfg):
     rng = np.random.default_rng(cfg["seed"])
     n, p = cfg["n"], cfg["p"]
@@ -186,18 +194,42 @@ def run_workload(args):
     else:
         trees = ctx.stats()["trees"]
         ctx.reset_stats()
+        reduce = nout_dev = None
+        if world > 1:
+            # sharded build: OOB counts and every sketch pass summed over the ranks (NCCL)
+            from rfx_b200.shard import _DeviceFloats
+            nd, _ = ctx.vote_buffers()
+            nout_t = torch.empty(R, dtype=torch.int32, device=dev)
+            torch.cuda.synchronize()
+            nout_t.copy_(torch.as_tensor(_IntView(nd, R), device=dev))
+            torch.distributed.all_reduce(nout_t)
+            nout_dev = nout_t.data_ptr()
+
+            def reduce(ptr, count):
+                t = torch.as_tensor(_DeviceFloats(ptr, count), device=dev)
+                torch.distributed.all_reduce(t)
+                torch.cuda.synchronize(dev)
         torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
         t0 = time.perf_counter()
-        ctx.lowrank_build(64, 16, 1, seed=12345)
+        ctx.lowrank_build(64, 16, 1, seed=12345, nout_dev=nout_dev, reduce=reduce)
         build_s = time.perf_counter() - t0
         st2 = ctx.stats()
+        if world > 1:
+            torch.distributed.barrier()
         t0 = time.perf_counter()
-        idx, val = ctx.lowrank_topk(50, 0, R)
+        rows_mine, idx, val = ctx.lowrank_topk_part(50, rank, world)
+        r0, r1 = 0, len(rows_mine)
         topk_s = time.perf_counter() - t0
+        if world > 1:
+            tt = torch.tensor([build_s, topk_s], device=dev, dtype=torch.float64)
+            torch.distributed.all_reduce(tt, op=torch.distributed.ReduceOp.MAX)
+            build_s, topk_s = float(tt[0]), float(tt[1])
         st3 = ctx.stats()
         tiles = st3["topk_tiles"]
         flops = tiles * 2.0 * 128 * 256 * 64
-        dense_flops = 2.0 * R * (((R + 255) // 256) * 256) * 64
+        dense_flops = 2.0 * (r1 - r0) * (((R + 255) // 256) * 256) * 64
         topk_ms = st3["topk_ms"]
         sk_gbs = st2["sketch_bytes"] / st2["sketch_ms"] / 1e6 if st2["sketch_ms"] else None
         line["lowrank"] = {
@@ -205,7 +237,8 @@ def run_workload(args):
             "build_s": build_s, "sketch_ms": st2["sketch_ms"], "sketch_gbs": sk_gbs,
             "sketch_frac_hbm": sk_gbs / hbm if sk_gbs else None,
             "topk_s": topk_s, "topk_kernel_ms": topk_ms, "tiles": int(tiles),
-            "tiles_dense": int(((R + 127) // 128) * ((R + 255) // 256)),
+            "tiles_dense": int(((r1 - r0 + 127) // 128) * ((R + 255) // 256)),
+            "rows_this_rank": [r0, r1],
             "tensor_tflops_executed": flops / topk_ms / 1e9 if topk_ms else None,
             "tensor_frac_executed": flops / topk_ms / 1e9 / bf16 if topk_ms else None,
             "dense_equivalent_tflops": dense_flops / topk_ms / 1e9 if topk_ms else None,

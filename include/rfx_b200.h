@@ -270,6 +270,15 @@ int rfx_lowrank_factors(void* ctx, float* A_host, int8_t* q_host, float* scale_h
 int rfx_lowrank_topk(void* ctx, int k, int row_begin, int row_end, int* idx_host,
                      float* val_host);
 
+/* The same top-k for part `part` of `nparts` equal shares of the product's internal row
+ * order (rows by descending scale_i |q_i|; a contiguous share of that order is a
+ * contiguous share of the kernel's work, unlike a range of row ids): rows_host [rows] gets
+ * the original row ids, idx_host / val_host [rows][k] their results.  *nrows_out = rows;
+ * with rows_host NULL only *nrows_out is set.  The shares of all parts cover every row once
+ * (how a sharded fit splits the top-k over its GPUs). */
+int rfx_lowrank_topk_part(void* ctx, int k, int part, int nparts, int* rows_host, int* idx_host,
+                          float* val_host, int* nrows_out);
+
 /* Rows [row_begin, row_end) of P (same kernel, every value written; diagonal included):
  * the reconstructed approximate proximity, out_host [rows][R]. */
 int rfx_lowrank_product(void* ctx, int row_begin, int row_end, float* out_host);

@@ -32,7 +32,9 @@ struct TopkArgs {
     const float* scale; // [Rpad] by stored position
     const float* norm;  // [Rpad] s_j * |q_j| by stored position, descending (with perm), or
                         // null: no early stop
-    int* out_idx;       // [r1 - r0][k]
+    int out_pos0;       // >= 0: results of stored position p at row p - out_pos0 of the
+                        // outputs; -1: at row (original id - r0)
+    int* out_idx;       // [rows][k]
     float* out_val;     // [r1 - r0][k]
     float* dense;       // [r1 - r0][dense_ld] by original column, when k == 0
     long long dense_ld;

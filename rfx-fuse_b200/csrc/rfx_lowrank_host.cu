@@ -155,7 +155,8 @@ CUtensorMap factor_map(Ctx& c, void* rows) {
 // One launch of the product kernel for original rows [r0, r1).  Top-k (k > 0) runs on the
 // rows stored by descending bound factor n (early stop); the dense product (k == 0) on the
 // identity order.
-void run_product(Ctx& c, int r0, int r1, int k, int* oi, float* ov, float* dense, long long ld) {
+void run_product(Ctx& c, int r0, int r1, int k, int* oi, float* ov, float* dense, long long ld,
+                 int blk0 = -1, int blk1 = -1) {
     cudaStream_t st = c.st;
     const bool ordered = k > 0;
     const CUtensorMap tm = factor_map(c, ordered ? c.lr_qbp.p : c.lr_qb.p);
@@ -171,8 +172,21 @@ void run_product(Ctx& c, int r0, int r1, int k, int* oi, float* ov, float* dense
     a.perm = ordered ? (const int*)c.lr_perm.p : nullptr;
     a.norm = ordered ? (const float*)c.lr_np.p : nullptr;
     a.blocks = nullptr;
+    a.out_pos0 = -1;
     int grid = (r1 - r0 + rfx::kTkRows - 1) / rfx::kTkRows;
-    if (ordered) {
+    if (ordered && blk0 >= 0) {
+        // an explicit range of stored-order blocks: every row in them, outputs by position
+        std::vector<int> blk;
+        for (int b = blk0; b < blk1; ++b) blk.push_back(b);
+        int* db = (int*)c.lr_blocks.get(std::max<size_t>(1, blk.size()) * 4);
+        RFX_CUDA(cudaMemcpyAsync(db, blk.data(), blk.size() * 4, cudaMemcpyHostToDevice, st));
+        RFX_CUDA(cudaStreamSynchronize(st));
+        a.blocks = db;
+        a.r0 = 0;
+        a.r1 = c.lr_R;
+        a.out_pos0 = blk0 * rfx::kTkRows;
+        grid = blk1 - blk0;
+    } else if (ordered) {
         // the 128-row blocks of the stored order that hold any requested row
         std::vector<int> blk;
         if (r0 == 0 && r1 == c.lr_R) {
@@ -449,6 +463,31 @@ int rfx_lowrank_topk(void* ctx, int k, int row_begin, int row_end, int* idx_host
         run_product(c, row_begin, row_end, k, oi, ov, nullptr, 0);
         RFX_CUDA(cudaMemcpyAsync(idx_host, oi, (size_t)rows * k * 4, cudaMemcpyDeviceToHost, c.st));
         RFX_CUDA(cudaMemcpyAsync(val_host, ov, (size_t)rows * k * 4, cudaMemcpyDeviceToHost, c.st));
+        RFX_CUDA(cudaStreamSynchronize(c.st));
+    });
+}
+
+int rfx_lowrank_topk_part(void* ctx, int k, int part, int nparts, int* rows_host, int* idx_host,
+                          float* val_host, int* nrows_out) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(c.lr_ready, RFX_ERR_STATE, "low-rank factors have not been built");
+        require(k >= 1 && k <= 64, RFX_ERR_ARG, "k must be in [1, 64]");
+        require(nparts >= 1 && part >= 0 && part < nparts && nrows_out, RFX_ERR_ARG, "bad part");
+        const int nblk = (c.lr_R + rfx::kTkRows - 1) / rfx::kTkRows;
+        const int b0 = (int)((long long)nblk * part / nparts), b1 = (int)((long long)nblk * (part + 1) / nparts);
+        const int p0 = b0 * rfx::kTkRows, p1 = std::min(c.lr_R, b1 * rfx::kTkRows);
+        const int rows = std::max(0, p1 - p0);
+        *nrows_out = rows;
+        if (!rows_host || rows == 0) return;
+        require(idx_host && val_host, RFX_ERR_ARG, "null output");
+        int* oi = (int*)c.lr_out_i.get((size_t)(b1 - b0) * rfx::kTkRows * k * 4);
+        float* ov = (float*)c.lr_out_v.get((size_t)(b1 - b0) * rfx::kTkRows * k * 4);
+        run_product(c, 0, c.lr_R, k, oi, ov, nullptr, 0, b0, b1);
+        RFX_CUDA(cudaMemcpyAsync(idx_host, oi, (size_t)rows * k * 4, cudaMemcpyDeviceToHost, c.st));
+        RFX_CUDA(cudaMemcpyAsync(val_host, ov, (size_t)rows * k * 4, cudaMemcpyDeviceToHost, c.st));
+        RFX_CUDA(cudaMemcpyAsync(rows_host, (const int*)c.lr_perm.p + p0, (size_t)rows * 4,
+                                 cudaMemcpyDeviceToHost, c.st));
         RFX_CUDA(cudaStreamSynchronize(c.st));
     });
 }

@@ -551,8 +551,9 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
                 cv[(n - 1) * kTkRows] = wv;
                 cj[(n - 1) * kTkRows] = wj;
             }
-            int* oi = a.out_idx + (size_t)(row - a.r0) * k;
-            float* ov = a.out_val + (size_t)(row - a.r0) * k;
+            const size_t orow = a.out_pos0 >= 0 ? (size_t)(pos - a.out_pos0) : (size_t)(row - a.r0);
+            int* oi = a.out_idx + orow * k;
+            float* ov = a.out_val + orow * k;
             for (int s = 0; s < k; ++s) {
                 oi[s] = s < cnt ? cj[s * kTkRows] : -1;
                 ov[s] = s < cnt ? cv[s * kTkRows] : -__int_as_float(0x7f800000);

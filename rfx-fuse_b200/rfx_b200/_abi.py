@@ -69,6 +69,7 @@ SYMBOLS = (
     "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats", "rfx_sync",
     "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk", "rfx_lowrank_product",
     "rfx_prox_apply", "rfx_lowrank_set_factors", "rfx_load_forest", "rfx_predict",
+    "rfx_lowrank_topk_part",
 )
 
 # int (*)(void* user, float* buf_dev, int64_t count): in-place sum over processes
@@ -118,6 +119,8 @@ def load_library(path: str = LIB_PATH):
     L.rfx_prox_apply.argtypes = [vp, vp, C.c_int, vp, vp]
     L.rfx_lowrank_set_factors.argtypes = [vp, C.POINTER(C.c_int8), _pf, C.c_int, C.c_int]
     L.rfx_load_forest.argtypes = [vp, C.POINTER(Forest)]
+    L.rfx_lowrank_topk_part.argtypes = [vp, C.c_int, C.c_int, C.c_int, _pi, _pi, _pf,
+                                        C.POINTER(C.c_int)]
     L.rfx_predict.argtypes = [vp, _pf, C.c_int, C.c_int, _pi, _pf, _pf]
     for name in ("rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
                  "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish",
@@ -125,7 +128,7 @@ def load_library(path: str = LIB_PATH):
                  "rfx_get_stream", "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats",
                  "rfx_sync", "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk",
                  "rfx_lowrank_product", "rfx_prox_apply", "rfx_lowrank_set_factors",
-                 "rfx_load_forest", "rfx_predict"):
+                 "rfx_load_forest", "rfx_predict", "rfx_lowrank_topk_part"):
         getattr(L, name).restype = C.c_int
     _LIB = L
     return L
@@ -304,6 +307,20 @@ class Context:
         check(self._lib.rfx_lowrank_topk(self.handle, int(k), int(r0), int(r1), ptr(idx, _pi),
                                          ptr(val, _pf)))
         return idx, val
+
+    def lowrank_topk_part(self, k: int, part: int, nparts: int):
+        """(rows int32 [m], idx int32 [m, k], val float32 [m, k]) for one share of the rows."""
+        m = C.c_int()
+        check(self._lib.rfx_lowrank_topk_part(self.handle, int(k), int(part), int(nparts), None,
+                                              None, None, C.byref(m)))
+        rows = np.zeros(m.value, np.int32)
+        idx = np.zeros((m.value, k), np.int32)
+        val = np.zeros((m.value, k), np.float32)
+        if m.value:
+            check(self._lib.rfx_lowrank_topk_part(self.handle, int(k), int(part), int(nparts),
+                                                  ptr(rows, _pi), ptr(idx, _pi), ptr(val, _pf),
+                                                  C.byref(m)))
+        return rows, idx, val
 
     def lowrank_product(self, r0: int, r1: int, R: int):
         out = np.zeros((r1 - r0, R), np.float32)

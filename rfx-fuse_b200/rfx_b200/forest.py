@@ -290,6 +290,10 @@ class _Forest:
         (indices int32 [rows, k], values float32 [rows, k]), value descending."""
         self._check_lowrank()
         R = self._lowrank_rows()
+        dist = getattr(self, "_shard_dist", None)
+        if dist is not None and row_begin == 0 and row_end is None:
+            from .shard import lowrank_topk_sharded  # collective over the fit's ranks
+            return lowrank_topk_sharded(self, k, dist)
         row_end = R if row_end is None else int(row_end)
         return self._context().lowrank_topk(int(k), int(row_begin), row_end)
 

@@ -11,7 +11,11 @@ results exact:
   rank (rank r continues from rank r-1's vector) -- a chain of point-to-point transfers of
   one [N] vector, not a reduction;
 * importance: per-tree rr rows are gathered and summed in tree order;
-* proximity: integer counts in a caller-owned device buffer, summed with one all-reduce.
+* proximity: integer counts in a caller-owned device buffer, summed with one all-reduce;
+* low-rank proximity: every rank stores its own trees' leaf groups; each sketch pass applies
+  the local trees to the block and the partial products are summed with one all-reduce
+  (the library calls back between its passes), so every rank ends with the same factors;
+  the top-k rows are then split over the ranks and gathered.
 
 The collectives are plain torch.distributed calls (NCCL over NVLink on GPUs, gloo on CPU
 for the tests); they run once per fit, outside the per-level work.
@@ -72,6 +76,31 @@ def votes_to_q(votes: np.ndarray, classwt) -> np.ndarray:
     return q
 
 
+class _DeviceFloats:
+    """Zero-copy view of `count` device floats for torch (CUDA array interface)."""
+
+    def __init__(self, ptr: int, count: int):
+        self.__cuda_array_interface__ = {"shape": (int(count),), "typestr": "<f4",
+                                         "data": (int(ptr), False), "version": 3}
+
+
+def lowrank_topk_sharded(est, k: int, dist):
+    """Top-k of all rows, split over the ranks by equal shares of the product kernel's row
+    order (rfx_lowrank_topk_part; each rank works on its own GPU from the identical factors)
+    and gathered: every rank returns the full result.  Collective: every rank must call it."""
+    rank, world = dist.get_rank(), dist.get_world_size()
+    rows, idx, val = est._context().lowrank_topk_part(int(k), rank, world)
+    parts = [None] * world
+    dist.all_gather_object(parts, (rows, idx, val))
+    R = sum(len(p[0]) for p in parts)
+    out_i = np.empty((R, k), np.int32)
+    out_v = np.empty((R, k), np.float32)
+    for r, i, v in parts:
+        out_i[r] = i
+        out_v[r] = v
+    return out_i, out_v
+
+
 def fit_sharded(est, X, y=None, dist=None, device=None):
     """Fit ``est`` (an rfx_b200 estimator) with its trees sharded over the process group.
 
@@ -112,7 +141,8 @@ def fit_sharded(est, X, y=None, dist=None, device=None):
     cat = feature_kinds(task, X, est.maxcat, est.categorical_features)
     prm = A.FitParams(task, n, p, mtry, est.minndsize, maxnode, est.iseed, 12345, est.n_bins,
                       est.maxcat, int(est.compute_importance), int(est.compute_proximity),
-                      est.prox_rows, est.batch_trees, int(task == A.TASK_REGRESSION))
+                      est.prox_rows, est.batch_trees, int(task == A.TASK_REGRESSION),
+                      est._lowrank_rank(), 0)
     ycls = np.ascontiguousarray(y, np.int32) if task == A.TASK_CLASSIFICATION else None
     yreg = np.ascontiguousarray(y, np.float32) if task == A.TASK_REGRESSION else None
     cw = None if getattr(est, "classwt", None) is None else np.ascontiguousarray(est.classwt, np.float32)
@@ -121,7 +151,7 @@ def fit_sharded(est, X, y=None, dist=None, device=None):
     ctx.load(prm, inp)
     N = 2 * n if task == A.TASK_UNSUPERVISED else n
     prox = None
-    if est.compute_proximity:
+    if est.compute_proximity and not est._lowrank_rank():
         _, length = ctx.prox_buffer()
         prox = torch.zeros(length, dtype=torch.int32, device=dev)
         torch.cuda.synchronize(dev)  # the library's stream does not order after torch's
@@ -170,6 +200,17 @@ def fit_sharded(est, X, y=None, dist=None, device=None):
         dist.all_reduce(prox)
         torch.cuda.synchronize(dev)
         est._sharded_prox = (prox, t_nout)
+    if est._lowrank_rank():
+        def reduce(ptr, count):
+            t = torch.as_tensor(_DeviceFloats(ptr, count), device=dev)
+            dist.all_reduce(t)
+            torch.cuda.synchronize(dev)
+
+        torch.cuda.synchronize(dev)
+        ctx.lowrank_build(est.rank, est.lowrank_oversample, est.lowrank_power_iters,
+                          seed=est.iseed, nout_dev=t_nout.data_ptr(), reduce=reduce)
+        est._sharded_nout = t_nout  # keeps the device counts alive
+        est._shard_dist = dist
     est.acc_ = acc
     est.n_rows_ = N
     est.nclass_ = ncl

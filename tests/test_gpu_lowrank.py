@@ -160,3 +160,11 @@ def test_topk_kernel_adversarial_factors(k):
     assert np.array_equal(val2.view(np.uint32), val_np[1234:3456].view(np.uint32))
     dense = ctx.lowrank_product(100, 300, R)
     assert np.array_equal(dense.view(np.uint32), P[100:300].view(np.uint32))
+    # shares of the kernel's row order (how a sharded fit splits the rows over GPUs)
+    seen = []
+    for part in range(3):
+        rows, ip, vp = ctx.lowrank_topk_part(k, part, 3)
+        assert np.array_equal(ip, idx_np[rows])
+        assert np.array_equal(vp.view(np.uint32), val_np[rows].view(np.uint32))
+        seen.append(rows)
+    assert np.array_equal(np.sort(np.concatenate(seen)), np.arange(R))
