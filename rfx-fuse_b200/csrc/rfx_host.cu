@@ -270,9 +270,14 @@ void load(Ctx& c, const rfx_fit_params* prm, const rfx_inputs* in) {
         D.totw = h;
     }
     {
-        const PermEntry& pe = permutation_for(c.device, (int)N);
-        D.perm = pe.perm;
-        c.perm_event = pe.done;
+        // the importance permutation (only importance reads it)
+        D.perm = nullptr;
+        c.perm_event = nullptr;
+        if (P.compute_importance) {
+            const PermEntry& pe = permutation_for(c.device, (int)N);
+            D.perm = pe.perm;
+            c.perm_event = pe.done;
+        }
     }
     // accumulators
     int* no = (int*)c.nout.get(N * 4);

@@ -77,40 +77,44 @@ __device__ __forceinline__ float inv_nout(const int* nout, int i) {
 }  // namespace
 
 // ---------------------------------------------------------------------------------------
-// Leaf groups of one batch of trees (block per tree).  For tree t:
+// Leaf groups of one batch of trees.  For tree t:
 //   code[t][row]  = 2*l (in-bag) or 2*l+1 (OOB) for rows < R, l the leaf's rank among the
 //                   tree's terminal nodes in node order; kNoGroup for rows >= R;
 //   order[t][...] = rows grouped by code: group g occupies [goff[t][g], goff[t][g+1]);
-//                   in-bag rows in their growth-segment order, OOB rows ascending;
+//                   in-bag rows in their growth-segment order (ascending), OOB rows ascending;
 //   ngroups[t]    = 2 * leaves.
-// tmp holds 2*M ints per tree (leaf rank of every node, then OOB cursors per leaf).
+// Built by k_lr_count (block per tree: leaf ranks, group sizes, offsets), k_lr_inbag (warp
+// per terminal node: the segment's rows), k_lr_oob_keys + a radix sort of the batch's
+// (tree, leaf, row) keys + k_lr_oob_place (the OOB rows, ascending inside each group).
+// lidx / oprefix: [T][M] ints (leaf rank of every node; exclusive prefix of the OOB group
+// sizes over leaves); noob_r[t]: the tree's OOB rows below R.
 // ---------------------------------------------------------------------------------------
-__global__ void k_lr_groups(Batch B, int N, int R, int G, uint16_t* __restrict__ code,
-                            int* __restrict__ order, int* __restrict__ goff,
-                            int* __restrict__ ngroups, int* __restrict__ tmp) {
+__global__ void k_lr_count(Batch B, int N, int R, int G, int* __restrict__ goff,
+                           int* __restrict__ ngroups, int* __restrict__ lidx_all,
+                           int* __restrict__ oprefix_all, int* __restrict__ noob_r) {
     __shared__ int wtot[32];
     const int t = blockIdx.x, M = B.M;
     const int nn = B.nnode[t];
     const int* status = B.status + (size_t)t * M;
-    int* lidx = tmp + (size_t)t * 2 * M;
-    int* cur = lidx + M;
-    uint16_t* ct = code + (size_t)t * N;
-    int* ot = order + (size_t)t * N;
+    int* lidx = lidx_all + (size_t)t * M;
+    int* opre = oprefix_all + (size_t)t * M;
     int* gt = goff + (size_t)t * G;
-    for (int i = threadIdx.x; i < N; i += blockDim.x) ct[i] = kNoGroup;
     for (int m = threadIdx.x; m < nn; m += blockDim.x) lidx[m] = status[m] == -1 ? 1 : 0;
     __syncthreads();
     const int L = block_scan_inplace(lidx, nn, wtot);  // lidx[m] = leaf rank of leaf m
     for (int g = threadIdx.x; g <= 2 * L; g += blockDim.x) gt[g] = 0;
+    for (int l = threadIdx.x; l < L; l += blockDim.x) opre[l] = 0;
     __syncthreads();
-    // group sizes: distinct in-bag rows of the leaf below R, OOB rows of the leaf below R
     for (int m = threadIdx.x; m < nn; m += blockDim.x) {
         if (status[m] != -1) continue;
         const size_t nm = (size_t)t * M + m;
-        const int* seg = B.seg[B.nd_buf[nm]] + (size_t)t * N + B.nd_start[nm];
         const int c = B.nd_cnt[nm];
-        int k = 0;
-        for (int q = 0; q < c; ++q) k += seg[q] < R ? 1 : 0;
+        int k = c;
+        if (R < N) {
+            const int* seg = B.seg[B.nd_buf[nm]] + (size_t)t * N + B.nd_start[nm];
+            k = 0;
+            for (int q = 0; q < c; ++q) k += seg[q] < R ? 1 : 0;
+        }
         gt[2 * lidx[m]] = k;
     }
     const int noob = B.noob[t];
@@ -119,50 +123,87 @@ __global__ void k_lr_groups(Batch B, int N, int R, int G, uint16_t* __restrict__
     __syncthreads();
     for (int i = threadIdx.x; i < noob; i += blockDim.x) {
         const int row = oob[i];
-        if (row < R) atomicAdd(&gt[2 * lidx[oleaf[row]] + 1], 1);
+        if (row < R) {
+            const int l = lidx[oleaf[row]];
+            atomicAdd(&gt[2 * l + 1], 1);
+            atomicAdd(&opre[l], 1);
+        }
     }
     __syncthreads();
+    const int tot_oob = block_scan_inplace(opre, L, wtot);
     block_scan_inplace(gt, 2 * L + 1, wtot);  // gt[g] = start of group g, gt[2L] = total
-    __syncthreads();
-    // in-bag rows: copy the leaf's segment (thread per leaf)
-    for (int m = threadIdx.x; m < nn; m += blockDim.x) {
-        if (status[m] != -1) continue;
-        const size_t nm = (size_t)t * M + m;
-        const int* seg = B.seg[B.nd_buf[nm]] + (size_t)t * N + B.nd_start[nm];
-        const int c = B.nd_cnt[nm];
-        const int l = lidx[m];
-        int pos = gt[2 * l];
-        for (int q = 0; q < c; ++q) {
-            const int row = seg[q];
-            if (row >= R) continue;
-            ot[pos++] = row;
+    if (threadIdx.x == 0) {
+        ngroups[t] = 2 * L;
+        noob_r[t] = tot_oob;
+    }
+}
+
+// In-bag rows (< R) of every terminal node into its group, segment order kept (warp per node).
+__global__ void k_lr_inbag(Batch B, int N, int R, int G, const int* __restrict__ lidx_all,
+                           const int* __restrict__ goff, uint16_t* __restrict__ code,
+                           int* __restrict__ order) {
+    const int t = blockIdx.y, M = B.M;
+    const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (m >= B.nnode[t]) return;
+    const size_t nm = (size_t)t * M + m;
+    if (B.status[nm] != -1) return;
+    const int l = lidx_all[(size_t)t * M + m];
+    const int* seg = B.seg[B.nd_buf[nm]] + (size_t)t * N + B.nd_start[nm];
+    const int c = B.nd_cnt[nm];
+    int pos = goff[(size_t)t * G + 2 * l];
+    int* ot = order + (size_t)t * N;
+    uint16_t* ct = code + (size_t)t * N;
+    for (int q0 = 0; q0 < c; q0 += 32) {
+        const int q = q0 + lane;
+        const int row = q < c ? seg[q] : R;
+        const bool keep = row < R;
+        const unsigned bal = __ballot_sync(0xffffffffu, keep);
+        if (keep) {
+            ot[pos + __popc(bal & ((1u << lane) - 1u))] = row;
             ct[row] = (uint16_t)(2 * l);
         }
-        cur[l] = gt[2 * l + 1];
+        pos += __popc(bal);
     }
-    __syncthreads();
-    // OOB rows: placed through per-leaf cursors, then each group sorted ascending
-    for (int i = threadIdx.x; i < noob; i += blockDim.x) {
-        const int row = oob[i];
-        if (row >= R) continue;
-        const int l = lidx[oleaf[row]];
-        ot[atomicAdd(&cur[l], 1)] = row;
-        ct[row] = (uint16_t)(2 * l + 1);
-    }
-    __syncthreads();
-    for (int l = threadIdx.x; l < L; l += blockDim.x) {
-        const int a = gt[2 * l + 1], b = gt[2 * l + 2];
-        for (int i = a + 1; i < b; ++i) {
-            const int v = ot[i];
-            int j = i - 1;
-            while (j >= a && ot[j] > v) {
-                ot[j + 1] = ot[j];
-                --j;
-            }
-            ot[j + 1] = v;
+}
+
+// One key (tree << 40 | leaf rank << 24 | row) per OOB row below R; nkeys counts them.
+__global__ void k_lr_oob_keys(Batch B, int N, int R, const int* __restrict__ lidx_all,
+                              uint16_t* __restrict__ code, unsigned long long* __restrict__ keys,
+                              int* __restrict__ nkeys) {
+    const int t = blockIdx.y, M = B.M;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int lane = threadIdx.x & 31;
+    bool have = false;
+    unsigned long long key = 0;
+    if (i < B.noob[t]) {
+        const int row = B.oob[(size_t)t * N + i];
+        if (row < R) {
+            const int l = lidx_all[(size_t)t * M + B.oob_leaf[(size_t)t * N + row]];
+            code[(size_t)t * N + row] = (uint16_t)(2 * l + 1);
+            key = ((unsigned long long)t << 40) | ((unsigned long long)l << 24) | (unsigned long long)row;
+            have = true;
         }
     }
-    if (threadIdx.x == 0) ngroups[t] = 2 * L;
+    const unsigned bal = __ballot_sync(0xffffffffu, have);
+    int base = 0;
+    if (lane == 0 && bal) base = atomicAdd(nkeys, __popc(bal));
+    base = __shfl_sync(0xffffffffu, base, 0);
+    if (have) keys[base + __popc(bal & ((1u << lane) - 1u))] = key;
+}
+
+// Sorted keys -> OOB group slots: key i of tree t, leaf l sits at goff[t][2l+1] + its rank
+// among the tree's leaf-l keys (i - obase[t] - oprefix[t][l]).
+__global__ void k_lr_oob_place(const unsigned long long* __restrict__ keys, int nkeys, int N, int M,
+                               int G, const int* __restrict__ obase,
+                               const int* __restrict__ oprefix_all, const int* __restrict__ goff,
+                               int* __restrict__ order) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= nkeys) return;
+    const unsigned long long key = keys[i];
+    const int t = (int)(key >> 40), l = (int)((key >> 24) & 0xFFFFu), row = (int)(key & 0xFFFFFFu);
+    const int rank = i - obase[t] - oprefix_all[(size_t)t * M + l];
+    order[(size_t)t * N + goff[(size_t)t * G + 2 * l + 1] + rank] = row;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -184,7 +225,26 @@ __global__ void k_lr_leafsum(const int* __restrict__ order, const int* __restric
     float acc[NQ];
 #pragma unroll
     for (int q = 0; q < NQ; ++q) acc[q] = 0.0f;
-    for (int k = a; k < b; ++k) {
+    int k = a;
+    for (; k + 4 <= b; k += 4) {  // four rows in flight, added in group order
+        const float* z0 = Z + (size_t)ot[k] * W + lane;
+        const float* z1 = Z + (size_t)ot[k + 1] * W + lane;
+        const float* z2 = Z + (size_t)ot[k + 2] * W + lane;
+        const float* z3 = Z + (size_t)ot[k + 3] * W + lane;
+        float v[4][NQ];
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+            v[0][q] = __ldg(z0 + 32 * q);
+            v[1][q] = __ldg(z1 + 32 * q);
+            v[2][q] = __ldg(z2 + 32 * q);
+            v[3][q] = __ldg(z3 + 32 * q);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int q = 0; q < NQ; ++q) acc[q] += v[u][q];
+    }
+    for (; k < b; ++k) {
         const float* z = Z + (size_t)ot[k] * W + lane;
 #pragma unroll
         for (int q = 0; q < NQ; ++q) acc[q] += __ldg(z + 32 * q);
@@ -318,24 +378,26 @@ __global__ void k_lr_gram(const float* __restrict__ A, int ra, const float* __re
     }
 }
 
-// G = sum of the partials in block order; symmetrise when `sym` ((G + G^T) / 2).
+// G = sum of the partials in block order (thread per entry).
 __global__ void k_lr_gram_reduce(const double* __restrict__ part, int nblk, int ra, int rb,
                                  int sym, double* __restrict__ G) {
+    (void)sym;
     const int nent = ra * rb;
     for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < nent; idx += gridDim.x * blockDim.x) {
         double s = 0.0;
         for (int b = 0; b < nblk; ++b) s += part[(size_t)b * nent + idx];
         G[idx] = s;
     }
-    if (sym) {
-        __syncthreads();  // single-block launch when sym
-        for (int idx = threadIdx.x; idx < nent; idx += blockDim.x) {
-            const int a = idx / rb, c = idx % rb;
-            if (a < c) {
-                const double m = 0.5 * (G[a * rb + c] + G[c * rb + a]);
-                G[a * rb + c] = m;
-                G[c * rb + a] = m;
-            }
+}
+
+// G <- (G + G^T) / 2 (one block).
+__global__ void k_lr_symmetrize(double* __restrict__ G, int r) {
+    for (int idx = threadIdx.x; idx < r * r; idx += blockDim.x) {
+        const int a = idx / r, c = idx % r;
+        if (a < c) {
+            const double m = 0.5 * (G[a * r + c] + G[c * r + a]);
+            G[a * r + c] = m;
+            G[c * r + a] = m;
         }
     }
 }

@@ -44,8 +44,15 @@ struct TopkArgs {
                                // polls, MMA wait polls, load wait polls
 };
 
-__global__ void k_lr_groups(Batch B, int N, int R, int G, uint16_t* code, int* order, int* goff,
-                            int* ngroups, int* tmp);
+__global__ void k_lr_count(Batch B, int N, int R, int G, int* goff, int* ngroups, int* lidx_all,
+                           int* oprefix_all, int* noob_r);
+__global__ void k_lr_inbag(Batch B, int N, int R, int G, const int* lidx_all, const int* goff,
+                           uint16_t* code, int* order);
+__global__ void k_lr_oob_keys(Batch B, int N, int R, const int* lidx_all, uint16_t* code,
+                              unsigned long long* keys, int* nkeys);
+__global__ void k_lr_oob_place(const unsigned long long* keys, int nkeys, int N, int M, int G,
+                               const int* obase, const int* oprefix_all, const int* goff,
+                               int* order);
 // k_lr_leafsum / k_lr_scatter for a sketch width of 32 * nq columns (1 <= nq <= 8);
 // false for another width.
 bool lr_launch_leafsum(int nq, dim3 grid, cudaStream_t st, const int* order, const int* goff,
@@ -59,6 +66,7 @@ __global__ void k_lr_omega(float* X, int R, int r, unsigned long long seed);
 __global__ void k_lr_gram(const float* A, int ra, const float* Bm, int rb, int R, int rows_per_block,
                           double* part);
 __global__ void k_lr_gram_reduce(const double* part, int nblk, int ra, int rb, int sym, double* G);
+__global__ void k_lr_symmetrize(double* G, int r);
 __global__ void k_lr_chol_inv(const double* Gm, int r, double* Uinv);
 __global__ void k_lr_rowmat(const float* Y, int R, int rin, const double* Mat, int rout, float* Out);
 __global__ void k_lr_eig_select(const double* Tm, int r, int k, double* Mk, double* lam_out);

@@ -90,14 +90,19 @@ void set_smem(const void* f, size_t bytes) {
 void gram(Ctx& c, const float* A, int ra, const float* B, int rb, int sym, double* G) {
     cudaStream_t st = c.st;
     const int R = c.R;
-    const int nblk = (int)std::max(1LL, std::min<long long>((R + 255) / 256, (long long)c.sm_count * 8));
+    const int nblk = (int)std::max(1LL, std::min<long long>((R + 255) / 256, (long long)c.sm_count * 2));
     const int rpb = (int)round_up((R + nblk - 1) / nblk, 32);
     double* part = (double*)c.lr_part.get((size_t)nblk * ra * rb * 8);
     rfx::k_lr_gram<<<nblk, 256, 0, st>>>(A, ra, B, rb, R, rpb, part);
     RFX_LAUNCH("k_lr_gram");
-    rfx::k_lr_gram_reduce<<<1, 256, 0, st>>>(part, nblk, ra, rb, sym, G);
+    rfx::k_lr_gram_reduce<<<(ra * rb + 127) / 128, 128, 0, st>>>(part, nblk, ra, rb, sym, G);
     RFX_LAUNCH("k_lr_gram_reduce");
     c.launches += 2;
+    if (sym) {
+        rfx::k_lr_symmetrize<<<1, 256, 0, st>>>(G, ra);
+        RFX_LAUNCH("k_lr_symmetrize");
+        c.launches += 1;
+    }
 }
 
 // Q = orthonormal basis of range(Y) by Cholesky-QR twice; Y is overwritten.
@@ -317,15 +322,55 @@ void lr_reserve(Ctx& c, int extra) {
 
 void lr_store_batch(Ctx& c, const rfx::Batch& B, int T) {
     lr_reserve(c, T);
-    const size_t N = c.N, G = c.lr_G;
-    int* tmp = (int*)c.lr_tmp.get((size_t)T * 2 * c.M * 4);
-    rfx::k_lr_groups<<<T, 1024, 0, c.st>>>(B, c.N, c.R, c.lr_G,
-                                           (uint16_t*)c.lr_code.p + (size_t)c.lr_n * N,
-                                           (int*)c.lr_order.p + (size_t)c.lr_n * N,
-                                           (int*)c.lr_goff.p + (size_t)c.lr_n * G,
-                                           (int*)c.lr_ngroups.p + c.lr_n, tmp);
-    RFX_LAUNCH("k_lr_groups");
-    c.launches += 1;
+    cudaStream_t st = c.st;
+    const size_t N = c.N, G = c.lr_G, M = c.M;
+    require(N < (1u << 24) && M <= 65535 && T <= 4096, RFX_ERR_UNSUPPORTED,
+            "low-rank leaf groups need < 2^24 rows, maxnode < 65536, <= 4096 trees per batch");
+    uint16_t* code = (uint16_t*)c.lr_code.p + (size_t)c.lr_n * N;
+    int* order = (int*)c.lr_order.p + (size_t)c.lr_n * N;
+    int* goff = (int*)c.lr_goff.p + (size_t)c.lr_n * G;
+    int* ngroups = (int*)c.lr_ngroups.p + c.lr_n;
+    int* tmp = (int*)c.lr_tmp.get((size_t)T * 2 * M * 4 + (size_t)(2 * T + 2) * 4);
+    int* lidx = tmp;
+    int* opre = tmp + (size_t)T * M;
+    int* noob_r = tmp + (size_t)2 * T * M;
+    int* nkeys_d = noob_r + T;
+    int* obase_d = (int*)c.lr_ids.get((size_t)(T + 1) * 4);
+    RFX_CUDA(cudaMemsetAsync(code, 0xFF, (size_t)T * N * 2, st));
+    RFX_CUDA(cudaMemsetAsync(nkeys_d, 0, 4, st));
+    rfx::k_lr_count<<<T, 1024, 0, st>>>(B, c.N, c.R, c.lr_G, goff, ngroups, lidx, opre, noob_r);
+    RFX_LAUNCH("k_lr_count");
+    rfx::k_lr_inbag<<<dim3((unsigned)((M + 7) / 8), (unsigned)T), 256, 0, st>>>(B, c.N, c.R, c.lr_G,
+                                                                               lidx, goff, code, order);
+    RFX_LAUNCH("k_lr_inbag");
+    unsigned long long* keys = (unsigned long long*)c.lr_keys.get((size_t)T * N * 8);
+    unsigned long long* sorted = (unsigned long long*)c.lr_order_s.get((size_t)T * N * 8);
+    rfx::k_lr_oob_keys<<<dim3((unsigned)((N + 255) / 256), (unsigned)T), 256, 0, st>>>(
+        B, c.N, c.R, lidx, code, keys, nkeys_d);
+    RFX_LAUNCH("k_lr_oob_keys");
+    std::vector<int> hv(T + 1);
+    RFX_CUDA(cudaMemcpyAsync(hv.data(), noob_r, (size_t)(T + 1) * 4, cudaMemcpyDeviceToHost, st));
+    RFX_CUDA(cudaStreamSynchronize(st));
+    const int nkeys = hv[T];
+    std::vector<int> ob(T);
+    for (int t = 0, a = 0; t < T; ++t) {
+        ob[t] = a;
+        a += hv[t];
+    }
+    RFX_CUDA(cudaMemcpyAsync(obase_d, ob.data(), (size_t)T * 4, cudaMemcpyHostToDevice, st));
+    int end_bit = 41;
+    while ((1 << (end_bit - 40)) < T) ++end_bit;
+    size_t tmp_bytes = 0;
+    RFX_CUDA(cub::DeviceRadixSort::SortKeys(nullptr, tmp_bytes, keys, sorted, nkeys, 0, end_bit, st));
+    void* ctmp = c.lr_cub.get(tmp_bytes);
+    RFX_CUDA(cub::DeviceRadixSort::SortKeys(ctmp, tmp_bytes, keys, sorted, nkeys, 0, end_bit, st));
+    if (nkeys > 0) {
+        rfx::k_lr_oob_place<<<(nkeys + 255) / 256, 256, 0, st>>>(sorted, nkeys, c.N, (int)M, c.lr_G,
+                                                                 obase_d, opre, goff, order);
+        RFX_LAUNCH("k_lr_oob_place");
+    }
+    RFX_CUDA(cudaStreamSynchronize(st));  // ob is a host vector
+    c.launches += 4;
     c.lr_n += T;
     c.lr_ready = false;
 }
