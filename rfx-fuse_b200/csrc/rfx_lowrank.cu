@@ -138,32 +138,37 @@ __global__ void k_lr_count(Batch B, int N, int R, int G, int* __restrict__ goff,
     }
 }
 
-// In-bag rows (< R) of every terminal node into its group, segment order kept (warp per node).
-__global__ void k_lr_inbag(Batch B, int N, int R, int G, const int* __restrict__ lidx_all,
+// In-bag rows (< R) of every terminal node into its group, segment order kept (grid-stride
+// warps over (tree, node)).
+__global__ void k_lr_inbag(Batch B, int N, int R, int G, int T, const int* __restrict__ lidx_all,
                            const int* __restrict__ goff, uint16_t* __restrict__ code,
                            int* __restrict__ order) {
-    const int t = blockIdx.y, M = B.M;
-    const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int M = B.M;
     const int lane = threadIdx.x & 31;
-    if (m >= B.nnode[t]) return;
-    const size_t nm = (size_t)t * M + m;
-    if (B.status[nm] != -1) return;
-    const int l = lidx_all[(size_t)t * M + m];
-    const int* seg = B.seg[B.nd_buf[nm]] + (size_t)t * N + B.nd_start[nm];
-    const int c = B.nd_cnt[nm];
-    int pos = goff[(size_t)t * G + 2 * l];
-    int* ot = order + (size_t)t * N;
-    uint16_t* ct = code + (size_t)t * N;
-    for (int q0 = 0; q0 < c; q0 += 32) {
-        const int q = q0 + lane;
-        const int row = q < c ? seg[q] : R;
-        const bool keep = row < R;
-        const unsigned bal = __ballot_sync(0xffffffffu, keep);
-        if (keep) {
-            ot[pos + __popc(bal & ((1u << lane) - 1u))] = row;
-            ct[row] = (uint16_t)(2 * l);
+    const long long nwarps = (long long)gridDim.x * (blockDim.x >> 5);
+    const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    for (int t = 0; t < T; ++t)
+    for (long long mm = wid, nn = B.nnode[t]; mm < nn; mm += nwarps) {
+        const int m = (int)mm;
+        const size_t nm = (size_t)t * M + m;
+        if (B.status[nm] != -1) continue;
+        const int l = lidx_all[nm];
+        const int* seg = B.seg[B.nd_buf[nm]] + (size_t)t * N + B.nd_start[nm];
+        const int c = B.nd_cnt[nm];
+        int pos = goff[(size_t)t * G + 2 * l];
+        int* ot = order + (size_t)t * N;
+        uint16_t* ct = code + (size_t)t * N;
+        for (int q0 = 0; q0 < c; q0 += 32) {
+            const int q = q0 + lane;
+            const int row = q < c ? seg[q] : R;
+            const bool keep = row < R;
+            const unsigned bal = __ballot_sync(0xffffffffu, keep);
+            if (keep) {
+                ot[pos + __popc(bal & ((1u << lane) - 1u))] = row;
+                ct[row] = (uint16_t)(2 * l);
+            }
+            pos += __popc(bal);
         }
-        pos += __popc(bal);
     }
 }
 
@@ -212,8 +217,9 @@ __global__ void k_lr_oob_place(const unsigned long long* __restrict__ keys, int 
 // ---------------------------------------------------------------------------------------
 template <int NQ>
 __global__ void k_lr_leafsum(const int* __restrict__ order, const int* __restrict__ goff,
-                             const int* __restrict__ ngroups, int N, int G,
+                             const int* __restrict__ ngroups, int N, int G, int T,
                              const float* __restrict__ Z, float* __restrict__ LS) {
+    (void)T;
     const int t = blockIdx.y;
     const int g = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
@@ -280,9 +286,9 @@ __global__ void k_lr_scatter(const uint16_t* __restrict__ code, int N, int R, in
 
 
 bool lr_launch_leafsum(int nq, dim3 grid, cudaStream_t st, const int* order, const int* goff,
-                       const int* ngroups, int N, int G, const float* Z, float* LS) {
+                       const int* ngroups, int N, int G, int T, const float* Z, float* LS) {
     switch (nq) {
-#define RFX_LS(Q) case Q: k_lr_leafsum<Q><<<grid, 256, 0, st>>>(order, goff, ngroups, N, G, Z, LS); return true;
+#define RFX_LS(Q) case Q: k_lr_leafsum<Q><<<grid, 256, 0, st>>>(order, goff, ngroups, N, G, T, Z, LS); return true;
         RFX_LS(1) RFX_LS(2) RFX_LS(3) RFX_LS(4) RFX_LS(5) RFX_LS(6) RFX_LS(7) RFX_LS(8)
 #undef RFX_LS
         default: return false;

@@ -46,8 +46,8 @@ struct TopkArgs {
 
 __global__ void k_lr_count(Batch B, int N, int R, int G, int* goff, int* ngroups, int* lidx_all,
                            int* oprefix_all, int* noob_r);
-__global__ void k_lr_inbag(Batch B, int N, int R, int G, const int* lidx_all, const int* goff,
-                           uint16_t* code, int* order);
+__global__ void k_lr_inbag(Batch B, int N, int R, int G, int T, const int* lidx_all,
+                           const int* goff, uint16_t* code, int* order);
 __global__ void k_lr_oob_keys(Batch B, int N, int R, const int* lidx_all, uint16_t* code,
                               unsigned long long* keys, int* nkeys);
 __global__ void k_lr_oob_place(const unsigned long long* keys, int nkeys, int N, int M, int G,
@@ -56,7 +56,7 @@ __global__ void k_lr_oob_place(const unsigned long long* keys, int nkeys, int N,
 // k_lr_leafsum / k_lr_scatter for a sketch width of 32 * nq columns (1 <= nq <= 8);
 // false for another width.
 bool lr_launch_leafsum(int nq, dim3 grid, cudaStream_t st, const int* order, const int* goff,
-                       const int* ngroups, int N, int G, const float* Z, float* LS);
+                       const int* ngroups, int N, int G, int T, const float* Z, float* LS);
 bool lr_launch_scatter(int nq, int grid, cudaStream_t st, const uint16_t* code, int N, int R, int T,
                        int G, const float* LS, float* Y);
 __global__ void k_lr_prep(const float* X, int R, int r, const int* nout, int W, float* Z);

@@ -42,8 +42,8 @@ void apply_counts(Ctx& c, const float* Z, int W, float* CZ) {
     for (int t0 = 0; t0 < c.lr_n; t0 += Tc) {
         const int T = std::min(Tc, c.lr_n - t0);
         const dim3 g((unsigned)((G - 1 + 7) / 8), (unsigned)T);
-        require(rfx::lr_launch_leafsum(nq, g, st, order + (size_t)t0 * N, goff + (size_t)t0 * G,
-                                       ng + t0, N, G, Z, LS),
+        require(rfx::lr_launch_leafsum(nq, g, st, order + (size_t)t0 * N,
+                                       goff + (size_t)t0 * G, ng + t0, N, G, T, Z, LS),
                 RFX_ERR_ARG, "sketch width out of range");
         RFX_LAUNCH("k_lr_leafsum");
         rfx::lr_launch_scatter(nq, (R + 7) / 8, st, code + (size_t)t0 * N, N, R, T, G, LS, CZ);
@@ -340,8 +340,7 @@ void lr_store_batch(Ctx& c, const rfx::Batch& B, int T) {
     RFX_CUDA(cudaMemsetAsync(nkeys_d, 0, 4, st));
     rfx::k_lr_count<<<T, 1024, 0, st>>>(B, c.N, c.R, c.lr_G, goff, ngroups, lidx, opre, noob_r);
     RFX_LAUNCH("k_lr_count");
-    rfx::k_lr_inbag<<<dim3((unsigned)((M + 7) / 8), (unsigned)T), 256, 0, st>>>(B, c.N, c.R, c.lr_G,
-                                                                               lidx, goff, code, order);
+    rfx::k_lr_inbag<<<c.sm_count * 8, 256, 0, st>>>(B, c.N, c.R, c.lr_G, T, lidx, goff, code, order);
     RFX_LAUNCH("k_lr_inbag");
     unsigned long long* keys = (unsigned long long*)c.lr_keys.get((size_t)T * N * 8);
     unsigned long long* sorted = (unsigned long long*)c.lr_order_s.get((size_t)T * N * 8);
