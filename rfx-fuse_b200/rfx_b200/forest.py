@@ -70,7 +70,7 @@ class _Forest:
     def __init__(self, nsample=1000, ntree=100, mdim=10, nclass=2, maxcat=10, mtry=0,
                  maxnode=0, minndsize=1, ncsplit=25, ncmax=25, iseed=12345,
                  compute_proximity=False, compute_importance=True,
-                 compute_local_importance=False, use_gpu=True, use_qlora=False,
+                 compute_local_importance=False, use_gpu=False, use_qlora=False,
                  quant_mode="nf4", use_sparse=False, sparsity_threshold=1e-6, batch_size=0,
                  nodesize=5, cutoff=0.01, show_progress=True, progress_desc="",
                  gpu_loss_function="gini", rank=32, power_iterations=30, n_threads_cpu=0,
@@ -79,7 +79,7 @@ class _Forest:
                  compute_leaf_assignments=False, categorical_features=None,
                  use_histogram=True, n_bins=256, class_weight="", classwt=None,
                  device=0, prox_rows=0, batch_trees=0, lowrank_oversample=16,
-                 lowrank_power_iters=1):
+                 lowrank_power_iters=1, synthetic_ratio=1.0):
         if use_casewise:
             raise NotImplementedError("use_casewise=True is not implemented on the device path")
         if use_rfgap:
@@ -115,6 +115,16 @@ class _Forest:
         self.prox_rows = int(prox_rows)
         self.batch_trees = int(batch_trees)
         self.nodesize = int(nodesize)  # stored, never read by the growers (as in the reference)
+        # stored as given, for the model file (model_io): not used by the device path
+        self.ncsplit, self.ncmax = int(ncsplit), int(ncmax)
+        self.use_gpu, self.use_sparse = bool(use_gpu), bool(use_sparse)
+        self.sparsity_threshold, self.cutoff = float(sparsity_threshold), float(cutoff)
+        self.batch_size, self.n_threads_cpu = int(batch_size), int(n_threads_cpu)
+        self.gpu_loss_function, self.power_iterations = str(gpu_loss_function), int(power_iterations)
+        self.importance_method, self.clique_M = str(importance_method), int(clique_M)
+        self.compute_proximity_importance = bool(compute_proximity_importance)
+        self.compute_leaf_assignments = bool(compute_leaf_assignments)
+        self.synthetic_ratio = float(synthetic_ratio)
         self._mtry_arg = int(mtry)
         self._maxnode = calculate_maxnode(self.nsample, self.minndsize, int(maxnode))
         self._mtry = self._resolve_mtry_ctor(int(mtry))
@@ -212,6 +222,14 @@ class _Forest:
     def _check(self):
         if not self._fitted:
             raise RuntimeError("Model must be fitted first")
+
+    def save(self, filepath):
+        """Write the model as the reference's RFX0 v1 file (RandomForest::save,
+        src/rf_random_forest.cpp:6037-6140); RFXFuse.load() reads it."""
+        if not self._fitted:
+            raise RuntimeError("Model must be fitted before saving")
+        from . import model_io
+        model_io.write(str(filepath), model_io.from_estimator(self))
 
     # ---- reference getters
     def feature_importances_(self):
@@ -402,6 +420,7 @@ class RandomForestRegressor(_Forest):
 
     def __init__(self, *args, **kw):
         kw.setdefault("compute_proximity", False)
+        kw.setdefault("gpu_loss_function", "mse")
         super().__init__(*args, **kw)
 
     def fit(self, X, y, sample_weights=None):
@@ -443,6 +462,7 @@ class RandomForestUnsupervised(_Classifying):
     def __init__(self, nsample=1000, ntree=100, mdim=10, maxcat=10, mtry=0, maxnode=0,
                  minndsize=1, ncsplit=25, ncmax=25, iseed=12345, compute_proximity=True,
                  compute_importance=True, **kw):
+        kw.setdefault("rank", 100)  # python/randomforest_py.cpp:5934-5974 defaults
         super().__init__(nsample=nsample, ntree=ntree, mdim=mdim, maxcat=maxcat, mtry=mtry,
                          maxnode=maxnode, minndsize=minndsize, ncsplit=ncsplit, ncmax=ncmax,
                          iseed=iseed, compute_proximity=compute_proximity,

@@ -52,6 +52,17 @@ CASES = {
 }
 
 
+def save_gz(model, path):
+    """model.save() (RFX0) gzip-compressed: the tree arrays are mostly zeros."""
+    import gzip
+    import tempfile
+    with tempfile.TemporaryDirectory() as d:
+        raw = os.path.join(d, "m.rfx")
+        model.save(raw)
+        with open(raw, "rb") as f, gzip.GzipFile(path, "wb", mtime=0) as g:
+            g.write(f.read())
+
+
 def predict_data(kind, n, p, seed, n_new):
     """Training data plus new rows for predict(): column p is a 5-level categorical; the new
     rows carry out-of-range categories and NaNs (the reference's edge branches)."""
@@ -94,6 +105,7 @@ def predict_golden():
             m = R.RandomForestRegressor(**common)
             m.fit(X, y)
             d = {"pred": np.asarray(m.predict(Xn))}
+        save_gz(m, os.path.join(HERE, f"{name}.rfx.gz"))  # the reference's RFX0 model file
         d.update(X=X, y=y, Xn=Xn, cat=cat, maxnode=np.int32(oracle.maxnode(n, kw["minndsize"], 0)))
         out[name] = d
     return out
@@ -129,6 +141,13 @@ def main():
     binning = {"X": Xb, "cat": cat, "edges": e, "nb": nb, "kind": kind, "xb": xb,
                "edges16": e16, "nb16": nb16, "kind16": kind16, "xb16": xb16}
     out.update(predict_golden())
+    # an unsupervised model file (RandomForestUnsupervised.save)
+    Xu, _ = synth("gmm", 300, 6, 5)
+    u = oracle.ref_module().RandomForestUnsupervised(nsample=300, ntree=2, mtry=2, minndsize=1,
+                                                     show_progress=False)
+    u.fit(Xu)
+    save_gz(u, os.path.join(HERE, "unsup_model.rfx.gz"))
+    out["unsup_model"] = {"X": Xu}
     for name, d in out.items():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **d)
     np.savez_compressed(os.path.join(HERE, "bootstrap.npz"), **boot)
