@@ -226,6 +226,21 @@ int rfx_load_forest(void* ctx, const rfx_forest* forest);
 int rfx_predict(void* ctx, const float* X_host, int n, int p, int* class_out, float* proba_out,
                 float* value_out);
 
+/* ---- Proximity-weighted imputation ---------------------------------------------------
+ * One round of rfx_impute_proximity's fill (python/rfx_impute.py:730-775, aggregation
+ * 'mean', top_k None) from this context's dense proximity counts (a fit over n rows with
+ * compute_proximity; n == its proximity rows).  xc_host [p][n] column-major current values,
+ * miss_host [p][n] (1 = missing in the original data), is_cat_host [p]; cells_host
+ * [ncells][2] (row, column) of the cells to fill, sorted by row; out_host [ncells] the new
+ * value, or NaN where no other observed row has positive proximity (the reference keeps
+ * the old value).  Continuous: proximity-weighted mean with the weights normalised first;
+ * categorical: the value with the largest proximity sum (ascending values, first maximum);
+ * every sum is numpy's pairwise float32 summation, so the values are the reference's, bit
+ * for bit. */
+int rfx_impute_round(void* ctx, const float* xc_host, const uint8_t* miss_host,
+                     const uint8_t* is_cat_host, int n, int p, const int* cells_host, int ncells,
+                     float* out_host);
+
 /* ---- Low-rank proximity (use_qlora=True, quant_mode="int8") --------------------------
  * Replaces LowRankProximityMatrix (include/rf_proximity_lowrank.hpp:27-439,
  * cuda/rf_proximity_lowrank.cu:414-1340) and get_lowrank_factors

@@ -69,7 +69,7 @@ SYMBOLS = (
     "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats", "rfx_sync",
     "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk", "rfx_lowrank_product",
     "rfx_prox_apply", "rfx_lowrank_set_factors", "rfx_load_forest", "rfx_predict",
-    "rfx_lowrank_topk_part",
+    "rfx_lowrank_topk_part", "rfx_impute_round",
 )
 
 # int (*)(void* user, float* buf_dev, int64_t count): in-place sum over processes
@@ -119,6 +119,7 @@ def load_library(path: str = LIB_PATH):
     L.rfx_prox_apply.argtypes = [vp, vp, C.c_int, vp, vp]
     L.rfx_lowrank_set_factors.argtypes = [vp, C.POINTER(C.c_int8), _pf, C.c_int, C.c_int]
     L.rfx_load_forest.argtypes = [vp, C.POINTER(Forest)]
+    L.rfx_impute_round.argtypes = [vp, _pf, _pu8, _pu8, C.c_int, C.c_int, _pi, C.c_int, _pf]
     L.rfx_lowrank_topk_part.argtypes = [vp, C.c_int, C.c_int, C.c_int, _pi, _pi, _pf,
                                         C.POINTER(C.c_int)]
     L.rfx_predict.argtypes = [vp, _pf, C.c_int, C.c_int, _pi, _pf, _pf]
@@ -128,7 +129,8 @@ def load_library(path: str = LIB_PATH):
                  "rfx_get_stream", "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats",
                  "rfx_sync", "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk",
                  "rfx_lowrank_product", "rfx_prox_apply", "rfx_lowrank_set_factors",
-                 "rfx_load_forest", "rfx_predict", "rfx_lowrank_topk_part"):
+                 "rfx_load_forest", "rfx_predict", "rfx_lowrank_topk_part",
+                 "rfx_impute_round"):
         getattr(L, name).restype = C.c_int
     _LIB = L
     return L
@@ -265,6 +267,21 @@ class Context:
         val = np.zeros(n, np.float32)
         check(self._lib.rfx_predict(self.handle, ptr(X, _pf), n, p, None, None, ptr(val, _pf)))
         return val
+
+    # ---- imputation ----
+    def impute_round(self, xc: np.ndarray, miss: np.ndarray, is_cat: np.ndarray, cells: np.ndarray):
+        """New values of `cells` ([m, 2] (row, column), sorted by row) from this context's
+        proximity; NaN = keep.  xc / miss are [p][n] (column-major)."""
+        xc = np.ascontiguousarray(xc, np.float32)
+        miss = np.ascontiguousarray(miss, np.uint8)
+        is_cat = np.ascontiguousarray(is_cat, np.uint8)
+        cells = np.ascontiguousarray(cells, np.int32)
+        p, n = xc.shape
+        out = np.zeros(cells.shape[0], np.float32)
+        check(self._lib.rfx_impute_round(self.handle, ptr(xc, _pf), ptr(miss, _pu8),
+                                         ptr(is_cat, _pu8), n, p, ptr(cells, _pi),
+                                         cells.shape[0], ptr(out, _pf)))
+        return out
 
     # ---- low-rank proximity ----
     def lowrank_build(self, rank: int, oversample: int = 16, power_iters: int = 1, seed: int = 0,

@@ -111,6 +111,31 @@ def predict_golden():
     return out
 
 
+def impute_data(n=400, seed=61):
+    """Continuous correlated columns, two small categorical columns, 15% cells missing."""
+    rng = np.random.default_rng(seed)
+    C = 0.4 * np.ones((5, 5)) + 0.6 * np.eye(5)
+    Xc = rng.multivariate_normal(np.zeros(5), C, size=n).astype(np.float32)
+    c1 = rng.integers(0, 4, n).astype(np.float32)
+    c2 = (Xc[:, 0] > 0).astype(np.float32) + rng.integers(0, 2, n)
+    X = np.concatenate([Xc, c1[:, None], c2[:, None]], axis=1)
+    X[rng.random(X.shape) < 0.15] = np.nan
+    return X
+
+
+def impute_golden():
+    """The reference's rfx_impute_proximity (python/rfx_impute.py:596-793) on impute_data()."""
+    sys.path.insert(0, oracle.ref_dir())
+    sys.path.insert(0, os.path.join(os.environ.get("RFX_REFERENCE", "/root/reference"), "python"))
+    import importlib
+    ri = importlib.import_module("rfx_impute")
+    X = impute_data()
+    Xo, info = ri.rfx_impute_proximity(X.copy(), ntree=25, n_iterations=3, use_gpu=False,
+                                       iseed=42, minndsize=1)
+    return {"X": X, "X_imputed": np.asarray(Xo, np.float32),
+            "n_iterations": np.int32(info["n_iterations"])}
+
+
 def main():
     if not oracle.ref_available():
         raise SystemExit("oracle/_ref is not built: run `make -C oracle ref`")
@@ -148,6 +173,7 @@ def main():
     u.fit(Xu)
     save_gz(u, os.path.join(HERE, "unsup_model.rfx.gz"))
     out["unsup_model"] = {"X": Xu}
+    out["impute"] = impute_golden()
     for name, d in out.items():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **d)
     np.savez_compressed(os.path.join(HERE, "bootstrap.npz"), **boot)
