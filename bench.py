@@ -26,6 +26,8 @@ Other workloads (--workload; each prints its own line, the default is config1):
   config3  classification n=1,000,000 p=200 10-class GMM, classwt [1..10]/10, mtry 14,
            nodesize 1, low-rank proximity rank 64 (int8 factors) + top-50 per row; adds
            "lowrank" (sketch GB/s, product TFLOP/s on the tensor cores, top-50 time).
+  config4  the imputation loop rfx_impute_proximity (n=100000 p=40, 15% missing, 5 rounds of
+           200-tree unsupervised forests with proximity and the device fill).
 """
 from __future__ import annotations
 
@@ -337,7 +339,7 @@ def main():
     ap.add_argument("--cpu-trees", type=int, default=8)
     ap.add_argument("--ref-step-trees", type=int, default=2)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="config1", choices=["config1", "config0", "config2", "config3"])
+    ap.add_argument("--workload", default="config1", choices=["config1", "config0", "config2", "config3", "config4"])
     args = ap.parse_args()
     args.step_trees_set = args.step_trees is not None
     if args.step_trees is None:

@@ -140,13 +140,18 @@ def rfx_impute_proximity(X, ntree=100, n_iterations=5, use_gpu=True, categorical
     miss_cm = np.ascontiguousarray(missing.T.astype(np.uint8))
     cat_u8 = np.ascontiguousarray(cat.astype(np.uint8))
     it = 0
+    timing = []
+    import time
     for it in range(n_iterations):
+        t0 = time.perf_counter()
         kw = dict(ntree=ntree, mtry=auto_mtry, nodesize=nodesize, iseed=iseed, use_gpu=use_gpu,
                   compute_proximity=True, compute_importance=False, show_progress=False)
         kw.update(rf_kwargs)
         model = RandomForestUnsupervised(prox_rows=n, device=device, **kw)
         model.fit(Xi)
+        t1 = time.perf_counter()
         new = model._context().impute_round(np.ascontiguousarray(Xi.T), miss_cm, cat_u8, cells)
+        timing.append((t1 - t0, time.perf_counter() - t1))
         # apply, and the reference's change sum (float32 under numpy 2 scalar rules) in its
         # visiting order: columns ascending, rows ascending
         vals = np.full((n, p), np.nan, np.float32)
@@ -163,5 +168,5 @@ def rfx_impute_proximity(X, ntree=100, n_iterations=5, use_gpu=True, categorical
             break
     info = {"n_missing_total": n_missing, "n_iterations": it + 1 if n_iterations > 0 else 0,
             "method": "proximity", "top_k": top_k, "aggregation": aggregation,
-            "encoders": encoders}
+            "encoders": encoders, "timing_fit_fill_s": timing}
     return Xi, info
