@@ -137,7 +137,7 @@ struct Ctx {
     bool f_classwt = false;
     DBuf f_nodes, f_root, f_cat, f_cw, p_X, p_xc, p_vote, p_val, p_cls, p_proba, p_pred;
     // imputation round (rfx_impute_host.cu)
-    DBuf i_x, i_miss, i_cat, i_S, i_scratch, i_cells, i_out;
+    DBuf i_x, i_miss, i_cat, i_S, i_scratch, i_cells, i_out, i_prof;
 
     // batch buffers
     int Tcap = 0;
@@ -159,7 +159,7 @@ struct Ctx {
                        &lr_code, &lr_order, &lr_goff, &lr_ngroups, &lr_tmp, &lr_X, &lr_Z,
                        &lr_CZ, &lr_Y, &lr_ls, &lr_part, &lr_small, &lr_A, &lr_q, &lr_qb, &lr_s, &lr_qbp, &lr_sp, &lr_perm, &lr_blocks, &lr_np, &lr_norm, &lr_ids, &lr_keys, &lr_order_s, &lr_cub, &f_nodes, &f_root, &f_cat, &f_cw, &p_X,
                        &p_xc, &p_vote, &p_val, &p_cls, &p_proba, &p_pred, &i_x, &i_miss, &i_cat,
-                       &i_S, &i_scratch, &i_cells, &i_out,
+                       &i_S, &i_scratch, &i_cells, &i_out, &i_prof,
                        &lr_err, &lr_out_i, &lr_out_v};
         cudaSetDevice(device);
         if (st) cudaStreamSynchronize(st);

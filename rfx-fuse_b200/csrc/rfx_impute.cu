@@ -8,9 +8,10 @@
 //   categorical: x_ij = the value v (ascending, first maximum) with the largest sum(p[x == v])
 // where every sum is numpy's pairwise float32 summation (blocks of <= 128 elements summed with
 // 8 accumulators, longer ranges split in halves rounded down to a multiple of 8).  Cells of
-// one round are independent (a cell reads only rows observed in its column), so each warp
-// takes one cell: it compacts the selected (p, x) pairs into its scratch in index order, the
-// lanes sum the leaves of the pairwise tree, and lane 0 combines them in the tree's order.
+// one round are independent (a cell reads only rows observed in its column).  A row's cells
+// share its proximity row, so each warp takes one row and reads that row once; per cell it
+// compacts the selected (p, x) pairs into its scratch in index order, the lanes sum the
+// leaves of the pairwise tree, and lane 0 combines them in the tree's order.
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -22,23 +23,63 @@ namespace {
 
 constexpr int kLeafMax = 128;
 
-// numpy's pairwise sum of one leaf (n <= 128): n < 8 sequentially from 0, otherwise eight
-// strided accumulators, combined ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then the tail.
-__device__ float leaf_sum(const float* a, int n) {
+// Element sources for the sums.  Buffers start on 16 bytes and every leaf of the pairwise
+// tree starts on a multiple of 8 elements, so a leaf's groups of 8 load as two float4.
+struct Plain {
+    const float* a;
+    __device__ float at(int i) const { return a[i]; }
+    __device__ void at8(int i, float (&x)[8]) const {
+        const float4 u = *reinterpret_cast<const float4*>(a + i);
+        const float4 v = *reinterpret_cast<const float4*>(a + i + 4);
+        x[0] = u.x; x[1] = u.y; x[2] = u.z; x[3] = u.w;
+        x[4] = v.x; x[5] = v.y; x[6] = v.z; x[7] = v.w;
+    }
+};
+
+// (w[i] / tot) * v[i]: the normalised weight times the value, as the reference forms it
+struct Scaled {
+    const float* w;
+    const float* v;
+    float tot;
+    __device__ float at(int i) const { return (w[i] / tot) * v[i]; }
+    __device__ void at8(int i, float (&x)[8]) const {
+        float a[8], b[8];
+        Plain{w}.at8(i, a);
+        Plain{v}.at8(i, b);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) x[k] = (a[k] / tot) * b[k];
+    }
+};
+
+// numpy's pairwise sum of one leaf [lo, lo + n), n <= 128: n < 8 sequentially from 0,
+// otherwise eight strided accumulators, combined ((r0+r1)+(r2+r3))+((r4+r5)+(r6+r7)), then
+// the tail.
+template <class F>
+__device__ float leaf_sum(const F& f, int lo, int n) {
     if (n < 8) {
         float r = 0.0f;
-        for (int i = 0; i < n; ++i) r += a[i];
+        for (int i = 0; i < n; ++i) r += f.at(lo + i);
         return r;
     }
     float r[8];
-#pragma unroll
-    for (int k = 0; k < 8; ++k) r[k] = a[k];
+    f.at8(lo, r);
     int i = 8;
-    for (; i < n - (n % 8); i += 8)
+    const int n8 = n - (n % 8);
+    for (; i + 8 < n8; i += 16) {  // two groups in flight
+        float x[8], y[8];
+        f.at8(lo + i, x);
+        f.at8(lo + i + 8, y);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) r[k] += a[i + k];
+        for (int k = 0; k < 8; ++k) r[k] = (r[k] + x[k]) + y[k];
+    }
+    for (; i < n8; i += 8) {
+        float x[8];
+        f.at8(lo + i, x);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) r[k] += x[k];
+    }
     float res = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
-    for (; i < n; ++i) res += a[i];
+    for (; i < n; ++i) res += f.at(lo + i);
     return res;
 }
 
@@ -65,21 +106,24 @@ __device__ float pairwise_combine(int len, const float* leafsum, int& leaf) {
     return l + r;
 }
 
-// Pairwise sum of buf[0, n) by one warp (leaves by the lanes, combination by lane 0).
-__device__ float warp_pairwise(const float* buf, int n, int2* leaves, float* leafsum, int lane) {
+// Pairwise sum of f over [0, n) by one warp (leaves by the lanes, combination by lane 0).
+// `fresh` = false reuses the leaf list of the previous call of the same n.
+template <class F>
+__device__ float warp_pairwise(const F& f, int n, int2* leaves, float* leafsum, int lane,
+                               bool fresh = true) {
     float r = 0.0f;
     if (n <= kLeafMax) {
-        if (lane == 0) r = leaf_sum(buf, n);
+        if (lane == 0) r = leaf_sum(f, 0, n);
         return __shfl_sync(0xffffffffu, r, 0);
     }
-    if (lane == 0) {
+    if (fresh && lane == 0) {
         int cnt = 0;
         pairwise_leaves(0, n, leaves, cnt);
         leaves[kImpLeafCountSlot].x = cnt;
     }
     __syncwarp();
     const int nl = leaves[kImpLeafCountSlot].x;
-    for (int l = lane; l < nl; l += 32) leafsum[l] = leaf_sum(buf + leaves[l].x, leaves[l].y);
+    for (int l = lane; l < nl; l += 32) leafsum[l] = leaf_sum(f, leaves[l].x, leaves[l].y);
     __syncwarp();
     if (lane == 0) {
         int leaf = 0;
@@ -90,90 +134,151 @@ __device__ float warp_pairwise(const float* buf, int n, int2* leaves, float* lea
 
 }  // namespace
 
-// One warp per missing cell (grid-stride).  S: finished proximity rows [r0, r0 + rows) of
-// width n (row stride ldS); xc: current values [p][n]; miss: [p][n] 1 = missing; cells:
-// (row, column) of the missing cells whose row lies in this block; out[c]: new value, or NaN
-// when the cell has no usable neighbour (the reference leaves it unchanged).
-__global__ void k_impute(ImputeArgs a) {
+// One warp per row that has missing cells (grid-stride over rows).  The warp first compacts
+// the row's usable neighbours (k != i, proximity > 0; ascending k) from the finished
+// proximity row, then serves each of the row's cells from that short list: it drops the
+// neighbours missing in the cell's column (order kept) and aggregates.  S: finished
+// proximity rows [r0, r0 + rows) of width n (row stride ldS); xc: current values [p][n];
+// miss: [p][n] 1 = missing; rows/row_cells: the rows of this block and their ranges of
+// cells; out[c]: new value, or NaN when the cell has no usable neighbour (the reference
+// leaves it unchanged).
+__global__ void __launch_bounds__(256, 4) k_impute(ImputeArgs a) {
+    constexpr int U = 8;  // row chunks of 32 in flight per lane
+    constexpr int V = 4;  // neighbour chunks of 32 in flight per lane
     const int lane = threadIdx.x & 31;
     const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int nwarps = gridDim.x * (blockDim.x >> 5);
-    const size_t n = a.n;
-    float* wbuf = a.scratch + (size_t)wid * a.scratch_stride;
-    float* vbuf = wbuf + n;
-    float* tbuf = vbuf + n;  // per-category subsequence
-    float* lp = tbuf + n;
-    if (reinterpret_cast<uintptr_t>(lp) & 7) ++lp;         // int2 alignment
-    int2* leaves = reinterpret_cast<int2*>(lp) + 1;         // [-1] carries the leaf count
+    const int n = a.n;
+    const int nn = impute_row_floats(n);
+    float* base = a.scratch + (size_t)wid * a.scratch_stride;
+    int* ridx = reinterpret_cast<int*>(base);  // neighbours of the row: index, proximity
+    float* rs = base + nn;
+    float* wbuf = rs + nn;                      // the cell's selection: weight, value
+    float* vbuf = wbuf + nn;
+    float* tbuf = vbuf + nn;                    // per-category subsequence
+    int2* leaves = reinterpret_cast<int2*>(tbuf + nn) + 1;  // [-1] carries the leaf count
     float* leafsum = reinterpret_cast<float*>(leaves + a.max_leaves + 1);
     const unsigned lt = (1u << lane) - 1u;
-    for (int c = wid; c < a.ncells; c += nwarps) {
-        const int i = a.cells[2 * c], j = a.cells[2 * c + 1];
+    for (int r = wid; r < a.nrows; r += nwarps) {
+        const int i = a.rows[r];
+        long long tp = clock64();
         const float* srow = a.S + (size_t)(i - a.r0) * a.ldS;
-        const uint8_t* mj = a.miss + (size_t)j * n;
-        const float* xj = a.xc + (size_t)j * n;
         int m = 0;
-        for (size_t k0 = 0; k0 < n; k0 += 32) {
-            const size_t k = k0 + lane;
-            float s = 0.0f;
-            bool sel = false;
-            if (k < n && (int)k != i && !mj[k]) {
-                s = srow[k];
-                sel = s > 0.0f;
+        for (int k0 = 0; k0 < n; k0 += 32 * U) {
+            float s[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int k = k0 + u * 32 + lane;
+                s[u] = k < n ? __ldcs(srow + k) : 0.0f;
             }
-            const unsigned bal = __ballot_sync(0xffffffffu, sel);
-            if (sel) {
-                const int pos = m + __popc(bal & lt);
-                wbuf[pos] = s;
-                vbuf[pos] = xj[k];
-            }
-            m += __popc(bal);
-        }
-        __syncwarp();
-        float result = __int_as_float(0x7fc00000);
-        if (m > 0) {
-            if (!a.is_cat[j]) {
-                const float tot = warp_pairwise(wbuf, m, leaves, leafsum, lane);
-                for (int q = lane; q < m; q += 32) wbuf[q] = (wbuf[q] / tot) * vbuf[q];
-                __syncwarp();
-                result = warp_pairwise(wbuf, m, leaves, leafsum, lane);
-            } else {
-                // distinct values ascending; weight of each = pairwise sum of its subsequence
-                float prev = -__int_as_float(0x7f800000);
-                bool first = true;
-                float best = 0.0f, best_v = 0.0f;
-                for (;;) {
-                    float nxt = __int_as_float(0x7f800000);
-                    for (int q = lane; q < m; q += 32) {
-                        const float v = vbuf[q];
-                        if ((first || v > prev) && v < nxt) nxt = v;
-                    }
-                    for (int o = 16; o > 0; o >>= 1) nxt = fminf(nxt, __shfl_xor_sync(0xffffffffu, nxt, o));
-                    bool any = false;
-                    for (int q = lane; q < m; q += 32) any |= vbuf[q] == nxt;
-                    if (!__any_sync(0xffffffffu, any)) break;
-                    int mc = 0;
-                    for (int q0 = 0; q0 < m; q0 += 32) {
-                        const int q = q0 + lane;
-                        const bool selc = q < m && vbuf[q] == nxt;
-                        const unsigned bal = __ballot_sync(0xffffffffu, selc);
-                        if (selc) tbuf[mc + __popc(bal & lt)] = wbuf[q];
-                        mc += __popc(bal);
-                    }
-                    __syncwarp();
-                    const float cntw = warp_pairwise(tbuf, mc, leaves, leafsum, lane);
-                    if (first || cntw > best) {
-                        best = cntw;
-                        best_v = nxt;
-                    }
-                    first = false;
-                    prev = nxt;
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int k = k0 + u * 32 + lane;
+                const bool sel = s[u] > 0.0f && k != i;
+                const unsigned bal = __ballot_sync(0xffffffffu, sel);
+                if (sel) {
+                    const int pos = m + __popc(bal & lt);
+                    ridx[pos] = k;
+                    rs[pos] = s[u];
                 }
-                result = best_v;
+                m += __popc(bal);
             }
         }
-        if (lane == 0) a.out[c] = result;
         __syncwarp();
+        if (a.prof && lane == 0) {
+            atomicAdd(a.prof + 0, (unsigned long long)m);
+            atomicMax(a.prof + 7, (unsigned long long)m);
+            atomicAdd(a.prof + 2, (unsigned long long)(clock64() - tp));
+        }
+        for (int c = a.row_cells[r]; c < a.row_cells[r + 1]; ++c) {
+            tp = clock64();
+            const int j = a.cells[2 * c + 1];
+            const uint8_t* mj = a.miss + (size_t)j * n;
+            const float* xj = a.xc + (size_t)j * n;
+            int mm = 0;
+            for (int t0 = 0; t0 < m; t0 += 32 * V) {
+                int k[V];
+                bool sel[V];
+                float sv[V], xv[V];
+#pragma unroll
+                for (int u = 0; u < V; ++u) {
+                    const int t = t0 + u * 32 + lane;
+                    k[u] = t < m ? ridx[t] : -1;
+                }
+#pragma unroll
+                for (int u = 0; u < V; ++u) sel[u] = k[u] >= 0 && !mj[k[u]];
+#pragma unroll
+                for (int u = 0; u < V; ++u) {
+                    const int t = t0 + u * 32 + lane;
+                    sv[u] = sel[u] ? rs[t] : 0.0f;
+                    xv[u] = sel[u] ? xj[k[u]] : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < V; ++u) {
+                    const unsigned bal = __ballot_sync(0xffffffffu, sel[u]);
+                    if (sel[u]) {
+                        const int pos = mm + __popc(bal & lt);
+                        wbuf[pos] = sv[u];
+                        vbuf[pos] = xv[u];
+                    }
+                    mm += __popc(bal);
+                }
+            }
+            __syncwarp();
+            if (a.prof && lane == 0) {
+                atomicAdd(a.prof + 1, (unsigned long long)mm);
+                atomicAdd(a.prof + 3, (unsigned long long)(clock64() - tp));
+                tp = clock64();
+            }
+            float result = __int_as_float(0x7fc00000);
+            if (mm > 0) {
+                if (!a.is_cat[j]) {
+                    const float tot = warp_pairwise(Plain{wbuf}, mm, leaves, leafsum, lane);
+                    result = warp_pairwise(Scaled{wbuf, vbuf, tot}, mm, leaves, leafsum, lane, false);
+                } else {
+                    // distinct values ascending; weight of each = pairwise sum of its subsequence
+                    float prev = -__int_as_float(0x7f800000);
+                    bool first = true;
+                    float best = 0.0f, best_v = 0.0f;
+                    for (;;) {
+                        float nxt = __int_as_float(0x7f800000);
+                        for (int q = lane; q < mm; q += 32) {
+                            const float v = vbuf[q];
+                            if ((first || v > prev) && v < nxt) nxt = v;
+                        }
+                        for (int o = 16; o > 0; o >>= 1) nxt = fminf(nxt, __shfl_xor_sync(0xffffffffu, nxt, o));
+                        bool any = false;
+                        for (int q = lane; q < mm; q += 32) any |= vbuf[q] == nxt;
+                        if (!__any_sync(0xffffffffu, any)) break;
+                        int mc = 0;
+                        for (int q0 = 0; q0 < mm; q0 += 32) {
+                            const int q = q0 + lane;
+                            const bool selc = q < mm && vbuf[q] == nxt;
+                            const unsigned bal = __ballot_sync(0xffffffffu, selc);
+                            if (selc) tbuf[mc + __popc(bal & lt)] = wbuf[q];
+                            mc += __popc(bal);
+                        }
+                        __syncwarp();
+                        const float cntw = warp_pairwise(Plain{tbuf}, mc, leaves, leafsum, lane);
+                        if (first || cntw > best) {
+                            best = cntw;
+                            best_v = nxt;
+                        }
+                        first = false;
+                        prev = nxt;
+                        if (a.prof && lane == 0) atomicAdd(a.prof + 6, 1ull);
+                    }
+                    result = best_v;
+                }
+            }
+            if (a.prof && lane == 0) {
+                const int cat = a.is_cat[j] ? 1 : 0;
+                atomicAdd(a.prof + 4 + cat, (unsigned long long)(clock64() - tp));
+                atomicAdd(a.prof + 8 + cat, 1ull);
+            }
+            if (lane == 0) a.out[c] = result;
+            __syncwarp();
+        }
     }
 }
 

@@ -15,18 +15,25 @@ struct ImputeArgs {
     const float* xc;         // [p][n] current values (column-major)
     const uint8_t* miss;     // [p][n] 1 = missing in the input
     const uint8_t* is_cat;   // [p]
-    const int* cells;        // [ncells][2] (row, column), rows in [r0, r0 + rows)
-    int ncells;
+    const int* cells;        // [ncells][2] (row, column), sorted by row
+    const int* rows;         // [nrows] rows with missing cells, in [r0, r0 + rows of S)
+    const int* row_cells;    // [nrows + 1] cells of rows[r]: [row_cells[r], row_cells[r + 1])
+    int nrows;
     float* out;              // [ncells] new value, NaN = unchanged
-    float* scratch;          // per warp: 3 n floats, then leaves and leaf sums
+    float* scratch;          // per warp: 5 n floats, then leaves and leaf sums
     long long scratch_stride;
     int max_leaves;
+    unsigned long long* prof;  // optional counters (RFX_IMPUTE_PROF), null = off
 };
 
-// floats of scratch one warp needs for n rows
+// floats of one n-long scratch buffer (a multiple of 8, so the next one starts on 32 bytes)
+__host__ __device__ inline int impute_row_floats(int n) { return (n + 7) / 8 * 8; }
+
+// floats of scratch one warp needs for n rows: five n-long buffers, the leaf list (int2, one
+// extra slot for the count) and the leaf sums
 inline long long impute_scratch_floats(int n, int max_leaves) {
-    long long f = 3LL * n + 2LL * (max_leaves + 2) + max_leaves + 2;
-    return (f + 3) / 4 * 4;
+    long long f = 5LL * impute_row_floats(n) + 2LL * (max_leaves + 2) + max_leaves + 2;
+    return (f + 7) / 8 * 8;
 }
 
 __global__ void k_impute(ImputeArgs a);

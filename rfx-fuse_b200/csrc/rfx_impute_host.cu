@@ -1,4 +1,6 @@
 // Host side of the imputation round (kernel in rfx_impute.cu, ABI in include/rfx_b200.h).
+#include <cstdio>
+#include <cstdlib>
 #include <vector>
 
 #include "rfx_ctx.h"
@@ -29,46 +31,85 @@ int rfx_impute_round(void* ctx, const float* xc_host, const uint8_t* miss_host,
         RFX_CUDA(cudaMemcpyAsync(xc, xc_host, P * N * 4, cudaMemcpyHostToDevice, st));
         RFX_CUDA(cudaMemcpyAsync(miss, miss_host, P * N, cudaMemcpyHostToDevice, st));
         RFX_CUDA(cudaMemcpyAsync(cat, is_cat_host, P, cudaMemcpyHostToDevice, st));
-        // finished proximity rows in blocks of at most 1 GiB
-        const int rows_per = (int)std::max<long long>(1, ((long long)1 << 30) / ((long long)N * 4));
+        // rows with missing cells and their ranges of cells
+        std::vector<int> rows, row_cells;
+        for (int q = 0; q < ncells; ++q) {
+            const int i = cells_host[2 * q];
+            require(i >= 0 && i < n && cells_host[2 * q + 1] >= 0 && cells_host[2 * q + 1] < p,
+                    RFX_ERR_ARG, "cell outside the matrix");
+            if (rows.empty() || rows.back() != i) {
+                rows.push_back(i);
+                row_cells.push_back(q);
+            }
+        }
+        row_cells.push_back(ncells);
+        const int nrows = (int)rows.size();
+        // finished proximity rows in blocks of at most 4 GiB
+        const int rows_per = (int)std::max<long long>(1, ((long long)1 << 32) / ((long long)N * 4));
         float* S = (float*)c.i_S.get((size_t)std::min<long long>(rows_per, n) * N * 4);
         const int max_leaves = n / 32 + 4;
         const long long stride = rfx::impute_scratch_floats(n, max_leaves);
-        const int blocks = c.sm_count * 2;
+        // 4 blocks of 8 warps per SM, fewer when the per-warp scratch passes 8 GiB in total
+        const long long fit = std::max<long long>(1, ((long long)1 << 33) / (stride * 4 * 8));
+        const int blocks = (int)std::min<long long>((long long)c.sm_count * 4, fit);
         float* scratch = (float*)c.i_scratch.get((size_t)blocks * 8 * stride * 4);
-        int* cells = (int*)c.i_cells.get((size_t)ncells * 8);
+        int* cells = (int*)c.i_cells.get((size_t)ncells * 8 + (size_t)(2 * nrows + 1) * 4);
+        int* drows = cells + 2 * (size_t)ncells;
+        int* drow_cells = drows + nrows;
         float* out = (float*)c.i_out.get((size_t)ncells * 4);
         RFX_CUDA(cudaMemcpyAsync(cells, cells_host, (size_t)ncells * 8, cudaMemcpyHostToDevice, st));
-        int q0 = 0;
-        for (int r0 = 0; r0 < n && q0 < ncells; r0 += rows_per) {
+        RFX_CUDA(cudaMemcpyAsync(drows, rows.data(), (size_t)nrows * 4, cudaMemcpyHostToDevice, st));
+        RFX_CUDA(cudaMemcpyAsync(drow_cells, row_cells.data(), (size_t)(nrows + 1) * 4,
+                                 cudaMemcpyHostToDevice, st));
+        static const bool want_prof = std::getenv("RFX_IMPUTE_PROF") != nullptr;
+        unsigned long long* prof = nullptr;
+        if (want_prof) {
+            prof = (unsigned long long*)c.i_prof.get(16 * 8);
+            RFX_CUDA(cudaMemsetAsync(prof, 0, 16 * 8, st));
+        }
+        int b0 = 0;
+        for (int r0 = 0; r0 < n && b0 < nrows; r0 += rows_per) {
             const int r1 = std::min(n, r0 + rows_per);
-            int q1 = q0;
-            while (q1 < ncells && cells_host[2 * q1] < r1) ++q1;
-            if (q1 == q0) continue;
-            RFX_CUDA(rfx::launch_prox_finish(c.prox, (const int*)c.nout.p, n, r0, r1, S, st));
+            int b1 = b0;
+            while (b1 < nrows && rows[b1] < r1) ++b1;
+            if (b1 == b0) continue;
+            // finish only the span of rows that have cells
+            const int f0 = rows[b0], f1 = rows[b1 - 1] + 1;
+            RFX_CUDA(rfx::launch_prox_finish(c.prox, (const int*)c.nout.p, n, f0, f1, S, st));
             rfx::ImputeArgs a;
             a.S = S;
             a.ldS = n;
-            a.r0 = r0;
+            a.r0 = f0;
             a.n = n;
             a.p = p;
             a.xc = xc;
             a.miss = miss;
             a.is_cat = cat;
-            a.cells = cells + 2 * (size_t)q0;
-            a.ncells = q1 - q0;
-            a.out = out + q0;
+            a.cells = cells;
+            a.rows = drows + b0;
+            a.row_cells = drow_cells + b0;
+            a.nrows = b1 - b0;
+            a.out = out;
             a.scratch = scratch;
             a.scratch_stride = stride;
             a.max_leaves = max_leaves;
-            const int grid = std::min(blocks, (a.ncells + 7) / 8);
+            a.prof = prof;
+            const int grid = std::min(blocks, (a.nrows + 7) / 8);
             rfx::k_impute<<<grid, 256, 0, st>>>(a);
             RFX_LAUNCH("k_impute");
             c.launches += 2;
-            q0 = q1;
+            b0 = b1;
         }
         RFX_CUDA(cudaMemcpyAsync(out_host, out, (size_t)ncells * 4, cudaMemcpyDeviceToHost, st));
         RFX_CUDA(cudaStreamSynchronize(st));
+        if (prof) {
+            unsigned long long hp[16] = {};
+            RFX_CUDA(cudaMemcpy(hp, prof, 16 * 8, cudaMemcpyDeviceToHost));
+            std::fprintf(stderr,
+                         "impute prof: rows %d sum_m %llu max_m %llu sum_mm %llu | cycles scan %llu "
+                         "compact %llu cont %llu cat %llu | cells cont %llu cat %llu distinct %llu\n",
+                         nrows, hp[0], hp[7], hp[1], hp[2], hp[3], hp[4], hp[5], hp[8], hp[9], hp[6]);
+        }
     });
 }
 
