@@ -14,6 +14,8 @@ constexpr uint32_t kFull = 0xffffffffu;
 constexpr unsigned long long kNoKey = ~0ull;
 constexpr int kBigSegment = 2048;  // segments above this are partitioned by a whole block
 constexpr int kSmallNode = 64;     // nodes up to this size are searched by one warp
+constexpr int kHistScratch = 256 + 3 * 1024;  // bytes of a warp's bin list + sums + counts
+constexpr int kListCap = 256;  // regression bin-list entries per warp in k_hist_small (>= kSmallNode)
 
 // ------------------------------------------------------------------------------------
 // MT19937, the generator of include/rf_utils.hpp:74-141: init_genrand seeding, standard

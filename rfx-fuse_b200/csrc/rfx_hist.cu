@@ -166,8 +166,87 @@ __device__ __forceinline__ unsigned long long scan_bins(bool regr, int nc, int c
     return key;
 }
 
+// ---------------------------------------------------------------------------------------
+// Regression scan over compacted bin lists.  A draw's non-empty bins (ascending) are a list
+// of (sum, sum of squares, count); the scan's serial float chains -- the totals, then the
+// running left/right sums -- run lane-serially, one draw per lane, so that one warp
+// instruction advances several draws' chains at once; the criterion of every candidate bin
+// is then evaluated in parallel over all lists.
+// ---------------------------------------------------------------------------------------
+constexpr uint32_t kLastEntry = 1u << 31;  // list entry flag: a draw's last bin (no split)
+
+// In place over one list of `len` entries: A/A2/K (bin sum, square sum, count) become the
+// running left sums and count; R/R2 receive the running right sums.
+__device__ __forceinline__ void regr_chains(float* A, float* A2, int* K, float* R, float* R2,
+                                            int len) {
+    float tot = 0.0f, tot2 = 0.0f;
+    int j = 0;
+    for (; j + 8 <= len; j += 8) {
+        float a[8], b[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) { a[u] = A[j + u]; b[u] = A2[j + u]; }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) { tot += a[u]; tot2 += b[u]; }
+    }
+    for (; j < len; ++j) { tot += A[j]; tot2 += A2[j]; }
+    float L = 0.0f, Rv = tot, L2 = 0.0f, Rv2 = tot2;
+    int kc = 0;
+    j = 0;
+    for (; j + 8 <= len; j += 8) {
+        float a[8], b[8];
+        int k[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) { a[u] = A[j + u]; b[u] = A2[j + u]; k[u] = K[j + u]; }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            kc += k[u];
+            L += a[u];
+            Rv -= a[u];
+            L2 += b[u];
+            Rv2 -= b[u];
+            A[j + u] = L;
+            A2[j + u] = L2;
+            K[j + u] = kc;
+            R[j + u] = Rv;
+            R2[j + u] = Rv2;
+        }
+    }
+    for (; j < len; ++j) {
+        kc += K[j];
+        L += A[j];
+        Rv -= A[j];
+        L2 += A2[j];
+        Rv2 -= A2[j];
+        A[j] = L;
+        A2[j] = L2;
+        K[j] = kc;
+        R[j] = Rv;
+        R2[j] = Rv2;
+    }
+}
+
+// Key of one candidate split (left sums mL/mL2 over mC rows, right sums mR/mR2, node rows c):
+// the reference's MSE criterion; candidates whose criterion is not below 1e20 (or NaN) never
+// win.  `mvbin` = (draw << 8) | bin.
+__device__ __forceinline__ unsigned long long regr_key(float mL, float mR, float mL2, float mR2,
+                                                       int mC, int c, uint32_t mvbin) {
+    const float cl = (float)mC, cr = (float)(c - mC);
+    const float ml = mL / cl, mr = mR / cr;
+    const float vl = mL2 / cl - ml * ml, vr = mR2 / cr - mr * mr;
+    const float tt = cl + cr;
+    const float mse = (cl * vl + cr * vr) / tt;
+    return mse < 1e20f ? ((unsigned long long)ord_of(mse) << 32) | mvbin : kNoKey;
+}
+
+__device__ __forceinline__ unsigned long long warp_min_key(unsigned long long k) {
+    for (int o = 16; o > 0; o >>= 1) k = min(k, __shfl_xor_sync(kFull, k, o));
+    return k;
+}
+
 // Per-warp scratch layout shared by both kernels (after any staging area):
 //   bl[256] uint8 | sy[256] f32 | sy2[256] f32 | cn[256] i32 | h[(256+1) * nclass] i32
+// (regression: k_hist uses h as the right sums R[256] | R2[256]; k_hist_small keeps its
+// list area at kHistScratch)
 __device__ __forceinline__ void warp_scratch(uint8_t* w, uint8_t*& bl, float*& sy, float*& sy2,
                                              int*& cn, int*& h) {
     bl = w;
@@ -210,9 +289,10 @@ __device__ __forceinline__ void hist_step(bool regr, int nc, bool valid, int b, 
 // current one, and stores them transposed (feature-major, padded stride) so that the 32
 // lanes of a warp read 32 consecutive bytes of their feature without bank conflicts.
 // ---------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) k_hist(Data D, Batch B, int cur, HistArgs a) {
+__global__ void __launch_bounds__(256, 4) k_hist(Data D, Batch B, int cur, HistArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ int snode[2];
+    __shared__ int slen[32];  // regression: list length of each warp's draw
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int nthr = blockDim.x;
     const bool regr = D.nclass == 1;
@@ -314,10 +394,65 @@ __global__ void __launch_bounds__(256) k_hist(Data D, Batch B, int cur, HistArgs
                 }
             }
         }
+        if (!regr) {
+            if (active) {
+                __syncwarp();
+                const unsigned long long key = scan_bins(regr, nc, c, mv, lane, bl, sy, sy2, cn, h);
+                if (lane == 0 && key != kNoKey) atomicMin(&B.nd_key[m], key);
+            }
+            continue;
+        }
+        // regression: every warp compacts its histogram in place to the list of non-empty
+        // bins, lanes of warp 0 run the draws' chains, every warp scores its own list
+        int nm = 0;
         if (active) {
             __syncwarp();
-            const unsigned long long key = scan_bins(regr, nc, c, mv, lane, bl, sy, sy2, cn, h);
-            if (lane == 0 && key != kNoKey) atomicMin(&B.nd_key[m], key);
+            nm = warp_nonempty_bins(cn, bl, lane);
+            for (int s0 = 0; s0 < nm; s0 += 32) {  // entry j <= bin bl[j]: forward in place
+                const int j = s0 + lane;
+                float x = 0.0f, x2 = 0.0f;
+                int k = 0;
+                if (j < nm) {
+                    const int b = bl[j];
+                    x = sy[b];
+                    x2 = sy2[b];
+                    k = cn[b];
+                }
+                __syncwarp();
+                if (j < nm) {
+                    sy[j] = x;
+                    sy2[j] = x2;
+                    cn[j] = k;
+                }
+                __syncwarp();
+            }
+        }
+        if (lane == 0) slen[wib] = nm;
+        __syncthreads();
+        if (wib == 0 && lane < a.warps) {
+            uint8_t* bl2;
+            float *a1, *a2;
+            int *k1, *h2;
+            warp_scratch(smem + (size_t)rs * CS + (size_t)CH * 8 + (size_t)lane * a.warp_bytes,
+                         bl2, a1, a2, k1, h2);
+            float* r1 = reinterpret_cast<float*>(h2);
+            regr_chains(a1, a2, k1, r1, r1 + kBins, slen[lane]);
+        }
+        __syncthreads();
+        if (active) {
+            const float* r1 = reinterpret_cast<const float*>(h);
+            unsigned long long best = kNoKey;
+            for (int j = lane; j < nm - 1; j += 32)
+                best = min(best, regr_key(sy[j], r1[j], sy2[j], r1[kBins + j], cn[j], c,
+                                          ((uint32_t)mv << 8) | bl[j]));
+            best = warp_min_key(best);
+            if (lane == 0 && best != kNoKey) atomicMin(&B.nd_key[m], best);
+            __syncwarp();
+            for (int k = lane; k < kBins; k += 32) {
+                sy[k] = 0.0f;
+                sy2[k] = 0.0f;
+                cn[k] = 0;
+            }
         }
     }
 }
@@ -339,6 +474,14 @@ __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, in
     float *sy, *sy2;
     int *cn, *h;
     warp_scratch(wbase, bl, sy, sy2, cn, h);
+    // regression list area after the histogram: sums, square sums, counts, right sums,
+    // right square sums, (draw, bin, last) words -- kListCap entries each
+    float* LA = reinterpret_cast<float*>(wbase + kHistScratch);
+    float* LA2 = LA + kListCap;
+    int* LK = reinterpret_cast<int*>(LA2 + kListCap);
+    float* LR = reinterpret_cast<float*>(LK + kListCap);
+    float* LR2 = LR + kListCap;
+    uint32_t* LDB = reinterpret_cast<uint32_t*>(LR2 + kListCap);
     for (int k = lane; k < warp_bytes / 4; k += 32)
         reinterpret_cast<uint32_t*>(bl)[k] = 0u;
     __syncwarp();
@@ -371,18 +514,70 @@ __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, in
             }
         }
         unsigned long long best = kNoKey;
-        for (int mv = 0; mv < B.mtry; ++mv) {
-            const int f = featp[mv];
+        if (!regr) {
+            for (int mv = 0; mv < B.mtry; ++mv) {
+                const int f = featp[mv];
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                if (hh * 32 < c) {
-                    const int i = hh * 32 + lane;
-                    const bool valid = i < c;
-                    const int b = valid ? (int)__ldg(rowp[hh] + f) : kBins;
-                    hist_step(regr, nc, valid, b, v[hh], v2[hh], lab[hh], lane, sy, sy2, cn, h);
+                for (int hh = 0; hh < 2; ++hh) {
+                    if (hh * 32 < c) {
+                        const int i = hh * 32 + lane;
+                        const bool valid = i < c;
+                        const int b = valid ? (int)__ldg(rowp[hh] + f) : kBins;
+                        hist_step(regr, nc, valid, b, v[hh], v2[hh], lab[hh], lane, sy, sy2, cn, h);
+                    }
                 }
+                best = min(best, scan_bins(regr, nc, c, mv, lane, bl, sy, sy2, cn, h));
             }
-            best = min(best, scan_bins(regr, nc, c, mv, lane, bl, sy, sy2, cn, h));
+        } else {
+            // regression: the draws' lists of non-empty bins fill the warp's list area (as
+            // many draws as fit, at most 32), then lane d runs draw d's chains and the
+            // whole list is scored in parallel
+            for (int mv = 0; mv < B.mtry;) {
+                int used = 0, nd = 0, my_off = 0, my_len = 0;
+                while (mv < B.mtry && nd < 32 && used + c <= kListCap) {
+                    const int f = featp[mv];
+#pragma unroll
+                    for (int hh = 0; hh < 2; ++hh) {
+                        if (hh * 32 < c) {
+                            const int i = hh * 32 + lane;
+                            const bool valid = i < c;
+                            const int b = valid ? (int)__ldg(rowp[hh] + f) : kBins;
+                            hist_step(true, 1, valid, b, v[hh], v2[hh], 0, lane, sy, sy2, cn, h);
+                        }
+                    }
+                    const int nm = warp_nonempty_bins(cn, bl, lane);
+                    for (int j = lane; j < nm; j += 32) {
+                        const int b = bl[j];
+                        const int e = used + j;
+                        LA[e] = sy[b];
+                        LA2[e] = sy2[b];
+                        LK[e] = cn[b];
+                        LDB[e] = ((uint32_t)mv << 8) | (uint32_t)b | (j == nm - 1 ? kLastEntry : 0u);
+                        sy[b] = 0.0f;
+                        sy2[b] = 0.0f;
+                        cn[b] = 0;
+                    }
+                    __syncwarp();
+                    if (lane == nd) {
+                        my_off = used;
+                        my_len = nm;
+                    }
+                    used += nm;
+                    ++nd;
+                    ++mv;
+                }
+                if (lane < nd)
+                    regr_chains(LA + my_off, LA2 + my_off, LK + my_off, LR + my_off,
+                                LR2 + my_off, my_len);
+                __syncwarp();
+                for (int e = lane; e < used; e += 32) {
+                    const uint32_t db = LDB[e];
+                    if (!(db & kLastEntry))
+                        best = min(best, regr_key(LA[e], LR[e], LA2[e], LR2[e], LK[e], c, db));
+                }
+                __syncwarp();
+            }
+            best = warp_min_key(best);
         }
         if (lane == 0) B.nd_key[m] = best;
         __syncwarp();

@@ -333,11 +333,18 @@ struct HistCfg {
 HistCfg hist_cfg(Ctx& c) {
     HistCfg h;
     const int pieces = c.D.rs / 16;
-    const int scratch = (int)round_up(256 + 3 * 1024 + (c.nclass > 1 ? (257 * c.nclass + 32) * 4 : 0), 16);
+    // per-warp histogram scratch; regression adds the right-sum arrays (k_hist) or the bin
+    // list area (k_hist_small, 24 bytes per entry)
+    const bool regr = c.nclass == 1;
+    const int scratch = (int)round_up(rfx::kHistScratch + (regr ? 2 * 1024 : (257 * c.nclass + 32) * 4), 16);
+    const int small_scratch = regr ? rfx::kHistScratch + 24 * rfx::kListCap : scratch;
     h.a.warps = 8;
     h.a.groups = (c.prm.mtry + h.a.warps - 1) / h.a.warps;
-    // rows per staged chunk: a multiple of 32 with at most 2 load units per thread
-    h.a.stage_rows = std::min(256, (2 * 256 * 4 / pieces) / 32 * 32);
+    // rows per staged chunk: a multiple of 32 with at most 2 load units per thread, small
+    // enough for 4 resident blocks per SM (56 KB each) where the row width allows
+    const int fixed = h.a.warps * (int)scratch + 4 * c.D.rs;
+    const int fit4 = (56 * 1024 - fixed) / (c.D.rs + 8);
+    h.a.stage_rows = std::max(32, std::min({256, (2 * 256 * 4 / pieces) / 32 * 32, fit4 / 32 * 32}));
     h.a.cstride = h.a.stage_rows + 4;
     h.a.warp_bytes = scratch;
     h.threads = 32 * h.a.warps;
@@ -347,7 +354,7 @@ HistCfg hist_cfg(Ctx& c) {
     int per_sm = 0;
     RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist, h.threads, h.smem));
     h.grid = c.sm_count * std::max(1, per_sm);
-    h.small_warp_bytes = scratch;
+    h.small_warp_bytes = small_scratch;
     h.small_smem = 8 * h.small_warp_bytes;
     RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   std::max(h.small_smem, 48 * 1024)));
