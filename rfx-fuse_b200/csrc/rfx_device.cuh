@@ -15,7 +15,12 @@ constexpr unsigned long long kNoKey = ~0ull;
 constexpr int kBigSegment = 2048;  // segments above this are partitioned by a whole block
 constexpr int kSmallNode = 64;     // nodes up to this size are searched by one warp
 constexpr int kHistScratch = 256 + 3 * 1024;  // bytes of a warp's bin list + sums + counts
-constexpr int kListCap = 256;  // regression bin-list entries per warp in k_hist_small (>= kSmallNode)
+constexpr int kSmallNodeRegr = 128;  // the same limit for regression (list-based scan)
+constexpr int kListCap = 256;  // regression bin-list entries per warp in k_hist_small (>= kSmallNodeRegr)
+// Rows of the largest node k_hist_small searches (the rest go to k_hist).
+__host__ __device__ __forceinline__ int small_node_limit(int nclass) {
+    return nclass == 1 ? kSmallNodeRegr : kSmallNode;
+}
 
 // ------------------------------------------------------------------------------------
 // MT19937, the generator of include/rf_utils.hpp:74-141: init_genrand seeding, standard
@@ -160,7 +165,7 @@ struct Batch {
     int* counters;    // [8]: 0 level total, 1 searched total, 2 next-level total, 4 big searched
     unsigned long long* hist_bytes;  // algorithmic bytes read by k_hist (sum of c_v*(mtry+L))
     unsigned long long* prox_pairs;  // proximity pair updates counted by k_prox
-    int* srch_big;    // [T][M] searched nodes with more than kSmallNode rows, in node order
+    int* srch_big;    // [T][M] searched nodes above small_node_limit rows, in node order
     int* srch_big_cnt;  // [T]
     int* srch_big_off;  // [T+1]
     long long* part_big;  // split nodes (t*M + node) with segments above kBigSegment; count in counters[5]

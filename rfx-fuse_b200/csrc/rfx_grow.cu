@@ -176,7 +176,7 @@ __global__ void __launch_bounds__(256) k_draw(Data D, Batch B) {
     for (int k0 = lo; k0 < hi; k0 += blockDim.x) {
         const int node = k0 + threadIdx.x;
         const bool f = node < hi && B.nd_flag[(size_t)t * B.M + node];
-        const bool fb = f && B.nd_cnt[(size_t)t * B.M + node] > kSmallNode;
+        const bool fb = f && B.nd_cnt[(size_t)t * B.M + node] > small_node_limit(D.nclass);
         int tot, btot;
         const int ex = block_excl_scan(f ? 1 : 0, ws, tot);
         const int bex = block_excl_scan(fb ? 1 : 0, ws, btot);

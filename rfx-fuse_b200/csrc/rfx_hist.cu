@@ -3,10 +3,10 @@
 // (src/rf_growtree.cpp:820-836, :929-955), for every searched node of a level at once.
 //
 // Two kernels share the work by node size:
-//   k_hist        nodes with more than kSmallNode rows: one block per (node, group of up to
+//   k_hist        nodes above small_node_limit rows (64, regression 128): one block per (node, group of up to
 //                 8 draws), one warp per drawn feature, the node's rows streamed through
 //                 shared memory in chunks;
-//   k_hist_small  nodes with at most kSmallNode rows (the great majority at deep levels):
+//   k_hist_small  nodes up to that limit (the great majority at deep levels):
 //                 one warp per node does all mtry draws from rows staged once.
 //
 // Each warp builds its feature's histogram: classification as integer class counts (the
@@ -289,7 +289,7 @@ __device__ __forceinline__ void hist_step(bool regr, int nc, bool valid, int b, 
 // current one, and stores them transposed (feature-major, padded stride) so that the 32
 // lanes of a warp read 32 consecutive bytes of their feature without bank conflicts.
 // ---------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256, 4) k_hist(Data D, Batch B, int cur, HistArgs a) {
+__global__ void __launch_bounds__(512, 2) k_hist(Data D, Batch B, int cur, HistArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ int snode[2];
     __shared__ int slen[32];  // regression: list length of each warp's draw
@@ -458,11 +458,13 @@ __global__ void __launch_bounds__(256, 4) k_hist(Data D, Batch B, int cur, HistA
 }
 
 // ---------------------------------------------------------------------------------------
-// Small nodes (c <= kSmallNode rows): one warp per searched node does all mtry draws.
-// Each lane holds up to two of the node's rows (address and target in registers) and
+// Small nodes (c <= small_node_limit rows): one warp per searched node does all mtry draws.
+// Each lane holds up to four of the node's rows (address and target in registers) and
 // reads the drawn feature's bin directly from the packed row; per-warp shared memory holds
 // only the histogram, which keeps many warps resident to hide the latency.
 // ---------------------------------------------------------------------------------------
+constexpr int kSmallRows = kSmallNodeRegr / 32;  // rows per lane in k_hist_small
+
 __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, int warp_bytes) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
@@ -492,19 +494,22 @@ __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, in
         const int node = B.srch[(size_t)t * B.M + (si - B.srch_off[t])];
         const size_t m = (size_t)t * B.M + node;
         const int c = B.nd_cnt[m];
-        if (c > kSmallNode) continue;  // k_hist
+        if (c > small_node_limit(nc)) continue;  // k_hist
         if (lane == 0 && B.hist_bytes)
             atomicAdd(B.hist_bytes, (unsigned long long)c * (unsigned long long)(B.mtry + (regr ? 4 : 1)));
         const int* seg = B.seg[cur] + (size_t)t * D.N + B.nd_start[m];
         const uint16_t* featp = B.feat + (size_t)t * B.M * B.mtry + (size_t)node * B.mtry;
         // each lane keeps its rows' address and target in registers; the bins are read
         // straight from the packed rows (L1-resident after the first draw)
-        const uint8_t* rowp[2] = {D.rows, D.rows};
-        float v[2] = {0.0f, 0.0f}, v2[2] = {0.0f, 0.0f};
-        int lab[2] = {0, 0};
+        const uint8_t* rowp[kSmallRows];
+        float v[kSmallRows], v2[kSmallRows];
+        int lab[kSmallRows];
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
+        for (int hh = 0; hh < kSmallRows; ++hh) {
             const int i = hh * 32 + lane;
+            rowp[hh] = D.rows;
+            v[hh] = v2[hh] = 0.0f;
+            lab[hh] = 0;
             if (i < c) {
                 rowp[hh] = D.rows + (size_t)seg[i] * rs;
                 const uint2 tg = __ldg(reinterpret_cast<const uint2*>(rowp[hh] + ro));
@@ -518,7 +523,7 @@ __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, in
             for (int mv = 0; mv < B.mtry; ++mv) {
                 const int f = featp[mv];
 #pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
+                for (int hh = 0; hh < kSmallRows; ++hh) {
                     if (hh * 32 < c) {
                         const int i = hh * 32 + lane;
                         const bool valid = i < c;
@@ -537,7 +542,7 @@ __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, in
                 while (mv < B.mtry && nd < 32 && used + c <= kListCap) {
                     const int f = featp[mv];
 #pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
+                    for (int hh = 0; hh < kSmallRows; ++hh) {
                         if (hh * 32 < c) {
                             const int i = hh * 32 + lane;
                             const bool valid = i < c;

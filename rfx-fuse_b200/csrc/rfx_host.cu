@@ -336,15 +336,21 @@ HistCfg hist_cfg(Ctx& c) {
     // per-warp histogram scratch; regression adds the right-sum arrays (k_hist) or the bin
     // list area (k_hist_small, 24 bytes per entry)
     const bool regr = c.nclass == 1;
-    const int scratch = (int)round_up(rfx::kHistScratch + (regr ? 2 * 1024 : (257 * c.nclass + 32) * 4), 16);
+    // (k_hist: +4 bytes so that the warps' lists start in different shared-memory banks when
+    // lanes of one warp read them side by side)
+    const int scratch = (int)round_up(rfx::kHistScratch + (regr ? 2 * 1024 : (257 * c.nclass + 32) * 4), 16) + 4;
     const int small_scratch = regr ? rfx::kHistScratch + 24 * rfx::kListCap : scratch;
-    h.a.warps = 8;
+    // regression: one block per node covers up to 16 draws (rows staged once per node, one
+    // chain phase); classification: groups of 8 draws
+    h.a.warps = regr ? std::max(1, std::min(16, c.prm.mtry)) : 8;
     h.a.groups = (c.prm.mtry + h.a.warps - 1) / h.a.warps;
     // rows per staged chunk: a multiple of 32 with at most 2 load units per thread, small
-    // enough for 4 resident blocks per SM (56 KB each) where the row width allows
+    // enough for 32 resident warps per SM where the row width allows
+    const int per_sm_target = std::max(1, 32 / h.a.warps);
+    const int budget = (228 * 1024) / per_sm_target - 1024;
     const int fixed = h.a.warps * (int)scratch + 4 * c.D.rs;
-    const int fit4 = (56 * 1024 - fixed) / (c.D.rs + 8);
-    h.a.stage_rows = std::max(32, std::min({256, (2 * 256 * 4 / pieces) / 32 * 32, fit4 / 32 * 32}));
+    const int fit = (budget - fixed) / (c.D.rs + 8);
+    h.a.stage_rows = std::max(32, std::min({256, (2 * 32 * h.a.warps * 4 / pieces) / 32 * 32, fit / 32 * 32}));
     h.a.cstride = h.a.stage_rows + 4;
     h.a.warp_bytes = scratch;
     h.threads = 32 * h.a.warps;
