@@ -464,6 +464,7 @@ __global__ void __launch_bounds__(512, 2) k_hist(Data D, Batch B, int cur, HistA
 // only the histogram, which keeps many warps resident to hide the latency.
 // ---------------------------------------------------------------------------------------
 constexpr int kSmallRows = kSmallNodeRegr / 32;  // rows per lane in k_hist_small
+constexpr int kSmallListOff = 64;                 // regression list area offset per warp
 
 __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, int warp_bytes) {
     extern __shared__ __align__(16) uint8_t smem[];
@@ -476,9 +477,12 @@ __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, in
     float *sy, *sy2;
     int *cn, *h;
     warp_scratch(wbase, bl, sy, sy2, cn, h);
-    // regression list area after the histogram: sums, square sums, counts, right sums,
-    // right square sums, (draw, bin, last) words -- kListCap entries each
-    float* LA = reinterpret_cast<float*>(wbase + kHistScratch);
+    // regression: the bin set's words and their rank offsets (8 + 8 words), then the list
+    // area: sums, square sums, counts, right sums, right square sums, (draw, bin, last)
+    // words -- kListCap entries each (no 256-bin histogram)
+    uint32_t* SW = reinterpret_cast<uint32_t*>(wbase);
+    int* SP = reinterpret_cast<int*>(SW + 8);
+    float* LA = reinterpret_cast<float*>(wbase + kSmallListOff);
     float* LA2 = LA + kListCap;
     int* LK = reinterpret_cast<int*>(LA2 + kListCap);
     float* LR = reinterpret_cast<float*>(LK + kListCap);
@@ -541,28 +545,71 @@ __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, in
                 int used = 0, nd = 0, my_off = 0, my_len = 0;
                 while (mv < B.mtry && nd < 32 && used + c <= kListCap) {
                     const int f = featp[mv];
+                    // the node's bins of this draw as a 256-bit set; a row's list entry is
+                    // its bin's rank in the set
+                    int bb[kSmallRows];
+                    uint32_t qmask[8];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) qmask[q] = 0u;
+#pragma unroll
+                    for (int hh = 0; hh < kSmallRows; ++hh) {
+                        bb[hh] = -1;
+                        if (hh * 32 < c) {
+                            const int i = hh * 32 + lane;
+                            if (i < c) bb[hh] = (int)__ldg(rowp[hh] + f);
+#pragma unroll
+                            for (int q = 0; q < 8; ++q)
+                                qmask[q] |= (bb[hh] >> 5) == q ? 1u << (bb[hh] & 31) : 0u;
+                        }
+                    }
+                    int nm = 0;
+                    uint32_t myw = 0u;
+                    int myp = 0;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const uint32_t wq = __reduce_or_sync(kFull, qmask[q]);
+                        if (lane == q) {
+                            myw = wq;
+                            myp = nm;
+                        }
+                        nm += __popc(wq);
+                    }
+                    if (lane < 8) {
+                        SW[lane] = myw;
+                        SP[lane] = myp;
+                    }
+                    for (int e = lane; e < nm; e += 32) {
+                        LA[used + e] = 0.0f;
+                        LA2[used + e] = 0.0f;
+                        LK[used + e] = 0;
+                    }
+                    __syncwarp();
+                    // per 32-row step, rows of the same bin add one rank at a time (row order)
 #pragma unroll
                     for (int hh = 0; hh < kSmallRows; ++hh) {
                         if (hh * 32 < c) {
-                            const int i = hh * 32 + lane;
-                            const bool valid = i < c;
-                            const int b = valid ? (int)__ldg(rowp[hh] + f) : kBins;
-                            hist_step(true, 1, valid, b, v[hh], v2[hh], 0, lane, sy, sy2, cn, h);
+                            const int b = bb[hh];
+                            const bool valid = b >= 0;
+                            int e = 0;
+                            if (valid) {
+                                const int q = b >> 5;
+                                e = used + SP[q] + __popc(SW[q] & ((1u << (b & 31)) - 1u));
+                                LDB[e] = ((uint32_t)mv << 8) | (uint32_t)b |
+                                         (e == used + nm - 1 ? kLastEntry : 0u);
+                            }
+                            const uint32_t peers = __match_any_sync(kFull, b);
+                            const int rank = __popc(peers & ((1u << lane) - 1u));
+                            const int maxr = __reduce_max_sync(kFull, valid ? __popc(peers) - 1 : 0);
+                            for (int qq = 0; qq <= maxr; ++qq) {
+                                if (valid && rank == qq) {
+                                    LA[e] += v[hh] * 1.0f;
+                                    LA2[e] += v2[hh] * 1.0f;
+                                    LK[e] += 1;
+                                }
+                                __syncwarp();
+                            }
                         }
                     }
-                    const int nm = warp_nonempty_bins(cn, bl, lane);
-                    for (int j = lane; j < nm; j += 32) {
-                        const int b = bl[j];
-                        const int e = used + j;
-                        LA[e] = sy[b];
-                        LA2[e] = sy2[b];
-                        LK[e] = cn[b];
-                        LDB[e] = ((uint32_t)mv << 8) | (uint32_t)b | (j == nm - 1 ? kLastEntry : 0u);
-                        sy[b] = 0.0f;
-                        sy2[b] = 0.0f;
-                        cn[b] = 0;
-                    }
-                    __syncwarp();
                     if (lane == nd) {
                         my_off = used;
                         my_len = nm;

@@ -339,7 +339,7 @@ HistCfg hist_cfg(Ctx& c) {
     // (k_hist: +4 bytes so that the warps' lists start in different shared-memory banks when
     // lanes of one warp read them side by side)
     const int scratch = (int)round_up(rfx::kHistScratch + (regr ? 2 * 1024 : (257 * c.nclass + 32) * 4), 16) + 4;
-    const int small_scratch = regr ? rfx::kHistScratch + 24 * rfx::kListCap : scratch;
+    const int small_scratch = regr ? 64 + 24 * rfx::kListCap : scratch;  // bin set + list area
     // regression: one block per node covers up to 16 draws (rows staged once per node, one
     // chain phase); classification: groups of 8 draws
     h.a.warps = regr ? std::max(1, std::min(16, c.prm.mtry)) : 8;
