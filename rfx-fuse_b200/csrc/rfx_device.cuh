@@ -177,6 +177,7 @@ struct Batch {
     float* d2;        // [T][N][p] regression importance squared errors per OOB rank
     float* d0;        // [T][N]
     float* rr;        // [T][p]
+    float* rsum;      // [T][p + 1] regression importance: row-order error sums
     float* tree_oob;  // [T][N] per-tree OOB predictions (NaN in-bag), optional
 };
 

@@ -120,6 +120,7 @@ void alloc_batch(Ctx& c, int Tcap) {
     B.right = (int*)c.b_right.get(T * 4);
     B.rightimp = (int*)c.b_rightimp.get(T * p * 4);
     B.rr = (float*)c.b_rr.get(T * p * 4);
+    B.rsum = (float*)c.b_rsum.get(T * (p + 1) * 4);
     if (c.task == RFX_TASK_REGRESSION && c.prm.compute_importance) {
         B.d2 = (float*)c.b_d2.get(T * N * p * 4);
         B.d0 = (float*)c.b_d0.get(T * N * 4);
@@ -460,12 +461,13 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
             rfx::k_imp_class_rr<<<T, 256, 0, st>>>(D, B);
         } else {
             rfx::k_imp_regr<<<rg, 256, 0, st>>>(D, B);
-            const int tr = (int)std::max<size_t>(1, std::min<size_t>(64, (48 * 1024) / ((p + 1) * 4)));
-            rfx::k_imp_regr_sum<<<T, 256, (size_t)tr * (p + 1) * 4, st>>>(D, B, tr);
+            const size_t warps = (size_t)T * ((p + 1 + 31) / 32);
+            rfx::k_imp_regr_sum<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(D, B);
+            rfx::k_imp_regr_rr<<<T, 256, 0, st>>>(D, B);
         }
         rfx::k_imp_fold<<<1, 256, 0, st>>>(D, B, (float*)c.avimp.p, (float*)c.sqsd.p);
         RFX_LAUNCH("importance kernels");
-        c.launches += 4;
+        c.launches += c.nclass > 1 ? 4 : 5;
     }
     if (c.prm.compute_proximity && c.prox) {
         if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev0, st));

@@ -37,7 +37,8 @@ __global__ void k_imp_used(Data D, Batch B);
 __global__ void k_imp_class(Data D, Batch B);
 __global__ void k_imp_class_rr(Data D, Batch B);
 __global__ void k_imp_regr(Data D, Batch B);
-__global__ void k_imp_regr_sum(Data D, Batch B, int tile_rows);
+__global__ void k_imp_regr_sum(Data D, Batch B);
+__global__ void k_imp_regr_rr(Data D, Batch B);
 __global__ void k_imp_fold(Data D, Batch B, float* avimp, float* sqsd);
 __global__ void k_prox(Data D, Batch B, int R, int* C);
 __global__ void k_prox_codes(Batch B, int N, int R, uint16_t* code, int* ocnt,

@@ -168,10 +168,8 @@ __global__ void k_imp_class_rr(Data D, Batch B) {
 
 // Regression importance, squared errors (cpu_varimp_regression, src/rf_varimp.cpp:477-597):
 // d0[j] for the unpermuted prediction, d2[j][k] with feature k permuted, per OOB rank j.
-__global__ void __launch_bounds__(256) k_imp_regr(Data D, Batch B) {
-    const int t = blockIdx.y;
-    const int j = blockIdx.x * blockDim.x + threadIdx.x;
-    if (j >= B.noob[t]) return;
+// The squared errors of OOB rank j of tree t into out[0, p).
+__device__ void imp_regr_row(const Data& D, const Batch& B, int t, int j, float* out) {
     const size_t mo = (size_t)t * B.M;
     const int *st = B.status + mo, *bv = B.bestvar + mo, *tm = B.treemap + 2 * mo;
     const float *xb = B.xbest + mo, *np = B.nodepred + mo;
@@ -183,23 +181,28 @@ __global__ void __launch_bounds__(256) k_imp_regr(Data D, Batch B) {
     B.d0[(size_t)t * D.N + j] = dd;
     const int prow = D.perm[row];
     const int nn = B.nnode[t];
-    float* out = B.d2 + ((size_t)t * D.N + j) * D.p;
     // The permuted walk for feature k follows the row's own path up to the first node that
-    // tests k; features never tested on the path keep the unpermuted error.
+    // tests k; features never tested on the path keep the unpermuted error.  Along the path
+    // only the nodes testing k can turn the walk, so it is followed from the recorded path
+    // and walked from the tree only where the permuted value leaves the path.
     constexpr int kMaxPath = 48;
     int path[kMaxPath];
+    int pf[kMaxPath];  // feature tested at path[q]
     int depth = 0;
+    int kend = 0;      // the row's terminal node
     bool deep = D.has_cat != 0;
     if (!deep) {
         int kt = 0, steps = 0;
         while (st[kt] == 1 && steps < 1000) {
             ++steps;
             if (depth == kMaxPath) { deep = true; break; }
-            path[depth++] = kt;
+            path[depth] = kt;
             const int mv = bv[kt];
+            pf[depth++] = mv;
             kt = D.xc[(size_t)mv * D.N + row] <= xb[kt] ? tm[2 * kt] : tm[2 * kt + 1];
             if (st[kt] != 1) break;
         }
+        kend = kt;
     }
     if (deep) {
         for (int k = 0; k < D.p; ++k) {
@@ -210,71 +213,89 @@ __global__ void __launch_bounds__(256) k_imp_regr(Data D, Batch B) {
     }
     for (int k = 0; k < D.p; ++k) out[k] = dd;
     for (int i = 0; i < depth; ++i) {
-        const int f = bv[path[i]];
+        const int f = pf[i];
         bool first = true;
-        for (int q = 0; q < i; ++q) first &= bv[path[q]] != f;
+        for (int q = 0; q < i; ++q) first &= pf[q] != f;
         if (!first) continue;
-        // resume the walk at path[i] with feature f read from the permuted row
-        int kt = path[i];
+        const float vf = D.xc[(size_t)f * D.N + prow];
+        int q = i, kt = -1;
+        bool left_path = false;
+        for (; q < depth; ++q) {
+            if (pf[q] != f) continue;
+            const int node = path[q];
+            kt = vf <= xb[node] ? tm[2 * node] : tm[2 * node + 1];
+            if (kt != (q + 1 < depth ? path[q + 1] : kend)) { left_path = true; break; }
+        }
+        if (!left_path) {  // the permuted walk reaches the row's own terminal node
+            kt = kend;
+            q = depth - 1;
+        }
         float pk = 0.0f;
-        for (int k = i; k < nn; ++k) {
-            if (st[kt] == -1) { pk = np[kt]; break; }
-            const int m = bv[kt];
-            const float v = D.xc[(size_t)m * D.N + (m == f ? prow : row)];
-            kt = v <= xb[kt] ? tm[2 * kt] : tm[2 * kt + 1];
-            if (kt < 0 || kt >= nn) break;
+        if (kt >= 0 && kt < nn) {
+            // the rest of the walk, with the step budget the full walk from path[i] has left
+            for (int k = q + 1; k < nn; ++k) {
+                if (st[kt] == -1) { pk = np[kt]; break; }
+                const int m = bv[kt];
+                const float v = D.xc[(size_t)m * D.N + (m == f ? prow : row)];
+                kt = v <= xb[kt] ? tm[2 * kt] : tm[2 * kt + 1];
+                if (kt < 0 || kt >= nn) break;
+            }
         }
         const float dk = pk - y;
         out[f] = 1.0f * dk * dk;
     }
 }
 
-// Serial sums over the OOB rows in row order (the reference's loop order), then
-// rr = mse_perm - mse_orig.  One block per tree: the block streams tiles of the row-major
-// [noob][p] squared errors through shared memory with coalesced loads; thread k then adds
-// feature k's column of the tile in row order, thread p the unpermuted errors.
-__global__ void __launch_bounds__(256) k_imp_regr_sum(Data D, Batch B, int kSumTile) {
-    extern __shared__ float tile[];  // [kSumTile][p + 1]
-    __shared__ float mse0;
-    const int t = blockIdx.x;
-    const int noob = B.noob[t];
+// One thread per OOB rank, rows written straight to d2 (the walks, not the stores, bound
+// this kernel: staging the block's rows in shared memory measured slower).
+__global__ void __launch_bounds__(256) k_imp_regr(Data D, Batch B) {
+    const int t = blockIdx.y;
+    const int j = blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= B.noob[t]) return;
+    imp_regr_row(D, B, t, j, B.d2 + ((size_t)t * D.N + j) * D.p);
+}
+
+// Serial sums over the OOB rows in row order (the reference's loop order).  One warp per
+// (tree, 32 columns): lane k keeps column k's running sum (k < p: the permuted errors of
+// feature k, k == p: the unpermuted errors) and reads one row of 32 consecutive floats per
+// step, 32 rows in flight.  rsum[t][k] = the sums.
+__global__ void __launch_bounds__(256) k_imp_regr_sum(Data D, Batch B) {
+    constexpr int U = 32;
     const int p = D.p, P1 = D.p + 1;
-    if (noob == 0) {
-        for (int k = threadIdx.x; k < p; k += blockDim.x) B.rr[(size_t)t * p + k] = 0.0f;
-        return;
+    const int nch = (P1 + 31) / 32;
+    const int g = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (g >= B.T * nch) return;
+    const int t = g / nch, k = (g - t * nch) * 32 + lane;
+    if (k > p) return;
+    const int noob = B.noob[t];
+    const float* src = k < p ? B.d2 + (size_t)t * D.N * p + k : B.d0 + (size_t)t * D.N;
+    const size_t stride = k < p ? (size_t)p : 1;
+    float s = 0.0f;
+    int j = 0;
+    for (; j + U <= noob; j += U) {
+        float x[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) x[u] = src[(size_t)(j + u) * stride];
+#pragma unroll
+        for (int u = 0; u < U; ++u) s += x[u];
     }
-    const float* d2 = B.d2 + (size_t)t * D.N * p;
-    const float* d0 = B.d0 + (size_t)t * D.N;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // columns threadIdx.x + 256*q (q < 4: p+1 <= 1024)
-    for (int j0 = 0; j0 < noob; j0 += kSumTile) {
-        const int rows = min(kSumTile, noob - j0);
-        __syncthreads();
-        for (int e = threadIdx.x; e < rows * p; e += blockDim.x) {
-            const int r = e / p, k = e - r * p;
-            tile[r * P1 + k] = d2[(size_t)(j0 + r) * p + k];
+    for (; j < noob; ++j) s += src[(size_t)j * stride];
+    B.rsum[(size_t)t * P1 + k] = s;
+}
+
+// rr = mse_perm - mse_orig per (tree, feature), 0 for a tree without OOB rows.
+__global__ void k_imp_regr_rr(Data D, Batch B) {
+    const int t = blockIdx.x, p = D.p;
+    const int noob = B.noob[t];
+    const float* sum = B.rsum + (size_t)t * (p + 1);
+    for (int k = threadIdx.x; k < p; k += blockDim.x) {
+        if (noob == 0) {
+            B.rr[(size_t)t * p + k] = 0.0f;
+        } else {
+            const float mse0 = sum[p] / (float)noob;
+            B.rr[(size_t)t * p + k] = sum[k] / (float)noob - mse0;
         }
-        for (int r = threadIdx.x; r < rows; r += blockDim.x) tile[r * P1 + p] = d0[j0 + r];
-        __syncthreads();
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int k = threadIdx.x + q * blockDim.x;
-            if (k <= p) {
-                float s = acc[q];
-                for (int r = 0; r < rows; ++r) s += tile[r * P1 + k];
-                acc[q] = s;
-            }
-        }
-    }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const int k = threadIdx.x + q * blockDim.x;
-        if (k == p) mse0 = acc[q] / (float)noob;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const int k = threadIdx.x + q * blockDim.x;
-        if (k < p) B.rr[(size_t)t * p + k] = acc[q] / (float)noob - mse0;
     }
 }
 
