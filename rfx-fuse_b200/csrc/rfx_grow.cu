@@ -71,90 +71,144 @@ __global__ void __launch_bounds__(1024) k_level_begin(Batch B) {
 }
 
 // ---------------------------------------------------------------------------------------
-// Node evaluation (one warp per node of the level): member count, class counts and
-// majority, or the serial float sums of y; the size, purity and variance tests that
+// Node evaluation (classification: one warp per node of the level; regression: one lane
+// per node of at most kLaneNode rows, one warp per larger node): member count, class
+// counts and majority, or the serial float sums of y; the size, purity and variance tests that
 // decide whether the node is searched (src/rf_growtree.cpp:700-774); crit0 (:783-795).
 // Nodes that are not searched become terminal here.
 // ---------------------------------------------------------------------------------------
+// Node record and stop tests from the node's sums (regression ts/ts2) or class counts.
+__device__ __forceinline__ void node_finalize(const Batch& B, size_t m, int c, int cur, bool regr,
+                                              float ts, float ts2, int maj, int nz) {
+    B.nd_buf[m] = (uint8_t)cur;
+    bool searched = c >= B.minsplit;
+    float crit0 = 0.0f;
+    if (regr) {
+        const float tw = (float)c;
+        B.nd_sum[m] = ts;
+        if (searched) {
+            if (tw > 1.0e-5f) {
+                const float mean = ts / tw;
+                const float var = ts2 / tw - mean * mean;
+                if (var < 1.0e-6f) searched = false;
+                crit0 = var;
+            } else {
+                searched = false;
+            }
+        }
+    } else {
+        B.nd_maj[m] = maj;
+        if (searched && nz <= 1) searched = false;
+    }
+    B.nd_crit0[m] = crit0;
+    B.nd_flag[m] = searched ? 1 : 0;
+    if (!searched) {
+        B.status[m] = -1;
+        B.nodeclass[m] = regr ? 0 : maj;
+        if (regr) {
+            B.nodepred[m] = c > 0 ? ts / (float)c : 0.0f;
+            B.tnodewt[m] = c > 0 ? 1.0f : 0.0f;
+        }
+    }
+}
+
+// Regression nodes up to this many rows are summed by one lane (32 nodes per warp).
+constexpr int kLaneNode = 64;
+
 __global__ void __launch_bounds__(256) k_node_eval(Data D, Batch B, int cur) {
     __shared__ int ccount[8][kMaxClass];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int total = B.counters[0];
     const int nwarps = gridDim.x * (blockDim.x >> 5);
     const bool regr = D.nclass == 1;
+    if (regr) {
+        // G level nodes per warp (G = nodes per warp of the grid, 1..32, so that every
+        // warp has work at the top levels): a lane sums a small node's rows serially (row
+        // order); the larger ones are summed by the whole warp, one after another
+        const int G = max(1, min(32, total / nwarps));
+        for (int w0 = (blockIdx.x * (blockDim.x >> 5) + wib) * G; w0 < total; w0 += nwarps * G) {
+            const int w = w0 + lane;
+            size_t m = 0;
+            int c = 0, start = 0, t = 0;
+            if (lane < G && w < total) {
+                t = tree_of(B.lvl_off, B.T, w);
+                m = (size_t)t * B.M + B.lvl_lo[t] + (w - B.lvl_off[t]);
+                start = B.nd_start[m];
+                c = B.nd_cnt[m];
+            }
+            const bool mine = lane < G && w < total && c <= kLaneNode;
+            if (mine) {
+                const int* seg = B.seg[cur] + (size_t)t * D.N + start;
+                float ts = 0.0f, ts2 = 0.0f;
+                constexpr int U = 8;
+                for (int i0 = 0; i0 < c; i0 += U) {
+                    float v[U];
+#pragma unroll
+                    for (int q = 0; q < U; ++q) v[q] = i0 + q < c ? D.yv[seg[i0 + q]] : 0.0f;
+#pragma unroll
+                    for (int q = 0; q < U; ++q) {
+                        if (i0 + q < c) {
+                            ts += v[q] * 1.0f;
+                            ts2 += v[q] * v[q] * 1.0f;
+                        }
+                    }
+                }
+                node_finalize(B, m, c, cur, true, ts, ts2, 0, 0);
+            }
+            unsigned big = __ballot_sync(kFull, lane < G && w < total && !mine);
+            while (big) {
+                const int src = __ffs(big) - 1;
+                big &= big - 1;
+                const size_t mb = __shfl_sync(kFull, (unsigned long long)m, src);
+                const int cb = __shfl_sync(kFull, c, src);
+                const int sb = __shfl_sync(kFull, start, src);
+                const int tb = __shfl_sync(kFull, t, src);
+                const int* seg = B.seg[cur] + (size_t)tb * D.N + sb;
+                // serial sums in row order (lane 0's copy is the one kept); 8 x 32 values
+                // are gathered per step so their loads are in flight together
+                float ts = 0.0f, ts2 = 0.0f;
+                constexpr int U = 8;
+                for (int b0 = 0; b0 < cb; b0 += 32 * U) {
+                    float v[U];
+#pragma unroll
+                    for (int q = 0; q < U; ++q) {
+                        const int i = b0 + q * 32 + lane;
+                        v[q] = i < cb ? D.yv[seg[i]] : 0.0f;
+                    }
+#pragma unroll
+                    for (int q = 0; q < U; ++q) {
+                        const int k = min(32, cb - (b0 + q * 32));
+                        for (int j = 0; j < k; ++j) {
+                            const float x = __shfl_sync(kFull, v[q], j);
+                            ts += x * 1.0f;
+                            ts2 += x * x * 1.0f;
+                        }
+                    }
+                }
+                if (lane == 0) node_finalize(B, mb, cb, cur, true, ts, ts2, 0, 0);
+                __syncwarp();
+            }
+        }
+        return;
+    }
     for (int w = blockIdx.x * (blockDim.x >> 5) + wib; w < total; w += nwarps) {
         const int t = tree_of(B.lvl_off, B.T, w);
         const int node = B.lvl_lo[t] + (w - B.lvl_off[t]);
         const size_t m = (size_t)t * B.M + node;
         const int start = B.nd_start[m], c = B.nd_cnt[m];
         const int* seg = B.seg[cur] + (size_t)t * D.N + start;
-        float ts = 0.0f, ts2 = 0.0f;
         int maj = 0, nz = 0;
-        if (regr) {
-            // serial sums in row order (lane 0's copy is the one kept); 8 x 32 values are
-            // gathered per step so their loads are in flight together
-            constexpr int U = 8;
-            for (int b0 = 0; b0 < c; b0 += 32 * U) {
-                float v[U];
-#pragma unroll
-                for (int q = 0; q < U; ++q) {
-                    const int i = b0 + q * 32 + lane;
-                    v[q] = i < c ? D.yv[seg[i]] : 0.0f;
-                }
-#pragma unroll
-                for (int q = 0; q < U; ++q) {
-                    const int k = min(32, c - (b0 + q * 32));
-                    for (int j = 0; j < k; ++j) {
-                        const float x = __shfl_sync(kFull, v[q], j);
-                        ts += x * 1.0f;
-                        ts2 += x * x * 1.0f;
-                    }
-                }
-            }
-        } else {
-            if (lane < kMaxClass) ccount[wib][lane] = 0;
-            __syncwarp();
-            for (int i = lane; i < c; i += 32) atomicAdd(&ccount[wib][D.lab[seg[i]]], 1);
-            __syncwarp();
-            int mx = 0;
-            for (int j = 0; j < D.nclass; ++j) {
-                const int k = ccount[wib][j];
-                if (k > 0) { ++nz; if (k > mx) { mx = k; maj = j; } }
-            }
-            __syncwarp();
+        if (lane < kMaxClass) ccount[wib][lane] = 0;
+        __syncwarp();
+        for (int i = lane; i < c; i += 32) atomicAdd(&ccount[wib][D.lab[seg[i]]], 1);
+        __syncwarp();
+        int mx = 0;
+        for (int j = 0; j < D.nclass; ++j) {
+            const int k = ccount[wib][j];
+            if (k > 0) { ++nz; if (k > mx) { mx = k; maj = j; } }
         }
-        if (lane == 0) {
-        B.nd_buf[m] = (uint8_t)cur;
-        bool searched = c >= B.minsplit;
-        float crit0 = 0.0f;
-        if (regr) {
-            const float tw = (float)c;
-            B.nd_sum[m] = ts;
-            if (searched) {
-                if (tw > 1.0e-5f) {
-                    const float mean = ts / tw;
-                    const float var = ts2 / tw - mean * mean;
-                    if (var < 1.0e-6f) searched = false;
-                    crit0 = var;
-                } else {
-                    searched = false;
-                }
-            }
-        } else {
-            B.nd_maj[m] = maj;
-            if (searched && nz <= 1) searched = false;
-        }
-        B.nd_crit0[m] = crit0;
-        B.nd_flag[m] = searched ? 1 : 0;
-        if (!searched) {
-            B.status[m] = -1;
-            B.nodeclass[m] = regr ? 0 : maj;
-            if (regr) {
-                B.nodepred[m] = c > 0 ? ts / (float)c : 0.0f;
-                B.tnodewt[m] = c > 0 ? 1.0f : 0.0f;
-            }
-        }
-        }
+        __syncwarp();
+        if (lane == 0) node_finalize(B, m, c, cur, false, 0.0f, 0.0f, maj, nz);
         __syncwarp();
     }
 }
