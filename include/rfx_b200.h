@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define RFX_ABI_VERSION 2
+#define RFX_ABI_VERSION 3
 
 enum {
     RFX_OK = 0,
@@ -60,6 +60,8 @@ typedef struct {
                                kept; every tree's leaf groups are stored instead for
                                rfx_lowrank_build.  Rank <= 64. */
     int keep_forest;        /* keep the grown trees on the device (packed) for rfx_predict */
+    int keep_leaves;        /* compute_leaf_assignments: keep every row's terminal node per
+                               tree and the per-tree OOB flags on the device (rfx_leaf_*) */
 } rfx_fit_params;
 
 typedef struct {
@@ -225,6 +227,57 @@ int rfx_load_forest(void* ctx, const rfx_forest* forest);
  * proba_out [n][nclass], value_out [n] (regression). */
 int rfx_predict(void* ctx, const float* X_host, int n, int p, int* class_out, float* proba_out,
                 float* value_out);
+
+/* ---- Leaf assignments, top-k similar rows, outliers -----------------------------------
+ * A fit with keep_leaves stores, per tree, every grown row's terminal node as int16 (the
+ * reference's leaf_assignments_ [tree][sample], src/rf_random_forest.cpp:1543-1610, found by
+ * walking the row down the tree like find_terminal_node, :3724-3770) and which rows were OOB
+ * (oob_trees_, :1577-1590).  Numeric features only (RFX_ERR_UNSUPPORTED at fit time when a
+ * categorical feature is present).  The queries below follow
+ * include/rf_random_forest.hpp:296-365. */
+/* get_leaf_assignments (python/randomforest_py.cpp:2373-2393): out [ntree][N] int16, N = the
+ * grown rows (2n for unsupervised); out may be NULL to read the shape only. */
+int rfx_leaf_assignments(void* ctx, int16_t* out, int* ntree_out, int* nrows_out);
+/* build_inverted_leaf_index (src/rf_random_forest.cpp:4644-4675): rows grouped by (tree, leaf),
+ * ascending inside a group.  The queries build it on first use, like the reference's bindings. */
+int rfx_leaf_index(void* ctx);
+/* get_top_k_similar (src/rf_random_forest.cpp:4677-4787) for nq training rows: counts of the
+ * trees where the query was OOB and the row shares its leaf, the nonzero ones ranked with the
+ * reference's std::partial_sort (descending count); similarity = count / (query's OOB trees).
+ * idx_out / sim_out [nq][k]; counts_out[q] = entries written (0: no OOB tree, no match, or an
+ * invalid query -- the reference returns an empty list). */
+int rfx_leaf_top_k_similar(void* ctx, const int* queries, int nq, int k, int exclude_self,
+                           int* idx_out, float* sim_out, int* counts_out);
+/* compute_proximity_from_leaves (src/rf_random_forest.cpp:4605-4642): matches over the trees
+ * where row i was OOB / their number; 0 when unavailable or out of range. */
+int rfx_leaf_proximity(void* ctx, int i, int j, float* out);
+/* predict_leaf_assignments (src/rf_random_forest.cpp:4789-4850) on the device forest (fit with
+ * keep_forest): X_host [n][p], out [n][ntree] int16.  A node whose feature is out of range, or a
+ * categorical value outside [0, cat), keeps the walk where it is (the reference's loop then
+ * runs out its maxnode steps on that node). */
+int rfx_predict_leaves(void* ctx, const float* X_host, int n, int p, int16_t* out);
+/* predict_top_k_similar (python/randomforest_py.cpp:2496-2560): for each new row the fraction
+ * of all trees where a training row shares its leaf, top k by std::partial_sort over every
+ * training row (the reference's tie order); idx_out / sim_out [n][k], k <= N. */
+int rfx_predict_top_k_similar(void* ctx, const float* X_host, int n, int p, int k, int* idx_out,
+                              float* sim_out);
+/* select_outlier_anchors (src/rf_random_forest.cpp:4305-4386): method 0 "random" (std::mt19937
+ * (iseed) shuffle of 0..N-1), 1 "diverse" (start at a uniform draw, then repeatedly the first
+ * row of least leaf proximity to the anchors so far); n_anchors >= N gives all rows.
+ * anchors_out [min(n_anchors, N)], count_out = entries. */
+int rfx_leaf_select_anchors(void* ctx, int n_anchors, int method, uint32_t iseed, int* anchors_out,
+                            int* count_out);
+/* compute_outlier_scores (src/rf_random_forest.cpp:4110-4277).  mode 0 "full": raw = (N - 1) /
+ * sum over the other rows of (shared trees / ntree)^2 over all trees; mode 1 "greedy": raw =
+ * n_anchors / the same sum over `anchors` (skipping the row itself).  Scores = (raw - median) /
+ * MAD, per class when labels (0-based, [N]) are given, else over all rows.  raw_out may be NULL.
+ * Greedy is the reference's arithmetic exactly; full sums the squares exactly in integers and
+ * rounds once (the reference adds float terms in hash-map order). */
+int rfx_leaf_outlier_scores(void* ctx, int mode, const int* anchors, int n_used, int n_anchors,
+                            const int* labels, float* scores_out, float* raw_out);
+/* compute_outliers' ranking (src/rf_random_forest.cpp:4279-4303): std::sort of (index, score)
+ * by score descending, first k.  Host only. */
+int rfx_rank_scores_desc(const float* scores, int n, int k, int* idx_out, float* val_out);
 
 /* ---- Proximity-weighted imputation ---------------------------------------------------
  * One round of rfx_impute_proximity's fill (python/rfx_impute.py:730-775, aggregation

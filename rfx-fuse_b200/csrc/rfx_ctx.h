@@ -136,6 +136,13 @@ struct Ctx {
     int f_T = 0, f_cap = 0, f_M = 0, f_p = 0, f_nclass = 0, f_task = 0;
     bool f_classwt = false;
     DBuf f_nodes, f_root, f_cat, f_cw, p_X, p_xc, p_vote, p_val, p_cls, p_proba, p_pred;
+    // leaf assignments (rfx_leaves.cu): int16 leaf [l_cap][N], OOB bit words [l_cap][l_words],
+    // the inverted index (rows grouped by (tree, leaf); group g = t * l_W + (uint16)leaf)
+    int l_T = 0, l_cap = 0, l_words = 0, l_W = 0;
+    bool l_index = false;
+    std::vector<int> l_anchors;  // the last selected outlier anchors (reused like the reference)
+    DBuf l_leaf, l_oob, l_rows, l_gs, l_ge, l_keys, l_cub, l_cnt, l_cidx, l_cval, l_nnz, l_q,
+        l_out, l_f;
     // imputation round (rfx_impute_host.cu)
     DBuf i_x, i_miss, i_cat, i_S, i_scratch, i_cells, i_out, i_prof;
 
@@ -159,7 +166,8 @@ struct Ctx {
                        &lr_code, &lr_order, &lr_goff, &lr_ngroups, &lr_tmp, &lr_X, &lr_Z,
                        &lr_CZ, &lr_Y, &lr_ls, &lr_part, &lr_small, &lr_A, &lr_q, &lr_qb, &lr_s, &lr_qbp, &lr_sp, &lr_perm, &lr_blocks, &lr_np, &lr_norm, &lr_ids, &lr_keys, &lr_order_s, &lr_cub, &f_nodes, &f_root, &f_cat, &f_cw, &p_X,
                        &p_xc, &p_vote, &p_val, &p_cls, &p_proba, &p_pred, &i_x, &i_miss, &i_cat,
-                       &i_S, &i_scratch, &i_cells, &i_out, &i_prof,
+                       &i_S, &i_scratch, &i_cells, &i_out, &i_prof, &l_leaf, &l_oob, &l_rows, &l_gs, &l_ge,
+                       &l_keys, &l_cub, &l_cnt, &l_cidx, &l_cval, &l_nnz, &l_q, &l_out, &l_f,
                        &lr_err, &lr_out_i, &lr_out_v};
         cudaSetDevice(device);
         if (st) cudaStreamSynchronize(st);
@@ -192,5 +200,9 @@ void lr_store_batch(Ctx& c, const rfx::Batch& B, int T);
 void forest_reserve(Ctx& c, int extra);
 void forest_store_batch(Ctx& c, const rfx::Batch& B, int T);
 void forest_reset(Ctx& c);
+
+// Leaf assignments (rfx_leaves.cu): forget the stored trees; store a grown batch's leaves.
+void leaves_reset(Ctx& c);
+void leaves_store_batch(Ctx& c, const rfx::Batch& B, int T);
 
 }  // namespace rfxh

@@ -193,6 +193,8 @@ void load(Ctx& c, const rfx_fit_params* prm, const rfx_inputs* in) {
     c.R = P.prox_rows > 0 ? std::min<int>(P.prox_rows, (int)N) : (int)N;
     require(!(P.compute_proximity && has_cat), RFX_ERR_UNSUPPORTED,
             "proximity with categorical features is not supported yet");
+    require(!(P.keep_leaves && has_cat), RFX_ERR_UNSUPPORTED,
+            "leaf assignments with categorical features are not supported yet");
     require(P.lowrank_rank >= 0 && P.lowrank_rank <= 64, RFX_ERR_UNSUPPORTED,
             "low-rank proximity rank must be in [0, 64]");
     require(P.lowrank_rank == 0 || P.maxnode + 1 < 65535, RFX_ERR_UNSUPPORTED,
@@ -297,6 +299,7 @@ void load(Ctx& c, const rfx_fit_params* prm, const rfx_inputs* in) {
     c.prox = nullptr;
     c.prox_len = 0;
     forest_reset(c);
+    leaves_reset(c);
     c.lr_rank = P.compute_proximity && P.lowrank_rank > 0 ? P.lowrank_rank : 0;
     c.lr_n = 0;
     c.lr_G = c.M + 2;
@@ -517,6 +520,7 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
     }
     if (c.lr_rank > 0) lr_store_batch(c, B, T);
     if (c.prm.keep_forest) forest_store_batch(c, B, T);
+    if (c.prm.keep_leaves) leaves_store_batch(c, B, T);
     if (keep) c.tree_oob_n += T;
     if (out) {
         auto cp = [&](void* dst, const void* src, size_t elems, size_t esz) {

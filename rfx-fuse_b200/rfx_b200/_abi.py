@@ -27,7 +27,7 @@ class FitParams(C.Structure):
     _fields_ = [(k, C.c_int) for k in (
         "task", "n", "p", "mtry", "minndsize", "maxnode", "iseed", "boot_seed", "nbins",
         "maxcat", "compute_importance", "compute_proximity", "prox_rows", "batch_trees",
-        "keep_tree_oob", "lowrank_rank", "keep_forest")]
+        "keep_tree_oob", "lowrank_rank", "keep_forest", "keep_leaves")]
 
 
 class Inputs(C.Structure):
@@ -69,13 +69,27 @@ SYMBOLS = (
     "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats", "rfx_sync",
     "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk", "rfx_lowrank_product",
     "rfx_prox_apply", "rfx_lowrank_set_factors", "rfx_load_forest", "rfx_predict",
-    "rfx_lowrank_topk_part", "rfx_impute_round",
+    "rfx_lowrank_topk_part", "rfx_impute_round", "rfx_leaf_assignments", "rfx_leaf_index",
+    "rfx_leaf_top_k_similar", "rfx_leaf_proximity", "rfx_predict_leaves",
+    "rfx_predict_top_k_similar", "rfx_leaf_select_anchors", "rfx_leaf_outlier_scores",
+    "rfx_rank_scores_desc",
 )
 
 # int (*)(void* user, float* buf_dev, int64_t count): in-place sum over processes
 REDUCE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_int64)
 
 _LIB = None
+
+
+def rank_scores_desc(scores, k: int):
+    """The reference's std::sort of (index, score) by score descending, first k."""
+    L = load_library()
+    sc = np.ascontiguousarray(scores, np.float32)
+    kk = min(int(k), sc.shape[0])
+    idx = np.zeros(max(kk, 1), np.int32)
+    val = np.zeros(max(kk, 1), np.float32)
+    check(L.rfx_rank_scores_desc(ptr(sc, _pf), sc.shape[0], kk, ptr(idx, _pi), ptr(val, _pf)))
+    return idx[:kk], val[:kk]
 
 
 def load_library(path: str = LIB_PATH):
@@ -123,6 +137,16 @@ def load_library(path: str = LIB_PATH):
     L.rfx_lowrank_topk_part.argtypes = [vp, C.c_int, C.c_int, C.c_int, _pi, _pi, _pf,
                                         C.POINTER(C.c_int)]
     L.rfx_predict.argtypes = [vp, _pf, C.c_int, C.c_int, _pi, _pf, _pf]
+    _pi16 = C.POINTER(C.c_int16)
+    L.rfx_leaf_assignments.argtypes = [vp, _pi16, _pi, _pi]
+    L.rfx_leaf_index.argtypes = [vp]
+    L.rfx_leaf_top_k_similar.argtypes = [vp, _pi, C.c_int, C.c_int, C.c_int, _pi, _pf, _pi]
+    L.rfx_leaf_proximity.argtypes = [vp, C.c_int, C.c_int, _pf]
+    L.rfx_predict_leaves.argtypes = [vp, _pf, C.c_int, C.c_int, _pi16]
+    L.rfx_predict_top_k_similar.argtypes = [vp, _pf, C.c_int, C.c_int, C.c_int, _pi, _pf]
+    L.rfx_leaf_select_anchors.argtypes = [vp, C.c_int, C.c_int, C.c_uint32, _pi, _pi]
+    L.rfx_leaf_outlier_scores.argtypes = [vp, C.c_int, _pi, C.c_int, C.c_int, _pi, _pf, _pf]
+    L.rfx_rank_scores_desc.argtypes = [_pf, C.c_int, C.c_int, _pi, _pf]
     for name in ("rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
                  "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish",
                  "rfx_prox_dense", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host",
@@ -130,7 +154,10 @@ def load_library(path: str = LIB_PATH):
                  "rfx_sync", "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk",
                  "rfx_lowrank_product", "rfx_prox_apply", "rfx_lowrank_set_factors",
                  "rfx_load_forest", "rfx_predict", "rfx_lowrank_topk_part",
-                 "rfx_impute_round"):
+                 "rfx_impute_round", "rfx_leaf_assignments", "rfx_leaf_index",
+                 "rfx_leaf_top_k_similar", "rfx_leaf_proximity", "rfx_predict_leaves",
+                 "rfx_predict_top_k_similar", "rfx_leaf_select_anchors",
+                 "rfx_leaf_outlier_scores", "rfx_rank_scores_desc"):
         getattr(L, name).restype = C.c_int
     _LIB = L
     return L
@@ -267,6 +294,74 @@ class Context:
         val = np.zeros(n, np.float32)
         check(self._lib.rfx_predict(self.handle, ptr(X, _pf), n, p, None, None, ptr(val, _pf)))
         return val
+
+    # ---- leaf assignments ----
+    def leaf_assignments(self):
+        """int16 [ntree][N] terminal node of every grown row in every tree."""
+        T, N = C.c_int(0), C.c_int(0)
+        check(self._lib.rfx_leaf_assignments(self.handle, None, C.byref(T), C.byref(N)))
+        out = np.zeros((T.value, N.value), np.int16)
+        check(self._lib.rfx_leaf_assignments(self.handle, out.ctypes.data_as(C.POINTER(C.c_int16)),
+                                             None, None))
+        return out
+
+    def leaf_index(self):
+        check(self._lib.rfx_leaf_index(self.handle))
+
+    def leaf_top_k_similar(self, queries, k: int, exclude_self: bool = True):
+        """Per query: (indices int32 [m], similarities float32 [m]), m <= k."""
+        q = np.ascontiguousarray(queries, np.int32).reshape(-1)
+        nq = q.shape[0]
+        idx = np.zeros((nq, max(k, 1)), np.int32)
+        sim = np.zeros((nq, max(k, 1)), np.float32)
+        cnt = np.zeros(nq, np.int32)
+        check(self._lib.rfx_leaf_top_k_similar(self.handle, ptr(q, _pi), nq, int(k),
+                                               int(bool(exclude_self)), ptr(idx, _pi),
+                                               ptr(sim, _pf), ptr(cnt, _pi)))
+        return [(idx[i, :cnt[i]].copy(), sim[i, :cnt[i]].copy()) for i in range(nq)]
+
+    def leaf_proximity(self, i: int, j: int) -> float:
+        out = C.c_float(0.0)
+        check(self._lib.rfx_leaf_proximity(self.handle, int(i), int(j), C.byref(out)))
+        return out.value
+
+    def predict_leaves(self, X: np.ndarray, ntree: int):
+        X = np.ascontiguousarray(X, np.float32)
+        n, p = X.shape
+        out = np.zeros((n, ntree), np.int16)
+        check(self._lib.rfx_predict_leaves(self.handle, ptr(X, _pf), n, p,
+                                           out.ctypes.data_as(C.POINTER(C.c_int16))))
+        return out
+
+    def predict_top_k_similar(self, X: np.ndarray, k: int):
+        X = np.ascontiguousarray(X, np.float32)
+        n, p = X.shape
+        idx = np.zeros((n, k), np.int32)
+        sim = np.zeros((n, k), np.float32)
+        check(self._lib.rfx_predict_top_k_similar(self.handle, ptr(X, _pf), n, p, int(k),
+                                                  ptr(idx, _pi), ptr(sim, _pf)))
+        return idx, sim
+
+    def select_anchors(self, n_anchors: int, method: int, iseed: int):
+        out = np.zeros(max(1, int(n_anchors)), np.int32)
+        cnt = C.c_int(0)
+        check(self._lib.rfx_leaf_select_anchors(self.handle, int(n_anchors), int(method),
+                                                C.c_uint32(int(iseed) & 0xFFFFFFFF),
+                                                ptr(out, _pi), C.byref(cnt)))
+        return out[:cnt.value].copy()
+
+    def outlier_scores(self, mode: int, anchors, n_anchors: int, labels, nrows: int):
+        """(normalised scores, raw measures), float32 [nrows] each."""
+        a = None if anchors is None else np.ascontiguousarray(anchors, np.int32)
+        lab = None if labels is None else np.ascontiguousarray(labels, np.int32)
+        sc = np.zeros(nrows, np.float32)
+        raw = np.zeros(nrows, np.float32)
+        check(self._lib.rfx_leaf_outlier_scores(self.handle, int(mode),
+                                                None if a is None else ptr(a, _pi),
+                                                0 if a is None else a.shape[0], int(n_anchors),
+                                                None if lab is None else ptr(lab, _pi),
+                                                ptr(sc, _pf), ptr(raw, _pf)))
+        return sc, raw
 
     # ---- imputation ----
     def impute_round(self, xc: np.ndarray, miss: np.ndarray, is_cat: np.ndarray, cells: np.ndarray):

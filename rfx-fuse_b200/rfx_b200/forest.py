@@ -154,7 +154,9 @@ class _Forest:
         prm = A.FitParams(task, n, p, mtry, self.minndsize, maxnode, self.iseed, 12345,
                           self.n_bins, self.maxcat, int(self.compute_importance),
                           int(self.compute_proximity), self.prox_rows, self.batch_trees, 0,
-                          self._lowrank_rank(), int(task != A.TASK_UNSUPERVISED))
+                          self._lowrank_rank(),
+                          int(task != A.TASK_UNSUPERVISED or self.compute_leaf_assignments),
+                          int(self.compute_leaf_assignments))
         ycls = yreg = sw = cw = None
         if task == A.TASK_CLASSIFICATION:
             ycls = np.ascontiguousarray(y, dtype=np.int32)
@@ -334,6 +336,87 @@ class _Forest:
         if length:
             ctx.copy_to_host(out, dev)
         return out
+
+    # ---- leaf assignments, similar rows, outliers (include/rf_random_forest.hpp:296-365) ----
+    _NO_LEAVES = ("Leaf assignments not available. Set compute_leaf_assignments=True when "
+                  "creating the model.")
+
+    def _check_leaves(self):
+        self._check()
+        if not self.compute_leaf_assignments:
+            raise RuntimeError(self._NO_LEAVES)
+
+    def get_leaf_assignments(self):
+        """int16 [ntree, n_samples]: terminal node of every training row in every tree."""
+        self._check_leaves()
+        return self._context().leaf_assignments()
+
+    def build_inverted_leaf_index(self):
+        self._check_leaves()
+        self._context().leaf_index()
+        self._leaf_index_built = True
+
+    def has_inverted_leaf_index(self):
+        return bool(getattr(self, "_leaf_index_built", False))
+
+    def get_top_k_similar(self, query_idx, k=10, exclude_self=True):
+        """(indices int32, similarities float32) of the training rows sharing the query's
+        leaf most often over the trees where the query was OOB."""
+        self._check_leaves()
+        self._leaf_index_built = True  # built on first use, as the reference's binding does
+        (idx, sim), = self._context().leaf_top_k_similar([int(query_idx)], int(k), exclude_self)
+        if idx.shape[0] == 0:
+            raise RuntimeError(self._NO_LEAVES)
+        return idx, sim
+
+    def compute_proximity_from_leaves(self, sample_i, sample_j):
+        self._check_leaves()
+        return self._context().leaf_proximity(int(sample_i), int(sample_j))
+
+    def predict_leaf_assignments(self, X):
+        """int16 [n_new, ntree] terminal nodes of new rows."""
+        self._check()
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        if X.ndim != 2:
+            raise RuntimeError("X must be 2-dimensional")
+        return self._context().predict_leaves(X, self.ntree)
+
+    def predict_top_k_similar(self, X, k=10):
+        """(indices int32 [n_new, k], similarities float32 [n_new, k]) over all trees."""
+        self._check_leaves()
+        self._leaf_index_built = True
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        if X.ndim != 2:
+            raise RuntimeError("X must be 2-dimensional")
+        return self._context().predict_top_k_similar(X, int(k))
+
+    def select_outlier_anchors(self, n_anchors=100, method="random"):
+        self._check_leaves()
+        a = self._context().select_anchors(int(n_anchors), 1 if method == "diverse" else 0,
+                                           self.iseed)
+        self._outlier_anchors = a
+        return a.copy()
+
+    def compute_outlier_scores(self, mode="full", n_anchors=100):
+        """Breiman-Cutler outlier scores ((raw - median) / MAD; per class for a classifier)."""
+        self._check_leaves()
+        anchors = None
+        if mode == "greedy":
+            a = getattr(self, "_outlier_anchors", None)
+            if a is None or len(a) == 0 or len(a) != int(n_anchors):
+                self.select_outlier_anchors(int(n_anchors), "random")
+            anchors = self._outlier_anchors
+        labels = self.acc_["labels"] if self._task_id == A.TASK_CLASSIFICATION else None
+        self._leaf_index_built = True
+        scores, _raw = self._context().outlier_scores(1 if mode == "greedy" else 0, anchors,
+                                                      int(n_anchors), labels, self.n_rows_)
+        self.outlier_scores_ = scores
+        return scores
+
+    def compute_outliers(self, k=10, mode="full", n_anchors=100):
+        """(indices, scores) of the k highest outlier scores."""
+        scores = self.compute_outlier_scores(mode, n_anchors)
+        return A.rank_scores_desc(scores, int(k))
 
 
 def _argmax_last(q: np.ndarray) -> np.ndarray:

@@ -136,6 +136,68 @@ def impute_golden():
             "n_iterations": np.int32(info["n_iterations"])}
 
 
+LEAF_CASES = {
+    # name: (task, data kind, n, p, seed, ntree, mtry, minndsize)
+    "leaves_class": (0, "multiclass", 500, 6, 41, 12, 3, 1),
+    "leaves_regr": (1, "regr", 450, 5, 42, 10, 2, 5),
+    "leaves_unsup": (2, "gmm", 200, 4, 43, 8, 2, 1),
+}
+
+
+def leaves_golden():
+    """Leaf assignments and the queries on them (include/rf_random_forest.hpp:296-365) from
+    the reference module: top-k similar rows, outlier scores (full and greedy), anchors,
+    new-row leaves and top-k similar."""
+    R = oracle.ref_module()
+    out = {}
+    for name, (task, kind, n, p, seed, ntree, mtry, nds) in LEAF_CASES.items():
+        X, y = synth(kind, n + 60, p, seed)
+        Xn = X[n:].copy()
+        X = X[:n]
+        common = dict(ntree=ntree, mtry=mtry, minndsize=nds, compute_importance=False,
+                      compute_proximity=False, show_progress=False, compute_leaf_assignments=True)
+        if task == 0:
+            m = R.RandomForestClassifier(nsample=n, **common)
+            m.fit(X, y[:n])
+        elif task == 1:
+            m = R.RandomForestRegressor(nsample=n, **common)
+            m.fit(X, y[:n])
+        else:
+            m = R.RandomForestUnsupervised(nsample=n, **common)
+            m.fit(X)
+        d = {"X": X, "Xn": Xn, "leaves": np.asarray(m.get_leaf_assignments())}
+        if y is not None:
+            d["y"] = np.asarray(y[:n])
+        N = d["leaves"].shape[1]
+        queries = np.array([0, 1, 7, N // 2, N - 1], np.int32)
+        for ex in (1, 0):
+            idx, sim = [], []
+            for q in queries:
+                try:
+                    a, b = m.get_top_k_similar(int(q), 10, bool(ex))
+                except RuntimeError:
+                    a, b = np.zeros(0, np.int32), np.zeros(0, np.float32)
+                a = np.full(10, -1, np.int32) if len(a) == 0 else np.pad(np.asarray(a, np.int32), (0, 10 - len(a)), constant_values=-1)
+                b = np.pad(np.asarray(b, np.float32), (0, 10 - len(b)), constant_values=np.nan) if len(b) else np.full(10, np.nan, np.float32)
+                idx.append(a)
+                sim.append(b)
+            d[f"topk_idx_ex{ex}"] = np.stack(idx)
+            d[f"topk_sim_ex{ex}"] = np.stack(sim)
+        d["queries"] = queries
+        d["anchors_random"] = np.asarray(m.select_outlier_anchors(25, "random"))
+        d["anchors_diverse"] = np.asarray(m.select_outlier_anchors(12, "diverse"))
+        d["outlier_greedy"] = np.asarray(m.compute_outlier_scores("greedy", 25))
+        d["outlier_full"] = np.asarray(m.compute_outlier_scores("full", 100))
+        oi, os_ = m.compute_outliers(7, "full", 100)
+        d["outliers_idx"], d["outliers_score"] = np.asarray(oi), np.asarray(os_)
+        d["new_leaves"] = np.asarray(m.predict_leaf_assignments(Xn))
+        ti, ts = m.predict_top_k_similar(Xn, 8)
+        d["new_topk_idx"], d["new_topk_sim"] = np.asarray(ti), np.asarray(ts)
+        d["iseed"] = np.int32(12345)
+        out[name] = d
+    return out
+
+
 def main():
     if not oracle.ref_available():
         raise SystemExit("oracle/_ref is not built: run `make -C oracle ref`")
@@ -182,4 +244,8 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) > 1 and sys.argv[1] == "leaves":  # only the leaf-query fixtures
+        for name, d in leaves_golden().items():
+            np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **d)
+    else:
+        main()

@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_no_device_here_is_reported():
     lib = rfx_b200.load_library()
-    assert lib.rfx_abi_version() == 2
+    assert lib.rfx_abi_version() == 3
     assert lib.rfx_device_count() >= 0
 
 
