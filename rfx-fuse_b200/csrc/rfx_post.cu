@@ -183,66 +183,66 @@ __device__ void imp_regr_row(const Data& D, const Batch& B, int t, int j, float*
     const int nn = B.nnode[t];
     // The permuted walk for feature k follows the row's own path up to the first node that
     // tests k; features never tested on the path keep the unpermuted error.  Along the path
-    // only the nodes testing k can turn the walk, so it is followed from the recorded path
-    // and walked from the tree only where the permuted value leaves the path.
-    constexpr int kMaxPath = 48;
-    int path[kMaxPath];
-    int pf[kMaxPath];  // feature tested at path[q]
-    int depth = 0;
-    int kend = 0;      // the row's terminal node
-    bool deep = D.has_cat != 0;
+    // only the nodes testing k can turn the walk, so one pass down the row's path checks, at
+    // every node, the permuted value of the node's feature (unless that feature's walk has
+    // already left the path) and walks the tree from where a permuted walk leaves it.
+    for (int k = 0; k < D.p; ++k) out[k] = dd;
+    bool deep = D.has_cat != 0 || D.p > 64;
     if (!deep) {
-        int kt = 0, steps = 0;
+        constexpr int kMaxPath = 48;
+        unsigned long long tested = 0, left = 0;  // features on the path / walks that left it
+        int kt = 0, steps = 0, depth = 0;
         while (st[kt] == 1 && steps < 1000) {
             ++steps;
             if (depth == kMaxPath) { deep = true; break; }
-            path[depth] = kt;
-            const int mv = bv[kt];
-            pf[depth++] = mv;
-            kt = D.xc[(size_t)mv * D.N + row] <= xb[kt] ? tm[2 * kt] : tm[2 * kt + 1];
+            const int f = bv[kt];
+            if (f < 0 || f >= D.p) { deep = true; break; }
+            const float th = xb[kt];
+            const int l = tm[2 * kt], r = tm[2 * kt + 1];
+            const int nx = D.xc[(size_t)f * D.N + row] <= th ? l : r;
+            tested |= 1ull << f;
+            if (!((left >> f) & 1ull)) {
+                int pk_kt = D.xc[(size_t)f * D.N + prow] <= th ? l : r;
+                if (pk_kt != nx) {
+                    left |= 1ull << f;
+                    // the rest of the walk, with the step budget the full walk from the
+                    // feature's first node has left after this node
+                    float pk = 0.0f;
+                    if (pk_kt >= 0 && pk_kt < nn) {
+                        for (int k = depth + 1; k < nn; ++k) {
+                            if (st[pk_kt] == -1) { pk = np[pk_kt]; break; }
+                            const int m = bv[pk_kt];
+                            const float v = D.xc[(size_t)m * D.N + (m == f ? prow : row)];
+                            pk_kt = v <= xb[pk_kt] ? tm[2 * pk_kt] : tm[2 * pk_kt + 1];
+                            if (pk_kt < 0 || pk_kt >= nn) break;
+                        }
+                    }
+                    const float dk = pk - y;
+                    out[f] = 1.0f * dk * dk;
+                }
+            }
+            ++depth;
+            kt = nx;
             if (st[kt] != 1) break;
         }
-        kend = kt;
+        // walks that never left the path end at the row's own terminal node
+        const unsigned long long stay = tested & ~left;
+        if (!deep && stay) {
+            if (kt >= 0 && kt < nn && st[kt] == -1) {
+                const float dk = np[kt] - y;
+                const float e = 1.0f * dk * dk;
+                for (int k = 0; k < D.p; ++k)
+                    if ((stay >> k) & 1ull) out[k] = e;
+            } else {
+                deep = true;
+            }
+        }
     }
     if (deep) {
         for (int k = 0; k < D.p; ++k) {
             const float dk = walk_perm_regr(D, st, bv, xb, tm, np, nn, row, prow, k) - y;
             out[k] = 1.0f * dk * dk;
         }
-        return;
-    }
-    for (int k = 0; k < D.p; ++k) out[k] = dd;
-    for (int i = 0; i < depth; ++i) {
-        const int f = pf[i];
-        bool first = true;
-        for (int q = 0; q < i; ++q) first &= pf[q] != f;
-        if (!first) continue;
-        const float vf = D.xc[(size_t)f * D.N + prow];
-        int q = i, kt = -1;
-        bool left_path = false;
-        for (; q < depth; ++q) {
-            if (pf[q] != f) continue;
-            const int node = path[q];
-            kt = vf <= xb[node] ? tm[2 * node] : tm[2 * node + 1];
-            if (kt != (q + 1 < depth ? path[q + 1] : kend)) { left_path = true; break; }
-        }
-        if (!left_path) {  // the permuted walk reaches the row's own terminal node
-            kt = kend;
-            q = depth - 1;
-        }
-        float pk = 0.0f;
-        if (kt >= 0 && kt < nn) {
-            // the rest of the walk, with the step budget the full walk from path[i] has left
-            for (int k = q + 1; k < nn; ++k) {
-                if (st[kt] == -1) { pk = np[kt]; break; }
-                const int m = bv[kt];
-                const float v = D.xc[(size_t)m * D.N + (m == f ? prow : row)];
-                kt = v <= xb[kt] ? tm[2 * kt] : tm[2 * kt + 1];
-                if (kt < 0 || kt >= nn) break;
-            }
-        }
-        const float dk = pk - y;
-        out[f] = 1.0f * dk * dk;
     }
 }
 
