@@ -111,15 +111,25 @@ __device__ __forceinline__ unsigned long long scan_bins(bool regr, int nc, int c
             }
         }
     } else {
-        // integer class prefix over the non-empty bins (lane k owns class k), in place
+        // integer class prefix over the non-empty bins (exact in any order): per class a
+        // warp scan over 32 bins at a time, compacted in place (entry j <= bin bl[j])
         __syncwarp();
-        if (lane < nc) {
-            int l = 0;
-            for (int j = 0; j < nm; ++j) {
-                l += h[bl[j] * nc + lane];
-                h[j * nc + lane] = l;
+        for (int k = 0; k < nc; ++k) {
+            int carry = 0;
+            for (int s0 = 0; s0 < nm; s0 += 32) {
+                const int j = s0 + lane;
+                int v = j < nm ? h[bl[j] * nc + k] : 0;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const int y = __shfl_up_sync(kFull, v, o);
+                    if (lane >= o) v += y;
+                }
+                __syncwarp();
+                if (j < nm) h[j * nc + k] = carry + v;
+                carry += __shfl_sync(kFull, v, 31);
+                __syncwarp();
             }
-            h[256 * nc + lane] = l;  // class totals
+            if (lane == 0) h[256 * nc + k] = carry;  // class totals
         }
         __syncwarp();
         const int* tc = h + 256 * nc;
