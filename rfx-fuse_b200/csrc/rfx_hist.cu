@@ -59,6 +59,43 @@ __device__ __forceinline__ uint32_t gather_byte(uint32_t a, uint32_t b, uint32_t
     return __byte_perm(lo, hi, 0x5410);
 }
 
+// Gini criterion of every candidate bin j < nm - 1 from the inclusive class prefixes
+// h[j * nc + k] and the class totals h[256 * nc + k] (node rows c): the lane's first minimum.
+__device__ __forceinline__ void class_best(int nc, int c, int nm, int lane, const int* h,
+                                           float& bestv, int& bestj) {
+    const int* tc = h + 256 * nc;
+    for (int j = lane; j < nm - 1; j += 32) {
+        int tl = 0;
+        for (int k = 0; k < nc; ++k) tl += h[j * nc + k];
+        const float tlf = (float)tl, trf = (float)(c - tl);
+        float gl = 1.0f, gr = 1.0f;
+        for (int k = 0; k < nc; ++k) {
+            const int lk = h[j * nc + k];
+            const float pl = (float)lk / tlf;
+            const float pr = (float)(tc[k] - lk) / trf;
+            gl -= pl * pl;
+            gr -= pr * pr;
+        }
+        const float tt = tlf + trf;
+        const float g = (tlf * gl + trf * gr) / tt;
+        if (g < bestv) { bestv = g; bestj = j; }
+    }
+}
+
+// Key of the warp's best (first minimum over the lanes' candidates) for draw mv.
+__device__ __forceinline__ unsigned long long best_key(bool regr, float bestv, int bestj, int mv,
+                                                       const uint8_t* bl) {
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, bestv, o);
+        const int oj = __shfl_xor_sync(kFull, bestj, o);
+        if (ov < bestv || (ov == bestv && oj < bestj)) { bestv = ov; bestj = oj; }
+    }
+    if (bestj == 0x7fffffff) return kNoKey;
+    const float crit = regr ? bestv : -(2.0f - bestv);
+    return ((unsigned long long)ord_of(crit) << 32) | ((unsigned long long)mv << 8) |
+           (unsigned long long)bl[bestj];
+}
+
 // Fold one draw's histogram (sy/sy2/cn or h/cn) into its best key; restores the zeroed
 // scratch.  `c` = node rows, `mv` = draw index.  All lanes call it.
 __device__ __forceinline__ unsigned long long scan_bins(bool regr, int nc, int c, int mv, int lane,
@@ -132,35 +169,9 @@ __device__ __forceinline__ unsigned long long scan_bins(bool regr, int nc, int c
             if (lane == 0) h[256 * nc + k] = carry;  // class totals
         }
         __syncwarp();
-        const int* tc = h + 256 * nc;
-        for (int j = lane; j < nm - 1; j += 32) {
-            int tl = 0;
-            for (int k = 0; k < nc; ++k) tl += h[j * nc + k];
-            const float tlf = (float)tl, trf = (float)(c - tl);
-            float gl = 1.0f, gr = 1.0f;
-            for (int k = 0; k < nc; ++k) {
-                const int lk = h[j * nc + k];
-                const float pl = (float)lk / tlf;
-                const float pr = (float)(tc[k] - lk) / trf;
-                gl -= pl * pl;
-                gr -= pr * pr;
-            }
-            const float tt = tlf + trf;
-            const float g = (tlf * gl + trf * gr) / tt;
-            if (g < bestv) { bestv = g; bestj = j; }
-        }
+        class_best(nc, c, nm, lane, h, bestv, bestj);
     }
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(kFull, bestv, o);
-        const int oj = __shfl_xor_sync(kFull, bestj, o);
-        if (ov < bestv || (ov == bestv && oj < bestj)) { bestv = ov; bestj = oj; }
-    }
-    unsigned long long key = kNoKey;
-    if (bestj != 0x7fffffff) {
-        const float crit = regr ? bestv : -(2.0f - bestv);
-        key = ((unsigned long long)ord_of(crit) << 32) | ((unsigned long long)mv << 8) |
-              (unsigned long long)bl[bestj];
-    }
+    const unsigned long long key = best_key(regr, bestv, bestj, mv, bl);
     __syncwarp();
     for (int j = lane; j < nm; j += 32) {
         const int b = bl[j];
@@ -534,18 +545,79 @@ __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, in
         }
         unsigned long long best = kNoKey;
         if (!regr) {
+            // classification: the draw's bins as a 256-bit set (words in the unused sums
+            // area), class counts per ranked bin with integer atomics, then per-class warp
+            // scans (exact in any order) and the criterion of scan_bins
+            uint32_t* CW = reinterpret_cast<uint32_t*>(sy);
+            int* CP = reinterpret_cast<int*>(sy) + 8;
             for (int mv = 0; mv < B.mtry; ++mv) {
                 const int f = featp[mv];
+                int bb[kSmallRows];
+                uint32_t qmask[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) qmask[q] = 0u;
 #pragma unroll
                 for (int hh = 0; hh < kSmallRows; ++hh) {
+                    bb[hh] = -1;
                     if (hh * 32 < c) {
                         const int i = hh * 32 + lane;
-                        const bool valid = i < c;
-                        const int b = valid ? (int)__ldg(rowp[hh] + f) : kBins;
-                        hist_step(regr, nc, valid, b, v[hh], v2[hh], lab[hh], lane, sy, sy2, cn, h);
+                        if (i < c) bb[hh] = (int)__ldg(rowp[hh] + f);
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            qmask[q] |= (bb[hh] >> 5) == q ? 1u << (bb[hh] & 31) : 0u;
                     }
                 }
-                best = min(best, scan_bins(regr, nc, c, mv, lane, bl, sy, sy2, cn, h));
+                int nm = 0;
+                uint32_t myw = 0u;
+                int myp = 0;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const uint32_t wq = __reduce_or_sync(kFull, qmask[q]);
+                    if (lane == q) {
+                        myw = wq;
+                        myp = nm;
+                    }
+                    nm += __popc(wq);
+                }
+                if (lane < 8) {
+                    CW[lane] = myw;
+                    CP[lane] = myp;
+                }
+                for (int e = lane; e < nm * nc; e += 32) h[e] = 0;
+                __syncwarp();
+#pragma unroll
+                for (int hh = 0; hh < kSmallRows; ++hh) {
+                    if (hh * 32 < c && bb[hh] >= 0) {
+                        const int b = bb[hh], q = b >> 5;
+                        const int e = CP[q] + __popc(CW[q] & ((1u << (b & 31)) - 1u));
+                        atomicAdd(&h[e * nc + lab[hh]], 1);
+                        bl[e] = (uint8_t)b;
+                    }
+                }
+                __syncwarp();
+                for (int k = 0; k < nc; ++k) {
+                    int carry = 0;
+                    for (int s0 = 0; s0 < nm; s0 += 32) {
+                        const int j = s0 + lane;
+                        int x = j < nm ? h[j * nc + k] : 0;
+#pragma unroll
+                        for (int o = 1; o < 32; o <<= 1) {
+                            const int y = __shfl_up_sync(kFull, x, o);
+                            if (lane >= o) x += y;
+                        }
+                        __syncwarp();
+                        if (j < nm) h[j * nc + k] = carry + x;
+                        carry += __shfl_sync(kFull, x, 31);
+                        __syncwarp();
+                    }
+                    if (lane == 0) h[256 * nc + k] = carry;
+                }
+                __syncwarp();
+                float bestv = 1e20f;
+                int bestj = 0x7fffffff;
+                class_best(nc, c, nm, lane, h, bestv, bestj);
+                best = min(best, best_key(false, bestv, bestj, mv, bl));
+                __syncwarp();
             }
         } else {
             // regression: the draws' lists of non-empty bins fill the warp's list area (as
