@@ -344,9 +344,10 @@ HistCfg hist_cfg(Ctx& c) {
     // lanes of one warp read them side by side)
     const int scratch = (int)round_up(rfx::kHistScratch + (regr ? 2 * 1024 : (257 * c.nclass + 32) * 4), 16) + 4;
     const int small_scratch = regr ? 64 + 24 * rfx::kListCap : scratch;  // bin set + list area
-    // regression: one block per node covers up to 16 draws (rows staged once per node, one
-    // chain phase); classification: groups of 8 draws
-    h.a.warps = regr ? std::max(1, std::min(16, c.prm.mtry)) : 8;
+    // one block per node covers up to 16 draws (rows staged once per node) when the warps'
+    // histograms fit in 96 KB; otherwise (many classes) groups of 8 draws
+    const int all = std::max(1, std::min(16, c.prm.mtry));
+    h.a.warps = (regr || all * scratch <= 96 * 1024) ? all : 8;
     h.a.groups = (c.prm.mtry + h.a.warps - 1) / h.a.warps;
     // rows per staged chunk: a multiple of 32 with at most 2 load units per thread, small
     // enough for 32 resident warps per SM where the row width allows
