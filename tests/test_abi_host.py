@@ -13,6 +13,7 @@ from rfx_b200 import _abi as A
 from rfx_b200.forest import _argmax_last, _isqrt_f32
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "rfx_b200.h")
 
 
 def declared_functions():
@@ -32,7 +33,9 @@ def test_library_exports_every_declared_symbol():
 
 def test_abi_version_and_no_device_here_is_reported():
     lib = rfx_b200.load_library()
-    assert lib.rfx_abi_version() == 3
+    with open(HEADER) as f:
+        want = int(re.search(r"#define RFX_ABI_VERSION (\d+)", f.read()).group(1))
+    assert lib.rfx_abi_version() == want
     assert lib.rfx_device_count() >= 0
 
 
