@@ -87,3 +87,19 @@ def test_categorical_detection_rule():
 def test_oob_argmax_ties_go_to_the_last_class():
     q = np.array([[1, 1, 0], [0, 2, 2], [3, 1, 1]], np.float32)
     assert _argmax_last(q).tolist() == [1, 2, 0]
+
+
+def test_rank_scores_desc_is_a_descending_sort():
+    """compute_outliers' ranking (host only): descending scores, first k; distinct scores
+    give the unique order, equal scores stay within their run."""
+    rng = np.random.default_rng(11)
+    s = rng.permutation(200).astype(np.float32) / np.float32(7.0)
+    idx, val = A.rank_scores_desc(s, 15)
+    ref = np.argsort(-s, kind="stable")[:15]
+    assert np.array_equal(idx, ref) and np.array_equal(val, s[ref])
+    t = np.repeat(np.arange(10, dtype=np.float32), 20)
+    idx, val = A.rank_scores_desc(t, 50)
+    assert np.all(np.diff(val) <= 0) and np.array_equal(val, t[idx])
+    assert len(set(idx.tolist())) == 50
+    idx, val = A.rank_scores_desc(s[:5], 9)
+    assert idx.shape == (5,)
