@@ -84,6 +84,8 @@ struct Ctx {
     int sm_count = 148;
     cudaStream_t st = nullptr;
     int* h_counters = nullptr;  // pinned
+    void* h_stage[2] = {nullptr, nullptr};  // pinned staging for copies into pageable memory
+    cudaEvent_t ev_stage[2] = {nullptr, nullptr};
 
     // loaded dataset
     bool loaded = false;
@@ -173,6 +175,10 @@ struct Ctx {
         if (st) cudaStreamSynchronize(st);
         for (DBuf* b : all) b->release();
         if (h_counters) cudaFreeHost(h_counters);
+        for (int b = 0; b < 2; ++b) {
+            if (h_stage[b]) cudaFreeHost(h_stage[b]);
+            if (ev_stage[b]) cudaEventDestroy(ev_stage[b]);
+        }
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
         if (st) cudaStreamDestroy(st);

@@ -5,6 +5,8 @@
 // rfx_grow grows batches of trees level by level (rfx_grow.cu) and folds each batch's OOB
 // votes, predictions, importance and proximity into device accumulators in tree order.
 #include <algorithm>
+#include <cstring>
+#include <thread>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -374,6 +376,60 @@ HistCfg hist_cfg(Ctx& c) {
     return h;
 }
 
+// Host memcpy split over a few threads (large staged chunks).
+void parallel_copy(char* dst, const char* src, size_t bytes) {
+    const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+    const size_t parts = std::min<size_t>(std::min<unsigned>(8u, hw), std::max<size_t>(1, bytes >> 22));
+    if (parts <= 1) {
+        std::memcpy(dst, src, bytes);
+        return;
+    }
+    std::vector<std::thread> th;
+    const size_t step = (bytes + parts - 1) / parts;
+    for (size_t k = 0; k < parts; ++k) {
+        const size_t off = k * step;
+        if (off >= bytes) break;
+        const size_t n = std::min(step, bytes - off);
+        th.emplace_back([=] { std::memcpy(dst + off, src + off, n); });
+    }
+    for (auto& t : th) t.join();
+}
+
+// Device -> host copy on the context's stream, complete on return.  A page-locked
+// destination takes one DMA; a pageable one (numpy arrays) goes through two pinned staging
+// buffers, the DMA of chunk i + 1 running while host threads copy chunk i out.
+void copy_d2h(Ctx& c, void* dst, const void* src, size_t bytes) {
+    if (bytes == 0) return;
+    cudaPointerAttributes at{};
+    const bool pinned = cudaPointerGetAttributes(&at, dst) == cudaSuccess && at.type == cudaMemoryTypeHost;
+    cudaGetLastError();  // the query's status is not an error of this context
+    constexpr size_t kChunk = (size_t)32 << 20;
+    if (pinned || bytes < ((size_t)4 << 20)) {
+        RFX_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, c.st));
+        RFX_CUDA(cudaStreamSynchronize(c.st));
+        return;
+    }
+    if (!c.h_stage[0]) {
+        for (int b = 0; b < 2; ++b) {
+            RFX_CUDA(cudaHostAlloc(&c.h_stage[b], kChunk, cudaHostAllocDefault));
+            RFX_CUDA(cudaEventCreateWithFlags(&c.ev_stage[b], cudaEventDisableTiming));
+        }
+    }
+    const size_t nch = (bytes + kChunk - 1) / kChunk;
+    auto issue = [&](size_t i) {
+        const size_t off = i * kChunk, n = std::min(kChunk, bytes - off);
+        RFX_CUDA(cudaMemcpyAsync(c.h_stage[i & 1], (const char*)src + off, n, cudaMemcpyDeviceToHost, c.st));
+        RFX_CUDA(cudaEventRecord(c.ev_stage[i & 1], c.st));
+    };
+    issue(0);
+    for (size_t i = 0; i < nch; ++i) {
+        if (i + 1 < nch) issue(i + 1);  // the other buffer: its host copy finished last round
+        RFX_CUDA(cudaEventSynchronize(c.ev_stage[i & 1]));
+        const size_t off = i * kChunk;
+        parallel_copy((char*)dst + off, (const char*)c.h_stage[i & 1], std::min(kChunk, bytes - off));
+    }
+}
+
 void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
     cudaStream_t st = c.st;
     rfx::Batch B = c.B;
@@ -525,8 +581,7 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
     if (keep) c.tree_oob_n += T;
     if (out) {
         auto cp = [&](void* dst, const void* src, size_t elems, size_t esz) {
-            if (dst) RFX_CUDA(cudaMemcpyAsync((char*)dst + (size_t)out_off * elems * esz, src,
-                                              (size_t)T * elems * esz, cudaMemcpyDeviceToHost, st));
+            if (dst) copy_d2h(c, (char*)dst + (size_t)out_off * elems * esz, src, (size_t)T * elems * esz);
         };
         cp(out->nodestatus, B.status, M, 4);
         cp(out->bestvar, B.bestvar, M, 4);
