@@ -275,6 +275,14 @@ int rfx_leaf_select_anchors(void* ctx, int n_anchors, int method, uint32_t iseed
  * rounds once (the reference adds float terms in hash-map order). */
 int rfx_leaf_outlier_scores(void* ctx, int mode, const int* anchors, int n_used, int n_anchors,
                             const int* labels, float* scores_out, float* raw_out);
+/* predict_outlier_scores (src/rf_random_forest.cpp:5210-5330; python/randomforest_py.cpp:
+ * 2649-2684) for new rows X_host [n][p]: proximity to every training row over all trees; raw =
+ * m / sum of squares over the positive proximities (mode 0 "full": all, in row order; mode 1
+ * "greedy": the n_anchors largest); normalised with the (median, MAD) of the last
+ * rfx_leaf_outlier_scores (classes [n] = predicted 0-based classes for per-class statistics,
+ * or NULL for the global ones).  RFX_ERR_STATE before any training outlier scores. */
+int rfx_predict_outlier_scores(void* ctx, const float* X_host, int n, int p, int mode,
+                               int n_anchors, const int* classes, float* scores_out);
 /* compute_outliers' ranking (src/rf_random_forest.cpp:4279-4303): std::sort of (index, score)
  * by score descending, first k.  Host only. */
 int rfx_rank_scores_desc(const float* scores, int n, int k, int* idx_out, float* val_out);

@@ -163,19 +163,56 @@ def leaf_proximity(leaves, oob, i, j):
     return np.float32(m) / np.float32(len(trees))
 
 
-def _normalise(raw, labels):
-    """(raw - median) / MAD, per class when labels are given (:4201-4272)."""
-    out = np.zeros_like(raw)
-    groups = ([np.nonzero(labels == c)[0] for c in np.unique(labels)] if labels is not None
-              else [np.arange(raw.shape[0])])
-    for g in groups:
-        v = raw[g]
+def outlier_stats(raw, labels=None):
+    """{class (or -1): (median, MAD)} of the raw measures (:4201-4272)."""
+    stats = {}
+    keys = np.unique(labels) if labels is not None else [-1]
+    for c in keys:
+        v = raw[labels == c] if labels is not None else raw
         med = np.sort(v)[len(v) // 2]
         dev = np.sort(np.abs((v - med).astype(np.float32)))
         mad = dev[len(v) // 2]
         if mad < np.float32(1e-10):
             mad = np.float32(1.0)
-        out[g] = ((v - med).astype(np.float32) / mad).astype(np.float32)
+        stats[int(c)] = (np.float32(med), np.float32(mad))
+    return stats
+
+
+def _normalise(raw, labels):
+    """(raw - median) / MAD, per class when labels are given (:4201-4272)."""
+    out = np.zeros_like(raw)
+    stats = outlier_stats(raw, labels)
+    for c, (med, mad) in stats.items():
+        g = np.nonzero(labels == c)[0] if labels is not None else np.arange(raw.shape[0])
+        out[g] = ((raw[g] - med).astype(np.float32) / mad).astype(np.float32)
+    return out
+
+
+def predict_outlier_scores(train_leaves, new_leaves, stats, greedy, n_anchors, classes=None):
+    """RandomForest::predict_outlier_scores (src/rf_random_forest.cpp:5210-5330): per new row
+    the proximity (shared trees / ntree, over all trees) to every training row; raw = count /
+    sum of squares over the positive ones (greedy: the n_anchors largest, in descending order;
+    full: all of them in row order), normalised with the training statistics (per predicted
+    class for a classifier)."""
+    T, N = train_leaves.shape
+    out = np.zeros(new_leaves.shape[0], np.float32)
+    for s in range(new_leaves.shape[0]):
+        cnt = np.zeros(N, np.int64)
+        for t in range(T):
+            cnt += train_leaves[t] == new_leaves[s, t]
+        prox = (cnt.astype(np.float32) / np.float32(T)).astype(np.float32)
+        pos = prox[prox > 0]
+        if greedy and n_anchors > 0:
+            pos = np.sort(pos)[::-1][:n_anchors]
+        ss = np.float32(0.0)
+        for v in pos:
+            ss = np.float32(ss + np.float32(v * v))
+        n = len(pos)
+        raw = (np.float32(n) / ss if (ss > np.float32(1e-10) and n > 0)
+               else np.float32(N) * np.float32(1e10))
+        key = int(classes[s]) if classes is not None else -1
+        med, mad = stats.get(key, (np.float32(0.0), np.float32(1.0)))
+        out[s] = np.float32(np.float32(raw - med) / mad)
     return out
 
 

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <map>
 #include <cstdint>
 #include <cstdlib>
 #include <stdexcept>
@@ -143,6 +144,7 @@ struct Ctx {
     int l_T = 0, l_cap = 0, l_words = 0, l_W = 0;
     bool l_index = false;
     std::vector<int> l_anchors;  // the last selected outlier anchors (reused like the reference)
+    std::map<int, std::pair<float, float>> l_norm;  // outlier (median, MAD) per class (-1: all)
     DBuf l_leaf, l_oob, l_rows, l_gs, l_ge, l_keys, l_cub, l_cnt, l_cidx, l_cval, l_nnz, l_q,
         l_out, l_f;
     // imputation round (rfx_impute_host.cu)

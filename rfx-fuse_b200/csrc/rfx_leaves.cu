@@ -263,6 +263,51 @@ __global__ void k_outlier_full(const int16_t* __restrict__ leaf, const int* __re
     }
 }
 
+// New-row outlier measures (predict_outlier_scores): per new row q, from cnt[q][i] = trees
+// where training row i shares its leaf, raw = n / sum of (cnt / T)^2 over the positive
+// entries -- full: all of them in row order; greedy: the n_anchors largest, in descending
+// order (from hist[q][c] = rows with count c; equal values, so the order among them is
+// immaterial).  Thread per new row.
+__global__ void k_outlier_new(const int* __restrict__ cnt, const int* __restrict__ hist, int N,
+                              int T, int nq, int greedy, int n_anchors, float* __restrict__ raw) {
+    const int q = blockIdx.x * blockDim.x + threadIdx.x;
+    if (q >= nq) return;
+    float ss = 0.0f;
+    int used = 0;
+    if (greedy && n_anchors > 0) {
+        const int* h = hist + (size_t)q * (T + 1);
+        int left = n_anchors;
+        for (int v = T; v >= 1 && left > 0; --v) {
+            const int k = min(h[v], left);
+            const float pr = (float)v / (float)T;
+            for (int e = 0; e < k; ++e) ss += pr * pr;
+            used += k;
+            left -= k;
+        }
+    } else {
+        const int* c = cnt + (size_t)q * N;
+        for (int i = 0; i < N; ++i) {
+            const int v = c[i];
+            if (v > 0) {
+                const float pr = (float)v / (float)T;
+                ss += pr * pr;
+                ++used;
+            }
+        }
+    }
+    raw[q] = (ss > 1e-10f && used > 0) ? (float)used / ss : (float)N * 1e10f;
+}
+
+// hist[q][c] += 1 for every training row with count c > 0.
+__global__ void k_outlier_new_hist(const int* __restrict__ cnt, int N, int T, int nq,
+                                   int* __restrict__ hist) {
+    const int q = blockIdx.y;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < N; i += gridDim.x * blockDim.x) {
+        const int v = cnt[(size_t)q * N + i];
+        if (v > 0) atomicAdd(&hist[(size_t)q * (T + 1) + v], 1);
+    }
+}
+
 // Diverse anchors, one step: mn[n] = min(mn[n], proximity of n to the last anchor).
 __global__ void k_anchor_update(const int16_t* __restrict__ leaf, int T, int N, int last,
                                 float* __restrict__ mn) {
@@ -679,15 +724,72 @@ int rfx_leaf_outlier_scores(void* ctx, int mode, const int* anchors, int n_used,
             float mad = dev[dev.size() / 2];
             if (mad < 1e-10f) mad = 1.0f;
             for (size_t e = 0; e < idx.size(); ++e) scores_out[idx[e]] = (r[idx[e]] - median) / mad;
+            return std::make_pair(median, mad);
         };
+        c.l_norm.clear();
         if (labels) {
             std::map<int, std::vector<int>> by_class;
             for (int i = 0; i < N; ++i) by_class[labels[i]].push_back(i);
-            for (auto& kv : by_class) normalise(kv.second);
+            for (auto& kv : by_class) c.l_norm[kv.first] = normalise(kv.second);
         } else {
             std::vector<int> all(N);
             std::iota(all.begin(), all.end(), 0);
-            normalise(all);
+            c.l_norm[-1] = normalise(all);
+        }
+    });
+}
+
+int rfx_predict_outlier_scores(void* ctx, const float* X_host, int n, int p, int mode,
+                               int n_anchors, const int* classes, float* scores_out) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(c.f_T > 0, RFX_ERR_STATE, "no forest on the device (fit with keep_forest)");
+        require_leaves(c);
+        require(!c.l_norm.empty(), RFX_ERR_STATE,
+                "outlier normalisation not available: compute the training outlier scores first");
+        build_index(c);
+        require(c.f_T == c.l_T, RFX_ERR_STATE, "the device forest and the leaf store differ");
+        require(X_host && scores_out && n >= 0 && p == c.f_p && (mode == 0 || mode == 1), RFX_ERR_ARG,
+                "bad arguments");
+        if (n == 0) return;
+        const int N = (int)c.N, T = c.l_T;
+        cudaStream_t st = c.st;
+        float* xc = upload_columns(c, X_host, n, p);
+        int16_t* nl = (int16_t*)c.l_f.get((size_t)n * T * 2);
+        const dim3 grid((unsigned)((n + 255) / 256), (unsigned)T);
+        rfx::k_leaf_predict<<<grid, 256, 0, st>>>((const rfx::PNode*)c.f_nodes.p, c.f_M, T, xc, n, p,
+                                                 (const int*)c.f_cat.p, nl);
+        RFX_LAUNCH("k_leaf_predict");
+        const int QB = 64;
+        int* cnt = (int*)c.l_cnt.get((size_t)QB * N * 4);
+        int* hist = (int*)c.l_cidx.get((size_t)QB * (T + 1) * 4);
+        float* raw = (float*)c.l_out.get((size_t)QB * 4 + 64);
+        std::vector<float> r(n);
+        for (int b0 = 0; b0 < n; b0 += QB) {
+            const int nb = std::min(QB, n - b0);
+            RFX_CUDA(cudaMemsetAsync(cnt, 0, (size_t)nb * N * 4, st));
+            rfx::k_leaf_query_new<<<(nb * 32 + 255) / 256, 256, 0, st>>>(
+                nl + (size_t)b0 * T, (const int*)c.l_gs.p, (const int*)c.l_ge.p,
+                (const int*)c.l_rows.p, N, T, c.l_W, nb, cnt);
+            if (mode == 1) {
+                RFX_CUDA(cudaMemsetAsync(hist, 0, (size_t)nb * (T + 1) * 4, st));
+                rfx::k_outlier_new_hist<<<dim3((unsigned)std::min(64, (N + 255) / 256), (unsigned)nb), 256, 0, st>>>(
+                    cnt, N, T, nb, hist);
+            }
+            rfx::k_outlier_new<<<(nb + 63) / 64, 64, 0, st>>>(cnt, hist, N, T, nb, mode, n_anchors, raw);
+            RFX_LAUNCH("new-row outlier kernels");
+            c.launches += mode == 1 ? 3 : 2;
+            RFX_CUDA(cudaMemcpyAsync(r.data() + b0, raw, (size_t)nb * 4, cudaMemcpyDeviceToHost, st));
+        }
+        RFX_CUDA(cudaStreamSynchronize(st));
+        c.launches += 1;
+        // the training statistics: per predicted class for a classifier, else over all rows
+        for (int s = 0; s < n; ++s) {
+            const int key = classes ? classes[s] : -1;
+            auto it = c.l_norm.find(key);
+            const float median = it != c.l_norm.end() ? it->second.first : 0.0f;
+            const float mad = it != c.l_norm.end() ? it->second.second : 1.0f;
+            scores_out[s] = (r[s] - median) / mad;
         }
     });
 }

@@ -72,7 +72,7 @@ SYMBOLS = (
     "rfx_lowrank_topk_part", "rfx_impute_round", "rfx_leaf_assignments", "rfx_leaf_index",
     "rfx_leaf_top_k_similar", "rfx_leaf_proximity", "rfx_predict_leaves",
     "rfx_predict_top_k_similar", "rfx_leaf_select_anchors", "rfx_leaf_outlier_scores",
-    "rfx_rank_scores_desc",
+    "rfx_rank_scores_desc", "rfx_predict_outlier_scores",
 )
 
 # int (*)(void* user, float* buf_dev, int64_t count): in-place sum over processes
@@ -147,6 +147,7 @@ def load_library(path: str = LIB_PATH):
     L.rfx_leaf_select_anchors.argtypes = [vp, C.c_int, C.c_int, C.c_uint32, _pi, _pi]
     L.rfx_leaf_outlier_scores.argtypes = [vp, C.c_int, _pi, C.c_int, C.c_int, _pi, _pf, _pf]
     L.rfx_rank_scores_desc.argtypes = [_pf, C.c_int, C.c_int, _pi, _pf]
+    L.rfx_predict_outlier_scores.argtypes = [vp, _pf, C.c_int, C.c_int, C.c_int, C.c_int, _pi, _pf]
     for name in ("rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
                  "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish",
                  "rfx_prox_dense", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host",
@@ -157,7 +158,8 @@ def load_library(path: str = LIB_PATH):
                  "rfx_impute_round", "rfx_leaf_assignments", "rfx_leaf_index",
                  "rfx_leaf_top_k_similar", "rfx_leaf_proximity", "rfx_predict_leaves",
                  "rfx_predict_top_k_similar", "rfx_leaf_select_anchors",
-                 "rfx_leaf_outlier_scores", "rfx_rank_scores_desc"):
+                 "rfx_leaf_outlier_scores", "rfx_rank_scores_desc",
+                 "rfx_predict_outlier_scores"):
         getattr(L, name).restype = C.c_int
     _LIB = L
     return L
@@ -362,6 +364,17 @@ class Context:
                                                 None if lab is None else ptr(lab, _pi),
                                                 ptr(sc, _pf), ptr(raw, _pf)))
         return sc, raw
+
+    def predict_outlier_scores(self, X: np.ndarray, mode: int, n_anchors: int, classes=None):
+        X = np.ascontiguousarray(X, np.float32)
+        n, p = X.shape
+        cl = None if classes is None else np.ascontiguousarray(classes, np.int32)
+        out = np.zeros(n, np.float32)
+        check(self._lib.rfx_predict_outlier_scores(self.handle, ptr(X, _pf), n, p, int(mode),
+                                                   int(n_anchors),
+                                                   None if cl is None else ptr(cl, _pi),
+                                                   ptr(out, _pf)))
+        return out
 
     # ---- imputation ----
     def impute_round(self, xc: np.ndarray, miss: np.ndarray, is_cat: np.ndarray, cells: np.ndarray):

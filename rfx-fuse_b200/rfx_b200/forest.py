@@ -413,6 +413,23 @@ class _Forest:
         self.outlier_scores_ = scores
         return scores
 
+    def predict_outlier_scores(self, X, mode="full", n_anchors=100):
+        """Outlier scores of new rows against the training rows, normalised with the
+        statistics of the last compute_outlier_scores (per predicted class for a classifier)."""
+        self._check_leaves()
+        if getattr(self, "outlier_scores_", None) is None:
+            raise RuntimeError("Outlier normalization stats not available. Call "
+                               "compute_outlier_scores() on training data first.")
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        if X.ndim != 2:
+            raise RuntimeError("X must be 2-dimensional")
+        classes = None
+        if self._task_id == A.TASK_CLASSIFICATION:
+            classes = np.searchsorted(self.classes_, self.predict(X)).astype(np.int32)
+        self._leaf_index_built = True
+        return self._context().predict_outlier_scores(X, 1 if mode == "greedy" else 0,
+                                                      int(n_anchors), classes)
+
     def compute_outliers(self, k=10, mode="full", n_anchors=100):
         """(indices, scores) of the k highest outlier scores."""
         scores = self.compute_outlier_scores(mode, n_anchors)

@@ -190,6 +190,10 @@ def leaves_golden():
         d["outlier_full"] = np.asarray(m.compute_outlier_scores("full", 100))
         oi, os_ = m.compute_outliers(7, "full", 100)
         d["outliers_idx"], d["outliers_score"] = np.asarray(oi), np.asarray(os_)
+        # new-row outlier scores, normalised by the (exact) greedy training statistics
+        m.compute_outlier_scores("greedy", 25)
+        d["new_outlier_full"] = np.asarray(m.predict_outlier_scores(Xn, "full", 100))
+        d["new_outlier_greedy"] = np.asarray(m.predict_outlier_scores(Xn, "greedy", 7))
         d["new_leaves"] = np.asarray(m.predict_leaf_assignments(Xn))
         ti, ts = m.predict_top_k_similar(Xn, 8)
         d["new_topk_idx"], d["new_topk_sim"] = np.asarray(ti), np.asarray(ts)

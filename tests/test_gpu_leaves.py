@@ -4,7 +4,8 @@
   module by make_golden.py): get_leaf_assignments, get_top_k_similar (both exclude_self
   settings, the reference's tie order), select_outlier_anchors (random and diverse),
   compute_outlier_scores (greedy bit for bit; full within the tolerance of
-  test_oracle_leaves), compute_outliers, predict_leaf_assignments, predict_top_k_similar;
+  test_oracle_leaves), compute_outliers, predict_outlier_scores, predict_leaf_assignments,
+  predict_top_k_similar;
 * against the oracle's restatement on the device-grown trees at a larger size.
 """
 import os
@@ -71,6 +72,10 @@ def test_leaf_queries_match_reference_golden(name):
     if np.all(np.diff(ref) < -1e-3):
         np.testing.assert_array_equal(oi, g["outliers_idx"])
     np.testing.assert_allclose(osc, ref, rtol=FULL_RTOL, atol=FULL_ATOL)
+    # new rows, normalised by the greedy training statistics (exact on both sides)
+    m.compute_outlier_scores("greedy", 25)
+    np.testing.assert_array_equal(m.predict_outlier_scores(g["Xn"], "full", 100), g["new_outlier_full"])
+    np.testing.assert_array_equal(m.predict_outlier_scores(g["Xn"], "greedy", 7), g["new_outlier_greedy"])
     np.testing.assert_array_equal(m.predict_leaf_assignments(g["Xn"]), g["new_leaves"])
     ti, ts = m.predict_top_k_similar(g["Xn"], 8)
     np.testing.assert_array_equal(ti, g["new_topk_idx"])
@@ -102,6 +107,11 @@ def test_leaf_queries_match_oracle_larger():
                                OL.outlier_scores(OL.outlier_raw_full(lv)), rtol=1e-6, atol=1e-6)
     nl = OL.predict_leaf_assignments(tr, Xn, np.ones(8, np.int32))
     np.testing.assert_array_equal(m.predict_leaf_assignments(Xn), nl)
+    st = OL.outlier_stats(OL.outlier_raw_full(lv))  # the last training scores were 'full'
+    for mode, na in (("full", 100), ("greedy", 9)):
+        np.testing.assert_allclose(m.predict_outlier_scores(Xn[:30], mode, na),
+                                   OL.predict_outlier_scores(lv, nl[:30], st, mode == "greedy", na),
+                                   rtol=1e-6, atol=1e-6)
     ti, ts = m.predict_top_k_similar(Xn[:40], 12)
     oi, os_ = OL.predict_top_k_similar(lv, nl[:40], 12)
     np.testing.assert_array_equal(ti, oi)

@@ -68,6 +68,22 @@ def test_outlier_scores(state):
     np.testing.assert_allclose(full, g["outlier_full"], rtol=FULL_RTOL, atol=FULL_ATOL)
 
 
+def test_predict_outlier_scores(state):
+    name, g, o, lv, oob = state
+    task = CASES[name][0]
+    p = g["X"].shape[1]
+    labels = g["y"] if task == 0 else None
+    stats = OL.outlier_stats(OL.outlier_raw_greedy(lv, g["anchors_random"], 25), labels)
+    nl = OL.predict_leaf_assignments(o, g["Xn"], np.ones(p, np.int32))
+    classes = None
+    if task == 0:
+        classes, _ = oracle.predict(0, o, g["Xn"], int(g["y"].max()) + 1, np.ones(p, np.int32))
+    full = OL.predict_outlier_scores(lv, nl, stats, False, 100, classes)
+    greedy = OL.predict_outlier_scores(lv, nl, stats, True, 7, classes)
+    np.testing.assert_array_equal(full, g["new_outlier_full"])
+    np.testing.assert_array_equal(greedy, g["new_outlier_greedy"])
+
+
 def test_predict_leaves_and_similar(state):
     name, g, o, lv, oob = state
     p = g["X"].shape[1]
