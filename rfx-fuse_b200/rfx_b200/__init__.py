@@ -11,9 +11,9 @@ All computation runs in librfx_b200.so (hand-written sm_100a CUDA); see include/
 from ._abi import Context, RfxError, load_library  # noqa: F401
 from .model_io import LoadedModel, load  # noqa: F401
 from .impute import rfx_impute_proximity  # noqa: F401
-from .forest import (RandomForestClassifier, RandomForestRegressor,  # noqa: F401
+from .forest import (TaskType, RandomForestClassifier, RandomForestRegressor,  # noqa: F401
                      RandomForestUnsupervised, calculate_maxnode, detect_categorical)
 
-__all__ = ["RandomForestClassifier", "RandomForestRegressor", "RandomForestUnsupervised",
+__all__ = ["TaskType", "RandomForestClassifier", "RandomForestRegressor", "RandomForestUnsupervised",
            "Context", "RfxError", "load_library", "calculate_maxnode", "detect_categorical",
            "LoadedModel", "load", "rfx_impute_proximity"]

@@ -10,11 +10,19 @@ there is one implementation here, the device one.
 """
 from __future__ import annotations
 
+import enum
 import math
 
 import numpy as np
 
 from . import _abi as A
+
+
+class TaskType(enum.IntEnum):
+    """The reference's task enum (include/rf_random_forest.hpp:29-33)."""
+    CLASSIFICATION = A.TASK_CLASSIFICATION
+    REGRESSION = A.TASK_REGRESSION
+    UNSUPERVISED = A.TASK_UNSUPERVISED
 
 MAX_NODE_CAP = 32001
 
@@ -255,6 +263,18 @@ class _Forest:
     def get_n_classes(self):
         return self.nclass_
 
+    def get_task_type(self):
+        return TaskType(self._TASK)
+
+    def cleanup(self):
+        """The reference frees its process-wide GPU pools here; this library keeps no memory
+        outside the model's own context, so there is nothing to release."""
+        return None
+
+    def compute_proximity_matrix(self):
+        """Alias of get_proximity_matrix (python/randomforest_py.cpp:2880)."""
+        return self.get_proximity_matrix()
+
     def get_proximity_matrix(self):
         """Dense float32 finishprox'd proximity (python/randomforest_py.cpp:2129-2181)."""
         self._check()
@@ -467,6 +487,7 @@ class _Classifying(_Forest):
 
 
 class RandomForestClassifier(_Classifying):
+    _TASK = A.TASK_CLASSIFICATION
     _task = A.TASK_CLASSIFICATION
 
     def _is_training_size(self, X):
@@ -516,6 +537,7 @@ class RandomForestClassifier(_Classifying):
 
 
 class RandomForestRegressor(_Forest):
+    _TASK = A.TASK_REGRESSION
     _task = A.TASK_REGRESSION
 
     def __init__(self, *args, **kw):
@@ -557,6 +579,7 @@ class RandomForestRegressor(_Forest):
 
 
 class RandomForestUnsupervised(_Classifying):
+    _TASK = A.TASK_UNSUPERVISED
     _task = A.TASK_UNSUPERVISED
 
     def __init__(self, nsample=1000, ntree=100, mdim=10, maxcat=10, mtry=0, maxnode=0,

@@ -210,6 +210,10 @@ class LoadedModel:
         self._ctx.load_forest(task, trees, m["cat"], nclass=max(m["nclass"], 1))
         self._loaded = True
 
+    def get_task_type(self):
+        from .forest import TaskType
+        return TaskType(self._m["task_type"])
+
     def predict(self, X):
         from . import _abi as A
         m = self._m

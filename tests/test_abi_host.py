@@ -103,3 +103,14 @@ def test_rank_scores_desc_is_a_descending_sort():
     assert len(set(idx.tolist())) == 50
     idx, val = A.rank_scores_desc(s[:5], 9)
     assert idx.shape == (5,)
+
+
+def test_task_type_and_aliases():
+    """get_task_type (the reference's TaskType values) and the compute_proximity_matrix alias."""
+    assert [int(t) for t in rfx_b200.TaskType] == [0, 1, 2]
+    assert rfx_b200.RandomForestClassifier().get_task_type() == rfx_b200.TaskType.CLASSIFICATION
+    assert rfx_b200.RandomForestRegressor().get_task_type() == rfx_b200.TaskType.REGRESSION
+    assert rfx_b200.RandomForestUnsupervised().get_task_type() == rfx_b200.TaskType.UNSUPERVISED
+    for cls in (rfx_b200.RandomForestClassifier, rfx_b200.RandomForestRegressor,
+                rfx_b200.RandomForestUnsupervised):
+        assert callable(cls.compute_proximity_matrix) and cls().cleanup() is None
