@@ -85,8 +85,7 @@ struct Ctx {
     int sm_count = 148;
     cudaStream_t st = nullptr;
     int* h_counters = nullptr;  // pinned
-    void* h_stage[2] = {nullptr, nullptr};  // pinned staging for copies into pageable memory
-    cudaEvent_t ev_stage[2] = {nullptr, nullptr};
+    cudaEvent_t ev_stage[2] = {nullptr, nullptr};  // copies through the pinned staging buffers
 
     // loaded dataset
     bool loaded = false;
@@ -178,7 +177,6 @@ struct Ctx {
         for (DBuf* b : all) b->release();
         if (h_counters) cudaFreeHost(h_counters);
         for (int b = 0; b < 2; ++b) {
-            if (h_stage[b]) cudaFreeHost(h_stage[b]);
             if (ev_stage[b]) cudaEventDestroy(ev_stage[b]);
         }
         if (ev0) cudaEventDestroy(ev0);

@@ -5,8 +5,6 @@
 // rfx_grow grows batches of trees level by level (rfx_grow.cu) and folds each batch's OOB
 // votes, predictions, importance and proximity into device accumulators in tree order.
 #include <algorithm>
-#include <cstring>
-#include <thread>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -16,6 +14,7 @@
 #include <random>
 #include <stdexcept>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/rfx_b200.h"
@@ -395,6 +394,18 @@ void parallel_copy(char* dst, const char* src, size_t bytes) {
     for (auto& t : th) t.join();
 }
 
+// Pinned staging buffers shared by every context of the process (portable, so any device's
+// stream may copy through them), allocated on first use and kept until exit; one copy at a
+// time holds them.
+struct Staging {
+    std::mutex mu;
+    void* buf[2] = {nullptr, nullptr};
+};
+Staging& staging() {
+    static Staging* s = new Staging;  // never destroyed: exit-time order does not matter
+    return *s;
+}
+
 // Device -> host copy on the context's stream, complete on return.  A page-locked
 // destination takes one DMA; a pageable one (numpy arrays) goes through two pinned staging
 // buffers, the DMA of chunk i + 1 running while host threads copy chunk i out.
@@ -409,16 +420,16 @@ void copy_d2h(Ctx& c, void* dst, const void* src, size_t bytes) {
         RFX_CUDA(cudaStreamSynchronize(c.st));
         return;
     }
-    if (!c.h_stage[0]) {
-        for (int b = 0; b < 2; ++b) {
-            RFX_CUDA(cudaHostAlloc(&c.h_stage[b], kChunk, cudaHostAllocDefault));
-            RFX_CUDA(cudaEventCreateWithFlags(&c.ev_stage[b], cudaEventDisableTiming));
-        }
-    }
+    Staging& sg = staging();
+    std::lock_guard<std::mutex> lock(sg.mu);
+    if (!sg.buf[0])
+        for (int b = 0; b < 2; ++b) RFX_CUDA(cudaHostAlloc(&sg.buf[b], kChunk, cudaHostAllocPortable));
+    if (!c.ev_stage[0])
+        for (int b = 0; b < 2; ++b) RFX_CUDA(cudaEventCreateWithFlags(&c.ev_stage[b], cudaEventDisableTiming));
     const size_t nch = (bytes + kChunk - 1) / kChunk;
     auto issue = [&](size_t i) {
         const size_t off = i * kChunk, n = std::min(kChunk, bytes - off);
-        RFX_CUDA(cudaMemcpyAsync(c.h_stage[i & 1], (const char*)src + off, n, cudaMemcpyDeviceToHost, c.st));
+        RFX_CUDA(cudaMemcpyAsync(sg.buf[i & 1], (const char*)src + off, n, cudaMemcpyDeviceToHost, c.st));
         RFX_CUDA(cudaEventRecord(c.ev_stage[i & 1], c.st));
     };
     issue(0);
@@ -426,7 +437,7 @@ void copy_d2h(Ctx& c, void* dst, const void* src, size_t bytes) {
         if (i + 1 < nch) issue(i + 1);  // the other buffer: its host copy finished last round
         RFX_CUDA(cudaEventSynchronize(c.ev_stage[i & 1]));
         const size_t off = i * kChunk;
-        parallel_copy((char*)dst + off, (const char*)c.h_stage[i & 1], std::min(kChunk, bytes - off));
+        parallel_copy((char*)dst + off, (const char*)sg.buf[i & 1], std::min(kChunk, bytes - off));
     }
 }
 
