@@ -13,13 +13,18 @@ constexpr int kBins = 256;        // histogram bins (uint8 codes)
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr unsigned long long kNoKey = ~0ull;
 constexpr int kBigSegment = 2048;  // segments above this are partitioned by a whole block
-constexpr int kSmallNode = 64;     // nodes up to this size are searched by one warp
-constexpr int kHistScratch = 256 + 3 * 1024;  // bytes of a warp's bin list + sums + counts
-constexpr int kSmallNodeRegr = 128;  // the same limit for regression (list-based scan)
-constexpr int kListCap = 256;  // regression bin-list entries per warp in k_hist_small (>= kSmallNodeRegr)
-// Rows of the largest node k_hist_small searches (the rest go to k_hist).
-__host__ __device__ __forceinline__ int small_node_limit(int nclass) {
-    return nclass == 1 ? kSmallNodeRegr : kSmallNode;
+constexpr int kSmallNode = 64;     // nodes up to this size go to the per-node small kernels
+// k_hist_lane (regression nodes of at most kSmallNode rows, one lane per drawn feature)
+constexpr int kLaneTile = 68;      // staged bins per lane (17 words: lanes in distinct banks)
+constexpr int kLaneSlots = 8;      // nodes per warp at most
+// shared memory of one k_hist_lane warp taking `slots` nodes
+__host__ __device__ __forceinline__ int lane_bytes(int slots) {
+    return kSmallNode * 32 * 9 + 2 * 1024 + 32 * kLaneTile + slots * kSmallNode * 8 + kLaneSlots * 4;
+}
+// Rows of the largest node the small kernels search (the rest go to k_hist_warp); 0 when
+// regression draws more than 32 features (k_hist_lane needs a lane per draw).
+__host__ __device__ __forceinline__ int small_node_limit(int nclass, int mtry) {
+    return (nclass == 1 && mtry > 32) ? 0 : kSmallNode;
 }
 
 // ------------------------------------------------------------------------------------
@@ -162,12 +167,18 @@ struct Batch {
     int* srch;        // [T][M] searched nodes of the level, in node order
     int* srch_cnt;    // [T]
     int* srch_off;    // [T+1]
-    int* counters;    // [8]: 0 level total, 1 searched total, 2 next-level total, 4 big searched
+    int* counters;    // [8]: 0 level total, 1 searched total, 2 next-level total, 4 big searched,
+                      //      5 big partitions, 6 small searched
     unsigned long long* hist_bytes;  // algorithmic bytes read by k_hist (sum of c_v*(mtry+L))
     unsigned long long* prox_pairs;  // proximity pair updates counted by k_prox
+    unsigned long long* diag;        // [4] optional histogram diagnostics (nullptr: off): exact
+                                     // criterion evaluations, conflict rounds, 32-row steps
     int* srch_big;    // [T][M] searched nodes above small_node_limit rows, in node order
     int* srch_big_cnt;  // [T]
     int* srch_big_off;  // [T+1]
+    int* srch_sml;    // [T][M] searched nodes of at most small_node_limit rows; total in counters[6]
+    int* srch_sml_cnt;  // [T]
+    int* srch_sml_off;  // [T+1]
     long long* part_big;  // split nodes (t*M + node) with segments above kBigSegment; count in counters[5]
     // post-growth
     int* oob_leaf;    // [T][N] terminal node of OOB rows (-1 in-bag)
@@ -181,13 +192,11 @@ struct Batch {
     float* tree_oob;  // [T][N] per-tree OOB predictions (NaN in-bag), optional
 };
 
-// Launch shape of k_hist (rfx_hist.cu).
+// Launch shape of k_hist_warp (rfx_hist.cu).
 struct HistArgs {
     int warps;       // warps per block = drawn features per work unit
     int groups;      // work units per searched node = ceil(mtry / warps)
-    int stage_rows;  // rows staged per chunk (multiple of 32)
-    int cstride;     // bytes per staged feature column (stage_rows + 4)
-    int warp_bytes;  // per-warp scratch
+    int warp_bytes;  // per-warp shared memory
 };
 
 // Locate the tree of a flattened task index given an exclusive prefix `off` of length T+1.

@@ -226,11 +226,13 @@ __global__ void __launch_bounds__(256) k_draw(Data D, Batch B) {
     const int lo = B.lvl_lo[t], hi = B.lvl_hi[t];
     int* srch = B.srch + (size_t)t * B.M;
     int* big = B.srch_big + (size_t)t * B.M;
+    int* sml = B.srch_sml + (size_t)t * B.M;
+    const int lim = small_node_limit(D.nclass, B.mtry);
     int carry = 0, bcarry = 0;
     for (int k0 = lo; k0 < hi; k0 += blockDim.x) {
         const int node = k0 + threadIdx.x;
         const bool f = node < hi && B.nd_flag[(size_t)t * B.M + node];
-        const bool fb = f && B.nd_cnt[(size_t)t * B.M + node] > small_node_limit(D.nclass);
+        const bool fb = f && B.nd_cnt[(size_t)t * B.M + node] > lim;
         int tot, btot;
         const int ex = block_excl_scan(f ? 1 : 0, ws, tot);
         const int bex = block_excl_scan(fb ? 1 : 0, ws, btot);
@@ -239,6 +241,7 @@ __global__ void __launch_bounds__(256) k_draw(Data D, Batch B) {
             B.nd_key[(size_t)t * B.M + node] = kNoKey;
         }
         if (fb) big[bcarry + bex] = node;
+        if (f && !fb) sml[(carry - bcarry) + (ex - bex)] = node;
         carry += tot;
         bcarry += btot;
     }
@@ -263,6 +266,7 @@ __global__ void __launch_bounds__(256) k_draw(Data D, Batch B) {
         const bool open = B.nnode[t] + 2 <= B.M;
         B.srch_cnt[t] = open ? S : 0;
         B.srch_big_cnt[t] = open ? bcarry : 0;
+        B.srch_sml_cnt[t] = open ? S - bcarry : 0;
     }
 }
 
@@ -286,11 +290,22 @@ __global__ void __launch_bounds__(1024) k_srch_scan(Batch B) {
         if (t < B.T) B.srch_big_off[t] = bcarry + ex;
         bcarry += tot;
     }
+    int scarry = 0;
+    for (int t0 = 0; t0 < B.T; t0 += blockDim.x) {
+        const int t = t0 + threadIdx.x;
+        const int w = t < B.T ? B.srch_sml_cnt[t] : 0;
+        int tot;
+        const int ex = block_excl_scan(w, ws, tot);
+        if (t < B.T) B.srch_sml_off[t] = scarry + ex;
+        scarry += tot;
+    }
     if (threadIdx.x == 0) {
         B.srch_off[B.T] = carry;
         B.srch_big_off[B.T] = bcarry;
+        B.srch_sml_off[B.T] = scarry;
         B.counters[1] = carry;
         B.counters[4] = bcarry;
+        B.counters[6] = scarry;
     }
 }
 

@@ -2,27 +2,38 @@
 // (src/rf_growtree.cpp:22-184) and the per-node comparison across the mtry draws
 // (src/rf_growtree.cpp:820-836, :929-955), for every searched node of a level at once.
 //
-// Two kernels share the work by node size:
-//   k_hist        nodes above small_node_limit rows (64, regression 128): one block per (node, group of up to
-//                 8 draws), one warp per drawn feature, the node's rows streamed through
-//                 shared memory in chunks;
-//   k_hist_small  nodes up to that limit (the great majority at deep levels):
-//                 one warp per node does all mtry draws from rows staged once.
+// Three kernels share the work by node size:
+//   k_hist_warp   nodes above kSmallNode rows: one block per (node, group of up to 16
+//                 draws), one warp per drawn feature streaming the node's rows 32 at a time
+//                 (bins and targets gathered from the packed rows, no block barriers);
+//   k_hist_lane   regression nodes up to kSmallNode rows: one LANE per (node, drawn
+//                 feature), several nodes per warp, the node's rows staged in shared memory
+//                 once and every lane running its feature's histogram serially;
+//   k_hist_small  classification nodes up to kSmallNode rows: one warp per node.
 //
-// Each warp builds its feature's histogram: classification as integer class counts (the
-// reference's float counts are small integers, so exact); regression as float sums that
-// equal the reference's row-order serial sums bin by bin -- rows that hit the same bin
-// within a 32-row step are added one rank at a time, in row order.
-//
-// Only non-empty bins can win (an empty bin repeats the previous bin's criterion and the
-// reference keeps the first of equal values), so the scan runs over the ascending list of
-// non-empty bins.  The scan's running left/right sums are serial float chains in the
-// reference and are computed in bin order; the criterion of every candidate bin is then
-// evaluated in parallel and the first minimum wins.
+// Exactness.  Classification histograms are integer class counts (the reference's float
+// counts are small integers).  Regression bin sums equal the reference's row-order serial
+// float sums bin by bin: in k_hist_warp the rows of a 32-row step that share a bin are
+// chained through register shuffles in row order and the last of them writes the bin back;
+// in k_hist_lane one lane adds its feature's rows in row order.
 //
 // Winner key = (order-preserving bits of the criterion, draw index, bin); the smallest key
 // over all draws of the node is the reference's choice (regression: lowest MSE, first draw
 // wins ties; classification: highest 2 - gini, i.e. lowest -(2 - gini), first draw wins).
+//
+// Approximate-then-exact criterion.  The reference evaluates its float criterion (five or
+// 2*nclass+1 IEEE divisions) at every bin.  Here every candidate bin first gets a cheap
+// approximation (reciprocals, warp-parallel prefix sums) with a rigorous bound E on its
+// distance from the reference's float value:
+//   regression      |mse_f - mse_h| <= E = 1.25 (P + 2^-19 Q) with P the propagated error of
+//                   the serial left/right float chains (recursive-summation bound
+//                   (2m + 64) u sum|S|, u = 2^-24, m = non-empty bins) and Q the magnitude of
+//                   the formula's terms (covers the rounding of both evaluations);
+//   classification  |g_f - g_h| <= E = 1.5 (2 nclass + 16) u (every term <= 1).
+// With U = min(g_h + E) over the node's draws, a bin whose g_h - E exceeds U (plus the width
+// of one rounding of 2 - gini for classification, whose conversion can merge two values)
+// cannot be the reference's choice; only the remaining candidates (usually one to three per
+// node) get the exact float criterion, from the exact serial chains.
 #include "rfx_device.cuh"
 #include "rfx_kernels.h"
 
@@ -32,9 +43,12 @@ namespace rfx {
 __device__ __forceinline__ int warp_nonempty_bins(const int* cnt, uint8_t* bl, int lane) {
     int k = 0;
     uint32_t bits = 0;
+    const int4 c0 = reinterpret_cast<const int4*>(cnt)[2 * lane];
+    const int4 c1 = reinterpret_cast<const int4*>(cnt)[2 * lane + 1];
+    const int cc[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
     for (int q = 0; q < 8; ++q)
-        if (cnt[lane * 8 + q] > 0) { bits |= 1u << q; ++k; }
+        if (cc[q] > 0) { bits |= 1u << q; ++k; }
     int x = k;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -50,13 +64,6 @@ __device__ __forceinline__ int warp_nonempty_bins(const int* cnt, uint8_t* bl, i
     const int m = __shfl_sync(kFull, x, 31);
     __syncwarp();
     return m;
-}
-
-// Byte q of each of four words -> one word (row r in byte r).
-__device__ __forceinline__ uint32_t gather_byte(uint32_t a, uint32_t b, uint32_t c, uint32_t d, int q) {
-    const uint32_t lo = __byte_perm(a, b, (uint32_t)(q | ((q + 4) << 4)));
-    const uint32_t hi = __byte_perm(c, d, (uint32_t)(q | ((q + 4) << 4)));
-    return __byte_perm(lo, hi, 0x5410);
 }
 
 // Gini criterion of every candidate bin j < nm - 1 from the inclusive class prefixes
@@ -96,156 +103,6 @@ __device__ __forceinline__ unsigned long long best_key(bool regr, float bestv, i
            (unsigned long long)bl[bestj];
 }
 
-// Fold one draw's histogram (sy/sy2/cn or h/cn) into its best key; restores the zeroed
-// scratch.  `c` = node rows, `mv` = draw index.  All lanes call it.
-__device__ __forceinline__ unsigned long long scan_bins(bool regr, int nc, int c, int mv, int lane,
-                                                        uint8_t* bl, float* sy, float* sy2,
-                                                        int* cn, int* h) {
-    const int nm = warp_nonempty_bins(cn, bl, lane);
-    float bestv = 1e20f;
-    int bestj = 0x7fffffff;
-    if (regr) {
-        // bins in 32-wide slices; the serial chains run redundantly on every lane from
-        // shuffled per-bin totals (one add per non-empty bin, no shared-memory round trips)
-        float tot = 0.0f, tot2 = 0.0f;
-        for (int s0 = 0; s0 < nm; s0 += 32) {
-            const int j = s0 + lane;
-            const int b = j < nm ? bl[j] : 0;
-            const float sa = j < nm ? sy[b] : 0.0f, qa = j < nm ? sy2[b] : 0.0f;
-            const int kmax = min(32, nm - s0);
-            for (int k = 0; k < kmax; ++k) {
-                tot += __shfl_sync(kFull, sa, k);
-                tot2 += __shfl_sync(kFull, qa, k);
-            }
-        }
-        float L = 0.0f, R = tot, L2 = 0.0f, R2 = tot2;
-        int kc = 0;
-        for (int s0 = 0; s0 < nm; s0 += 32) {
-            const int j = s0 + lane;
-            const int b = j < nm ? bl[j] : 0;
-            const float sa = j < nm ? sy[b] : 0.0f, qa = j < nm ? sy2[b] : 0.0f;
-            const int ka = j < nm ? cn[b] : 0;
-            float mL = 0.0f, mR = 0.0f, mL2 = 0.0f, mR2 = 0.0f;
-            int mC = 0;
-            const int kmax = min(32, nm - s0);
-            for (int k = 0; k < kmax; ++k) {
-                const float a = __shfl_sync(kFull, sa, k);
-                const float a2 = __shfl_sync(kFull, qa, k);
-                kc += __shfl_sync(kFull, ka, k);
-                L += a;
-                R -= a;
-                L2 += a2;
-                R2 -= a2;
-                if (k == lane) { mL = L; mR = R; mL2 = L2; mR2 = R2; mC = kc; }
-            }
-            if (j < nm - 1) {
-                const float cl = (float)mC, cr = (float)(c - mC);
-                const float ml = mL / cl, mr = mR / cr;
-                const float vl = mL2 / cl - ml * ml, vr = mR2 / cr - mr * mr;
-                const float tt = cl + cr;
-                const float mse = (cl * vl + cr * vr) / tt;
-                if (mse < bestv) { bestv = mse; bestj = j; }
-            }
-        }
-    } else {
-        // integer class prefix over the non-empty bins (exact in any order): per class a
-        // warp scan over 32 bins at a time, compacted in place (entry j <= bin bl[j])
-        __syncwarp();
-        for (int k = 0; k < nc; ++k) {
-            int carry = 0;
-            for (int s0 = 0; s0 < nm; s0 += 32) {
-                const int j = s0 + lane;
-                int v = j < nm ? h[bl[j] * nc + k] : 0;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const int y = __shfl_up_sync(kFull, v, o);
-                    if (lane >= o) v += y;
-                }
-                __syncwarp();
-                if (j < nm) h[j * nc + k] = carry + v;
-                carry += __shfl_sync(kFull, v, 31);
-                __syncwarp();
-            }
-            if (lane == 0) h[256 * nc + k] = carry;  // class totals
-        }
-        __syncwarp();
-        class_best(nc, c, nm, lane, h, bestv, bestj);
-    }
-    const unsigned long long key = best_key(regr, bestv, bestj, mv, bl);
-    __syncwarp();
-    for (int j = lane; j < nm; j += 32) {
-        const int b = bl[j];
-        if (regr) {
-            sy[b] = 0.0f;
-            sy2[b] = 0.0f;
-        } else {
-            for (int k = 0; k < nc; ++k) { h[j * nc + k] = 0; h[b * nc + k] = 0; }
-        }
-        cn[b] = 0;
-    }
-    __syncwarp();
-    return key;
-}
-
-// ---------------------------------------------------------------------------------------
-// Regression scan over compacted bin lists.  A draw's non-empty bins (ascending) are a list
-// of (sum, sum of squares, count); the scan's serial float chains -- the totals, then the
-// running left/right sums -- run lane-serially, one draw per lane, so that one warp
-// instruction advances several draws' chains at once; the criterion of every candidate bin
-// is then evaluated in parallel over all lists.
-// ---------------------------------------------------------------------------------------
-constexpr uint32_t kLastEntry = 1u << 31;  // list entry flag: a draw's last bin (no split)
-
-// In place over one list of `len` entries: A/A2/K (bin sum, square sum, count) become the
-// running left sums and count; R/R2 receive the running right sums.
-__device__ __forceinline__ void regr_chains(float* A, float* A2, int* K, float* R, float* R2,
-                                            int len) {
-    float tot = 0.0f, tot2 = 0.0f;
-    int j = 0;
-    for (; j + 8 <= len; j += 8) {
-        float a[8], b[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) { a[u] = A[j + u]; b[u] = A2[j + u]; }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) { tot += a[u]; tot2 += b[u]; }
-    }
-    for (; j < len; ++j) { tot += A[j]; tot2 += A2[j]; }
-    float L = 0.0f, Rv = tot, L2 = 0.0f, Rv2 = tot2;
-    int kc = 0;
-    j = 0;
-    for (; j + 8 <= len; j += 8) {
-        float a[8], b[8];
-        int k[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) { a[u] = A[j + u]; b[u] = A2[j + u]; k[u] = K[j + u]; }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            kc += k[u];
-            L += a[u];
-            Rv -= a[u];
-            L2 += b[u];
-            Rv2 -= b[u];
-            A[j + u] = L;
-            A2[j + u] = L2;
-            K[j + u] = kc;
-            R[j + u] = Rv;
-            R2[j + u] = Rv2;
-        }
-    }
-    for (; j < len; ++j) {
-        kc += K[j];
-        L += A[j];
-        Rv -= A[j];
-        L2 += A2[j];
-        Rv2 -= A2[j];
-        A[j] = L;
-        A2[j] = L2;
-        K[j] = kc;
-        R[j] = Rv;
-        R2[j] = Rv2;
-    }
-}
-
 // Key of one candidate split (left sums mL/mL2 over mC rows, right sums mR/mR2, node rows c):
 // the reference's MSE criterion; candidates whose criterion is not below 1e20 (or NaN) never
 // win.  `mvbin` = (draw << 8) | bin.
@@ -259,258 +116,578 @@ __device__ __forceinline__ unsigned long long regr_key(float mL, float mR, float
     return mse < 1e20f ? ((unsigned long long)ord_of(mse) << 32) | mvbin : kNoKey;
 }
 
+// The reference's gini for the left prefix counts lk = hp[k * 256] (k < nc), class totals
+// tk[k], node rows c.
+__device__ __forceinline__ float class_gini_exact(const int* hp, const int* tk, int nc, int c) {
+    int tl = 0;
+    for (int k = 0; k < nc; ++k) tl += hp[k * 256];
+    const float tlf = (float)tl, trf = (float)(c - tl);
+    float gl = 1.0f, gr = 1.0f;
+    for (int k = 0; k < nc; ++k) {
+        const int lk = hp[k * 256];
+        const float pl = (float)lk / tlf;
+        const float pr = (float)(tk[k] - lk) / trf;
+        gl -= pl * pl;
+        gr -= pr * pr;
+    }
+    const float tt = tlf + trf;
+    return (tlf * gl + trf * gr) / tt;
+}
+
 __device__ __forceinline__ unsigned long long warp_min_key(unsigned long long k) {
     for (int o = 16; o > 0; o >>= 1) k = min(k, __shfl_xor_sync(kFull, k, o));
     return k;
 }
 
-// Per-warp scratch layout shared by both kernels (after any staging area):
-//   bl[256] uint8 | sy[256] f32 | sy2[256] f32 | cn[256] i32 | h[(256+1) * nclass] i32
-// (regression: k_hist uses h as the right sums R[256] | R2[256]; k_hist_small keeps its
-// list area at kHistScratch)
-__device__ __forceinline__ void warp_scratch(uint8_t* w, uint8_t*& bl, float*& sy, float*& sy2,
-                                             int*& cn, int*& h) {
-    bl = w;
-    sy = reinterpret_cast<float*>(w + 256);
-    sy2 = sy + kBins;
-    cn = reinterpret_cast<int*>(sy2 + kBins);
-    h = cn + kBins;
+__device__ __forceinline__ float warp_min_f(float x) {
+    for (int o = 16; o > 0; o >>= 1) x = fminf(x, __shfl_xor_sync(kFull, x, o));
+    return x;
 }
 
-// Histogram of one feature over the 32-row step starting at row s0 (bins `b`, targets v/v2
-// or label), rows in order.  All lanes call it.
-__device__ __forceinline__ void hist_step(bool regr, int nc, bool valid, int b, float v, float v2,
-                                          int label, int lane, float* sy, float* sy2, int* cn,
-                                          int* h) {
-    const uint32_t peers = __match_any_sync(kFull, b);
-    const int rank = __popc(peers & ((1u << lane) - 1u));
-    if (regr) {
-        const int maxr = __reduce_max_sync(kFull, valid ? __popc(peers) - 1 : 0);
-        for (int qq = 0; qq <= maxr; ++qq) {
-            if (valid && rank == qq) {
-                sy[b] += v * 1.0f;
-                sy2[b] += v2 * 1.0f;
-                cn[b] += 1;
-            }
+__device__ __forceinline__ float warp_sum_f(float x) {
+    for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(kFull, x, o);
+    return x;
+}
+
+template <class T>
+__device__ __forceinline__ T warp_incl_scan(T x, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const T y = __shfl_up_sync(kFull, x, o);
+        if (lane >= o) x += y;
+    }
+    return x;
+}
+
+// ---------------------------------------------------------------------------------------
+// k_hist_warp: nodes above kSmallNode rows.
+//
+// Per-warp shared memory (warp_bytes):
+//   regression      SS float2[256] (bin sum, sum of squares) | KC int[256] | BL u8[256]
+//                   (non-empty bins, ascending) | CF u8[256] (candidate flags) | TAG u32[256]
+//                   (round tags, all-ones between steps)
+//   classification  H int[nclass][256] (class-major counts, then inclusive prefixes) |
+//                   KC int[256] | BL u8[256] | TK int[32] (class totals)
+// ---------------------------------------------------------------------------------------
+constexpr int kWarpUnroll = 4;  // 32-row steps whose loads are in flight together
+
+template <bool REGR>
+__device__ __forceinline__ void hist_warp(const Data& D, const Batch& B, int cur, const HistArgs& a,
+                                          uint8_t* smem, unsigned* s_umin) {
+    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+    const int nc = D.nclass;
+    const int rs = D.rs, ro = D.ro;
+    uint8_t* wbase = smem + (size_t)wib * a.warp_bytes;
+    const int hbytes = REGR ? 2048 : 1024 * nc;
+    float2* SS = reinterpret_cast<float2*>(wbase);
+    int* H = reinterpret_cast<int*>(wbase);
+    int* KC = reinterpret_cast<int*>(wbase + hbytes);
+    uint8_t* BL = wbase + hbytes + 1024;
+    uint8_t* CF = BL + 256;
+    int* TK = reinterpret_cast<int*>(BL + 256);
+    unsigned* TAG = reinterpret_cast<unsigned*>(BL + 512);  // regression: per-bin round tags
+    if (REGR)
+        for (int k = lane; k < 256; k += 32) TAG[k] = 0xffffffffu;
+    if (threadIdx.x < 2) s_umin[threadIdx.x] = 0xffffffffu;
+    __syncthreads();
+    const int total = B.counters[4] * a.groups;
+    int it = 0;
+    for (int task = blockIdx.x; task < total; task += gridDim.x, ++it) {
+        const int si = task / a.groups, grp = task - si * a.groups;
+        const int t = tree_of(B.srch_big_off, B.T, si);
+        const int node = B.srch_big[(size_t)t * B.M + (si - B.srch_big_off[t])];
+        const size_t m = (size_t)t * B.M + node;
+        const int start = B.nd_start[m], c = B.nd_cnt[m];
+        const int* seg = B.seg[cur] + (size_t)t * D.N + start;
+        const int mv = grp * a.warps + wib;
+        const bool active = mv < B.mtry;
+        unsigned* umin = &s_umin[it & 1];
+        if (threadIdx.x == 0 && grp == 0 && B.hist_bytes)
+            atomicAdd(B.hist_bytes, (unsigned long long)c * (unsigned long long)(B.mtry + (REGR ? 4 : 1)));
+        float lo[8];
+        int binq[8];
+        int nm = 0;
+        bool dense = false;
+        const int f = active ? (int)B.feat[(size_t)t * B.M * B.mtry + (size_t)node * B.mtry + mv] : 0;
+        if (active) {
+            // ---- zero the histogram
+            uint4* z = reinterpret_cast<uint4*>(wbase);
+            const int words = (hbytes + 1024) / 16;
+            for (int k = lane; k < words; k += 32) z[k] = make_uint4(0, 0, 0, 0);
             __syncwarp();
         }
-    } else {
-        if (valid) {
-            atomicAdd(&h[b * nc + label], 1);
-            if (rank == 0) atomicAdd(&cn[b], __popc(peers));
+        if (active) {
+            // ---- accumulate, 32 rows per step in row order (bins and targets gathered from
+            // the packed rows; the loads of kWarpUnroll steps in flight together)
+            for (int s0 = 0; s0 < c; s0 += 32 * kWarpUnroll) {
+                int bb[kWarpUnroll];
+                uint2 tg[kWarpUnroll];
+                int r[kWarpUnroll];
+#pragma unroll
+                for (int u = 0; u < kWarpUnroll; ++u) {
+                    const int i = s0 + u * 32 + lane;
+                    r[u] = i < c ? __ldg(seg + i) : -1;
+                }
+#pragma unroll
+                for (int u = 0; u < kWarpUnroll; ++u) {
+                    bb[u] = -1;
+                    tg[u] = make_uint2(0, 0);
+                    if (r[u] >= 0) {
+                        const uint8_t* row = D.rows + (size_t)r[u] * rs;
+                        bb[u] = (int)__ldg(row + f);
+                        tg[u] = __ldg(reinterpret_cast<const uint2*>(row + ro));
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < kWarpUnroll; ++u) {
+                    if (s0 + u * 32 >= c) break;
+                    const int b = bb[u];
+                    const bool valid = b >= 0;
+                    if (REGR) {
+                        // rounds: in each, the lowest pending lane of every bin (the earliest
+                        // row) adds its target; the bin's next row goes in the next round
+                        const float v = __uint_as_float(tg[u].x), v2 = __uint_as_float(tg[u].y);
+                        if (valid) atomicAdd(&KC[b], 1);
+                        bool pend = valid;
+                        int rounds = 0;
+                        while (__any_sync(kFull, pend)) {
+                            ++rounds;
+                            if (pend) atomicMin(&TAG[b], (unsigned)lane);
+                            __syncwarp();
+                            const bool first = pend && TAG[b] == (unsigned)lane;
+                            if (first) {
+                                float2 h = SS[b];
+                                h.x += v;
+                                h.y += v2;
+                                SS[b] = h;
+                                TAG[b] = 0xffffffffu;
+                            }
+                            pend = pend && !first;
+                            __syncwarp();
+                        }
+                        if (B.diag && lane == 0) {
+                            atomicAdd(&B.diag[1], (unsigned long long)rounds);
+                            atomicAdd(&B.diag[2], 1ull);
+                        }
+                    } else if (valid) {
+                        atomicAdd(&H[(int)tg[u].x * 256 + b], 1);
+                        atomicAdd(&KC[b], 1);
+                    }
+                }
+            }
+            __syncwarp();
+            __syncwarp();
+            nm = warp_nonempty_bins(KC, BL, lane);
+            // ---- approximate criterion over the lane's entries: dense (bins 8*lane..+7)
+            // or, for few non-empty bins, the lane's share of the compacted list
+            dense = nm > 96;
+            const int E = dense ? 8 : (nm + 31) >> 5;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                lo[q] = __int_as_float(0x7f800000);
+                binq[q] = -1;
+                if (q < E) {
+                    if (dense) binq[q] = lane * 8 + q;
+                    else if (lane * E + q < nm) binq[q] = BL[lane * E + q];
+                }
+            }
+            float hmin = __int_as_float(0x7f800000);
+            const float rtt = __frcp_rn((float)c);
+            if (REGR) {
+                float S[8], S2[8];
+                int K[8];
+                float ps = 0.0f, ps2 = 0.0f, sa = 0.0f;
+                int pk = 0;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    S[q] = S2[q] = 0.0f;
+                    K[q] = 0;
+                    if (binq[q] >= 0) {
+                        const float2 h = SS[binq[q]];
+                        S[q] = h.x;
+                        S2[q] = h.y;
+                        K[q] = KC[binq[q]];
+                    }
+                    sa += fabsf(S[q]);
+                    ps += S[q];
+                    ps2 += S2[q];
+                    pk += K[q];
+                    S[q] = ps;    // inclusive local prefixes from here on
+                    S2[q] = ps2;
+                    K[q] = K[q] > 0 ? pk : -1;  // -1: empty bin (never a candidate)
+                }
+                const float is = warp_incl_scan(ps, lane), is2 = warp_incl_scan(ps2, lane);
+                const int ik = warp_incl_scan(pk, lane);
+                const float es = is - ps, es2 = is2 - ps2;  // approximate exclusive prefixes
+                const int ek = ik - pk;
+                const float tot = __shfl_sync(kFull, is, 31), tot2 = __shfl_sync(kFull, is2, 31);
+                const float A = warp_sum_f(sa);
+                const float d = (float)(2 * nm + 64) * 0x1p-24f;
+                const float dA = d * A, dA2 = d * fabsf(tot2) * 1.001f;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    if (K[q] < 0) continue;
+                    const int kc = ek + K[q];
+                    if (kc >= c) continue;
+                    const float Lh = es + S[q], L2h = es2 + S2[q];
+                    const float Rh = tot - Lh, R2h = tot2 - L2h;
+                    const float rcl = __frcp_rn((float)kc), rcr = __frcp_rn((float)(c - kc));
+                    const float t1 = Lh * Lh * rcl, t2 = Rh * Rh * rcr, P = L2h + R2h;
+                    const float mse = (P - t1 - t2) * rtt;
+                    const float pert = (2.0f * dA2 + (2.0f * fabsf(Lh) + 3.0f * dA) * dA * rcl +
+                                        (2.0f * fabsf(Rh) + 3.0f * dA) * dA * rcr) * rtt;
+                    const float Q = (fabsf(P) + t1 + t2) * rtt + pert;
+                    const float Eb = 1.25f * (pert + 0x1p-19f * Q) + 1e-30f;
+                    lo[q] = mse - Eb;
+                    hmin = fminf(hmin, mse + Eb);
+                }
+            } else {
+                float SL[8], SR[8];
+                int kc[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) { SL[q] = SR[q] = 0.0f; kc[q] = 0; }
+                for (int k = 0; k < nc; ++k) {
+                    int hv[8];
+                    int pk = 0;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        hv[q] = binq[q] >= 0 ? H[k * 256 + binq[q]] : 0;
+                        pk += hv[q];
+                        hv[q] = pk;
+                    }
+                    const int ik = warp_incl_scan(pk, lane);
+                    const int ek = ik - pk;
+                    const int tk = __shfl_sync(kFull, ik, 31);
+                    if (lane == 0) TK[k] = tk;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        const int lk = ek + hv[q];
+                        const float fl = (float)lk, fr = (float)(tk - lk);
+                        SL[q] += fl * fl;
+                        SR[q] += fr * fr;
+                        kc[q] += lk;
+                        if (binq[q] >= 0) H[k * 256 + binq[q]] = lk;  // left prefix, in place
+                    }
+                }
+                const float Ec = 1.5f * (float)(2 * nc + 16) * 0x1p-24f;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    if (binq[q] < 0 || KC[binq[q]] == 0 || kc[q] >= c) continue;
+                    const float rcl = __frcp_rn((float)kc[q]), rcr = __frcp_rn((float)(c - kc[q]));
+                    const float g = 1.0f - (SL[q] * rcl + SR[q] * rcr) * rtt;
+                    lo[q] = g - Ec;
+                    hmin = fminf(hmin, g + Ec);
+                }
+            }
+            hmin = warp_min_f(hmin);
+            if (lane == 0 && hmin < __int_as_float(0x7f800000)) atomicMin(umin, ord_of(hmin));
+        }
+        __syncthreads();
+        if (threadIdx.x == 0) s_umin[(it + 1) & 1] = 0xffffffffu;
+        if (!active) continue;
+        const unsigned uo = *umin;
+        if (uo == 0xffffffffu) continue;
+        const float thr = REGR ? float_of(uo) : float_of(uo) + 0x1p-21f;
+        // ---- exact criterion for the candidates
+        bool any = false;
+        int bmax = -1;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const bool cq = binq[q] >= 0 && lo[q] <= thr;
+            if (REGR && binq[q] >= 0) CF[binq[q]] = cq ? 1 : 0;
+            if (cq) { any = true; bmax = max(bmax, binq[q]); }
+        }
+        if (!__any_sync(kFull, any)) continue;
+        if (REGR) {
+            bmax = __reduce_max_sync(kFull, (unsigned)(bmax + 1)) - 1;
+            __syncwarp();
+            if (lane == 0) {
+                // the reference's serial chains over the non-empty bins (empty bins add +0)
+                float tot = 0.0f, tot2 = 0.0f;
+                int j = 0;
+                for (; j + 8 <= nm; j += 8) {
+                    float2 h[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) h[u] = SS[BL[j + u]];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) { tot += h[u].x; tot2 += h[u].y; }
+                }
+                for (; j < nm; ++j) {
+                    const float2 h = SS[BL[j]];
+                    tot += h.x;
+                    tot2 += h.y;
+                }
+                float L = 0.0f, R = tot, L2 = 0.0f, R2 = tot2;
+                int kc = 0;
+                unsigned long long best = kNoKey;
+                for (j = 0; j < nm; ++j) {
+                    const int b = BL[j];
+                    if (b > bmax) break;
+                    const float2 h = SS[b];
+                    kc += KC[b];
+                    L += h.x;
+                    R -= h.x;
+                    L2 += h.y;
+                    R2 -= h.y;
+                    if (CF[b]) {
+                        best = min(best, regr_key(L, R, L2, R2, kc, c, ((uint32_t)mv << 8) | (uint32_t)b));
+                        if (B.diag) atomicAdd(&B.diag[0], 1ull);
+                    }
+                }
+                if (best != kNoKey) atomicMin(&B.nd_key[m], best);
+            }
+            __syncwarp();
+        } else {
+            unsigned long long kb = kNoKey;  // (gini bits, bin): the draw's first minimum
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                if (binq[q] >= 0 && lo[q] <= thr) {
+                    const float g = class_gini_exact(H + binq[q], TK, nc, c);
+                    kb = min(kb, ((unsigned long long)ord_of(g) << 32) | (unsigned long long)binq[q]);
+                }
+            }
+            kb = warp_min_key(kb);
+            if (lane == 0 && kb != kNoKey) {
+                const float g = float_of((uint32_t)(kb >> 32));
+                const unsigned long long key = ((unsigned long long)ord_of(-(2.0f - g)) << 32) |
+                                               ((unsigned long long)mv << 8) | (kb & 0xffull);
+                atomicMin(&B.nd_key[m], key);
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(512, 2) k_hist_warp_regr(Data D, Batch B, int cur, HistArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ unsigned s_umin[2];
+    hist_warp<true>(D, B, cur, a, smem, s_umin);
+}
+
+__global__ void __launch_bounds__(512, 1) k_hist_warp_class(Data D, Batch B, int cur, HistArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ unsigned s_umin[2];
+    hist_warp<false>(D, B, cur, a, smem, s_umin);
+}
+
+// ---------------------------------------------------------------------------------------
+// k_hist_lane: regression nodes of at most kSmallNode rows.  A warp takes `slots` nodes of
+// the level's small list; lane = slot * mtry + draw.  The nodes' rows (drawn bins and
+// targets) are staged in shared memory by the whole warp, then every lane builds its draw's
+// histogram as a list of the non-empty bins (a 256-bit set gives each bin its list index),
+// adding its rows in row order, and runs the reference's serial chains over the list.
+//
+// Filter.  With the exact chain values L, R (left/right sums), the reference's MSE times
+// the node size is P - G + d, where P = L2 + R2 is within 2m u T2 of T2 = sum of the node's
+// squared targets (m <= kSmallNode list entries), G = L^2/cl + R^2/cr, and |d| <= 16.1 u T2
+// (rounding of the float formula; G <= P).  The approximation G_h (hardware reciprocals) is
+// within 5.1 u T2 of G.  So the reference's choice has G_h >= max G_h - 2 (2 kSmallNode + 22) u T2
+// over all draws of the node; only those entries get the exact criterion (the window below
+// is that bound times 1.25).
+//
+// Per-warp shared memory (lane_bytes(slots)):
+//   LS float2[kSmallNode][32] (bin sum, sum of squares) | LK u8[kSmallNode][32] (counts) |
+//   BM u32[8][32] (bin sets) | BS u32[8][32] (list index of each set word) |
+//   TL u8[32][kLaneTile] (bins, lane-major) | TG float2[slots][kSmallNode] (targets) |
+//   UM u32[kLaneSlots] (ordered max G_h per node)
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+__global__ void __launch_bounds__(32) k_hist_lane(Data D, Batch B, int cur, int slots) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int lane = threadIdx.x;
+    float2* LS = reinterpret_cast<float2*>(smem);
+    uint8_t* LK = smem + kSmallNode * 32 * 8;
+    uint32_t* BM = reinterpret_cast<uint32_t*>(LK + kSmallNode * 32);
+    uint32_t* BS = BM + 256;
+    uint8_t* TL = reinterpret_cast<uint8_t*>(BS + 256);
+    float2* TG = reinterpret_cast<float2*>(TL + 32 * kLaneTile);
+    unsigned* UM = reinterpret_cast<unsigned*>(TG + slots * kSmallNode);
+    const int mtry = B.mtry, rs = D.rs, ro = D.ro;
+    const int total = B.counters[6];
+    const int slot = lane / mtry, d = lane - slot * mtry;
+    const bool lane_on = slot < slots;
+    const uint8_t* tl = TL + lane * kLaneTile;
+    for (int g0 = blockIdx.x * slots; g0 < total; g0 += gridDim.x * slots) {
+        int my_t = 0, my_node = 0, my_c = 0, my_start = 0;
+        if (lane < slots && g0 + lane < total) {
+            const int si = g0 + lane;
+            my_t = tree_of(B.srch_sml_off, B.T, si);
+            my_node = B.srch_sml[(size_t)my_t * B.M + (si - B.srch_sml_off[my_t])];
+            const size_t mm = (size_t)my_t * B.M + my_node;
+            my_c = B.nd_cnt[mm];
+            my_start = B.nd_start[mm];
+        }
+        if (lane < slots) UM[lane] = 0u;
+        // ---- stage: lanes take rows, every drawn feature's bin and the target
+        for (int s = 0; s < slots; ++s) {
+            const int c = __shfl_sync(kFull, my_c, s);
+            if (c == 0) continue;
+            const int t = __shfl_sync(kFull, my_t, s), node = __shfl_sync(kFull, my_node, s);
+            const int start = __shfl_sync(kFull, my_start, s);
+            const int* seg = B.seg[cur] + (size_t)t * D.N + start;
+            const uint16_t* featp = B.feat + (size_t)t * B.M * mtry + (size_t)node * mtry;
+            const int fl = lane < mtry ? (int)featp[lane] : 0;
+            if (lane == 0 && B.hist_bytes)
+                atomicAdd(B.hist_bytes, (unsigned long long)c * (unsigned long long)(mtry + 4));
+            for (int i0 = 0; i0 < c; i0 += 32) {
+                const int i = i0 + lane;
+                const bool ok = i < c;
+                const uint8_t* row = D.rows + (ok ? (size_t)__ldg(seg + i) * rs : 0);
+                if (ok) TG[s * kSmallNode + i] = __ldg(reinterpret_cast<const float2*>(row + ro));
+                uint8_t* dst = TL + (s * mtry) * kLaneTile + i;
+                for (int dd = 0; dd < mtry; ++dd) {
+                    const int fd = __shfl_sync(kFull, fl, dd);
+                    if (ok) dst[dd * kLaneTile] = __ldg(row + fd);
+                }
+            }
+        }
+        __syncwarp();
+        const int sl = lane_on ? slot : 0;
+        const int cs = __shfl_sync(kFull, my_c, sl);
+        const int c = lane_on ? cs : 0;
+        const int t = __shfl_sync(kFull, my_t, sl);
+        const int node = __shfl_sync(kFull, my_node, sl);
+        const float2* tg = TG + sl * kSmallNode;
+        // ---- bin set and list indices
+#pragma unroll
+        for (int q = 0; q < 8; ++q) BM[q * 32 + lane] = 0u;
+        for (int i = 0; i < c; ++i) {
+            const int b = tl[i];
+            BM[(b >> 5) * 32 + lane] |= 1u << (b & 31);
+        }
+        int nm = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            BS[q * 32 + lane] = (uint32_t)nm;
+            nm += __popc(BM[q * 32 + lane]);
+        }
+        for (int j = 0; j < nm; ++j) {
+            LS[j * 32 + lane] = make_float2(0.0f, 0.0f);
+            LK[j * 32 + lane] = 0;
+        }
+        auto entry = [&](int b) -> int {
+            const int q = b >> 5;
+            return (int)BS[q * 32 + lane] + __popc(BM[q * 32 + lane] & ((1u << (b & 31)) - 1u));
+        };
+        // ---- histogram in row order, four rows at a time (equal entries forwarded)
+        int i = 0;
+        for (; i + 4 <= c; i += 4) {
+            const uint32_t bw = *reinterpret_cast<const uint32_t*>(tl + i);
+            const int e0 = entry(bw & 0xff), e1 = entry((bw >> 8) & 0xff);
+            const int e2 = entry((bw >> 16) & 0xff), e3 = entry(bw >> 24);
+            const float2 y0 = tg[i], y1 = tg[i + 1], y2 = tg[i + 2], y3 = tg[i + 3];
+            const float2 a0 = LS[e0 * 32 + lane], a1 = LS[e1 * 32 + lane];
+            const float2 a2 = LS[e2 * 32 + lane], a3 = LS[e3 * 32 + lane];
+            const int k0 = LK[e0 * 32 + lane], k1 = LK[e1 * 32 + lane];
+            const int k2 = LK[e2 * 32 + lane], k3 = LK[e3 * 32 + lane];
+            const float2 n0 = make_float2(a0.x + y0.x, a0.y + y0.y);
+            const int m0 = k0 + 1;
+            const bool f10 = e1 == e0;
+            const float2 b1 = f10 ? n0 : a1;
+            const float2 n1 = make_float2(b1.x + y1.x, b1.y + y1.y);
+            const int m1 = (f10 ? m0 : k1) + 1;
+            const bool f21 = e2 == e1, f20 = e2 == e0;
+            const float2 b2 = f21 ? n1 : (f20 ? n0 : a2);
+            const float2 n2 = make_float2(b2.x + y2.x, b2.y + y2.y);
+            const int m2 = (f21 ? m1 : (f20 ? m0 : k2)) + 1;
+            const bool f32 = e3 == e2, f31 = e3 == e1, f30 = e3 == e0;
+            const float2 b3 = f32 ? n2 : (f31 ? n1 : (f30 ? n0 : a3));
+            const float2 n3 = make_float2(b3.x + y3.x, b3.y + y3.y);
+            const int m3 = (f32 ? m2 : (f31 ? m1 : (f30 ? m0 : k3))) + 1;
+            LS[e0 * 32 + lane] = n0;
+            LK[e0 * 32 + lane] = (uint8_t)m0;
+            LS[e1 * 32 + lane] = n1;
+            LK[e1 * 32 + lane] = (uint8_t)m1;
+            LS[e2 * 32 + lane] = n2;
+            LK[e2 * 32 + lane] = (uint8_t)m2;
+            LS[e3 * 32 + lane] = n3;
+            LK[e3 * 32 + lane] = (uint8_t)m3;
+        }
+        for (; i < c; ++i) {
+            const int e = entry(tl[i]);
+            const float2 a = LS[e * 32 + lane];
+            const float2 y = tg[i];
+            LS[e * 32 + lane] = make_float2(a.x + y.x, a.y + y.y);
+            LK[e * 32 + lane] = (uint8_t)(LK[e * 32 + lane] + 1);
+        }
+        // ---- the reference's chains: totals, then left/right sums with G_h
+        float tot = 0.0f, tot2 = 0.0f;
+        for (int j = 0; j < nm; ++j) {
+            const float2 e = LS[j * 32 + lane];
+            tot += e.x;
+            tot2 += e.y;
+        }
+        float gmax = -1.0f;
+        {
+            float L = 0.0f, R = tot;
+            int kc = 0;
+            for (int j = 0; j < nm - 1; ++j) {
+                const float S = LS[j * 32 + lane].x;
+                kc += LK[j * 32 + lane];
+                L += S;
+                R -= S;
+                const float G = L * L * rcp_approx((float)kc) + R * R * rcp_approx((float)(c - kc));
+                gmax = fmaxf(gmax, G);
+            }
+        }
+        if (lane_on && gmax >= 0.0f) atomicMax(&UM[slot], ord_of(gmax));
+        __syncwarp();
+        const unsigned um = lane_on ? UM[slot] : 0u;
+        const float thr = um ? float_of(um) - 0x1.8p-16f * tot2 : 0.0f;
+        if (um != 0u && gmax >= thr) {
+            float L = 0.0f, R = tot, L2 = 0.0f, R2 = tot2;
+            int kc = 0;
+            unsigned long long best = kNoKey;
+            for (int j = 0; j < nm - 1; ++j) {
+                const float2 e = LS[j * 32 + lane];
+                kc += LK[j * 32 + lane];
+                L += e.x;
+                R -= e.x;
+                L2 += e.y;
+                R2 -= e.y;
+                const float G = L * L * rcp_approx((float)kc) + R * R * rcp_approx((float)(c - kc));
+                if (G >= thr) {
+                    // bin of list entry j: the (j - BS[q])-th set bit of word q
+                    int q = 0;
+                    while (q < 7 && (int)BS[(q + 1) * 32 + lane] <= j) ++q;
+                    uint32_t w = BM[q * 32 + lane];
+                    for (int k = j - (int)BS[q * 32 + lane]; k > 0; --k) w &= w - 1u;
+                    const int b = q * 32 + __ffs(w) - 1;
+                    best = min(best, regr_key(L, R, L2, R2, kc, c, ((uint32_t)d << 8) | (uint32_t)b));
+                    if (B.diag) atomicAdd(&B.diag[0], 1ull);
+                }
+            }
+            if (best != kNoKey) atomicMin(&B.nd_key[(size_t)t * B.M + node], best);
         }
         __syncwarp();
     }
 }
 
 // ---------------------------------------------------------------------------------------
-// Large nodes.  The block streams the node's packed rows (uint8 bins of every feature +
-// the target) from L2 through shared memory: each thread loads 4 consecutive rows x 16
-// bytes into registers, the next chunk's loads in flight while the warps work on the
-// current one, and stores them transposed (feature-major, padded stride) so that the 32
-// lanes of a warp read 32 consecutive bytes of their feature without bank conflicts.
+// k_hist_small: classification nodes of at most kSmallNode rows, one warp per searched
+// node doing all mtry draws.  Each lane holds up to two of the node's rows (address and
+// label in registers) and reads the drawn feature's bin directly from the packed row; the
+// draw's bins form a 256-bit set ranking each row's bin, class counts go to the ranked
+// entries, and per-class warp scans give the prefixes of the criterion.
+// Per-warp scratch: bl u8[256] | set words + rank offsets (16 words) | h int[(256+1) nclass]
 // ---------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(512, 2) k_hist(Data D, Batch B, int cur, HistArgs a) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ int snode[2];
-    __shared__ int slen[32];  // regression: list length of each warp's draw
-    const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const int nthr = blockDim.x;
-    const bool regr = D.nclass == 1;
-    const int nc = D.nclass;
-    const int rs = D.rs, ro = D.ro;
-    const int pieces = rs >> 4;
-    const int CH = a.stage_rows;
-    const int CS = a.cstride;
-    uint8_t* col = smem;                                                    // [rs][CS]
-    uint32_t* ytgt = reinterpret_cast<uint32_t*>(smem + (size_t)rs * CS);   // [CH][2]
-    uint8_t* wbase = smem + (size_t)rs * CS + (size_t)CH * 8 + (size_t)wib * a.warp_bytes;
-    uint8_t* bl;
-    float *sy, *sy2;
-    int *cn, *h;
-    warp_scratch(wbase, bl, sy, sy2, cn, h);
-    for (int k = lane; k < a.warp_bytes / 4; k += 32) reinterpret_cast<uint32_t*>(wbase)[k] = 0u;
-    __syncwarp();
-    const int total = B.counters[4] * a.groups;
-    const int units = (CH >> 2) * pieces;
-    for (int task = blockIdx.x; task < total; task += gridDim.x) {
-        const int si = task / a.groups, grp = task - si * a.groups;
-        if (threadIdx.x == 0) {
-            const int t = tree_of(B.srch_big_off, B.T, si);
-            snode[0] = t;
-            snode[1] = B.srch_big[(size_t)t * B.M + (si - B.srch_big_off[t])];
-        }
-        __syncthreads();
-        const int t = snode[0], node = snode[1];
-        const size_t m = (size_t)t * B.M + node;
-        const int start = B.nd_start[m], c = B.nd_cnt[m];
-        const int* seg = B.seg[cur] + (size_t)t * D.N + start;
-        const uint16_t* featp = B.feat + (size_t)t * B.M * B.mtry + (size_t)node * B.mtry;
-        if (threadIdx.x == 0 && grp == 0 && B.hist_bytes)
-            atomicAdd(B.hist_bytes, (unsigned long long)c * (unsigned long long)(B.mtry + (regr ? 4 : 1)));
-        const int mv = grp * a.warps + wib;
-        const bool active = mv < B.mtry;
-        const int f = active ? featp[mv] : 0;
-        uint4 reg[2][4];
-        auto load_chunk = [&](int c0) {
-            const int ch = min(CH, c - c0);
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int unit = threadIdx.x + u * nthr;
-                if (unit < units) {
-                    const int rg = unit / pieces, pc = unit - rg * pieces;
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        const int i = rg * 4 + r;
-                        reg[u][r] = i < ch ? __ldg(reinterpret_cast<const uint4*>(D.rows + (size_t)seg[c0 + i] * rs) + pc)
-                                           : make_uint4(0, 0, 0, 0);
-                    }
-                }
-            }
-        };
-        auto store_chunk = [&]() {
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-                const int unit = threadIdx.x + u * nthr;
-                if (unit < units) {
-                    const int rg = unit / pieces, pc = unit - rg * pieces;
-                    const uint32_t* w0 = reinterpret_cast<const uint32_t*>(&reg[u][0]);
-                    const uint32_t* w1 = reinterpret_cast<const uint32_t*>(&reg[u][1]);
-                    const uint32_t* w2 = reinterpret_cast<const uint32_t*>(&reg[u][2]);
-                    const uint32_t* w3 = reinterpret_cast<const uint32_t*>(&reg[u][3]);
-#pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int w = j >> 2, q = j & 3;
-                        *reinterpret_cast<uint32_t*>(col + (size_t)(pc * 16 + j) * CS + rg * 4) =
-                            gather_byte(w0[w], w1[w], w2[w], w3[w], q);
-                    }
-                    if (pc == (ro >> 4)) {
-                        const bool hi = (ro & 15) != 0;  // target in words 2,3 of the piece
-#pragma unroll
-                        for (int r = 0; r < 4; ++r) {
-                            const uint4 v = reg[u][r];
-                            reinterpret_cast<uint2*>(ytgt)[rg * 4 + r] =
-                                hi ? make_uint2(v.z, v.w) : make_uint2(v.x, v.y);
-                        }
-                    }
-                }
-            }
-        };
-        if (c > 0) load_chunk(0);
-        for (int c0 = 0; c0 < c; c0 += CH) {
-            const int ch = min(CH, c - c0);
-            __syncthreads();
-            store_chunk();
-            __syncthreads();
-            if (c0 + CH < c) load_chunk(c0 + CH);  // in flight during the histogram work
-            if (active) {
-                const uint8_t* fcol = col + (size_t)f * CS;
-                for (int s0 = 0; s0 < ch; s0 += 32) {
-                    const int i = s0 + lane;
-                    const bool valid = i < ch;
-                    const int b = valid ? fcol[i] : kBins;
-                    const uint2 yy = reinterpret_cast<const uint2*>(ytgt)[i];
-                    hist_step(regr, nc, valid, b, __uint_as_float(yy.x), __uint_as_float(yy.y),
-                              (int)yy.x, lane, sy, sy2, cn, h);
-                }
-            }
-        }
-        if (!regr) {
-            if (active) {
-                __syncwarp();
-                const unsigned long long key = scan_bins(regr, nc, c, mv, lane, bl, sy, sy2, cn, h);
-                if (lane == 0 && key != kNoKey) atomicMin(&B.nd_key[m], key);
-            }
-            continue;
-        }
-        // regression: every warp compacts its histogram in place to the list of non-empty
-        // bins, lanes of warp 0 run the draws' chains, every warp scores its own list
-        int nm = 0;
-        if (active) {
-            __syncwarp();
-            nm = warp_nonempty_bins(cn, bl, lane);
-            for (int s0 = 0; s0 < nm; s0 += 32) {  // entry j <= bin bl[j]: forward in place
-                const int j = s0 + lane;
-                float x = 0.0f, x2 = 0.0f;
-                int k = 0;
-                if (j < nm) {
-                    const int b = bl[j];
-                    x = sy[b];
-                    x2 = sy2[b];
-                    k = cn[b];
-                }
-                __syncwarp();
-                if (j < nm) {
-                    sy[j] = x;
-                    sy2[j] = x2;
-                    cn[j] = k;
-                }
-                __syncwarp();
-            }
-        }
-        if (lane == 0) slen[wib] = nm;
-        __syncthreads();
-        if (wib == 0 && lane < a.warps) {
-            uint8_t* bl2;
-            float *a1, *a2;
-            int *k1, *h2;
-            warp_scratch(smem + (size_t)rs * CS + (size_t)CH * 8 + (size_t)lane * a.warp_bytes,
-                         bl2, a1, a2, k1, h2);
-            float* r1 = reinterpret_cast<float*>(h2);
-            regr_chains(a1, a2, k1, r1, r1 + kBins, slen[lane]);
-        }
-        __syncthreads();
-        if (active) {
-            const float* r1 = reinterpret_cast<const float*>(h);
-            unsigned long long best = kNoKey;
-            for (int j = lane; j < nm - 1; j += 32)
-                best = min(best, regr_key(sy[j], r1[j], sy2[j], r1[kBins + j], cn[j], c,
-                                          ((uint32_t)mv << 8) | bl[j]));
-            best = warp_min_key(best);
-            if (lane == 0 && best != kNoKey) atomicMin(&B.nd_key[m], best);
-            __syncwarp();
-            for (int k = lane; k < kBins; k += 32) {
-                sy[k] = 0.0f;
-                sy2[k] = 0.0f;
-                cn[k] = 0;
-            }
-        }
-    }
-}
-
-// ---------------------------------------------------------------------------------------
-// Small nodes (c <= small_node_limit rows): one warp per searched node does all mtry draws.
-// Each lane holds up to four of the node's rows (address and target in registers) and
-// reads the drawn feature's bin directly from the packed row; per-warp shared memory holds
-// only the histogram, which keeps many warps resident to hide the latency.
-// ---------------------------------------------------------------------------------------
-constexpr int kSmallRows = kSmallNodeRegr / 32;  // rows per lane in k_hist_small
-constexpr int kSmallListOff = 64;                 // regression list area offset per warp
+constexpr int kSmallRows = kSmallNode / 32;  // rows per lane in k_hist_small
 
 __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, int warp_bytes) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
-    const bool regr = D.nclass == 1;
     const int nc = D.nclass;
     const int rs = D.rs, ro = D.ro;
     uint8_t* wbase = smem + (size_t)wib * warp_bytes;
-    uint8_t* bl;
-    float *sy, *sy2;
-    int *cn, *h;
-    warp_scratch(wbase, bl, sy, sy2, cn, h);
-    // regression: the bin set's words and their rank offsets (8 + 8 words), then the list
-    // area: sums, square sums, counts, right sums, right square sums, (draw, bin, last)
-    // words -- kListCap entries each (no 256-bin histogram)
-    uint32_t* SW = reinterpret_cast<uint32_t*>(wbase);
-    int* SP = reinterpret_cast<int*>(SW + 8);
-    float* LA = reinterpret_cast<float*>(wbase + kSmallListOff);
-    float* LA2 = LA + kListCap;
-    int* LK = reinterpret_cast<int*>(LA2 + kListCap);
-    float* LR = reinterpret_cast<float*>(LK + kListCap);
-    float* LR2 = LR + kListCap;
-    uint32_t* LDB = reinterpret_cast<uint32_t*>(LR2 + kListCap);
-    for (int k = lane; k < warp_bytes / 4; k += 32)
-        reinterpret_cast<uint32_t*>(bl)[k] = 0u;
+    uint8_t* bl = wbase;
+    uint32_t* CW = reinterpret_cast<uint32_t*>(wbase + 256);
+    int* CP = reinterpret_cast<int*>(CW + 8);
+    int* h = reinterpret_cast<int*>(CW + 16);
+    for (int k = lane; k < warp_bytes / 4; k += 32) reinterpret_cast<uint32_t*>(wbase)[k] = 0u;
     __syncwarp();
     const int total = B.counters[1];
     const int nwarps = gridDim.x * (blockDim.x >> 5);
@@ -519,199 +696,88 @@ __global__ void __launch_bounds__(256) k_hist_small(Data D, Batch B, int cur, in
         const int node = B.srch[(size_t)t * B.M + (si - B.srch_off[t])];
         const size_t m = (size_t)t * B.M + node;
         const int c = B.nd_cnt[m];
-        if (c > small_node_limit(nc)) continue;  // k_hist
+        if (c > kSmallNode) continue;  // k_hist_warp
         if (lane == 0 && B.hist_bytes)
-            atomicAdd(B.hist_bytes, (unsigned long long)c * (unsigned long long)(B.mtry + (regr ? 4 : 1)));
+            atomicAdd(B.hist_bytes, (unsigned long long)c * (unsigned long long)(B.mtry + 1));
         const int* seg = B.seg[cur] + (size_t)t * D.N + B.nd_start[m];
         const uint16_t* featp = B.feat + (size_t)t * B.M * B.mtry + (size_t)node * B.mtry;
-        // each lane keeps its rows' address and target in registers; the bins are read
-        // straight from the packed rows (L1-resident after the first draw)
         const uint8_t* rowp[kSmallRows];
-        float v[kSmallRows], v2[kSmallRows];
         int lab[kSmallRows];
 #pragma unroll
         for (int hh = 0; hh < kSmallRows; ++hh) {
             const int i = hh * 32 + lane;
             rowp[hh] = D.rows;
-            v[hh] = v2[hh] = 0.0f;
             lab[hh] = 0;
             if (i < c) {
                 rowp[hh] = D.rows + (size_t)seg[i] * rs;
-                const uint2 tg = __ldg(reinterpret_cast<const uint2*>(rowp[hh] + ro));
-                v[hh] = __uint_as_float(tg.x);
-                v2[hh] = __uint_as_float(tg.y);
-                lab[hh] = (int)tg.x;
+                lab[hh] = __ldg(reinterpret_cast<const int*>(rowp[hh] + ro));
             }
         }
         unsigned long long best = kNoKey;
-        if (!regr) {
-            // classification: the draw's bins as a 256-bit set (words in the unused sums
-            // area), class counts per ranked bin with integer atomics, then per-class warp
-            // scans (exact in any order) and the criterion of scan_bins
-            uint32_t* CW = reinterpret_cast<uint32_t*>(sy);
-            int* CP = reinterpret_cast<int*>(sy) + 8;
-            for (int mv = 0; mv < B.mtry; ++mv) {
-                const int f = featp[mv];
-                int bb[kSmallRows];
-                uint32_t qmask[8];
+        for (int mv = 0; mv < B.mtry; ++mv) {
+            const int f = featp[mv];
+            int bb[kSmallRows];
+            uint32_t qmask[8];
 #pragma unroll
-                for (int q = 0; q < 8; ++q) qmask[q] = 0u;
+            for (int q = 0; q < 8; ++q) qmask[q] = 0u;
 #pragma unroll
-                for (int hh = 0; hh < kSmallRows; ++hh) {
-                    bb[hh] = -1;
-                    if (hh * 32 < c) {
-                        const int i = hh * 32 + lane;
-                        if (i < c) bb[hh] = (int)__ldg(rowp[hh] + f);
+            for (int hh = 0; hh < kSmallRows; ++hh) {
+                bb[hh] = -1;
+                if (hh * 32 < c) {
+                    const int i = hh * 32 + lane;
+                    if (i < c) bb[hh] = (int)__ldg(rowp[hh] + f);
 #pragma unroll
-                        for (int q = 0; q < 8; ++q)
-                            qmask[q] |= (bb[hh] >> 5) == q ? 1u << (bb[hh] & 31) : 0u;
-                    }
+                    for (int q = 0; q < 8; ++q)
+                        qmask[q] |= (bb[hh] >> 5) == q ? 1u << (bb[hh] & 31) : 0u;
                 }
-                int nm = 0;
-                uint32_t myw = 0u;
-                int myp = 0;
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    const uint32_t wq = __reduce_or_sync(kFull, qmask[q]);
-                    if (lane == q) {
-                        myw = wq;
-                        myp = nm;
-                    }
-                    nm += __popc(wq);
-                }
-                if (lane < 8) {
-                    CW[lane] = myw;
-                    CP[lane] = myp;
-                }
-                for (int e = lane; e < nm * nc; e += 32) h[e] = 0;
-                __syncwarp();
-#pragma unroll
-                for (int hh = 0; hh < kSmallRows; ++hh) {
-                    if (hh * 32 < c && bb[hh] >= 0) {
-                        const int b = bb[hh], q = b >> 5;
-                        const int e = CP[q] + __popc(CW[q] & ((1u << (b & 31)) - 1u));
-                        atomicAdd(&h[e * nc + lab[hh]], 1);
-                        bl[e] = (uint8_t)b;
-                    }
-                }
-                __syncwarp();
-                for (int k = 0; k < nc; ++k) {
-                    int carry = 0;
-                    for (int s0 = 0; s0 < nm; s0 += 32) {
-                        const int j = s0 + lane;
-                        int x = j < nm ? h[j * nc + k] : 0;
-#pragma unroll
-                        for (int o = 1; o < 32; o <<= 1) {
-                            const int y = __shfl_up_sync(kFull, x, o);
-                            if (lane >= o) x += y;
-                        }
-                        __syncwarp();
-                        if (j < nm) h[j * nc + k] = carry + x;
-                        carry += __shfl_sync(kFull, x, 31);
-                        __syncwarp();
-                    }
-                    if (lane == 0) h[256 * nc + k] = carry;
-                }
-                __syncwarp();
-                float bestv = 1e20f;
-                int bestj = 0x7fffffff;
-                class_best(nc, c, nm, lane, h, bestv, bestj);
-                best = min(best, best_key(false, bestv, bestj, mv, bl));
-                __syncwarp();
             }
-        } else {
-            // regression: the draws' lists of non-empty bins fill the warp's list area (as
-            // many draws as fit, at most 32), then lane d runs draw d's chains and the
-            // whole list is scored in parallel
-            for (int mv = 0; mv < B.mtry;) {
-                int used = 0, nd = 0, my_off = 0, my_len = 0;
-                while (mv < B.mtry && nd < 32 && used + c <= kListCap) {
-                    const int f = featp[mv];
-                    // the node's bins of this draw as a 256-bit set; a row's list entry is
-                    // its bin's rank in the set
-                    int bb[kSmallRows];
-                    uint32_t qmask[8];
+            int nm = 0;
+            uint32_t myw = 0u;
+            int myp = 0;
 #pragma unroll
-                    for (int q = 0; q < 8; ++q) qmask[q] = 0u;
+            for (int q = 0; q < 8; ++q) {
+                const uint32_t wq = __reduce_or_sync(kFull, qmask[q]);
+                if (lane == q) {
+                    myw = wq;
+                    myp = nm;
+                }
+                nm += __popc(wq);
+            }
+            if (lane < 8) {
+                CW[lane] = myw;
+                CP[lane] = myp;
+            }
+            for (int e = lane; e < nm * nc; e += 32) h[e] = 0;
+            __syncwarp();
 #pragma unroll
-                    for (int hh = 0; hh < kSmallRows; ++hh) {
-                        bb[hh] = -1;
-                        if (hh * 32 < c) {
-                            const int i = hh * 32 + lane;
-                            if (i < c) bb[hh] = (int)__ldg(rowp[hh] + f);
-#pragma unroll
-                            for (int q = 0; q < 8; ++q)
-                                qmask[q] |= (bb[hh] >> 5) == q ? 1u << (bb[hh] & 31) : 0u;
-                        }
-                    }
-                    int nm = 0;
-                    uint32_t myw = 0u;
-                    int myp = 0;
-#pragma unroll
-                    for (int q = 0; q < 8; ++q) {
-                        const uint32_t wq = __reduce_or_sync(kFull, qmask[q]);
-                        if (lane == q) {
-                            myw = wq;
-                            myp = nm;
-                        }
-                        nm += __popc(wq);
-                    }
-                    if (lane < 8) {
-                        SW[lane] = myw;
-                        SP[lane] = myp;
-                    }
-                    for (int e = lane; e < nm; e += 32) {
-                        LA[used + e] = 0.0f;
-                        LA2[used + e] = 0.0f;
-                        LK[used + e] = 0;
-                    }
+            for (int hh = 0; hh < kSmallRows; ++hh) {
+                if (hh * 32 < c && bb[hh] >= 0) {
+                    const int b = bb[hh], q = b >> 5;
+                    const int e = CP[q] + __popc(CW[q] & ((1u << (b & 31)) - 1u));
+                    atomicAdd(&h[e * nc + lab[hh]], 1);
+                    bl[e] = (uint8_t)b;
+                }
+            }
+            __syncwarp();
+            for (int k = 0; k < nc; ++k) {
+                int carry = 0;
+                for (int s0 = 0; s0 < nm; s0 += 32) {
+                    const int j = s0 + lane;
+                    int x = j < nm ? h[j * nc + k] : 0;
+                    x = warp_incl_scan(x, lane);
                     __syncwarp();
-                    // per 32-row step, rows of the same bin add one rank at a time (row order)
-#pragma unroll
-                    for (int hh = 0; hh < kSmallRows; ++hh) {
-                        if (hh * 32 < c) {
-                            const int b = bb[hh];
-                            const bool valid = b >= 0;
-                            int e = 0;
-                            if (valid) {
-                                const int q = b >> 5;
-                                e = used + SP[q] + __popc(SW[q] & ((1u << (b & 31)) - 1u));
-                                LDB[e] = ((uint32_t)mv << 8) | (uint32_t)b |
-                                         (e == used + nm - 1 ? kLastEntry : 0u);
-                            }
-                            const uint32_t peers = __match_any_sync(kFull, b);
-                            const int rank = __popc(peers & ((1u << lane) - 1u));
-                            const int maxr = __reduce_max_sync(kFull, valid ? __popc(peers) - 1 : 0);
-                            for (int qq = 0; qq <= maxr; ++qq) {
-                                if (valid && rank == qq) {
-                                    LA[e] += v[hh] * 1.0f;
-                                    LA2[e] += v2[hh] * 1.0f;
-                                    LK[e] += 1;
-                                }
-                                __syncwarp();
-                            }
-                        }
-                    }
-                    if (lane == nd) {
-                        my_off = used;
-                        my_len = nm;
-                    }
-                    used += nm;
-                    ++nd;
-                    ++mv;
+                    if (j < nm) h[j * nc + k] = carry + x;
+                    carry += __shfl_sync(kFull, x, 31);
+                    __syncwarp();
                 }
-                if (lane < nd)
-                    regr_chains(LA + my_off, LA2 + my_off, LK + my_off, LR + my_off,
-                                LR2 + my_off, my_len);
-                __syncwarp();
-                for (int e = lane; e < used; e += 32) {
-                    const uint32_t db = LDB[e];
-                    if (!(db & kLastEntry))
-                        best = min(best, regr_key(LA[e], LR[e], LA2[e], LR2[e], LK[e], c, db));
-                }
-                __syncwarp();
+                if (lane == 0) h[256 * nc + k] = carry;
             }
-            best = warp_min_key(best);
+            __syncwarp();
+            float bestv = 1e20f;
+            int bestj = 0x7fffffff;
+            class_best(nc, c, nm, lane, h, bestv, bestj);
+            best = min(best, best_key(false, bestv, bestj, mv, bl));
+            __syncwarp();
         }
         if (lane == 0) B.nd_key[m] = best;
         __syncwarp();

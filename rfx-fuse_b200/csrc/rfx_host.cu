@@ -105,17 +105,21 @@ void alloc_batch(Ctx& c, int Tcap) {
     B.nxt_lo = lvl + 2 * T;
     B.nxt_hi = lvl + 3 * T;
     B.nnode = lvl + 4 * T;
-    B.lvl_off = (int*)c.b_srchoff.get((T + 1) * 12);
+    B.lvl_off = (int*)c.b_srchoff.get((T + 1) * 16);
     B.srch_off = B.lvl_off + (T + 1);
     B.srch_big_off = B.srch_off + (T + 1);
+    B.srch_sml_off = B.srch_big_off + (T + 1);
     B.srch_big = (int*)c.b_srchbig.get(T * M * 4);
+    B.srch_sml = (int*)c.b_srchsml.get(T * M * 4);
     B.part_big = (long long*)c.b_partbig.get(T * (N / rfx::kBigSegment + 2) * 8);
     B.srch = (int*)c.b_srch.get(T * M * 4);
-    B.srch_cnt = (int*)c.b_srchcnt.get(T * 8);
+    B.srch_cnt = (int*)c.b_srchcnt.get(T * 12);
     B.srch_big_cnt = B.srch_cnt + T;
-    B.counters = (int*)c.b_counters.get(64);
+    B.srch_sml_cnt = B.srch_cnt + 2 * T;
+    B.counters = (int*)c.b_counters.get(128);
     B.hist_bytes = reinterpret_cast<unsigned long long*>(B.counters + 8);
     B.prox_pairs = reinterpret_cast<unsigned long long*>(B.counters + 10);
+    B.diag = c.level_log ? reinterpret_cast<unsigned long long*>(B.counters + 12) : nullptr;
     B.oob_leaf = (int*)c.b_oobleaf.get(T * N * 4);
     B.used = (uint8_t*)c.b_used.get(T * p);
     B.right = (int*)c.b_right.get(T * 4);
@@ -323,7 +327,7 @@ void load(Ctx& c, const rfx_fit_params* prm, const rfx_inputs* in) {
     Tcap = (int)std::max<size_t>(1, std::min<size_t>((size_t)Tcap, budget / per_tree));
     Tcap = std::min(Tcap, 4096);
     alloc_batch(c, Tcap);
-    RFX_CUDA(cudaMemsetAsync(c.B.counters, 0, 64, st));
+    RFX_CUDA(cudaMemsetAsync(c.B.counters, 0, 128, st));
     RFX_CUDA(cudaStreamSynchronize(st));
     c.loaded = true;
 }
@@ -332,46 +336,54 @@ void load(Ctx& c, const rfx_fit_params* prm, const rfx_inputs* in) {
 struct HistCfg {
     rfx::HistArgs a;
     int threads, smem, grid;
-    int small_warp_bytes, small_smem, small_grid;
+    int small_warp_bytes, small_smem, small_grid;  // k_hist_small (classification)
+    int lane_slots, lane_grid, lane_bytes;         // k_hist_lane (regression)
 };
 
 HistCfg hist_cfg(Ctx& c) {
     HistCfg h;
-    const int pieces = c.D.rs / 16;
-    // per-warp histogram scratch; regression adds the right-sum arrays (k_hist) or the bin
-    // list area (k_hist_small, 24 bytes per entry)
     const bool regr = c.nclass == 1;
-    // (k_hist: +4 bytes so that the warps' lists start in different shared-memory banks when
-    // lanes of one warp read them side by side)
-    const int scratch = (int)round_up(rfx::kHistScratch + (regr ? 2 * 1024 : (257 * c.nclass + 32) * 4), 16) + 4;
-    const int small_scratch = regr ? 64 + 24 * rfx::kListCap : scratch;  // bin set + list area
-    // one block per node covers up to 16 draws (rows staged once per node) when the warps'
-    // histograms fit in 96 KB; otherwise (many classes) groups of 8 draws
-    const int all = std::max(1, std::min(16, c.prm.mtry));
-    h.a.warps = (regr || all * scratch <= 96 * 1024) ? all : 8;
-    h.a.groups = (c.prm.mtry + h.a.warps - 1) / h.a.warps;
-    // rows per staged chunk: a multiple of 32 with at most 2 load units per thread, small
-    // enough for 32 resident warps per SM where the row width allows
-    const int per_sm_target = std::max(1, 32 / h.a.warps);
-    const int budget = (228 * 1024) / per_sm_target - 1024;
-    const int fixed = h.a.warps * (int)scratch + 4 * c.D.rs;
-    const int fit = (budget - fixed) / (c.D.rs + 8);
-    h.a.stage_rows = std::max(32, std::min({256, (2 * 32 * h.a.warps * 4 / pieces) / 32 * 32, fit / 32 * 32}));
-    h.a.cstride = h.a.stage_rows + 4;
-    h.a.warp_bytes = scratch;
+    const int mtry = c.prm.mtry;
+    // k_hist_warp: per-warp histogram (regression: bin sums + counts; classification: class
+    // counts, class-major) + counts, bin list, candidate flags, class totals
+    const int wb = regr ? 2048 + 1024 + 512 + 1024 : 1024 * c.nclass + 1024 + 512 + 128;
+    h.a.warp_bytes = (int)round_up(wb, 16);
+    const int fit = std::max(1, (200 * 1024) / h.a.warp_bytes);
+    h.a.warps = std::max(1, std::min({16, mtry, fit}));
+    h.a.groups = (mtry + h.a.warps - 1) / h.a.warps;
     h.threads = 32 * h.a.warps;
-    h.smem = c.D.rs * h.a.cstride + h.a.stage_rows * 8 + h.a.warps * h.a.warp_bytes;
-    RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  std::max(h.smem, 48 * 1024)));
+    h.smem = h.a.warps * h.a.warp_bytes;
     int per_sm = 0;
-    RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist, h.threads, h.smem));
+    if (regr) {
+        RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist_warp_regr, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      std::max(h.smem, 48 * 1024)));
+        RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist_warp_regr, h.threads, h.smem));
+    } else {
+        RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist_warp_class, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      std::max(h.smem, 48 * 1024)));
+        RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist_warp_class, h.threads, h.smem));
+    }
     h.grid = c.sm_count * std::max(1, per_sm);
-    h.small_warp_bytes = small_scratch;
+    // k_hist_small (classification): bin list, set words, class prefixes + totals
+    h.small_warp_bytes = (int)round_up(256 + 64 + (257 * c.nclass) * 4, 16);
     h.small_smem = 8 * h.small_warp_bytes;
-    RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  std::max(h.small_smem, 48 * 1024)));
-    RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist_small, 256, h.small_smem));
-    h.small_grid = c.sm_count * std::max(1, per_sm);
+    h.small_grid = 0;
+    h.lane_slots = 0;
+    h.lane_grid = 0;
+    h.lane_bytes = 0;
+    if (!regr) {
+        RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist_small, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      std::max(h.small_smem, 48 * 1024)));
+        RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist_small, 256, h.small_smem));
+        h.small_grid = c.sm_count * std::max(1, per_sm);
+    } else if (mtry <= 32) {
+        h.lane_slots = std::min(rfx::kLaneSlots, 32 / mtry);
+        h.lane_bytes = rfx::lane_bytes(h.lane_slots);
+        RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist_lane, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      h.lane_bytes));
+        RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist_lane, 32, h.lane_bytes));
+        h.lane_grid = c.sm_count * std::max(1, per_sm);
+    }
     return h;
 }
 
@@ -494,14 +506,20 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
         rfx::k_draw<<<T, 256, 0, st>>>(D, B);
         rfx::k_srch_scan<<<1, 1024, 0, st>>>(B);
         if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev0, st));
-        rfx::k_hist<<<hc.grid, hc.threads, hc.smem, st>>>(D, B, cur, hc.a);
-        rfx::k_hist_small<<<hc.small_grid, 256, hc.small_smem, st>>>(D, B, cur, hc.small_warp_bytes);
+        if (c.nclass == 1) {
+            rfx::k_hist_warp_regr<<<hc.grid, hc.threads, hc.smem, st>>>(D, B, cur, hc.a);
+            if (hc.lane_grid > 0)
+                rfx::k_hist_lane<<<hc.lane_grid, 32, hc.lane_bytes, st>>>(D, B, cur, hc.lane_slots);
+        } else {
+            rfx::k_hist_warp_class<<<hc.grid, hc.threads, hc.smem, st>>>(D, B, cur, hc.a);
+            rfx::k_hist_small<<<hc.small_grid, 256, hc.small_smem, st>>>(D, B, cur, hc.small_warp_bytes);
+        }
         if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev1, st));
         rfx::k_commit<<<T, 1024, 0, st>>>(D, B);
         rfx::k_partition<<<gw, 256, 0, st>>>(D, B, cur);
         rfx::k_partition_big<<<c.sm_count * 2, 256, 0, st>>>(D, B, cur);
         RFX_LAUNCH("level kernels");
-        RFX_CUDA(cudaMemcpyAsync(c.h_counters, B.counters, 16, cudaMemcpyDeviceToHost, st));
+        RFX_CUDA(cudaMemcpyAsync(c.h_counters, B.counters, c.level_log ? 80 : 16, cudaMemcpyDeviceToHost, st));
         RFX_CUDA(cudaStreamSynchronize(st));
         c.launches += 9;
         c.levels += 1;
@@ -511,8 +529,11 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
             c.hist_ms += ms;
             c.hist_launches += 1;
             if (c.level_log)
-                std::fprintf(stderr, "[rfx] tree0=%d level=%d nodes=%d searched=%d next=%d hist_ms=%.3f\n",
-                             tree0, level, c.h_counters[0], c.h_counters[1], c.h_counters[2], ms);
+                std::fprintf(stderr, "[rfx] tree0=%d level=%d nodes=%d searched=%d big=%d small=%d next=%d hist_ms=%.3f exact=%llu rounds=%llu steps=%llu\n",
+                             tree0, level, c.h_counters[0], c.h_counters[1], c.h_counters[4], c.h_counters[6], c.h_counters[2], ms,
+                             *reinterpret_cast<unsigned long long*>(c.h_counters + 12),
+                             *reinterpret_cast<unsigned long long*>(c.h_counters + 14),
+                             *reinterpret_cast<unsigned long long*>(c.h_counters + 16));
         }
         if (c.h_counters[2] == 0) break;
         cur ^= 1;
@@ -644,7 +665,7 @@ void* rfx_create(int device) {
         RFX_CUDA(cudaSetDevice(device));
         RFX_CUDA(cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device));
         RFX_CUDA(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking));
-        RFX_CUDA(cudaMallocHost(&c->h_counters, 64));
+        RFX_CUDA(cudaMallocHost(&c->h_counters, 128));
     });
     if (rc != RFX_OK) {
         delete c;

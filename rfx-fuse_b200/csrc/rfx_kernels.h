@@ -26,7 +26,9 @@ __global__ void k_partition(Data D, Batch B, int cur);
 __global__ void k_partition_big(Data D, Batch B, int cur);
 
 // rfx_hist.cu
-__global__ void k_hist(Data D, Batch B, int cur, HistArgs a);
+__global__ void k_hist_warp_regr(Data D, Batch B, int cur, HistArgs a);
+__global__ void k_hist_warp_class(Data D, Batch B, int cur, HistArgs a);
+__global__ void k_hist_lane(Data D, Batch B, int cur, int slots);
 __global__ void k_hist_small(Data D, Batch B, int cur, int warp_bytes);
 
 // rfx_post.cu
