@@ -108,6 +108,7 @@ struct Ctx {
     bool profiling = false;
     bool level_log = std::getenv("RFX_LEVEL_LOG") != nullptr;  // per-level trace on stderr
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    std::vector<cudaEvent_t> ev_hist;  // per-level histogram timing within a level group
     long long launches = 0, hist_launches = 0, levels = 0, trees = 0;
     double hist_ms = 0.0;
     double prox_ms = 0.0;
@@ -179,6 +180,7 @@ struct Ctx {
         for (int b = 0; b < 2; ++b) {
             if (ev_stage[b]) cudaEventDestroy(ev_stage[b]);
         }
+        for (cudaEvent_t e : ev_hist) cudaEventDestroy(e);
         if (ev0) cudaEventDestroy(ev0);
         if (ev1) cudaEventDestroy(ev1);
         if (st) cudaStreamDestroy(st);

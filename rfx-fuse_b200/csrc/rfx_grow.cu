@@ -45,7 +45,7 @@ __device__ __forceinline__ int block_excl_scan(int v, int* wsum, int& total) {
 }
 
 // Level ranges of every tree, their prefix (flattened task index -> tree) and total width.
-__global__ void __launch_bounds__(1024) k_level_begin(Batch B) {
+__global__ void __launch_bounds__(1024) k_level_begin(Batch B, int level) {
     __shared__ int ws[32];
     int carry = 0;
     for (int t0 = 0; t0 < B.T; t0 += blockDim.x) {
@@ -65,6 +65,7 @@ __global__ void __launch_bounds__(1024) k_level_begin(Batch B) {
     if (threadIdx.x == 0) {
         B.lvl_off[B.T] = carry;
         B.counters[0] = carry;
+        if (carry > 0) B.counters[7] = level + 1;  // levels that had nodes
         B.counters[2] = 0;
         B.counters[5] = 0;
     }

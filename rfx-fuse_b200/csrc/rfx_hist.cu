@@ -522,21 +522,37 @@ __global__ void __launch_bounds__(32) k_hist_lane(Data D, Batch B, int cur, int 
             my_start = B.nd_start[mm];
         }
         if (lane < slots) UM[lane] = 0u;
-        // ---- stage: lanes take rows, every drawn feature's bin and the target
-        for (int s = 0; s < slots; ++s) {
+        // ---- stage: lanes take rows, every drawn feature's bin and the target (row ids of
+        // all slots first, so that their loads are in flight together)
+        int rid[2 * kLaneSlots];
+#pragma unroll
+        for (int s = 0; s < kLaneSlots; ++s) {
+            rid[2 * s] = rid[2 * s + 1] = -1;
+            if (s < slots) {
+                const int c = __shfl_sync(kFull, my_c, s);
+                const int t = __shfl_sync(kFull, my_t, s);
+                const int start = __shfl_sync(kFull, my_start, s);
+                const int* seg = B.seg[cur] + (size_t)t * D.N + start;
+                if (lane < c) rid[2 * s] = __ldg(seg + lane);
+                if (lane + 32 < c) rid[2 * s + 1] = __ldg(seg + lane + 32);
+            }
+        }
+#pragma unroll
+        for (int s = 0; s < kLaneSlots; ++s) {
+            if (s >= slots) break;
             const int c = __shfl_sync(kFull, my_c, s);
             if (c == 0) continue;
             const int t = __shfl_sync(kFull, my_t, s), node = __shfl_sync(kFull, my_node, s);
-            const int start = __shfl_sync(kFull, my_start, s);
-            const int* seg = B.seg[cur] + (size_t)t * D.N + start;
             const uint16_t* featp = B.feat + (size_t)t * B.M * mtry + (size_t)node * mtry;
             const int fl = lane < mtry ? (int)featp[lane] : 0;
             if (lane == 0 && B.hist_bytes)
                 atomicAdd(B.hist_bytes, (unsigned long long)c * (unsigned long long)(mtry + 4));
-            for (int i0 = 0; i0 < c; i0 += 32) {
-                const int i = i0 + lane;
-                const bool ok = i < c;
-                const uint8_t* row = D.rows + (ok ? (size_t)__ldg(seg + i) * rs : 0);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                if (h * 32 >= c) break;
+                const int i = h * 32 + lane;
+                const bool ok = rid[2 * s + h] >= 0;
+                const uint8_t* row = D.rows + (ok ? (size_t)rid[2 * s + h] * rs : 0);
                 if (ok) TG[s * kSmallNode + i] = __ldg(reinterpret_cast<const float2*>(row + ro));
                 uint8_t* dst = TL + (s * mtry) * kLaneTile + i;
                 for (int dd = 0; dd < mtry; ++dd) {

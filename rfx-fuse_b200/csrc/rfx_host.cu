@@ -453,6 +453,8 @@ void copy_d2h(Ctx& c, void* dst, const void* src, size_t bytes) {
     }
 }
 
+constexpr int kLevelGroup = 8;  // tree levels enqueued per host synchronisation
+
 void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
     cudaStream_t st = c.st;
     rfx::Batch B = c.B;
@@ -498,45 +500,62 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
     c.trees += T;
     const HistCfg hc = hist_cfg(c);
     const int gw = c.sm_count * 8;
-    int cur = 0;
-    for (int level = 0;; ++level) {
+    // Levels are enqueued kLevelGroup at a time with one host synchronisation per group: a
+    // level after the last one has no nodes, so its kernels find no work (the ping-pong
+    // segment buffers are not touched) and k_level_begin records the number of levels that
+    // had nodes (counters[7]).  RFX_LEVEL_LOG synchronises every level for its trace.
+    const int group = c.level_log ? 1 : kLevelGroup;
+    if (c.profiling && c.ev_hist.empty()) {
+        c.ev_hist.resize(2 * kLevelGroup);
+        for (auto& e : c.ev_hist) RFX_CUDA(cudaEventCreate(&e));
+    }
+    int level = 0;
+    for (;;) {
         require(level < 1000000, RFX_ERR_DEVICE, "tree growth did not terminate");
-        rfx::k_level_begin<<<1, 1024, 0, st>>>(B);
-        rfx::k_node_eval<<<gw, 256, 0, st>>>(D, B, cur);
-        rfx::k_draw<<<T, 256, 0, st>>>(D, B);
-        rfx::k_srch_scan<<<1, 1024, 0, st>>>(B);
-        if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev0, st));
-        if (c.nclass == 1) {
-            rfx::k_hist_warp_regr<<<hc.grid, hc.threads, hc.smem, st>>>(D, B, cur, hc.a);
-            if (hc.lane_grid > 0)
-                rfx::k_hist_lane<<<hc.lane_grid, 32, hc.lane_bytes, st>>>(D, B, cur, hc.lane_slots);
-        } else {
-            rfx::k_hist_warp_class<<<hc.grid, hc.threads, hc.smem, st>>>(D, B, cur, hc.a);
-            rfx::k_hist_small<<<hc.small_grid, 256, hc.small_smem, st>>>(D, B, cur, hc.small_warp_bytes);
+        const int lv0 = level;
+        for (int k = 0; k < group; ++k, ++level) {
+            const int cl = level & 1;
+            rfx::k_level_begin<<<1, 1024, 0, st>>>(B, level);
+            rfx::k_node_eval<<<gw, 256, 0, st>>>(D, B, cl);
+            rfx::k_draw<<<T, 256, 0, st>>>(D, B);
+            rfx::k_srch_scan<<<1, 1024, 0, st>>>(B);
+            if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev_hist[2 * k], st));
+            if (c.nclass == 1) {
+                rfx::k_hist_warp_regr<<<hc.grid, hc.threads, hc.smem, st>>>(D, B, cl, hc.a);
+                if (hc.lane_grid > 0)
+                    rfx::k_hist_lane<<<hc.lane_grid, 32, hc.lane_bytes, st>>>(D, B, cl, hc.lane_slots);
+            } else {
+                rfx::k_hist_warp_class<<<hc.grid, hc.threads, hc.smem, st>>>(D, B, cl, hc.a);
+                rfx::k_hist_small<<<hc.small_grid, 256, hc.small_smem, st>>>(D, B, cl, hc.small_warp_bytes);
+            }
+            if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev_hist[2 * k + 1], st));
+            rfx::k_commit<<<T, 1024, 0, st>>>(D, B);
+            rfx::k_partition<<<gw, 256, 0, st>>>(D, B, cl);
+            rfx::k_partition_big<<<c.sm_count * 2, 256, 0, st>>>(D, B, cl);
+            RFX_LAUNCH("level kernels");
+            c.launches += 9;
         }
-        if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev1, st));
-        rfx::k_commit<<<T, 1024, 0, st>>>(D, B);
-        rfx::k_partition<<<gw, 256, 0, st>>>(D, B, cur);
-        rfx::k_partition_big<<<c.sm_count * 2, 256, 0, st>>>(D, B, cur);
-        RFX_LAUNCH("level kernels");
-        RFX_CUDA(cudaMemcpyAsync(c.h_counters, B.counters, c.level_log ? 80 : 16, cudaMemcpyDeviceToHost, st));
+        RFX_CUDA(cudaMemcpyAsync(c.h_counters, B.counters, c.level_log ? 80 : 32, cudaMemcpyDeviceToHost, st));
         RFX_CUDA(cudaStreamSynchronize(st));
-        c.launches += 9;
-        c.levels += 1;
+        const int real = std::min(level, c.h_counters[7]);  // levels so far that had nodes
         if (c.profiling) {
-            float ms = 0.0f;
-            RFX_CUDA(cudaEventElapsedTime(&ms, c.ev0, c.ev1));
-            c.hist_ms += ms;
-            c.hist_launches += 1;
-            if (c.level_log)
-                std::fprintf(stderr, "[rfx] tree0=%d level=%d nodes=%d searched=%d big=%d small=%d next=%d hist_ms=%.3f exact=%llu rounds=%llu steps=%llu\n",
-                             tree0, level, c.h_counters[0], c.h_counters[1], c.h_counters[4], c.h_counters[6], c.h_counters[2], ms,
-                             *reinterpret_cast<unsigned long long*>(c.h_counters + 12),
-                             *reinterpret_cast<unsigned long long*>(c.h_counters + 14),
-                             *reinterpret_cast<unsigned long long*>(c.h_counters + 16));
+            for (int k = 0; k < real - lv0; ++k) {
+                float ms = 0.0f;
+                RFX_CUDA(cudaEventElapsedTime(&ms, c.ev_hist[2 * k], c.ev_hist[2 * k + 1]));
+                c.hist_ms += ms;
+                c.hist_launches += 1;
+                if (c.level_log)
+                    std::fprintf(stderr, "[rfx] tree0=%d level=%d nodes=%d searched=%d big=%d small=%d next=%d hist_ms=%.3f exact=%llu rounds=%llu steps=%llu\n",
+                                 tree0, lv0 + k, c.h_counters[0], c.h_counters[1], c.h_counters[4], c.h_counters[6], c.h_counters[2], ms,
+                                 *reinterpret_cast<unsigned long long*>(c.h_counters + 12),
+                                 *reinterpret_cast<unsigned long long*>(c.h_counters + 14),
+                                 *reinterpret_cast<unsigned long long*>(c.h_counters + 16));
+            }
         }
-        if (c.h_counters[2] == 0) break;
-        cur ^= 1;
+        if (c.h_counters[2] == 0) {
+            c.levels += real;
+            break;
+        }
     }
     const dim3 rg((unsigned)((N + 255) / 256), (unsigned)T);
     rfx::k_oob_drop<<<rg, 256, 0, st>>>(D, B);

@@ -17,7 +17,7 @@ __global__ void k_bootstrap(Data D, Batch B);
 __global__ void k_compact(Data D, Batch B);
 
 // rfx_grow.cu
-__global__ void k_level_begin(Batch B);
+__global__ void k_level_begin(Batch B, int level);
 __global__ void k_node_eval(Data D, Batch B, int cur);
 __global__ void k_draw(Data D, Batch B);
 __global__ void k_srch_scan(Batch B);
