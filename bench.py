@@ -7,16 +7,25 @@ Workload: regression, n=200,000 rows x p=50 float32 f
 importance, no proximity; maxnode = calculate_maxnode(n, 5) = 32001 (nsample=n passed).
 Synthetic data, seeded (numpy default_rng(20261201 + 1)).
 
-A step grows `--step-trees` trees of that forest (bootstrap, level-wise growth, OOB drop,
-OOB prediction fold, permutation importance).  Metric: fit trees/s for the whole job.
+A step fits config[1]'s whole 500-tree forest on the device-resident dataset: the trees are
+split over the N GPUs (rank r grows the id block [r*500/N, (r+1)*500/N), strong scaling),
+then the forest-level results are combined across the ranks inside the timed region (OOB
+counts all-reduced, the OOB prediction sums folded in tree order rank by rank, importance
+rows gathered and summed in tree order).  Metric: fit trees/s for the whole job.
 
-  value  device-resident: dataset loaded and binned in HBM before timing; each step is one
-         rfx_grow call; CUDA events on the library's stream; max over ranks.
-  e2e    the public API call a user makes, RandomForestRegressor(ntree=step_trees).fit(X, y),
-         from pinned host X/y to host tree arrays and OOB results, every step.
+  value  device-resident: dataset loaded and binned in HBM before timing; CUDA events on the
+         library's stream; max over ranks.  "checksum" hashes the combined arrays, so runs
+         at different N can be compared (they are bit-identical).
+  e2e    the public API a user calls: RandomForestRegressor(ntree=500).fit(X, y) (N > 1:
+         rfx_b200.shard.fit_sharded) from pinned host X/y, including the upload and binning,
+         the tree arrays' download and the combine, every step.
+  proximity  the proximity half of the metric, from a config[0] forest (100 trees, OOB x
+         in-bag counts + finishprox) in the same invocation (rank 0).
 
 --impl reference times the reference's own CPU implementation (oracle/_ref, compiled from
-the reference sources; else the CPU port) on the same workload with all host threads.
+the reference sources; else the CPU port) on the same workload with all host threads: each
+step is one fit of --ref-step-trees trees, and the per-tree rate excludes the one-time
+prepare_data (measured by a 1-tree fit and reported separately).
 
 Other workloads (--workload; each prints its own line, the default is config1):
   config0  classification n=10000 p=20, 100 trees, mtry 4, nodesize 1, OOB x in-bag proximity
@@ -118,18 +127,6 @@ def measured_peaks():
         return 6650.0, "fallback"
 
 
-def profile_traffic():
-    """Per-launch DRAM traffic of the histogram kernels from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "k_hist_config1.md")
-    try:
-        for line in open(path):
-            if line.startswith("traffic_bytes_per_level_full:"):
-                return float(line.split(":", 1)[1].strip())
-    except OSError:
-        pass
-    return None
-
-
 class Quiet:
     """Silence C-level stdout (the reference prints banners) while keeping our JSON clean."""
 
@@ -169,31 +166,54 @@ def cpu_reference_fit(X, y, ntree):
     return time.perf_counter() - t, "port", 1
 
 
+def cpu_tree_rate(X, y, k, fits=1):
+    """Per-tree rate of the reference CPU fit excluding its one-time prepare_data: a 1-tree fit
+    gives prepare + one tree, each k-tree fit adds k - 1 trees.  Returns (trees/s, prepare_s,
+    kind, cores, [seconds of the k-tree fits], one-tree seconds)."""
+    t1, kind, cores = cpu_reference_fit(X, y, 1)
+    tk = []
+    for _ in range(fits):
+        dt, kind, cores = cpu_reference_fit(X, y, k)
+        tk.append(dt)
+    per_tree = (sum(tk) / len(tk) - t1) / (k - 1)
+    rate = fits * (k - 1) / (sum(tk) - fits * t1)
+    return rate, t1 - per_tree, kind, cores, tk, t1
+
+
+def arm_config(trees):
+    """The config both arms print (identical, so the two lines compare)."""
+    return {"workload": WORKLOAD, "forest_trees": trees}
+
+
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
     X, y = make_data(CFG["n"], CFG["p"])
-    k = args.ref_step_trees
+    k = max(2, args.ref_step_trees)
+    t1, kind, cores = cpu_reference_fit(X, y, 1)  # prepare_data + one tree
     for _ in range(args.warmup):
         cpu_reference_fit(X, y, k)
     times = []
-    kind = cores = None
     for _ in range(args.steps):
         dt, kind, cores = cpu_reference_fit(X, y, k)
         times.append(dt)
-    total = sum(times)
-    value = args.steps * k / total
+    value = args.steps * (k - 1) / (sum(times) - args.steps * t1)
+    prepare = t1 - (sum(times) / len(times) - t1) / (k - 1)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "trees/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": 1000 * total / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
-        "config": {"workload": WORKLOAD, "step_trees": k},
+        "ms_per_step": 1000.0 * CFG["ntree"] / value, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": arm_config(CFG["ntree"]),
         "cpu_baseline": {"value": value, "unit": "trees/s", "cores": cores, "kind": kind,
-                         "sample": f"{args.steps} fits of {k} trees each on the full config[1] data "
-                                   "(each fit includes the reference's one-time prepare_data)"},
+                         "sample": f"{args.steps} fits of {k} trees on the full config[1] data; "
+                                   f"per-tree rate = (k - 1) trees / (t_k - t_1) with t_1 a 1-tree "
+                                   f"fit ({t1:.2f} s), so the one-time prepare_data "
+                                   f"({prepare:.2f} s) is excluded",
+                         "prepare_data_s": prepare, "fit_s": times},
         "e2e": {"value": value, "unit": "trees/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "details": {"ms_per_step_is": "time of the 500-tree forest at the measured per-tree rate"},
     }
     print(json.dumps(line), flush=True)
     return 0
@@ -207,85 +227,110 @@ def run_rfx(args):
 
 
 def run_config1(args):
+    import hashlib
+
     import torch
 
     import rfx_b200
     from rfx_b200 import _abi as A
+    from rfx_b200.shard import combine, fit_sharded, tree_block
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
     if world > 1:
         import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        dist.init_process_group("nccl", device_id=dev)
     n, p = CFG["n"], CFG["p"]
     X, y = make_data(n, p)
     M = calc_maxnode(n, CFG["minndsize"])
-    S = args.step_trees
+    T = args.forest_trees
+    t0, t1 = tree_block(T, rank, world)
+    k = t1 - t0
     ctx = rfx_b200.Context(local)
     prm = A.FitParams(A.TASK_REGRESSION, n, p, CFG["mtry"], CFG["minndsize"], M, 12345, 12345,
-                      CFG["nbins"], 10, 1, 0, 0, args.batch_trees, 0)
+                      CFG["nbins"], 10, 1, 0, 0, args.batch_trees, 1)
     inp = A.Inputs(A.ptr(X, A._pf), None, A.ptr(y, A._pf), None, None, None)
     ctx.load(prm, inp)
-    stream = torch.cuda.ExternalStream(ctx.stream(), device=torch.device("cuda", local))
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")
-    # weak scaling: every rank grows its own trees, with distinct tree ids
-    next_tree = rank * 1_000_000
-    for _ in range(args.warmup):
-        ctx.grow(next_tree, S)
-        next_tree += S
-    ctx.reset_stats()
-    ctx.set_profiling(True)
-    clocks = Clocks(local)
-    if world > 1:
-        torch.distributed.barrier()
-    torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        ev0.record(stream)
+    lib = torch.cuda.ExternalStream(ctx.stream(), device=dev)
+    rr = np.zeros((k, p), np.float32)
+    used = np.zeros((k, p), np.uint8)
+    trees = A.Trees(None, None, None, None, None, None, None, None, None, None,
+                    A.ptr(rr, A._pf), A.ptr(used, A._pu8))
+    with torch.cuda.stream(lib):
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+        def step():
+            ctx.reset_forest()
+            ctx.grow(t0, k, trees)
+            acc, _ = combine(ctx, A.TASK_REGRESSION, n, p, 1, rr, used, dist, T, None, dev)
+            return acc
+
+        for _ in range(args.warmup):
+            step()
+        ctx.reset_stats()
+        ctx.set_profiling(True)
+        clocks = Clocks(local)
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(lib)
         for _ in range(args.steps):
             flush.zero_()  # L2 flush between steps (256 MiB > 126 MB L2)
-            ctx.grow(next_tree, S)
-            next_tree += S
-        ev1.record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        torch.distributed.barrier()
+            acc = step()
+        ev1.record(lib)
+        torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
     ck = clocks.stop()
     ms = ev0.elapsed_time(ev1)
     st = ctx.stats()
     ctx.set_profiling(False)
-    if world > 1:
-        t = torch.tensor([ms], device=f"cuda:{local}", dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    value = world * args.steps * S / (ms / 1000.0)
+    value = args.steps * T / (ms / 1000.0)
+    h = hashlib.sha1()
+    for key in ("nout", "oob_sum", "avimp", "sqsd"):
+        h.update(np.ascontiguousarray(acc[key]).tobytes())
+    checksum = h.hexdigest()[:16]
 
     # ---- e2e: the public estimator API with pinned host buffers
     Xp = torch.empty((n, p), dtype=torch.float32, pin_memory=True).numpy()
     yp = torch.empty((n,), dtype=torch.float32, pin_memory=True).numpy()
     Xp[:] = X
     yp[:] = y
-    est = rfx_b200.RandomForestRegressor(nsample=n, ntree=S, mtry=CFG["mtry"],
-                                         minndsize=CFG["minndsize"], compute_importance=True,
-                                         device=local, batch_trees=args.batch_trees)
-    est.fit(Xp, yp)  # warm-up
+
+    def e2e_fit():
+        est = rfx_b200.RandomForestRegressor(nsample=n, ntree=T, mtry=CFG["mtry"],
+                                             minndsize=CFG["minndsize"], compute_importance=True,
+                                             device=local, batch_trees=args.batch_trees)
+        if dist is not None:
+            fit_sharded(est, Xp, yp, dist, local)
+        else:
+            est.fit(Xp, yp)
+        return est.get_oob_error()
+
+    e2e_fit()  # warm-up
     e2e_steps = max(1, args.e2e_steps)
-    if world > 1:
-        torch.distributed.barrier()
+    if dist is not None:
+        dist.barrier()
     torch.cuda.synchronize()
-    t0 = time.perf_counter()
+    ts = time.perf_counter()
     for _ in range(e2e_steps):
-        est.fit(Xp, yp)
-        _ = est.get_oob_error()
+        e2e_fit()
     torch.cuda.synchronize()
-    e2e_s = time.perf_counter() - t0
-    if world > 1:
-        t = torch.tensor([e2e_s], device=f"cuda:{local}", dtype=torch.float64)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    e2e_s = time.perf_counter() - ts
+    if dist is not None:
+        t = torch.tensor([e2e_s], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e_value = world * e2e_steps * S / e2e_s
-    h2d = Xp.nbytes + yp.nbytes + 4 * p
-    d2h = S * M * 4 * 9 + S * 4 + S * p * 5 + n * 4 * 2 + p * 8
+    e2e_value = e2e_steps * T / e2e_s
+    h2d = world * (Xp.nbytes + yp.nbytes + 4 * p)
+    d2h = T * M * 4 * 9 + T * 4 + T * p * 5 + n * 4 * 2 + p * 8
 
     peak, peak_kind = measured_peaks()
     hist_s = st["hist_ms"] / 1000.0
@@ -294,36 +339,49 @@ def run_config1(args):
     line = {
         "metric": METRIC, "value": value, "unit": "trees/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded numpy, config[1] shapes and distributions)",
-        "config": {"workload": WORKLOAD, "step_trees": S, "trees_per_rank_timed": args.steps * S,
-                   "parallelism": f"trees sharded over {world} GPU(s), no collective in the step",
-                   "l2": "flushed between steps (256 MiB write on the library stream)",
-                   "batch_trees": args.batch_trees or "auto"},
+        "config": arm_config(T),
+        "checksum": checksum,
+        "details": {"step": f"one {T}-tree forest: reset, grow this rank's block, combine",
+                    "trees_this_rank": k,
+                    "parallelism": f"trees sharded over {world} GPU(s) (strong scaling); "
+                                   "combine: nout all-reduce, ordered OOB fold (send/recv "
+                                   "chain), importance all-gather, on the library stream",
+                    "l2": "flushed between steps (256 MiB write on the library stream)",
+                    "batch_trees": args.batch_trees or "auto"},
         "e2e": {"value": e2e_value, "unit": "trees/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h), "steps": e2e_steps,
-                "call": "rfx_b200.RandomForestRegressor(ntree=step_trees).fit(X, y) + get_oob_error()"},
+                "call": ("rfx_b200.shard.fit_sharded(RandomForestRegressor(ntree=500), X, y)"
+                         if world > 1 else "rfx_b200.RandomForestRegressor(ntree=500).fit(X, y)")
+                        + " + get_oob_error()"},
         "gpu_launches": int(st["kernel_launches"]),
-        "roofline": {"bound": "hbm", "kernel": "k_hist + k_hist_small (one tree level)",
+        "roofline": {"bound": "hbm", "kernel": "histogram search (k_hist_warp + k_hist_lane, "
+                                                "one tree level)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": (achieved / peak) if achieved else None,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                     "traffic": profile_traffic(),
+                     "traffic": None,
                      "algorithmic_bytes_per_level": per_level_bytes,
                      "levels": int(st["hist_launches"]), "kernel_ms": st["hist_ms"],
-                     "share_of_step": st["hist_ms"] / ms if ms else None},
+                     "share_of_step": st["hist_ms"] / (ms * world) if ms else None},
         "clocks": ck,
     }
+    if rank == 0 and not args.no_proximity:
+        from bench_workloads import proximity_probe
+        line["proximity"] = proximity_probe(local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        k = args.cpu_trees
-        dt, kind, cores = cpu_reference_fit(X, y, k)
-        line["cpu_baseline"] = {"value": k / dt, "unit": "trees/s", "cores": cores, "kind": kind,
-                                "sample": f"one reference fit of {k} trees on the full config[1] "
-                                          f"data ({dt:.1f} s, includes one-time prepare_data)"}
+        rate, prep, kind, cores, tk, t1s = cpu_tree_rate(X, y, args.cpu_trees)
+        line["cpu_baseline"] = {
+            "value": rate, "unit": "trees/s", "cores": cores, "kind": kind,
+            "sample": f"reference fits of 1 and {args.cpu_trees} trees on the full config[1] "
+                      f"data ({t1s:.1f} s, {tk[0]:.1f} s): ({args.cpu_trees} - 1) trees / time "
+                      f"difference, excluding the one-time prepare_data ({prep:.1f} s)"}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.destroy_process_group()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
 
 
@@ -335,10 +393,12 @@ def main():
     ap.add_argument("--impl", default="rfx", choices=["rfx", "reference"])
     ap.add_argument("--step-trees", type=int, default=None)
     ap.add_argument("--batch-trees", type=int, default=0)
-    ap.add_argument("--e2e-steps", type=int, default=2)
-    ap.add_argument("--cpu-trees", type=int, default=8)
-    ap.add_argument("--ref-step-trees", type=int, default=2)
+    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--cpu-trees", type=int, default=3)
+    ap.add_argument("--ref-step-trees", type=int, default=4)
+    ap.add_argument("--forest-trees", type=int, default=CFG["ntree"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-proximity", action="store_true")
     ap.add_argument("--workload", default="config1", choices=["config1", "config0", "config2", "config3", "config4"])
     args = ap.parse_args()
     args.step_trees_set = args.step_trees is not None

@@ -322,6 +322,66 @@ def run_workload(args):
     return 0
 
 
+def proximity_probe(local):
+    """The proximity half of the metric for bench.py's default line: config[0]'s 100-tree
+    classification forest with OOB x in-bag proximity counts (one untimed warm-up forest, one
+    timed), then finishprox of the 10000 x 10000 matrix into device memory."""
+    import torch
+
+    import rfx_b200
+    from rfx_b200 import _abi as A
+    cfg = WL["config0"]
+    dev = torch.device("cuda", local)
+    X, y, _ = make(cfg)
+    n, p = cfg["n"], cfg["p"]
+    M = calc_maxnode(n, cfg["minndsize"])
+    ctx = rfx_b200.Context(local)
+    prm = A.FitParams(0, n, p, cfg["mtry"], cfg["minndsize"], M, 12345, 12345, 256, 10, 0, 1, 0,
+                      0, 0, 0)
+    ctx.load(prm, A.Inputs(A.ptr(X, A._pf), A.ptr(y, A._pi), None, None, None, None))
+    stream = torch.cuda.ExternalStream(ctx.stream(), device=dev)
+    R = n
+    ctx.grow(0, cfg["ntree"])
+    ctx.reset_forest()
+    ctx.reset_stats()
+    ctx.set_profiling(True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        ctx.grow(0, cfg["ntree"])
+        e1.record(stream)
+    torch.cuda.synchronize()
+    fit_ms = e0.elapsed_time(e1)
+    st = ctx.stats()
+    ctx.set_profiling(False)
+    pairs = st["prox_pair_updates"]
+    dense = torch.empty((R, R), dtype=torch.float32, device=dev)
+    up, _ = ctx.prox_buffer()
+    nout_dev, _ = ctx.vote_buffers()
+    ctx.prox_finish(up, nout_dev, R, 0, R, dense.data_ptr())  # warm
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        f0.record(stream)
+        ctx.prox_finish(up, nout_dev, R, 0, R, dense.data_ptr())
+        f1.record(stream)
+    torch.cuda.synchronize()
+    fin_ms = f0.elapsed_time(f1)
+    fin_bytes = 4.0 * R * (R - 1) / 2 + 4.0 * R * R + 4.0 * R
+    hbm, _, peak_kind = peaks()
+    ctx.close()
+    return {
+        "workload": cfg["workload"], "trees": cfg["ntree"], "fit_ms": fit_ms,
+        "trees_per_s": cfg["ntree"] / (fit_ms / 1000.0),
+        "pair_updates": pairs, "pair_updates_per_s": pairs / (fit_ms / 1000.0),
+        "counting_ms": st["prox_ms"],
+        "counting_pair_updates_per_s": pairs / (st["prox_ms"] / 1000.0) if st["prox_ms"] else None,
+        "finish": {"kernel": "k_prox_finish", "rows": R, "ms": fin_ms, "bytes": fin_bytes,
+                   "achieved_gbs": fin_bytes / fin_ms / 1e6, "peak_gbs": hbm,
+                   "frac": fin_bytes / fin_ms / 1e6 / hbm, "peak_source": peak_kind},
+    }
+
+
 def cpu_config0(X, y, k):
     import oracle
     cores = os.cpu_count() or 1
@@ -356,7 +416,7 @@ def run_workload_reference(args):
     if args.workload != "config0":
         print(json.dumps({"impl": "reference", "unavailable":
                           f"{args.workload}: the reference CPU proximity does not fit this host "
-                          "(n^2 doubles) - see DESIGN.md"}), flush=True)
+                          "(its dense n x n double matrix exceeds host memory)"}), flush=True)
         return 0
     cfg = WL["config0"]
     X, y, _ = make(cfg)

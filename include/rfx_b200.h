@@ -116,6 +116,13 @@ int rfx_load(void* ctx, const rfx_fit_params* prm, const rfx_inputs* in);
  * `out` (may be NULL) receives the per-tree arrays of these trees. */
 int rfx_grow(void* ctx, int tree_begin, int ntree, rfx_trees* out);
 
+/* Start a new forest on the loaded dataset: zero the forest-level accumulators (OOB counts,
+ * votes or OOB prediction sums, importance, proximity counts) and forget the stored trees,
+ * keeping the binned data and the buffers.  The reference builds a new RandomForest per fit
+ * (src/rf_random_forest.cpp:521, 691, 988); this is its counterpart for repeated fits on
+ * device-resident data. */
+int rfx_reset_forest(void* ctx);
+
 /* Copy the accumulators to the host. */
 int rfx_results(void* ctx, rfx_accum* res);
 
@@ -139,6 +146,15 @@ int rfx_get_vote_buffers(void* ctx, int** nout_dev, int** votes_dev);
  * double result (diag 1).  Stream-ordered on the context's stream. */
 int rfx_prox_finish(void* ctx, const int* upper_dev, const int* nout_dev, int R,
                     int row_begin, int row_end, float* out_dev);
+
+/* Finished values of the packed upper-triangle elements [elem_begin, elem_begin + elem_count)
+ * of the R x R proximity (element e = (i, j), i < j, e = i (2R - i - 1) / 2 + j - i - 1):
+ * upper_dev and out_dev hold that slice (index e - elem_begin), nout_dev all R counts.  The
+ * finishprox arithmetic of rfx_prox_finish (src/rf_finishprox.cpp:12-74) needs only C_ij and
+ * the two row scales, so each rank of a tree-sharded fit finishes the slice its NCCL
+ * reduce-scatter left it.  Device pointers; returns after the slice is written. */
+int rfx_prox_finish_packed(void* ctx, const int* upper_dev, int64_t elem_begin, int64_t elem_count,
+                           const int* nout_dev, int R, float* out_dev);
 
 /* Same as rfx_prox_finish on the context's own counts and nout, rows [row_begin, row_end)
  * of the R x R matrix written to host memory out_host[(i-row_begin)*R + j]; processed in

@@ -33,12 +33,20 @@ def _p(a, t):
     return None if a is None else a.ctypes.data_as(t)
 
 
+def reference_tree():
+    """The reference source tree: $RFX_REFERENCE, else a directory named ``reference`` beside
+    this repository; None when neither exists."""
+    cand = os.environ.get("RFX_REFERENCE") or os.path.join(
+        os.path.dirname(os.path.dirname(HERE)), "reference")
+    return cand if os.path.isdir(cand) else None
+
+
 def build(ref: bool = False) -> None:
     """Compile the oracle (and, when the reference tree is present, oracle/_ref)."""
     subprocess.run(["make", "-s", "-C", HERE, "all"], check=True)
-    if ref and os.path.isdir(os.environ.get("RFX_REFERENCE", "/root/reference")):
-        subprocess.run(["make", "-s", "-j8", "-C", HERE, "ref",
-                        "REF=" + os.environ.get("RFX_REFERENCE", "/root/reference")], check=True)
+    tree = reference_tree() if ref else None
+    if tree:
+        subprocess.run(["make", "-s", "-j8", "-C", HERE, "ref", "REF=" + tree], check=True)
 
 
 class OrcParams(C.Structure):

@@ -98,7 +98,7 @@ struct Ctx {
     cudaEvent_t perm_event = nullptr;  // owned by the process-wide permutation cache
 
     // accumulators
-    DBuf nout, votes, oob_sum, avimp, sqsd, prox_own, qtmp, cw_dev, tree_oob_all;
+    DBuf nout, votes, oob_sum, avimp, sqsd, prox_own, qtmp, cw_dev, tree_oob_all, fin_inv;
     int* prox = nullptr;
     int64_t prox_len = 0;
     int trees_done = 0;
@@ -161,7 +161,7 @@ struct Ctx {
     ~Ctx() {
         DBuf* all[] = {&xc, &rows, &edges, &nb, &kind, &cat, &lab, &yreg, &yv, &perm, &ks, &cumw,
                        &totw, &keys_a, &keys_b, &nout, &votes, &oob_sum, &avimp, &sqsd,
-                       &prox_own, &qtmp, &cw_dev, &tree_oob_all, &b_nin, &b_seg0, &b_seg1,
+                       &prox_own, &qtmp, &cw_dev, &tree_oob_all, &fin_inv, &b_nin, &b_seg0, &b_seg1,
                        &b_ninbag, &b_oob, &b_noob, &b_mt, &b_mtpos, &b_status, &b_bestvar,
                        &b_xbest, &b_treemap, &b_nodeclass, &b_nodepred, &b_tnodewt, &b_ndstart,
                        &b_ndcnt, &b_ndbuf, &b_ndflag, &b_ndcrit0, &b_ndmaj, &b_ndsum, &b_ndkey,

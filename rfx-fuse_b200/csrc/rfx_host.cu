@@ -714,6 +714,28 @@ int rfx_grow(void* ctx, int tree_begin, int ntree, rfx_trees* out) {
     });
 }
 
+int rfx_reset_forest(void* ctx) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(c.loaded, RFX_ERR_STATE, "rfx_reset_forest before rfx_load");
+        const size_t N = c.N, p = c.p;
+        cudaStream_t st = c.st;
+        RFX_CUDA(cudaMemsetAsync(c.nout.p, 0, N * 4, st));
+        if (c.nclass > 1) RFX_CUDA(cudaMemsetAsync(c.votes.p, 0, N * c.nclass * 4, st));
+        else RFX_CUDA(cudaMemsetAsync(c.oob_sum.p, 0, N * 4, st));
+        RFX_CUDA(cudaMemsetAsync(c.avimp.p, 0, p * 4, st));
+        RFX_CUDA(cudaMemsetAsync(c.sqsd.p, 0, p * 4, st));
+        if (c.prox) RFX_CUDA(cudaMemsetAsync(c.prox, 0, (size_t)c.prox_len * 4, st));
+        forest_reset(c);
+        leaves_reset(c);
+        c.lr_n = 0;
+        c.lr_ready = false;
+        c.trees_done = 0;
+        c.tree_oob_n = 0;
+        RFX_CUDA(cudaStreamSynchronize(st));
+    });
+}
+
 int rfx_results(void* ctx, rfx_accum* r) {
     return guarded([&] {
         Ctx& c = *as_ctx(ctx);
@@ -767,6 +789,7 @@ int rfx_set_prox_buffer(void* ctx, int* upper_dev, int64_t len) {
             c.prox = (int*)c.prox_own.get((size_t)len * 4);
         } else {
             c.prox = upper_dev;
+            c.prox_own.release();  // the caller's buffer replaces the context's own
         }
         RFX_CUDA(cudaMemsetAsync(c.prox, 0, (size_t)len * 4, c.st));
         RFX_CUDA(cudaStreamSynchronize(c.st));
@@ -799,6 +822,21 @@ int rfx_prox_finish(void* ctx, const int* upper_dev, const int* nout_dev, int R,
         require(R >= 1 && row_begin >= 0 && row_begin <= row_end && row_end <= R, RFX_ERR_ARG,
                 "bad row range");
         RFX_CUDA(rfx::launch_prox_finish(upper_dev, nout_dev, R, row_begin, row_end, out_dev, c.st));
+        RFX_CUDA(cudaStreamSynchronize(c.st));
+    });
+}
+
+int rfx_prox_finish_packed(void* ctx, const int* upper_dev, int64_t elem_begin, int64_t elem_count,
+                           const int* nout_dev, int R, float* out_dev) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(upper_dev && nout_dev && out_dev, RFX_ERR_ARG, "null pointer");
+        const int64_t L = (int64_t)R * (R - 1) / 2;
+        require(R >= 2 && elem_begin >= 0 && elem_count >= 0 && elem_begin + elem_count <= L,
+                RFX_ERR_ARG, "bad element range");
+        double* inv = (double*)c.fin_inv.get((size_t)R * 8);
+        RFX_CUDA(rfx::launch_prox_finish_packed(upper_dev, elem_begin, elem_count, nout_dev, R, inv,
+                                                out_dev, c.st));
         RFX_CUDA(cudaStreamSynchronize(c.st));
     });
 }

@@ -50,6 +50,9 @@ __global__ void k_prox_finish(const int* C, const int* nout, int R, int r0, int 
 // k_prox_finish over rows [r0, r1) with its tile grid.
 cudaError_t launch_prox_finish(const int* C, const int* nout, int R, int r0, int r1, float* out,
                                cudaStream_t st);
+// k_prox_finish_packed (with the 1 / nout scales) over the packed elements [e0, e0 + len).
+cudaError_t launch_prox_finish_packed(const int* C, long long e0, long long len, const int* nout,
+                                      int R, double* inv, float* out, cudaStream_t st);
 __global__ void k_votes_to_q(const int* votes, const float* w, int N, int nclass, float* q);
 __global__ void k_oob_fold(const float* tree_oob, int ntrees, int N, float* vec);
 

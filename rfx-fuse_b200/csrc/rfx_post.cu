@@ -1,5 +1,7 @@
 // After growth: OOB leaf drop, OOB votes / predictions, permutation importance, proximity
 // co-membership counts and the finishprox normalisation.
+#include <algorithm>
+
 #include "rfx_device.cuh"
 #include "rfx_kernels.h"
 
@@ -548,6 +550,64 @@ cudaError_t launch_prox_finish(const int* C, const int* nout, int R, int r0, int
     const dim3 grid((unsigned)((R + kFinTile - 1) / kFinTile),
                     (unsigned)((r1 - r0 + kFinTile - 1) / kFinTile));
     k_prox_finish<<<grid, 256, 0, st>>>(C, nout, R, r0, r1, out);
+    return cudaGetLastError();
+}
+
+// 1 / nout (1 where nout is 0): the row scales of finishprox.
+__global__ void k_inv_nout(const int* __restrict__ nout, int R, double* __restrict__ inv) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < R; i += gridDim.x * blockDim.x)
+        inv[i] = nout[i] > 0 ? 1.0 / (double)nout[i] : 1.0;
+}
+
+// Finished values of the packed upper-triangle elements [e0, e0 + len), element e = (i, j),
+// e = i (2R - i - 1) / 2 + (j - i - 1): the same double operations as k_prox_finish, which
+// only need C_ij and the two row scales -- so a rank finishes its own slice of a
+// reduce-scattered triangle.  C and out hold the slice (index e - e0).  A warp covers 32 x
+// kPackRun consecutive elements, lane-interleaved so that loads and stores coalesce.
+constexpr int kPackRun = 8;
+__global__ void __launch_bounds__(256) k_prox_finish_packed(const int* __restrict__ C, long long e0,
+                                                            long long len, const double* __restrict__ inv,
+                                                            int R, float* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const long long R2 = 2LL * R;
+    const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+    for (long long w = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5);
+         w * 32 * kPackRun < len; w += warps) {
+        const long long b = w * 32 * kPackRun + lane;  // first element of this lane
+        if (b >= len) continue;
+        const long long e = e0 + b;
+        // row of e: the largest i with i (2R - i - 1) / 2 <= e (double estimate, then exact)
+        const double a = (double)(R2 - 1);
+        long long i = (long long)((a - sqrt(fmax(a * a - 8.0 * (double)e, 0.0))) * 0.5);
+        i = max(0LL, min(i, (long long)R - 2));
+        while (i > 0 && i * (R2 - i - 1) / 2 > e) --i;
+        while (i < R - 2 && (i + 1) * (R2 - i - 2) / 2 <= e) ++i;
+        long long j = e - i * (R2 - i - 1) / 2 + i + 1;
+        double si = inv[i];
+#pragma unroll
+        for (int k = 0; k < kPackRun; ++k) {
+            const long long q = b + (long long)k * 32;
+            if (q >= len) break;
+            const double h = (double)C[q] / 2.0;
+            out[q] = (float)(0.5 * (h * si + h * inv[j]));
+            j += 32;  // the lane's next element
+            while (j >= R && i < R - 2) {
+                j -= R - i - 2;  // continue on row i + 1, whose first column is i + 2
+                ++i;
+                si = inv[i];
+            }
+        }
+    }
+}
+
+cudaError_t launch_prox_finish_packed(const int* C, long long e0, long long len, const int* nout,
+                                      int R, double* inv, float* out, cudaStream_t st) {
+    k_inv_nout<<<(R + 255) / 256, 256, 0, st>>>(nout, R, inv);
+    if (len > 0) {
+        const long long per_block = 8LL * 32 * kPackRun;
+        const unsigned grid = (unsigned)std::min<long long>((len + per_block - 1) / per_block, 148LL * 16);
+        k_prox_finish_packed<<<grid, 256, 0, st>>>(C, e0, len, inv, R, out);
+    }
     return cudaGetLastError();
 }
 

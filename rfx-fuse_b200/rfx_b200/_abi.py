@@ -65,7 +65,7 @@ SYMBOLS = (
     "rfx_last_error", "rfx_abi_version", "rfx_device_count", "rfx_create", "rfx_destroy",
     "rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
     "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish", "rfx_prox_dense",
-    "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host", "rfx_get_stream",
+    "rfx_prox_finish_packed", "rfx_reset_forest", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host", "rfx_get_stream",
     "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats", "rfx_sync",
     "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk", "rfx_lowrank_product",
     "rfx_prox_apply", "rfx_lowrank_set_factors", "rfx_load_forest", "rfx_predict",
@@ -117,6 +117,8 @@ def load_library(path: str = LIB_PATH):
     L.rfx_get_vote_buffers.argtypes = [vp, C.POINTER(vp), C.POINTER(vp)]
     L.rfx_prox_finish.argtypes = [vp, vp, vp, C.c_int, C.c_int, C.c_int, vp]
     L.rfx_prox_dense.argtypes = [vp, C.c_int, C.c_int, _pf]
+    L.rfx_prox_finish_packed.argtypes = [vp, vp, C.c_int64, C.c_int64, vp, C.c_int, vp]
+    L.rfx_reset_forest.argtypes = [vp]
     L.rfx_oob_fold.argtypes = [vp, vp]
     L.rfx_votes_to_q.argtypes = [vp, vp, _pf, C.c_int, C.c_int, vp]
     L.rfx_copy_to_host.argtypes = [vp, vp, vp, C.c_size_t]
@@ -150,7 +152,7 @@ def load_library(path: str = LIB_PATH):
     L.rfx_predict_outlier_scores.argtypes = [vp, _pf, C.c_int, C.c_int, C.c_int, C.c_int, _pi, _pf]
     for name in ("rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
                  "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish",
-                 "rfx_prox_dense", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host",
+                 "rfx_prox_finish_packed", "rfx_reset_forest", "rfx_prox_dense", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host",
                  "rfx_get_stream", "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats",
                  "rfx_sync", "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk",
                  "rfx_lowrank_product", "rfx_prox_apply", "rfx_lowrank_set_factors",
@@ -210,6 +212,9 @@ class Context:
         check(self._lib.rfx_grow(self.handle, tree_begin, ntree,
                                  C.byref(trees) if trees is not None else None))
 
+    def reset_forest(self):
+        check(self._lib.rfx_reset_forest(self.handle))
+
     def results(self, acc: Accum):
         check(self._lib.rfx_results(self.handle, C.byref(acc)))
 
@@ -234,6 +239,12 @@ class Context:
     def prox_finish(self, upper_dev: int, nout_dev: int, R: int, r0: int, r1: int, out_dev: int):
         check(self._lib.rfx_prox_finish(self.handle, C.c_void_p(upper_dev), C.c_void_p(nout_dev),
                                         R, r0, r1, C.c_void_p(out_dev)))
+
+    def prox_finish_packed(self, upper_dev: int, e0: int, count: int, nout_dev: int, R: int,
+                           out_dev: int):
+        check(self._lib.rfx_prox_finish_packed(self.handle, C.c_void_p(upper_dev), int(e0),
+                                               int(count), C.c_void_p(nout_dev), int(R),
+                                               C.c_void_p(out_dev)))
 
     def oob_fold(self, vec_dev: int):
         check(self._lib.rfx_oob_fold(self.handle, C.c_void_p(vec_dev)))

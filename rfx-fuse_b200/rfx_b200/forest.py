@@ -290,15 +290,10 @@ class _Forest:
         _, length = ctx.prox_buffer()
         R = int(round((1 + math.sqrt(1 + 8 * length)) / 2)) if length else (
             self.prox_rows or self.n_rows_)
-        sharded = getattr(self, "_sharded_prox", None)
-        if sharded is not None:
-            # counts and nout summed over the ranks (rfx_b200.shard.fit_sharded)
-            import torch
-            counts, nout = sharded
-            dense = torch.empty((R, R), dtype=torch.float32, device=counts.device)
-            torch.cuda.synchronize(counts.device)
-            ctx.prox_finish(counts.data_ptr(), nout.data_ptr(), R, 0, R, dense.data_ptr())
-            return dense.cpu().numpy()
+        if getattr(self, "_sharded_prox", None) is not None:
+            # reduce-scattered counts of a tree-sharded fit: a collective over its ranks
+            from .shard import sharded_proximity_dense
+            return sharded_proximity_dense(self)
         out = np.empty((R, R), np.float32)
         ctx.prox_dense(0, R, out)
         return out

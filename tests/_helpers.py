@@ -41,14 +41,14 @@ def synth(kind: str, n: int, p: int, seed: int):
 
 def gpu_fit(task, X, y=None, *, ntree, mtry, minndsize, maxnode, iseed=12345, nbins=256,
             sample_weights=None, cat=None, classwt=None, importance=True, proximity=False,
-            batch_trees=0, maxcat=10, ctx=None, tree_chunks=None):
+            batch_trees=0, maxcat=10, ctx=None, tree_chunks=None, prox_rows=0, fetch_prox=True):
     """Device fit through the C ABI; returns a dict shaped like oracle.fit's."""
     X = np.ascontiguousarray(X, np.float32)
     n, p = X.shape
     N = 2 * n if task == 2 else n
     ncl = len(np.unique(y)) if task == 0 else (2 if task == 2 else 1)
     prm = A.FitParams(task, n, p, mtry, minndsize, maxnode, iseed, 12345, nbins, maxcat,
-                      int(importance), int(proximity), 0, batch_trees, 0)
+                      int(importance), int(proximity), prox_rows, batch_trees, 0)
     ycls = np.ascontiguousarray(y, np.int32) if task == 0 else None
     yreg = np.ascontiguousarray(y, np.float32) if task == 1 else None
     sw = None if sample_weights is None else np.ascontiguousarray(sample_weights, np.float32)
@@ -88,7 +88,7 @@ def gpu_fit(task, X, y=None, *, ntree, mtry, minndsize, maxnode, iseed=12345, nb
         ac.votes = ac.q = ac.labels = None
     ctx.results(ac)
     r.update(acc)
-    if proximity:
+    if proximity and fetch_prox:
         dev, length = ctx.prox_buffer()
         up = np.empty(length, np.int32)
         ctx.copy_to_host(up, dev)
@@ -137,3 +137,60 @@ def compare_fit(g, o, task, proximity=False, importance=True):
     if proximity:
         assert_same("prox_upper", g["prox_upper"], upper_from_pairs(o["prox_pairs"]))
         assert_same("prox", g["prox"], o["prox"].astype(np.float32))
+
+
+def inbag_leaves(g, X, t):
+    """Terminal node of every row of X in tree t of a device fit (raw x <= split, the walk
+    the grower's partition makes; every feature quantitative)."""
+    st, bv, xb, tm = g["nodestatus"][t], g["bestvar"][t], g["xbestsplit"][t], g["treemap"][t]
+    node = np.zeros(X.shape[0], np.int64)
+    rows = np.arange(X.shape[0])
+    for _ in range(100000):
+        live = st[node] == 1
+        if not live.any():
+            return node
+        r = rows[live]
+        nd = node[live]
+        left = X[r, bv[nd]] <= xb[nd]
+        node[r] = np.where(left, tm[2 * nd], tm[2 * nd + 1])
+    raise AssertionError("tree walk did not terminate")
+
+
+def expected_counts(g, X, R, rows):
+    """C[i, j] = P_ij + P_ji for the given rows i (all j < R): the reference's dense proximity
+    (src/rf_proximity.cpp:99-230): OOB row i in leaf k meets every distinct in-bag row of k."""
+    C = np.zeros((len(rows), R), np.int32)
+    for t in range(g["nin"].shape[0]):
+        leaf = inbag_leaves(g, X[:R], t)
+        oob = g["nin"][t, :R] == 0
+        assert np.array_equal(leaf[oob], g["oob_leaf"][t, :R][oob])
+        eq = leaf[rows][:, None] == leaf[None, :]
+        C += (eq & (oob[rows][:, None] & ~oob[None, :])).astype(np.int32)
+        C += (eq & (~oob[rows][:, None] & oob[None, :])).astype(np.int32)
+    return C
+
+
+def device_upper_rows(ctx, R, rows):
+    """C[i, i+1:R] of the given rows from the device's packed upper triangle."""
+    dev, length = ctx.prox_buffer()
+    assert length == R * (R - 1) // 2
+    out = {}
+    for i in rows:
+        off = i * (2 * R - i - 1) // 2
+        seg = np.empty(R - i - 1, np.int32)
+        if len(seg):
+            ctx.copy_to_host(seg, int(dev) + 4 * int(off))
+        out[int(i)] = seg
+    return out
+
+
+def finish_rows(C, rows, nout):
+    """finishprox (src/rf_finishprox.cpp:12-74, the oracle's double operations) for the given
+    rows of C = P + P^T, as float32."""
+    inv = np.where(nout > 0, 1.0 / np.maximum(nout, 1).astype(np.float64), 1.0)
+    a = C.astype(np.float64) / 2.0
+    si = a * inv[rows][:, None]
+    sj = a * inv[None, :C.shape[1]]
+    S = 0.5 * (si + sj)
+    S[np.arange(len(rows)), rows] = 1.0
+    return S.astype(np.float32)

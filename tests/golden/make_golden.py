@@ -126,7 +126,10 @@ def impute_data(n=400, seed=61):
 def impute_golden():
     """The reference's rfx_impute_proximity (python/rfx_impute.py:596-793) on impute_data()."""
     sys.path.insert(0, oracle.ref_dir())
-    sys.path.insert(0, os.path.join(os.environ.get("RFX_REFERENCE", "/root/reference"), "python"))
+    tree = oracle.reference_tree()
+    if tree is None:
+        raise SystemExit("set RFX_REFERENCE to the reference source tree")
+    sys.path.insert(0, os.path.join(tree, "python"))
     import importlib
     ri = importlib.import_module("rfx_impute")
     X = impute_data()

@@ -102,3 +102,19 @@ def test_tree_blocks_partition_the_forest():
         blocks = [tree_block(1000, r, world) for r in range(world)]
         assert blocks[0][0] == 0 and blocks[-1][1] == 1000
         assert all(blocks[i][1] == blocks[i + 1][0] for i in range(world - 1))
+
+
+@pytest.mark.parametrize("length", [0, 1, 10, 4950, 1_249_975_000])
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_prox_slices_cover_the_triangle(length, world):
+    from rfx_b200.shard import prox_slice
+    ends = 0
+    padded = None
+    for r in range(world):
+        e0, cnt, pad = prox_slice(length, r, world)
+        assert e0 == ends or cnt == 0
+        ends = e0 + cnt
+        padded = pad if padded is None else padded
+        assert pad == padded and pad % world == 0
+        assert cnt <= pad // world
+    assert ends == length and padded >= length
