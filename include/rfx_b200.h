@@ -31,7 +31,8 @@ enum {
     RFX_ERR_OOM = -3,          /* device allocation failed */
     RFX_ERR_UNSUPPORTED = -4,  /* option outside what the device path implements */
     RFX_ERR_STATE = -5,        /* call order violated (e.g. grow before load) */
-    RFX_ERR_DEVICE = -6        /* a kernel reported an internal consistency error */
+    RFX_ERR_DEVICE = -6,       /* a kernel reported an internal consistency error */
+    RFX_ERR_CANCELLED = -7     /* the progress callback asked to stop */
 };
 
 enum { RFX_TASK_CLASSIFICATION = 0, RFX_TASK_REGRESSION = 1, RFX_TASK_UNSUPERVISED = 2 };
@@ -122,6 +123,14 @@ int rfx_grow(void* ctx, int tree_begin, int ntree, rfx_trees* out);
  * (src/rf_random_forest.cpp:521, 691, 988); this is its counterpart for repeated fits on
  * device-resident data. */
 int rfx_reset_forest(void* ctx);
+
+/* Progress of rfx_grow / rfx_fit, the reference's progress_callback_(itree + 1, ntree)
+ * (src/rf_random_forest.cpp:600-601; the wrapper drives tqdm from it,
+ * python/randomforest_py.cpp:1560-1690).  Called on the caller's thread after every batch
+ * of trees with the trees grown so far by this call and the call's total; a nonzero return
+ * stops the call with RFX_ERR_CANCELLED after the batch.  NULL removes the callback. */
+typedef int (*rfx_progress_fn)(void* user, int trees_done, int ntree);
+int rfx_set_progress(void* ctx, rfx_progress_fn fn, void* user);
 
 /* Copy the accumulators to the host. */
 int rfx_results(void* ctx, rfx_accum* res);

@@ -219,8 +219,17 @@ def ref_available():
     return os.path.exists(os.path.join(ref_dir(), "libref_harness.so"))
 
 
-def ref_lib():
-    global _REF
+_REF_STOCK = None
+
+
+def ref_lib(stock: bool = False):
+    """The reference harness; ``stock``: the build with the reference's stock flags only
+    (``make ref-stock``: GCC free to contract into FMAs) instead of -ffp-contract=off."""
+    global _REF, _REF_STOCK
+    if stock:
+        if _REF_STOCK is None:
+            _REF_STOCK = C.CDLL(os.path.join(HERE, "_ref_stock", "libref_harness.so"))
+        return _REF_STOCK
     if _REF is None:
         _REF = C.CDLL(os.path.join(ref_dir(), "libref_harness.so"))
     return _REF
@@ -259,10 +268,11 @@ def ref_binning(X, cat=None, nbins=256):
 
 
 def ref_fit(task, X, y=None, *, ntree, mtry, minndsize, maxnode=0, iseed=12345, nbins=256,
-            sample_weights=None, cat=None, classwt=None, importance=True, proximity=False):
+            sample_weights=None, cat=None, classwt=None, importance=True, proximity=False,
+            stock=False):
     X = np.ascontiguousarray(X, np.float32)
     n, p = X.shape
-    L = ref_lib()
+    L = ref_lib(stock)
     M = L.ref_effective_maxnode(task, n, minndsize, maxnode)
     N = 2 * n if task == 2 else n
     ycls = np.ascontiguousarray(y, np.int32) if task == 0 else None

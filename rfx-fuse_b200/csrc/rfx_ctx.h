@@ -104,6 +104,10 @@ struct Ctx {
     int trees_done = 0;
     int tree_oob_cap = 0, tree_oob_n = 0;
 
+    // progress callback (rfx_set_progress), called between batches
+    rfx_progress_fn progress = nullptr;
+    void* progress_user = nullptr;
+
     // measurement
     bool profiling = false;
     bool level_log = std::getenv("RFX_LEVEL_LOG") != nullptr;  // per-level trace on stderr

@@ -199,6 +199,14 @@ struct HistArgs {
     int warp_bytes;  // per-warp shared memory
 };
 
+// Launch shape of k_hist_pipe (rfx_hist.cu).
+struct PipeArgs {
+    int warps;    // consumer warps (one drawn feature each); the block adds a producer warp
+    int groups;   // work units per searched node = ceil(mtry / warps)
+    int ch;       // rows per staged chunk (<= 64)
+    int rstride;  // bytes per staged row (rs + 16)
+};
+
 // Locate the tree of a flattened task index given an exclusive prefix `off` of length T+1.
 __device__ __forceinline__ int tree_of(const int* off, int T, int idx) {
     int lo = 0, hi = T;  // off[lo] <= idx < off[hi]

@@ -457,6 +457,335 @@ __device__ __forceinline__ void hist_warp(const Data& D, const Batch& B, int cur
     }
 }
 
+// ---------------------------------------------------------------------------------------
+// k_hist_pipe: regression nodes above kSmallNode rows, warp-specialised.  A block takes one
+// searched node and up to `warps` of its draws.  Warp 0 (producer) streams the node's packed
+// rows into a ring of kPipeBufs chunks of `ch` rows in shared memory (16-byte cp.async; row
+// stride rs + 16 bytes, the 16-byte multiple that spreads 32 consecutive rows over the most
+// banks: a lane reading one byte of its row meets at most 3 others in its bank); warps
+// 1..warps (consumers) each build one drawn feature's
+// histogram from the staged rows, 32 rows per step, in the conflict rounds of k_hist_warp.
+// Chunks are handed over with mbarriers (full: the producer's copies have landed; empty:
+// every consumer is done with the buffer), so the producer runs up to kPipeBufs - 1 chunks
+// ahead and no block-wide barrier sits in the row loop.  One histogram entry per bin,
+// HE[bin] = {sum, sum of squares, count, round tag}: a round's read and write are one 16-byte
+// access each.  Every wait is bounded (about one second); on expiry the block records
+// counters[3] and returns after its own copies have landed.
+//
+// Shared memory: mbarriers full[kPipeBufs], empty[kPipeBufs], cons | umin[2] | ring
+// [kPipeBufs][ch][rs + 16] | per consumer HE float4[256] | BL u8[256] | CF u8[256].
+// ---------------------------------------------------------------------------------------
+constexpr int kPipeBufs = 4;
+constexpr int kPipeDraw = 256 * 16 + 512;  // shared memory per consumer warp
+constexpr unsigned long long kPipeWaitNs = 1000000000ull;
+
+__device__ __forceinline__ unsigned pipe_smem(const void* p) {
+    return (unsigned)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ unsigned long long pipe_now() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void pipe_init(uint64_t* b, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(pipe_smem(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ bool pipe_wait(uint64_t* b, unsigned parity) {
+    const unsigned a = pipe_smem(b);
+    const unsigned long long t0 = pipe_now();
+    for (unsigned spin = 1;; ++spin) {
+        unsigned ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (ok) return true;
+        if ((spin & 63u) == 0 && pipe_now() - t0 > kPipeWaitNs) return false;
+    }
+}
+__device__ __forceinline__ void pipe_arrive(uint64_t* b) {
+    asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}\n" ::"r"(pipe_smem(b))
+                 : "memory");
+}
+__device__ __forceinline__ void pipe_copy16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(pipe_smem(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void pipe_arrive_on_copies(uint64_t* b) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(pipe_smem(b)) : "memory");
+}
+__device__ __forceinline__ void pipe_wait_copies() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Node of histogram task `task` (a.groups tasks per big searched node).
+__device__ __forceinline__ void pipe_task(const Batch& B, int task, int groups, int& t, int& node,
+                                          int& grp) {
+    const int si = task / groups;
+    grp = task - si * groups;
+    t = tree_of(B.srch_big_off, B.T, si);
+    node = B.srch_big[(size_t)t * B.M + (si - B.srch_big_off[t])];
+}
+
+__global__ void __launch_bounds__(544, 2) k_hist_pipe(Data D, Batch B, int cur, PipeArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + kPipeBufs;
+    uint64_t* cons = empty + kPipeBufs;  // the consumers' per-node barrier
+    unsigned* s_umin = reinterpret_cast<unsigned*>(smem + 96);
+    uint8_t* ring = smem + 128;
+    const int ch = a.ch, RS = a.rstride, W = a.warps;
+    uint8_t* dbase = ring + (size_t)kPipeBufs * ch * RS;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rs = D.rs, ro = D.ro, pieces = rs >> 4;
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < kPipeBufs; ++b) {
+            pipe_init(&full[b], 32);
+            pipe_init(&empty[b], W);
+        }
+        pipe_init(cons, W);
+        s_umin[0] = s_umin[1] = 0xffffffffu;
+    }
+    __syncthreads();
+    const int total = B.counters[4] * a.groups;
+    long long g = 0;  // chunk counter, identical sequence in every warp
+    if (warp == 0) {
+        // ---- producer: lane l copies rows l and l + 32 of each chunk (16-byte pieces); the
+        // next chunk's row ids are loaded while the current chunk's copies are issued
+        for (int task = blockIdx.x; task < total; task += gridDim.x) {
+            int t, node, grp;
+            pipe_task(B, task, a.groups, t, node, grp);
+            const size_t m = (size_t)t * B.M + node;
+            const int c = B.nd_cnt[m];
+            const int* seg = B.seg[cur] + (size_t)t * D.N + B.nd_start[m];
+            int r0 = lane < c ? __ldg(seg + lane) : -1;
+            int r1 = lane + 32 < min(c, ch) ? __ldg(seg + 32 + lane) : -1;
+            for (int c0 = 0; c0 < c; c0 += ch, ++g) {
+                const int b = (int)(g % kPipeBufs);
+                const long long u = g / kPipeBufs;
+                const int n1 = c0 + ch < c ? min(ch, c - c0 - ch) : 0;  // rows of the next chunk
+                const int q0 = lane < n1 ? __ldg(seg + c0 + ch + lane) : -1;
+                const int q1 = lane + 32 < n1 ? __ldg(seg + c0 + ch + 32 + lane) : -1;
+                if (u > 0 && !pipe_wait(&empty[b], (unsigned)((u - 1) & 1))) {
+                    atomicExch(&B.counters[3], 1);
+                    pipe_wait_copies();
+                    return;
+                }
+                uint8_t* dst = ring + (size_t)b * ch * RS + (size_t)lane * RS;
+                if (r0 >= 0) {
+                    const uint8_t* src = D.rows + (size_t)r0 * rs;
+                    for (int pc = 0; pc < pieces; ++pc) pipe_copy16(dst + 16 * pc, src + 16 * pc);
+                }
+                if (r1 >= 0) {
+                    const uint8_t* src = D.rows + (size_t)r1 * rs;
+                    for (int pc = 0; pc < pieces; ++pc)
+                        pipe_copy16(dst + (size_t)32 * RS + 16 * pc, src + 16 * pc);
+                }
+                pipe_arrive_on_copies(&full[b]);
+                r0 = q0;
+                r1 = q1;
+            }
+        }
+        pipe_wait_copies();
+        return;
+    }
+    // ---- consumers
+    const int cw = warp - 1;
+    float4* HE = reinterpret_cast<float4*>(dbase + (size_t)cw * kPipeDraw);
+    uint8_t* BL = dbase + (size_t)cw * kPipeDraw + 4096;
+    uint8_t* CF = BL + 256;
+    const float tag0 = __uint_as_float(0xffffffffu);
+    int it = 0;
+    for (int task = blockIdx.x; task < total; task += gridDim.x, ++it) {
+        int t, node, grp;
+        pipe_task(B, task, a.groups, t, node, grp);
+        const size_t m = (size_t)t * B.M + node;
+        const int c = B.nd_cnt[m];
+        const int mv = grp * W + cw;
+        const bool active = mv < B.mtry;
+        const int f = active ? (int)B.feat[(size_t)t * B.M * B.mtry + (size_t)node * B.mtry + mv] : 0;
+        unsigned* umin = &s_umin[it & 1];
+        if (cw == 0 && lane == 0 && grp == 0 && B.hist_bytes)
+            atomicAdd(B.hist_bytes, (unsigned long long)c * (unsigned long long)(B.mtry + 4));
+        for (int k = lane; k < 256; k += 32) HE[k] = make_float4(0.0f, 0.0f, 0.0f, tag0);
+        __syncwarp();
+        for (int c0 = 0; c0 < c; c0 += ch, ++g) {
+            const int b = (int)(g % kPipeBufs);
+            if (!pipe_wait(&full[b], (unsigned)((g / kPipeBufs) & 1))) {
+                atomicExch(&B.counters[3], 1);
+                return;
+            }
+            if (active) {
+                const int n = min(ch, c - c0);
+                const uint8_t* buf = ring + (size_t)b * ch * RS;
+                for (int s0 = 0; s0 < n; s0 += 32) {
+                    const int i = s0 + lane;
+                    const bool valid = i < n;
+                    const uint8_t* row = buf + (size_t)(valid ? i : 0) * RS;
+                    const int bn = valid ? (int)row[f] : 0;
+                    const float2 vv = valid ? *reinterpret_cast<const float2*>(row + ro)
+                                            : make_float2(0.0f, 0.0f);
+                    const float v = vv.x, v2 = vv.y;
+                    // rounds: the lowest pending lane of every bin (the earliest row) adds
+                    bool pend = valid;
+                    while (__any_sync(kFull, pend)) {
+                        if (pend) atomicMin(reinterpret_cast<unsigned*>(&HE[bn].w), (unsigned)lane);
+                        __syncwarp();
+                        bool first = false;
+                        float4 h;
+                        if (pend) {
+                            h = HE[bn];
+                            first = __float_as_uint(h.w) == (unsigned)lane;
+                        }
+                        if (first) {
+                            h.x += v;
+                            h.y += v2;
+                            h.z += 1.0f;
+                            h.w = tag0;
+                            HE[bn] = h;
+                        }
+                        pend = pend && !first;
+                        __syncwarp();
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) pipe_arrive(&empty[b]);
+        }
+        // ---- approximate criterion (k_hist_warp's, over HE)
+        float lo[8];
+        int binq[8];
+        int nm = 0;
+        if (active) {
+            {
+                int k = 0;
+                uint32_t bits = 0;
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                    if (HE[lane * 8 + q].z > 0.0f) { bits |= 1u << q; ++k; }
+                const int x = warp_incl_scan(k, lane);
+                int off = x - k;
+                while (bits) {
+                    const int q = __ffs(bits) - 1;
+                    bits &= bits - 1;
+                    BL[off++] = (uint8_t)(lane * 8 + q);
+                }
+                nm = __shfl_sync(kFull, x, 31);
+                __syncwarp();
+            }
+            const bool dense = nm > 96;
+            const int E = dense ? 8 : (nm + 31) >> 5;
+            float S[8], S2[8];
+            int K[8];
+            float ps = 0.0f, ps2 = 0.0f, sa = 0.0f;
+            int pk = 0;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                lo[q] = __int_as_float(0x7f800000);
+                binq[q] = -1;
+                if (q < E) {
+                    if (dense) binq[q] = lane * 8 + q;
+                    else if (lane * E + q < nm) binq[q] = BL[lane * E + q];
+                }
+                S[q] = S2[q] = 0.0f;
+                K[q] = 0;
+                if (binq[q] >= 0) {
+                    const float4 h = HE[binq[q]];
+                    S[q] = h.x;
+                    S2[q] = h.y;
+                    K[q] = (int)h.z;
+                }
+                sa += fabsf(S[q]);
+                ps += S[q];
+                ps2 += S2[q];
+                pk += K[q];
+                S[q] = ps;
+                S2[q] = ps2;
+                K[q] = K[q] > 0 ? pk : -1;
+            }
+            const float is = warp_incl_scan(ps, lane), is2 = warp_incl_scan(ps2, lane);
+            const int ik = warp_incl_scan(pk, lane);
+            const float es = is - ps, es2 = is2 - ps2;
+            const int ek = ik - pk;
+            const float tot = __shfl_sync(kFull, is, 31), tot2 = __shfl_sync(kFull, is2, 31);
+            const float A = warp_sum_f(sa);
+            const float d = (float)(2 * nm + 64) * 0x1p-24f;
+            const float dA = d * A, dA2 = d * fabsf(tot2) * 1.001f;
+            const float rtt = __frcp_rn((float)c);
+            float hmin = __int_as_float(0x7f800000);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                if (K[q] < 0) continue;
+                const int kc = ek + K[q];
+                if (kc >= c) continue;
+                const float Lh = es + S[q], L2h = es2 + S2[q];
+                const float Rh = tot - Lh, R2h = tot2 - L2h;
+                const float rcl = __frcp_rn((float)kc), rcr = __frcp_rn((float)(c - kc));
+                const float t1 = Lh * Lh * rcl, t2 = Rh * Rh * rcr, P = L2h + R2h;
+                const float mse = (P - t1 - t2) * rtt;
+                const float pert = (2.0f * dA2 + (2.0f * fabsf(Lh) + 3.0f * dA) * dA * rcl +
+                                    (2.0f * fabsf(Rh) + 3.0f * dA) * dA * rcr) * rtt;
+                const float Q = (fabsf(P) + t1 + t2) * rtt + pert;
+                const float Eb = 1.25f * (pert + 0x1p-19f * Q) + 1e-30f;
+                lo[q] = mse - Eb;
+                hmin = fminf(hmin, mse + Eb);
+            }
+            hmin = warp_min_f(hmin);
+            if (lane == 0 && hmin < __int_as_float(0x7f800000)) atomicMin(umin, ord_of(hmin));
+        }
+        // every consumer's bound is in umin (a bounded wait, so that no warp can hang here)
+        __syncwarp();
+        if (lane == 0) pipe_arrive(cons);
+        if (!pipe_wait(cons, (unsigned)(it & 1))) {
+            atomicExch(&B.counters[3], 1);
+            return;
+        }
+        if (cw == 0 && lane == 0) s_umin[(it + 1) & 1] = 0xffffffffu;
+        if (!active) continue;
+        const unsigned uo = *umin;
+        if (uo == 0xffffffffu) continue;
+        const float thr = float_of(uo);
+        bool any = false;
+        int bmax = -1;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const bool cq = binq[q] >= 0 && lo[q] <= thr;
+            if (binq[q] >= 0) CF[binq[q]] = cq ? 1 : 0;
+            if (cq) { any = true; bmax = max(bmax, binq[q]); }
+        }
+        if (!__any_sync(kFull, any)) continue;
+        bmax = __reduce_max_sync(kFull, (unsigned)(bmax + 1)) - 1;
+        __syncwarp();
+        if (lane == 0) {
+            // the reference's serial chains over the non-empty bins (empty bins add +0)
+            float tot = 0.0f, tot2 = 0.0f;
+            for (int j = 0; j < nm; ++j) {
+                const float4 h = HE[BL[j]];
+                tot += h.x;
+                tot2 += h.y;
+            }
+            float L = 0.0f, R = tot, L2 = 0.0f, R2 = tot2;
+            int kc = 0;
+            unsigned long long best = kNoKey;
+            for (int j = 0; j < nm; ++j) {
+                const int bb = BL[j];
+                if (bb > bmax) break;
+                const float4 h = HE[bb];
+                kc += (int)h.z;
+                L += h.x;
+                R -= h.x;
+                L2 += h.y;
+                R2 -= h.y;
+                if (CF[bb]) {
+                    best = min(best, regr_key(L, R, L2, R2, kc, c, ((uint32_t)mv << 8) | (uint32_t)bb));
+                    if (B.diag) atomicAdd(&B.diag[0], 1ull);
+                }
+            }
+            if (best != kNoKey) atomicMin(&B.nd_key[m], best);
+        }
+        __syncwarp();
+    }
+}
+
 __global__ void __launch_bounds__(512, 2) k_hist_warp_regr(Data D, Batch B, int cur, HistArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ unsigned s_umin[2];

@@ -338,6 +338,8 @@ struct HistCfg {
     int threads, smem, grid;
     int small_warp_bytes, small_smem, small_grid;  // k_hist_small (classification)
     int lane_slots, lane_grid, lane_bytes;         // k_hist_lane (regression)
+    rfx::PipeArgs pa;                              // k_hist_pipe (regression)
+    int pipe_threads = 0, pipe_smem = 0, pipe_grid = 0;
 };
 
 HistCfg hist_cfg(Ctx& c) {
@@ -364,6 +366,24 @@ HistCfg hist_cfg(Ctx& c) {
         RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist_warp_class, h.threads, h.smem));
     }
     h.grid = c.sm_count * std::max(1, per_sm);
+    // k_hist_pipe (regression): a producer warp + up to 16 consumer warps, a ring of four
+    // 64-row chunks; RFX_HIST_PIPE=0 keeps k_hist_warp
+    const char* pe = std::getenv("RFX_HIST_PIPE");
+    if (regr && !(pe && pe[0] == '0')) {
+        h.pa.warps = std::min(16, mtry);
+        h.pa.groups = (mtry + h.pa.warps - 1) / h.pa.warps;
+        h.pa.ch = 64;
+        h.pa.rstride = c.D.rs + 16;
+        h.pipe_threads = 32 * (h.pa.warps + 1);
+        h.pipe_smem = 128 + 4 * h.pa.ch * h.pa.rstride + h.pa.warps * (256 * 16 + 512);
+        if (h.pipe_smem <= 220 * 1024) {
+            RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist_pipe, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          h.pipe_smem));
+            RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist_pipe,
+                                                                   h.pipe_threads, h.pipe_smem));
+            h.pipe_grid = c.sm_count * std::max(1, per_sm);
+        }
+    }
     // k_hist_small (classification): bin list, set words, class prefixes + totals
     h.small_warp_bytes = (int)round_up(256 + 64 + (257 * c.nclass) * 4, 16);
     h.small_smem = 8 * h.small_warp_bytes;
@@ -521,6 +541,9 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
             rfx::k_srch_scan<<<1, 1024, 0, st>>>(B);
             if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev_hist[2 * k], st));
             if (c.nclass == 1) {
+                if (hc.pipe_grid > 0)
+                rfx::k_hist_pipe<<<hc.pipe_grid, hc.pipe_threads, hc.pipe_smem, st>>>(D, B, cl, hc.pa);
+            else
                 rfx::k_hist_warp_regr<<<hc.grid, hc.threads, hc.smem, st>>>(D, B, cl, hc.a);
                 if (hc.lane_grid > 0)
                     rfx::k_hist_lane<<<hc.lane_grid, 32, hc.lane_bytes, st>>>(D, B, cl, hc.lane_slots);
@@ -537,6 +560,8 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
         }
         RFX_CUDA(cudaMemcpyAsync(c.h_counters, B.counters, c.level_log ? 80 : 32, cudaMemcpyDeviceToHost, st));
         RFX_CUDA(cudaStreamSynchronize(st));
+        require(c.h_counters[3] == 0, RFX_ERR_DEVICE,
+                "a histogram pipeline wait timed out (the kernel stopped and reported it)");
         const int real = std::min(level, c.h_counters[7]);  // levels so far that had nodes
         if (c.profiling) {
             for (int k = 0; k < real - lv0; ++k) {
@@ -709,8 +734,18 @@ int rfx_grow(void* ctx, int tree_begin, int ntree, rfx_trees* out) {
         for (int b0 = 0; b0 < ntree; b0 += c.Tcap) {
             const int T = std::min(c.Tcap, ntree - b0);
             grow_batch(c, tree_begin + b0, T, out, b0);
+            c.trees_done += T;
+            if (c.progress && c.progress(c.progress_user, b0 + T, ntree) != 0)
+                throw RfxError(RFX_ERR_CANCELLED, "stopped by the progress callback");
         }
-        c.trees_done += ntree;
+    });
+}
+
+int rfx_set_progress(void* ctx, rfx_progress_fn fn, void* user) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        c.progress = fn;
+        c.progress_user = user;
     });
 }
 
@@ -821,7 +856,11 @@ int rfx_prox_finish(void* ctx, const int* upper_dev, const int* nout_dev, int R,
         require(upper_dev && nout_dev && out_dev, RFX_ERR_ARG, "null pointer");
         require(R >= 1 && row_begin >= 0 && row_begin <= row_end && row_end <= R, RFX_ERR_ARG,
                 "bad row range");
-        RFX_CUDA(rfx::launch_prox_finish(upper_dev, nout_dev, R, row_begin, row_end, out_dev, c.st));
+        if (row_begin == 0 && row_end == R)
+            RFX_CUDA(rfx::launch_prox_finish_full(upper_dev, nout_dev, R,
+                                                  (double*)c.fin_inv.get((size_t)R * 8), out_dev, c.st));
+        else
+            RFX_CUDA(rfx::launch_prox_finish(upper_dev, nout_dev, R, row_begin, row_end, out_dev, c.st));
         RFX_CUDA(cudaStreamSynchronize(c.st));
     });
 }
@@ -853,7 +892,11 @@ int rfx_prox_dense(void* ctx, int row_begin, int row_end, float* out_host) {
         for (int r0 = row_begin; r0 < row_end; r0 += rows_per) {
             const int r1 = std::min(row_end, r0 + rows_per);
             const long long total = (long long)(r1 - r0) * R;
-            RFX_CUDA(rfx::launch_prox_finish(c.prox, (const int*)c.nout.p, R, r0, r1, tmp, c.st));
+            if (r0 == 0 && r1 == R)  // the whole matrix in one pass: tile pairs
+                RFX_CUDA(rfx::launch_prox_finish_full(c.prox, (const int*)c.nout.p, R,
+                                                      (double*)c.fin_inv.get((size_t)R * 8), tmp, c.st));
+            else
+                RFX_CUDA(rfx::launch_prox_finish(c.prox, (const int*)c.nout.p, R, r0, r1, tmp, c.st));
             RFX_CUDA(cudaMemcpyAsync(out_host + (size_t)(r0 - row_begin) * R, tmp, (size_t)total * 4,
                                      cudaMemcpyDeviceToHost, c.st));
             RFX_CUDA(cudaStreamSynchronize(c.st));

@@ -28,6 +28,7 @@ __global__ void k_partition_big(Data D, Batch B, int cur);
 // rfx_hist.cu
 __global__ void k_hist_warp_regr(Data D, Batch B, int cur, HistArgs a);
 __global__ void k_hist_warp_class(Data D, Batch B, int cur, HistArgs a);
+__global__ void k_hist_pipe(Data D, Batch B, int cur, PipeArgs a);
 __global__ void k_hist_lane(Data D, Batch B, int cur, int slots);
 __global__ void k_hist_small(Data D, Batch B, int cur, int warp_bytes);
 
@@ -50,6 +51,9 @@ __global__ void k_prox_finish(const int* C, const int* nout, int R, int r0, int 
 // k_prox_finish over rows [r0, r1) with its tile grid.
 cudaError_t launch_prox_finish(const int* C, const int* nout, int R, int r0, int r1, float* out,
                                cudaStream_t st);
+// The whole R x R finished matrix (tile pairs; inv: R doubles of scratch for 1 / nout).
+cudaError_t launch_prox_finish_full(const int* C, const int* nout, int R, double* inv, float* out,
+                                    cudaStream_t st);
 // k_prox_finish_packed (with the 1 / nout scales) over the packed elements [e0, e0 + len).
 cudaError_t launch_prox_finish_packed(const int* C, long long e0, long long len, const int* nout,
                                       int R, double* inv, float* out, cudaStream_t st);

@@ -559,6 +559,74 @@ __global__ void k_inv_nout(const int* __restrict__ nout, int R, double* __restri
         inv[i] = nout[i] > 0 ? 1.0 / (double)nout[i] : 1.0;
 }
 
+// The whole R x R finished matrix from tile pairs: block (bi <= bj) reads the counts of the
+// upper tile (rows of tile bi, columns of tile bj) once -- rows of the packed triangle, so
+// the loads coalesce -- and writes them finished to both the tile and its mirror (the
+// mirror's rows through a shared-memory transpose); diagonal tiles fill both halves and the
+// unit diagonal.  Per element the double operations of k_prox_finish; inv = 1 / nout.
+__global__ void __launch_bounds__(256) k_prox_finish_full(const int* __restrict__ C,
+                                                          const double* __restrict__ inv, int R,
+                                                          int nb, float* __restrict__ out) {
+    __shared__ float tile[kFinTile][kFinTile + 1];
+    __shared__ double sc_i[kFinTile], sc_j[kFinTile];
+    __shared__ long long rowbase[kFinTile];
+    // pair index -> (bi, bj), bi <= bj, row-major over the upper triangle of tiles
+    const long long pidx = blockIdx.x;
+    int bi = (int)((2.0 * nb + 1 - sqrt((2.0 * nb + 1) * (2.0 * nb + 1) - 8.0 * (double)pidx)) / 2.0);
+    bi = max(0, min(bi, nb - 1));
+    auto first = [&](int b) { return (long long)b * nb - (long long)b * (b - 1) / 2; };
+    while (bi > 0 && first(bi) > pidx) --bi;
+    while (bi + 1 < nb && first(bi + 1) <= pidx) ++bi;
+    const int bj = bi + (int)(pidx - first(bi));
+    const int i0 = bi * kFinTile, j0 = bj * kFinTile;
+    const long long R2 = 2LL * R;
+    const int tid = threadIdx.x;
+    if (tid < kFinTile) {
+        const int i = i0 + tid;
+        sc_i[tid] = i < R ? inv[i] : 1.0;
+        rowbase[tid] = (long long)i * (R2 - i - 1) / 2 - i - 1;  // + j = packed index of (i, j)
+    } else if (tid < 2 * kFinTile) {
+        const int j = j0 + tid - kFinTile;
+        sc_j[tid - kFinTile] = j < R ? inv[j] : 1.0;
+    }
+    __syncthreads();
+    const bool diag = bi == bj;
+    for (int e = tid; e < kFinTile * kFinTile; e += blockDim.x) {
+        const int ii = e / kFinTile, jj = e % kFinTile;
+        const int i = i0 + ii, j = j0 + jj;
+        if (i >= R || j >= R) continue;
+        float v;
+        if (i == j) {
+            v = 1.0f;
+        } else if (diag && j < i) {
+            continue;  // written as the mirror of (j, i)
+        } else {
+            const double h = (double)C[rowbase[ii] + j] / 2.0;
+            v = (float)(0.5 * (h * sc_i[ii] + h * sc_j[jj]));
+        }
+        tile[ii][jj] = v;
+        out[(size_t)i * R + j] = v;
+    }
+    __syncthreads();
+    for (int e = tid; e < kFinTile * kFinTile; e += blockDim.x) {
+        const int jj = e / kFinTile, ii = e % kFinTile;  // consecutive threads: row j, ascending i
+        const int i = i0 + ii, j = j0 + jj;
+        if (i >= R || j >= R || i >= j) continue;
+        out[(size_t)j * R + i] = tile[ii][jj];
+    }
+}
+
+cudaError_t launch_prox_finish_full(const int* C, const int* nout, int R, double* inv, float* out,
+                                    cudaStream_t st) {
+    if (R <= 0) return cudaSuccess;
+    k_inv_nout<<<(R + 255) / 256, 256, 0, st>>>(nout, R, inv);
+    const int nb = (R + kFinTile - 1) / kFinTile;
+    const long long pairs = (long long)nb * (nb + 1) / 2;
+    k_prox_finish_full<<<(unsigned)pairs, 256, 0, st>>>(C, inv, R, nb, out);
+    return cudaGetLastError();
+}
+
+
 // Finished values of the packed upper-triangle elements [e0, e0 + len), element e = (i, j),
 // e = i (2R - i - 1) / 2 + (j - i - 1): the same double operations as k_prox_finish, which
 // only need C_ij and the two row scales -- so a rank finishes its own slice of a

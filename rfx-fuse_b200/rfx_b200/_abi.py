@@ -15,7 +15,7 @@ LIB_PATH = os.path.join(HERE, "librfx_b200.so")
 
 RFX_OK = 0
 ERRORS = {-1: "RFX_ERR_ARG", -2: "RFX_ERR_CUDA", -3: "RFX_ERR_OOM", -4: "RFX_ERR_UNSUPPORTED",
-          -5: "RFX_ERR_STATE", -6: "RFX_ERR_DEVICE"}
+          -5: "RFX_ERR_STATE", -6: "RFX_ERR_DEVICE", -7: "RFX_ERR_CANCELLED"}
 TASK_CLASSIFICATION, TASK_REGRESSION, TASK_UNSUPERVISED = 0, 1, 2
 
 _pi = C.POINTER(C.c_int)
@@ -65,7 +65,7 @@ SYMBOLS = (
     "rfx_last_error", "rfx_abi_version", "rfx_device_count", "rfx_create", "rfx_destroy",
     "rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
     "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish", "rfx_prox_dense",
-    "rfx_prox_finish_packed", "rfx_reset_forest", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host", "rfx_get_stream",
+    "rfx_prox_finish_packed", "rfx_reset_forest", "rfx_set_progress", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host", "rfx_get_stream",
     "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats", "rfx_sync",
     "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk", "rfx_lowrank_product",
     "rfx_prox_apply", "rfx_lowrank_set_factors", "rfx_load_forest", "rfx_predict",
@@ -77,6 +77,8 @@ SYMBOLS = (
 
 # int (*)(void* user, float* buf_dev, int64_t count): in-place sum over processes
 REDUCE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_int64)
+# int (*)(void* user, int trees_done, int ntree): progress between batches; nonzero stops
+PROGRESS_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_int, C.c_int)
 
 _LIB = None
 
@@ -119,6 +121,7 @@ def load_library(path: str = LIB_PATH):
     L.rfx_prox_dense.argtypes = [vp, C.c_int, C.c_int, _pf]
     L.rfx_prox_finish_packed.argtypes = [vp, vp, C.c_int64, C.c_int64, vp, C.c_int, vp]
     L.rfx_reset_forest.argtypes = [vp]
+    L.rfx_set_progress.argtypes = [vp, PROGRESS_FN, vp]
     L.rfx_oob_fold.argtypes = [vp, vp]
     L.rfx_votes_to_q.argtypes = [vp, vp, _pf, C.c_int, C.c_int, vp]
     L.rfx_copy_to_host.argtypes = [vp, vp, vp, C.c_size_t]
@@ -152,7 +155,7 @@ def load_library(path: str = LIB_PATH):
     L.rfx_predict_outlier_scores.argtypes = [vp, _pf, C.c_int, C.c_int, C.c_int, C.c_int, _pi, _pf]
     for name in ("rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
                  "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish",
-                 "rfx_prox_finish_packed", "rfx_reset_forest", "rfx_prox_dense", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host",
+                 "rfx_prox_finish_packed", "rfx_reset_forest", "rfx_set_progress", "rfx_prox_dense", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host",
                  "rfx_get_stream", "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats",
                  "rfx_sync", "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk",
                  "rfx_lowrank_product", "rfx_prox_apply", "rfx_lowrank_set_factors",
@@ -211,6 +214,21 @@ class Context:
     def grow(self, tree_begin: int, ntree: int, trees: Trees | None = None):
         check(self._lib.rfx_grow(self.handle, tree_begin, ntree,
                                  C.byref(trees) if trees is not None else None))
+
+    def set_progress(self, fn=None):
+        """fn(trees_done, ntree) -> truthy to stop, called between batches; None removes it."""
+        if fn is None:
+            self._progress = None
+            check(self._lib.rfx_set_progress(self.handle, PROGRESS_FN(0), None))
+            return
+
+        def _cb(_user, done, total):
+            try:
+                return 1 if fn(int(done), int(total)) else 0
+            except Exception:  # a failing callback stops the fit rather than crash it
+                return 1
+        self._progress = PROGRESS_FN(_cb)  # kept alive while registered
+        check(self._lib.rfx_set_progress(self.handle, self._progress, None))
 
     def reset_forest(self):
         check(self._lib.rfx_reset_forest(self.handle))

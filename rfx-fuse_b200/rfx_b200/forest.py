@@ -4,9 +4,10 @@ RandomForestClassifier / RandomForestRegressor / RandomForestUnsupervised keep t
 reference constructor arguments and defaults, and resolve them the same way
 (python/randomforest_py.cpp:1270-1320, 1367-1500, 3066-3240, 4628-5040).  ``fit`` runs the
 whole forest on the GPU through librfx_b200.so; the getters return what the reference's
-getters return.  Arguments that only select among the reference's own implementations
-(use_gpu, use_sparse, gpu_loss_function, show_progress, ...) are accepted and ignored:
-there is one implementation here, the device one.
+getters return.  ``show_progress`` draws the reference's tqdm bar (one update per batch of
+trees).  Arguments that only select among the reference's own implementations (use_gpu,
+use_sparse, gpu_loss_function, ...) are accepted and ignored: there is one implementation
+here, the device one.
 """
 from __future__ import annotations
 
@@ -123,6 +124,7 @@ class _Forest:
         self.prox_rows = int(prox_rows)
         self.batch_trees = int(batch_trees)
         self.nodesize = int(nodesize)  # stored, never read by the growers (as in the reference)
+        self.show_progress, self.progress_desc = bool(show_progress), str(progress_desc)
         # stored as given, for the model file (model_io): not used by the device path
         self.ncsplit, self.ncmax = int(ncsplit), int(ncmax)
         self.use_gpu, self.use_sparse = bool(use_gpu), bool(use_sparse)
@@ -138,6 +140,19 @@ class _Forest:
         self._mtry = self._resolve_mtry_ctor(int(mtry))
         self._ctx = None
         self._fitted = False
+
+    def _progress_bar(self, total):
+        """The reference wrapper's tqdm bar (python/randomforest_py.cpp:1560-1600), or None."""
+        if not self.show_progress:
+            return None
+        try:
+            import tqdm
+        except ImportError:
+            return None
+        return tqdm.tqdm(total=total, desc=self.progress_desc, unit="tree", unit_scale=False,
+                         leave=False, dynamic_ncols=True, miniters=1,
+                         bar_format="{desc}: {percentage:3.0f}%|{bar}| {n}/{total} {unit} "
+                                    "[{elapsed}<{remaining}, {rate_fmt}]")
 
     # ---- resolution rules of the reference wrappers
     def _resolve_mtry_ctor(self, mtry):
@@ -191,7 +206,18 @@ class _Forest:
             None, None, A.ptr(tr["tree_rr"], A._pf), A.ptr(tr["tree_used"], A._pu8))
         ctx = self._context()
         ctx.load(prm, inp)
-        ctx.grow(0, T, trees)
+        bar = self._progress_bar(T)
+        try:
+            if bar is not None:
+                def _update(done, _total):
+                    bar.update(done - bar.n)
+                    return False
+                ctx.set_progress(_update)
+            ctx.grow(0, T, trees)
+        finally:
+            if bar is not None:
+                ctx.set_progress(None)
+                bar.close()
         ncl = {A.TASK_REGRESSION: 1, A.TASK_UNSUPERVISED: 2}.get(task)
         if ncl is None:
             ncl = len(np.unique(ycls))
