@@ -484,7 +484,7 @@ __device__ __forceinline__ unsigned pipe_smem(const void* p) {
 }
 __device__ __forceinline__ unsigned long long pipe_now() {
     unsigned long long t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
 __device__ __forceinline__ void pipe_init(uint64_t* b, unsigned count) {
