@@ -176,6 +176,8 @@ struct Batch {
     int* srch_big;    // [T][M] searched nodes above small_node_limit rows, in node order
     int* srch_big_cnt;  // [T]
     int* srch_big_off;  // [T+1]
+    int4* big_rec;    // flat over the level's big searched nodes: {tree, node, start, rows}
+    int4* sml_rec;    // the same for the small searched nodes
     int* srch_sml;    // [T][M] searched nodes of at most small_node_limit rows; total in counters[6]
     int* srch_sml_cnt;  // [T]
     int* srch_sml_off;  // [T+1]

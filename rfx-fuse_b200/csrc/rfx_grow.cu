@@ -310,6 +310,21 @@ __global__ void __launch_bounds__(1024) k_srch_scan(Batch B) {
     }
 }
 
+// Flat task records of the level's big and small searched nodes (one block per tree), so
+// that the histogram kernels find a task's tree, node, segment start and size with one load.
+__global__ void __launch_bounds__(256) k_task_records(Batch B) {
+    const int t = blockIdx.x;
+    const size_t base = (size_t)t * B.M;
+    const int nb = B.srch_big_cnt[t], ns = B.srch_sml_cnt[t];
+    for (int i = threadIdx.x; i < nb + ns; i += blockDim.x) {
+        const bool big = i < nb;
+        const int node = big ? B.srch_big[base + i] : B.srch_sml[base + (i - nb)];
+        const int4 r = make_int4(t, node, B.nd_start[base + node], B.nd_cnt[base + node]);
+        if (big) B.big_rec[B.srch_big_off[t] + i] = r;
+        else B.sml_rec[B.srch_sml_off[t] + (i - nb)] = r;
+    }
+}
+
 // ---------------------------------------------------------------------------------------
 // Commit the level (one block per tree, nodes in id order): accept rule
 // (src/rf_growtree.cpp:1000-1028), child ids under the maxnode cap (:1030-1045, :1066-1073),

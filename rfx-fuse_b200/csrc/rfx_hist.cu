@@ -194,10 +194,9 @@ __device__ __forceinline__ void hist_warp(const Data& D, const Batch& B, int cur
     int it = 0;
     for (int task = blockIdx.x; task < total; task += gridDim.x, ++it) {
         const int si = task / a.groups, grp = task - si * a.groups;
-        const int t = tree_of(B.srch_big_off, B.T, si);
-        const int node = B.srch_big[(size_t)t * B.M + (si - B.srch_big_off[t])];
+        const int4 rec = B.big_rec[si];  // {tree, node, start, rows}
+        const int t = rec.x, node = rec.y, start = rec.z, c = rec.w;
         const size_t m = (size_t)t * B.M + node;
-        const int start = B.nd_start[m], c = B.nd_cnt[m];
         const int* seg = B.seg[cur] + (size_t)t * D.N + start;
         const int mv = grp * a.warps + wib;
         const bool active = mv < B.mtry;
@@ -517,15 +516,6 @@ __device__ __forceinline__ void pipe_arrive_on_copies(uint64_t* b) {
 }
 __device__ __forceinline__ void pipe_wait_copies() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// Node of histogram task `task` (a.groups tasks per big searched node).
-__device__ __forceinline__ void pipe_task(const Batch& B, int task, int groups, int& t, int& node,
-                                          int& grp) {
-    const int si = task / groups;
-    grp = task - si * groups;
-    t = tree_of(B.srch_big_off, B.T, si);
-    node = B.srch_big[(size_t)t * B.M + (si - B.srch_big_off[t])];
-}
-
 __global__ void __launch_bounds__(544, 2) k_hist_pipe(Data D, Batch B, int cur, PipeArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -551,39 +541,55 @@ __global__ void __launch_bounds__(544, 2) k_hist_pipe(Data D, Batch B, int cur, 
     if (warp == 0) {
         // ---- producer: lane l copies rows l and l + 32 of each chunk (16-byte pieces); the
         // next chunk's row ids are loaded while the current chunk's copies are issued
-        for (int task = blockIdx.x; task < total; task += gridDim.x) {
-            int t, node, grp;
-            pipe_task(B, task, a.groups, t, node, grp);
-            const size_t m = (size_t)t * B.M + node;
-            const int c = B.nd_cnt[m];
-            const int* seg = B.seg[cur] + (size_t)t * D.N + B.nd_start[m];
-            int r0 = lane < c ? __ldg(seg + lane) : -1;
-            int r1 = lane + 32 < min(c, ch) ? __ldg(seg + 32 + lane) : -1;
-            for (int c0 = 0; c0 < c; c0 += ch, ++g) {
-                const int b = (int)(g % kPipeBufs);
-                const long long u = g / kPipeBufs;
-                const int n1 = c0 + ch < c ? min(ch, c - c0 - ch) : 0;  // rows of the next chunk
-                const int q0 = lane < n1 ? __ldg(seg + c0 + ch + lane) : -1;
-                const int q1 = lane + 32 < n1 ? __ldg(seg + c0 + ch + 32 + lane) : -1;
-                if (u > 0 && !pipe_wait(&empty[b], (unsigned)((u - 1) & 1))) {
-                    atomicExch(&B.counters[3], 1);
-                    pipe_wait_copies();
-                    return;
-                }
-                uint8_t* dst = ring + (size_t)b * ch * RS + (size_t)lane * RS;
-                if (r0 >= 0) {
-                    const uint8_t* src = D.rows + (size_t)r0 * rs;
-                    for (int pc = 0; pc < pieces; ++pc) pipe_copy16(dst + 16 * pc, src + 16 * pc);
-                }
-                if (r1 >= 0) {
-                    const uint8_t* src = D.rows + (size_t)r1 * rs;
-                    for (int pc = 0; pc < pieces; ++pc)
-                        pipe_copy16(dst + (size_t)32 * RS + 16 * pc, src + 16 * pc);
-                }
-                pipe_arrive_on_copies(&full[b]);
-                r0 = q0;
-                r1 = q1;
+        // one flat sequence of chunks over the block's tasks; the next chunk's row ids (the
+        // next task's first chunk at a task's end) load while this chunk's copies issue
+        auto rec_of = [&](int task) {
+            return task < total ? B.big_rec[task / a.groups] : make_int4(0, 0, 0, 0);
+        };
+        auto ids = [&](const int4& r, int c0, int& q0, int& q1) {
+            const int n = min(ch, r.w - c0);
+            const int* seg = B.seg[cur] + (size_t)r.x * D.N + r.z + c0;
+            q0 = lane < n ? __ldg(seg + lane) : -1;
+            q1 = lane + 32 < n ? __ldg(seg + 32 + lane) : -1;
+        };
+        int task = blockIdx.x, c0 = 0;
+        int4 rec = rec_of(task);
+        int r0 = -1, r1 = -1;
+        if (task < total) ids(rec, 0, r0, r1);
+        while (task < total) {
+            int ntask = task, nc0 = c0 + ch;
+            int4 nrec = rec;
+            if (nc0 >= rec.w) {
+                ntask = task + gridDim.x;
+                nc0 = 0;
+                nrec = rec_of(ntask);
             }
+            int q0 = -1, q1 = -1;
+            if (ntask < total) ids(nrec, nc0, q0, q1);
+            const int b = (int)(g % kPipeBufs);
+            const long long u = g / kPipeBufs;
+            if (u > 0 && !pipe_wait(&empty[b], (unsigned)((u - 1) & 1))) {
+                atomicExch(&B.counters[3], 1);
+                pipe_wait_copies();
+                return;
+            }
+            uint8_t* dst = ring + (size_t)b * ch * RS + (size_t)lane * RS;
+            if (r0 >= 0) {
+                const uint8_t* src = D.rows + (size_t)r0 * rs;
+                for (int pc = 0; pc < pieces; ++pc) pipe_copy16(dst + 16 * pc, src + 16 * pc);
+            }
+            if (r1 >= 0) {
+                const uint8_t* src = D.rows + (size_t)r1 * rs;
+                for (int pc = 0; pc < pieces; ++pc)
+                    pipe_copy16(dst + (size_t)32 * RS + 16 * pc, src + 16 * pc);
+            }
+            pipe_arrive_on_copies(&full[b]);
+            ++g;
+            task = ntask;
+            c0 = nc0;
+            rec = nrec;
+            r0 = q0;
+            r1 = q1;
         }
         pipe_wait_copies();
         return;
@@ -595,14 +601,27 @@ __global__ void __launch_bounds__(544, 2) k_hist_pipe(Data D, Batch B, int cur, 
     uint8_t* CF = BL + 256;
     const float tag0 = __uint_as_float(0xffffffffu);
     int it = 0;
+    // the drawn feature of a task (-1: this warp has no draw in it)
+    auto feat_of = [&](int task, const int4& r) {
+        const int mv_ = (task - (task / a.groups) * a.groups) * W + cw;
+        return (task < total && mv_ < B.mtry)
+                   ? (int)B.feat[(size_t)r.x * B.M * B.mtry + (size_t)r.y * B.mtry + mv_] : -1;
+    };
+    int4 nrec = blockIdx.x < total ? B.big_rec[blockIdx.x / a.groups] : make_int4(0, 0, 0, 0);
+    int nf = feat_of(blockIdx.x, nrec);
     for (int task = blockIdx.x; task < total; task += gridDim.x, ++it) {
-        int t, node, grp;
-        pipe_task(B, task, a.groups, t, node, grp);
+        const int4 rec = nrec;  // {tree, node, start, rows}; the next task's is prefetched
+        const int fcur = nf;
+        if (task + (int)gridDim.x < total) {
+            nrec = B.big_rec[(task + gridDim.x) / a.groups];
+            nf = feat_of(task + gridDim.x, nrec);
+        }
+        const int t = rec.x, node = rec.y, c = rec.w;
+        const int grp = task - (task / a.groups) * a.groups;
         const size_t m = (size_t)t * B.M + node;
-        const int c = B.nd_cnt[m];
         const int mv = grp * W + cw;
         const bool active = mv < B.mtry;
-        const int f = active ? (int)B.feat[(size_t)t * B.M * B.mtry + (size_t)node * B.mtry + mv] : 0;
+        const int f = active ? fcur : 0;
         unsigned* umin = &s_umin[it & 1];
         if (cw == 0 && lane == 0 && grp == 0 && B.hist_bytes)
             atomicAdd(B.hist_bytes, (unsigned long long)c * (unsigned long long)(B.mtry + 4));
@@ -843,12 +862,11 @@ __global__ void __launch_bounds__(32) k_hist_lane(Data D, Batch B, int cur, int 
     for (int g0 = blockIdx.x * slots; g0 < total; g0 += gridDim.x * slots) {
         int my_t = 0, my_node = 0, my_c = 0, my_start = 0;
         if (lane < slots && g0 + lane < total) {
-            const int si = g0 + lane;
-            my_t = tree_of(B.srch_sml_off, B.T, si);
-            my_node = B.srch_sml[(size_t)my_t * B.M + (si - B.srch_sml_off[my_t])];
-            const size_t mm = (size_t)my_t * B.M + my_node;
-            my_c = B.nd_cnt[mm];
-            my_start = B.nd_start[mm];
+            const int4 rec = B.sml_rec[g0 + lane];  // {tree, node, start, rows}
+            my_t = rec.x;
+            my_node = rec.y;
+            my_start = rec.z;
+            my_c = rec.w;
         }
         if (lane < slots) UM[lane] = 0u;
         // ---- stage: lanes take rows, every drawn feature's bin and the target (row ids of

@@ -111,6 +111,8 @@ void alloc_batch(Ctx& c, int Tcap) {
     B.srch_sml_off = B.srch_big_off + (T + 1);
     B.srch_big = (int*)c.b_srchbig.get(T * M * 4);
     B.srch_sml = (int*)c.b_srchsml.get(T * M * 4);
+    B.big_rec = (int4*)c.b_bigrec.get(T * M * 16);
+    B.sml_rec = (int4*)c.b_smlrec.get(T * M * 16);
     B.part_big = (long long*)c.b_partbig.get(T * (N / rfx::kBigSegment + 2) * 8);
     B.srch = (int*)c.b_srch.get(T * M * 4);
     B.srch_cnt = (int*)c.b_srchcnt.get(T * 12);
@@ -370,7 +372,9 @@ HistCfg hist_cfg(Ctx& c) {
     // 64-row chunks; RFX_HIST_PIPE=0 keeps k_hist_warp
     const char* pe = std::getenv("RFX_HIST_PIPE");
     if (regr && !(pe && pe[0] == '0')) {
-        h.pa.warps = std::min(16, mtry);
+        int pw = 16;
+        if (const char* e = std::getenv("RFX_PIPE_WARPS")) pw = std::max(1, std::min(16, std::atoi(e)));
+        h.pa.warps = std::min(pw, mtry);
         h.pa.groups = (mtry + h.pa.warps - 1) / h.pa.warps;
         h.pa.ch = 64;
         h.pa.rstride = c.D.rs + 16;
@@ -539,6 +543,7 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
             rfx::k_node_eval<<<gw, 256, 0, st>>>(D, B, cl);
             rfx::k_draw<<<T, 256, 0, st>>>(D, B);
             rfx::k_srch_scan<<<1, 1024, 0, st>>>(B);
+            rfx::k_task_records<<<T, 256, 0, st>>>(B);
             if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev_hist[2 * k], st));
             if (c.nclass == 1) {
                 if (hc.pipe_grid > 0)
@@ -556,7 +561,7 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
             rfx::k_partition<<<gw, 256, 0, st>>>(D, B, cl);
             rfx::k_partition_big<<<c.sm_count * 2, 256, 0, st>>>(D, B, cl);
             RFX_LAUNCH("level kernels");
-            c.launches += 9;
+            c.launches += 10;
         }
         RFX_CUDA(cudaMemcpyAsync(c.h_counters, B.counters, c.level_log ? 80 : 32, cudaMemcpyDeviceToHost, st));
         RFX_CUDA(cudaStreamSynchronize(st));

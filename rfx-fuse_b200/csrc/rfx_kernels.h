@@ -21,6 +21,7 @@ __global__ void k_level_begin(Batch B, int level);
 __global__ void k_node_eval(Data D, Batch B, int cur);
 __global__ void k_draw(Data D, Batch B);
 __global__ void k_srch_scan(Batch B);
+__global__ void k_task_records(Batch B);
 __global__ void k_commit(Data D, Batch B);
 __global__ void k_partition(Data D, Batch B, int cur);
 __global__ void k_partition_big(Data D, Batch B, int cur);
