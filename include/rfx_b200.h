@@ -180,7 +180,12 @@ int rfx_prox_dense(void* ctx, int row_begin, int row_end, float* out_host);
  * one fixed device array of RFX_STATIC_SCRATCH_FLOATS floats (16 MiB) that every GPU which
  * loads the library keeps until the process exits; R must not exceed that size (one row
  * has to fit), otherwise RFX_ERR_ARG.  The first call on a device looks up the array's
- * device address (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * device address (cudaGetSymbolAddress), so make that first call before any stream capture;
+ * with lazy module loading (CUDA's default) that first call is also when the 16 MiB are
+ * reserved, so a caller whose pool takes the whole budget should make it (a warm-up call)
+ * at start-up.  The address is kept for the life of the process: after cudaDeviceReset, or
+ * any teardown of the device's primary context, the kept address is stale and the function
+ * must not be called again in that process.
  * No cudaMalloc / cudaFree is called.  All calls share the array, which keeps the last
  * call's rows; it is fully rewritten before each use, so nothing needs clearing, but calls
  * that overlap on the GPU (other threads or streams) race on it.  Returns after the rows

@@ -448,8 +448,9 @@ Staging& staging() {
 void copy_d2h(Ctx& c, void* dst, const void* src, size_t bytes) {
     if (bytes == 0) return;
     cudaPointerAttributes at{};
-    const bool pinned = cudaPointerGetAttributes(&at, dst) == cudaSuccess && at.type == cudaMemoryTypeHost;
-    cudaGetLastError();  // the query's status is not an error of this context
+    const cudaError_t qe = cudaPointerGetAttributes(&at, dst);
+    if (qe != cudaSuccess) cudaGetLastError();  // only the query's own status is dropped
+    const bool pinned = qe == cudaSuccess && at.type == cudaMemoryTypeHost;
     constexpr size_t kChunk = (size_t)32 << 20;
     if (pinned || bytes < ((size_t)4 << 20)) {
         RFX_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, c.st));
@@ -458,8 +459,25 @@ void copy_d2h(Ctx& c, void* dst, const void* src, size_t bytes) {
     }
     Staging& sg = staging();
     std::lock_guard<std::mutex> lock(sg.mu);
-    if (!sg.buf[0])
-        for (int b = 0; b < 2; ++b) RFX_CUDA(cudaHostAlloc(&sg.buf[b], kChunk, cudaHostAllocPortable));
+    if (!sg.buf[0] || !sg.buf[1]) {
+        // both buffers or neither: allocate into locals and publish the pair
+        void* nb[2] = {nullptr, nullptr};
+        for (int b = 0; b < 2; ++b) {
+            const cudaError_t ae = cudaHostAlloc(&nb[b], kChunk, cudaHostAllocPortable);
+            if (ae != cudaSuccess) {
+                if (nb[0]) cudaFreeHost(nb[0]);
+                throw RfxError(RFX_ERR_OOM, std::string("cudaHostAlloc: ") + cudaGetErrorString(ae));
+            }
+        }
+        sg.buf[0] = nb[0];
+        sg.buf[1] = nb[1];
+    }
+    // on any exit, this context's copies into the shared buffers have finished before the
+    // lock is released
+    struct Drain {
+        cudaStream_t st;
+        ~Drain() { cudaStreamSynchronize(st); }
+    } drain{c.st};
     if (!c.ev_stage[0])
         for (int b = 0; b < 2; ++b) RFX_CUDA(cudaEventCreateWithFlags(&c.ev_stage[b], cudaEventDisableTiming));
     const size_t nch = (bytes + kChunk - 1) / kChunk;
