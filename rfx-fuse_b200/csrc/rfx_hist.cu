@@ -169,7 +169,8 @@ __device__ __forceinline__ T warp_incl_scan(T x, int lane) {
 //   classification  H int[nclass][256] (class-major counts, then inclusive prefixes) |
 //                   KC int[256] | BL u8[256] | TK int[32] (class totals)
 // ---------------------------------------------------------------------------------------
-constexpr int kWarpUnroll = 4;  // 32-row steps whose loads are in flight together
+constexpr int kWarpUnroll = 4;  // 32-row steps whose loads are in flight together (regression)
+constexpr int kWarpUnrollClass = 8;  // classification: rows mostly come from DRAM
 
 template <bool REGR>
 __device__ __forceinline__ void hist_warp(const Data& D, const Batch& B, int cur, const HistArgs& a,
@@ -218,17 +219,18 @@ __device__ __forceinline__ void hist_warp(const Data& D, const Batch& B, int cur
         if (active) {
             // ---- accumulate, 32 rows per step in row order (bins and targets gathered from
             // the packed rows; the loads of kWarpUnroll steps in flight together)
-            for (int s0 = 0; s0 < c; s0 += 32 * kWarpUnroll) {
-                int bb[kWarpUnroll];
-                uint2 tg[kWarpUnroll];
-                int r[kWarpUnroll];
+            constexpr int kU = REGR ? kWarpUnroll : kWarpUnrollClass;
+            for (int s0 = 0; s0 < c; s0 += 32 * kU) {
+                int bb[kU];
+                uint2 tg[kU];
+                int r[kU];
 #pragma unroll
-                for (int u = 0; u < kWarpUnroll; ++u) {
+                for (int u = 0; u < kU; ++u) {
                     const int i = s0 + u * 32 + lane;
                     r[u] = i < c ? __ldg(seg + i) : -1;
                 }
 #pragma unroll
-                for (int u = 0; u < kWarpUnroll; ++u) {
+                for (int u = 0; u < kU; ++u) {
                     bb[u] = -1;
                     tg[u] = make_uint2(0, 0);
                     if (r[u] >= 0) {
@@ -238,7 +240,7 @@ __device__ __forceinline__ void hist_warp(const Data& D, const Batch& B, int cur
                     }
                 }
 #pragma unroll
-                for (int u = 0; u < kWarpUnroll; ++u) {
+                for (int u = 0; u < kU; ++u) {
                     if (s0 + u * 32 >= c) break;
                     const int b = bb[u];
                     const bool valid = b >= 0;
