@@ -62,6 +62,14 @@ WORKLOAD = ("config[1]: regression n=200000 p=50 U(-1,1), ntree=500 forest, mtry
             "no proximity, maxnode=32001")
 
 
+# DRAM bytes (read + write) of one k_hist_pipe launch of a 250-tree level, measured once with
+# ncu (dram__bytes_read.sum + dram__bytes_write.sum; levels 0 and 9: 146.8 MB and 149.1 MB)
+# and carried here as a constant; the capture is summarised under profiles/.
+HIST_TRAFFIC_BYTES = 147.9e6
+HIST_TRAFFIC_SOURCE = ("ncu capture of k_hist_pipe, levels 0 and 9 of a 250-tree batch "
+                       "(146.8 MB, 149.1 MB per launch), constant")
+
+
 def make_data(n, p, seed=20261201 + 1):
     rng = np.random.default_rng(seed)
     X = rng.uniform(-1.0, 1.0, size=(n, p)).astype(np.float32)
@@ -361,7 +369,8 @@ def run_config1(args):
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": (achieved / peak) if achieved else None,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                     "traffic": None,
+                     "traffic": HIST_TRAFFIC_BYTES,
+                     "traffic_source": HIST_TRAFFIC_SOURCE,
                      "algorithmic_bytes_per_level": per_level_bytes,
                      "levels": int(st["hist_launches"]), "kernel_ms": st["hist_ms"],
                      "share_of_step": st["hist_ms"] / (ms * world) if ms else None},
