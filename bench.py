@@ -338,7 +338,9 @@ def run_config1(args):
         e2e_s = float(t.item())
     e2e_value = e2e_steps * T / e2e_s
     h2d = world * (Xp.nbytes + yp.nbytes + 4 * p)
-    d2h = T * M * 4 * 9 + T * 4 + T * p * 5 + n * 4 * 2 + p * 8
+    # what each fit copies back: node counts, per-tree importance rows (rr float + used
+    # byte), nout and the OOB sums, avimp and sqsd (the tree arrays stay on the device)
+    d2h = T * 4 + T * p * 5 + n * 4 * 2 + p * 8
 
     peak, peak_kind = measured_peaks()
     hist_s = st["hist_ms"] / 1000.0

@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define RFX_ABI_VERSION 3
+#define RFX_ABI_VERSION 4
 
 enum {
     RFX_OK = 0,
@@ -63,6 +63,8 @@ typedef struct {
     int keep_forest;        /* keep the grown trees on the device (packed) for rfx_predict */
     int keep_leaves;        /* compute_leaf_assignments: keep every row's terminal node per
                                tree and the per-tree OOB flags on the device (rfx_leaf_*) */
+    int keep_trees;         /* keep the tree arrays (reference layout) of every tree grown
+                               since the load on the device, for rfx_get_trees */
 } rfx_fit_params;
 
 typedef struct {
@@ -131,6 +133,13 @@ int rfx_reset_forest(void* ctx);
  * stops the call with RFX_ERR_CANCELLED after the batch.  NULL removes the callback. */
 typedef int (*rfx_progress_fn)(void* user, int trees_done, int ntree);
 int rfx_set_progress(void* ctx, rfx_progress_fn fn, void* user);
+
+/* Tree arrays of the trees [tree_begin, tree_begin + count) grown since rfx_load (or
+ * rfx_reset_forest), by position in growth order, from the device tree store that
+ * keep_trees fills (the reference's RandomForest members, src/rf_random_forest.cpp:358-452:
+ * the caller's host arrays).  Only nodestatus .. tnodewt are read from `out`; NULL
+ * pointers are skipped.  RFX_ERR_STATE when the fit did not keep its trees. */
+int rfx_get_trees(void* ctx, int tree_begin, int count, rfx_trees* out);
 
 /* Copy the accumulators to the host. */
 int rfx_results(void* ctx, rfx_accum* res);

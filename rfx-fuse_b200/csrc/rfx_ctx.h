@@ -104,6 +104,12 @@ struct Ctx {
     int trees_done = 0;
     int tree_oob_cap = 0, tree_oob_n = 0;
 
+    // device tree store (keep_trees): reference-layout arrays of the trees grown since the
+    // load, [ts_cap][maxnode] (treemap [ts_cap][2 maxnode], nnode [ts_cap])
+    DBuf ts_status, ts_bestvar, ts_xbest, ts_treemap, ts_nodeclass, ts_nnode, ts_nodepred,
+        ts_tnodewt;
+    int ts_cap = 0, ts_n = 0;
+
     // progress callback (rfx_set_progress), called between batches
     rfx_progress_fn progress = nullptr;
     void* progress_user = nullptr;
@@ -176,7 +182,8 @@ struct Ctx {
                        &p_xc, &p_vote, &p_val, &p_cls, &p_proba, &p_pred, &i_x, &i_miss, &i_cat,
                        &i_S, &i_scratch, &i_cells, &i_out, &i_prof, &l_leaf, &l_oob, &l_rows, &l_gs, &l_ge,
                        &l_keys, &l_cub, &l_cnt, &l_cidx, &l_cval, &l_nnz, &l_q, &l_out, &l_f,
-                       &lr_err, &lr_out_i, &lr_out_v};
+                       &lr_err, &lr_out_i, &lr_out_v, &ts_status, &ts_bestvar, &ts_xbest, &ts_treemap,
+                       &ts_nodeclass, &ts_nnode, &ts_nodepred, &ts_tnodewt};
         cudaSetDevice(device);
         if (st) cudaStreamSynchronize(st);
         for (DBuf* b : all) b->release();

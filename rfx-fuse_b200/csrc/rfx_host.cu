@@ -319,6 +319,7 @@ void load(Ctx& c, const rfx_fit_params* prm, const rfx_inputs* in) {
     c.trees_done = 0;
     c.tree_oob_n = 0;
     c.tree_oob_cap = 0;
+    c.ts_n = 0;
     // batch capacity
     size_t per_tree = N * 4 * 6 + (size_t)c.M * (4 * 12 + 2 * P.mtry + 16) + (size_t)p * 16;
     if (c.task == RFX_TASK_REGRESSION && P.compute_importance) per_tree += N * (size_t)(p + 1) * 4;
@@ -676,6 +677,23 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
     }
     if (c.lr_rank > 0) lr_store_batch(c, B, T);
     if (c.prm.keep_forest) forest_store_batch(c, B, T);
+    if (c.prm.keep_trees) {
+        // device-to-device into the tree store (the host copies only when asked)
+        const size_t o = (size_t)c.ts_n;
+        auto st_cp = [&](DBuf& dst, const void* src, size_t per) {
+            RFX_CUDA(cudaMemcpyAsync((char*)dst.p + o * per, src, (size_t)T * per,
+                                     cudaMemcpyDeviceToDevice, st));
+        };
+        st_cp(c.ts_status, B.status, M * 4);
+        st_cp(c.ts_bestvar, B.bestvar, M * 4);
+        st_cp(c.ts_xbest, B.xbest, M * 4);
+        st_cp(c.ts_treemap, B.treemap, 2 * M * 4);
+        st_cp(c.ts_nodeclass, B.nodeclass, M * 4);
+        st_cp(c.ts_nnode, B.nnode, 4);
+        st_cp(c.ts_nodepred, B.nodepred, M * 4);
+        st_cp(c.ts_tnodewt, B.tnodewt, M * 4);
+        c.ts_n += T;
+    }
     if (c.prm.keep_leaves) leaves_store_batch(c, B, T);
     if (keep) c.tree_oob_n += T;
     if (out) {
@@ -747,6 +765,8 @@ int rfx_load(void* ctx, const rfx_fit_params* prm, const rfx_inputs* in) {
     return guarded([&] { load(*as_ctx(ctx), prm, in); });
 }
 
+void trees_reserve(Ctx& c, int need);
+
 int rfx_grow(void* ctx, int tree_begin, int ntree, rfx_trees* out) {
     return guarded([&] {
         Ctx& c = *as_ctx(ctx);
@@ -754,6 +774,7 @@ int rfx_grow(void* ctx, int tree_begin, int ntree, rfx_trees* out) {
         require(tree_begin >= 0 && ntree >= 0, RFX_ERR_ARG, "bad tree range");
         lr_reserve(c, ntree);
         if (c.prm.keep_forest) forest_reserve(c, ntree);
+        if (c.prm.keep_trees) trees_reserve(c, c.ts_n + ntree);
         for (int b0 = 0; b0 < ntree; b0 += c.Tcap) {
             const int T = std::min(c.Tcap, ntree - b0);
             grow_batch(c, tree_begin + b0, T, out, b0);
@@ -790,7 +811,52 @@ int rfx_reset_forest(void* ctx) {
         c.lr_ready = false;
         c.trees_done = 0;
         c.tree_oob_n = 0;
+        c.ts_n = 0;
         RFX_CUDA(cudaStreamSynchronize(st));
+    });
+}
+
+// Room for `need` trees in the device tree store, keeping the stored ones.
+void trees_reserve(Ctx& c, int need) {
+    if (need <= c.ts_cap) return;
+    const int cap = std::max(need, 2 * c.ts_cap);
+    const size_t M = c.M;
+    DBuf* bufs[8] = {&c.ts_status, &c.ts_bestvar, &c.ts_xbest, &c.ts_treemap, &c.ts_nodeclass,
+                     &c.ts_nnode, &c.ts_nodepred, &c.ts_tnodewt};
+    const size_t per[8] = {M * 4, M * 4, M * 4, 2 * M * 4, M * 4, 4, M * 4, M * 4};
+    for (int k = 0; k < 8; ++k) {
+        DBuf nb;
+        nb.get((size_t)cap * per[k]);
+        if (c.ts_n > 0)
+            RFX_CUDA(cudaMemcpyAsync(nb.p, bufs[k]->p, (size_t)c.ts_n * per[k],
+                                     cudaMemcpyDeviceToDevice, c.st));
+        RFX_CUDA(cudaStreamSynchronize(c.st));
+        bufs[k]->release();
+        *bufs[k] = nb;
+        nb.p = nullptr;
+    }
+    c.ts_cap = cap;
+}
+
+int rfx_get_trees(void* ctx, int tree_begin, int count, rfx_trees* out) {
+    return guarded([&] {
+        Ctx& c = *as_ctx(ctx);
+        require(c.loaded && c.prm.keep_trees, RFX_ERR_STATE, "the fit did not keep its trees (keep_trees)");
+        require(out != nullptr && tree_begin >= 0 && count >= 0 && tree_begin + count <= c.ts_n,
+                RFX_ERR_ARG, "bad tree range");
+        const size_t M = c.M;
+        auto cp = [&](void* dst, const DBuf& src, size_t per) {
+            if (dst && count > 0)
+                copy_d2h(c, dst, (const char*)src.p + (size_t)tree_begin * per, (size_t)count * per);
+        };
+        cp(out->nodestatus, c.ts_status, M * 4);
+        cp(out->bestvar, c.ts_bestvar, M * 4);
+        cp(out->xbestsplit, c.ts_xbest, M * 4);
+        cp(out->treemap, c.ts_treemap, 2 * M * 4);
+        cp(out->nodeclass, c.ts_nodeclass, M * 4);
+        cp(out->nnode, c.ts_nnode, 4);
+        cp(out->nodepred, c.ts_nodepred, M * 4);
+        cp(out->tnodewt, c.ts_tnodewt, M * 4);
     });
 }
 

@@ -27,7 +27,7 @@ class FitParams(C.Structure):
     _fields_ = [(k, C.c_int) for k in (
         "task", "n", "p", "mtry", "minndsize", "maxnode", "iseed", "boot_seed", "nbins",
         "maxcat", "compute_importance", "compute_proximity", "prox_rows", "batch_trees",
-        "keep_tree_oob", "lowrank_rank", "keep_forest", "keep_leaves")]
+        "keep_tree_oob", "lowrank_rank", "keep_forest", "keep_leaves", "keep_trees")]
 
 
 class Inputs(C.Structure):
@@ -65,7 +65,8 @@ SYMBOLS = (
     "rfx_last_error", "rfx_abi_version", "rfx_device_count", "rfx_create", "rfx_destroy",
     "rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
     "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish", "rfx_prox_dense",
-    "rfx_prox_finish_packed", "rfx_reset_forest", "rfx_set_progress", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host", "rfx_get_stream",
+    "rfx_prox_finish_packed", "rfx_reset_forest", "rfx_set_progress", "rfx_get_trees",
+    "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host", "rfx_get_stream",
     "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats", "rfx_sync",
     "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk", "rfx_lowrank_product",
     "rfx_prox_apply", "rfx_lowrank_set_factors", "rfx_load_forest", "rfx_predict",
@@ -121,6 +122,7 @@ def load_library(path: str = LIB_PATH):
     L.rfx_prox_dense.argtypes = [vp, C.c_int, C.c_int, _pf]
     L.rfx_prox_finish_packed.argtypes = [vp, vp, C.c_int64, C.c_int64, vp, C.c_int, vp]
     L.rfx_reset_forest.argtypes = [vp]
+    L.rfx_get_trees.argtypes = [vp, C.c_int, C.c_int, C.POINTER(Trees)]
     L.rfx_set_progress.argtypes = [vp, PROGRESS_FN, vp]
     L.rfx_oob_fold.argtypes = [vp, vp]
     L.rfx_votes_to_q.argtypes = [vp, vp, _pf, C.c_int, C.c_int, vp]
@@ -155,7 +157,8 @@ def load_library(path: str = LIB_PATH):
     L.rfx_predict_outlier_scores.argtypes = [vp, _pf, C.c_int, C.c_int, C.c_int, C.c_int, _pi, _pf]
     for name in ("rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
                  "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish",
-                 "rfx_prox_finish_packed", "rfx_reset_forest", "rfx_set_progress", "rfx_prox_dense", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host",
+                 "rfx_prox_finish_packed", "rfx_reset_forest", "rfx_set_progress", "rfx_get_trees",
+                 "rfx_prox_dense", "rfx_oob_fold", "rfx_votes_to_q", "rfx_copy_to_host",
                  "rfx_get_stream", "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats",
                  "rfx_sync", "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk",
                  "rfx_lowrank_product", "rfx_prox_apply", "rfx_lowrank_set_factors",
@@ -229,6 +232,9 @@ class Context:
                 return 1
         self._progress = PROGRESS_FN(_cb)  # kept alive while registered
         check(self._lib.rfx_set_progress(self.handle, self._progress, None))
+
+    def get_trees(self, tree_begin: int, count: int, trees: "Trees"):
+        check(self._lib.rfx_get_trees(self.handle, int(tree_begin), int(count), C.byref(trees)))
 
     def reset_forest(self):
         check(self._lib.rfx_reset_forest(self.handle))

@@ -179,7 +179,7 @@ class _Forest:
                           int(self.compute_proximity), self.prox_rows, self.batch_trees, 0,
                           self._lowrank_rank(),
                           int(task != A.TASK_UNSUPERVISED or self.compute_leaf_assignments),
-                          int(self.compute_leaf_assignments))
+                          int(self.compute_leaf_assignments), 1)
         ycls = yreg = sw = cw = None
         if task == A.TASK_CLASSIFICATION:
             ycls = np.ascontiguousarray(y, dtype=np.int32)
@@ -193,17 +193,12 @@ class _Forest:
                        A.ptr(cat, A._pi), A.ptr(cw, A._pf))
         N = 2 * n if task == A.TASK_UNSUPERVISED else n
         T, M = self.ntree, maxnode
-        tr = {
-            "nodestatus": np.zeros((T, M), np.int32), "bestvar": np.zeros((T, M), np.int32),
-            "xbestsplit": np.zeros((T, M), np.float32), "treemap": np.zeros((T, 2 * M), np.int32),
-            "nodeclass": np.zeros((T, M), np.int32), "nnode": np.zeros(T, np.int32),
-            "nodepred": np.zeros((T, M), np.float32), "tnodewt": np.zeros((T, M), np.float32),
-            "tree_rr": np.zeros((T, p), np.float32), "tree_used": np.zeros((T, p), np.uint8),
-        }
-        trees = A.Trees(*[A.ptr(tr[k], t) for k, t in (
-            ("nodestatus", A._pi), ("bestvar", A._pi), ("xbestsplit", A._pf), ("treemap", A._pi),
-            ("nodeclass", A._pi), ("nnode", A._pi), ("nodepred", A._pf), ("tnodewt", A._pf))],
-            None, None, A.ptr(tr["tree_rr"], A._pf), A.ptr(tr["tree_used"], A._pu8))
+        # the tree arrays stay in the device tree store (keep_trees); trees_ fetches them on
+        # first use.  Only the node counts and the per-tree importance rows come back now.
+        tr = {"nnode": np.zeros(T, np.int32), "tree_rr": np.zeros((T, p), np.float32),
+              "tree_used": np.zeros((T, p), np.uint8)}
+        trees = A.Trees(None, None, None, None, None, A.ptr(tr["nnode"], A._pi), None, None,
+                        None, None, A.ptr(tr["tree_rr"], A._pf), A.ptr(tr["tree_used"], A._pu8))
         ctx = self._context()
         ctx.load(prm, inp)
         bar = self._progress_bar(T)
@@ -236,7 +231,8 @@ class _Forest:
         if self._lowrank_rank():
             ctx.lowrank_build(self.rank, self.lowrank_oversample, self.lowrank_power_iters,
                               seed=self.iseed)
-        self.trees_ = tr
+        self._trees = tr
+        self._trees_full = False
         self.acc_ = acc
         self.n_rows_ = N
         self.nclass_ = ncl
@@ -246,6 +242,32 @@ class _Forest:
         self._fitted = True
         self._finalize(y)
         return None
+
+    @property
+    def trees_(self):
+        """The forest's tree arrays in the reference layout ([ntree, maxnode]; treemap
+        [ntree, 2 maxnode]), copied from the device tree store on first use."""
+        if not getattr(self, "_trees_full", True):
+            T, M = self.ntree, self._maxnode_eff
+            tr = self._trees
+            for k, shape, dt in (("nodestatus", (T, M), np.int32), ("bestvar", (T, M), np.int32),
+                                 ("xbestsplit", (T, M), np.float32),
+                                 ("treemap", (T, 2 * M), np.int32),
+                                 ("nodeclass", (T, M), np.int32),
+                                 ("nodepred", (T, M), np.float32),
+                                 ("tnodewt", (T, M), np.float32)):
+                tr[k] = np.empty(shape, dt)
+            self._context().get_trees(0, T, A.Trees(*[A.ptr(tr[k], t) for k, t in (
+                ("nodestatus", A._pi), ("bestvar", A._pi), ("xbestsplit", A._pf),
+                ("treemap", A._pi), ("nodeclass", A._pi), ("nnode", A._pi),
+                ("nodepred", A._pf), ("tnodewt", A._pf))], None, None, None, None))
+            self._trees_full = True
+        return self._trees
+
+    @trees_.setter
+    def trees_(self, value):
+        self._trees = value
+        self._trees_full = True
 
     def _finalize(self, y):
         acc = self.acc_
