@@ -22,7 +22,7 @@
 extern "C" {
 #endif
 
-#define RFX_ABI_VERSION 4
+#define RFX_ABI_VERSION 5
 
 enum {
     RFX_OK = 0,
@@ -340,6 +340,21 @@ int rfx_rank_scores_desc(const float* scores, int n, int k, int* idx_out, float*
 int rfx_impute_round(void* ctx, const float* xc_host, const uint8_t* miss_host,
                      const uint8_t* is_cat_host, int n, int p, const int* cells_host, int ncells,
                      float* out_host);
+
+/* Aggregations of rfx_impute_round_ex (rfx_impute_proximity's `aggregation`). */
+#define RFX_IMPUTE_MEAN 0   /* 'mean' / 'weighted_mean' */
+#define RFX_IMPUTE_MEDIAN 1 /* 'median': np.median; categorical: the most frequent value */
+
+/* rfx_impute_round with the reference's top_k and aggregation (python/rfx_impute.py:744-762).
+ * top_k -1 = None (all qualifying rows, row order); top_k >= 0: when more rows qualify, the
+ * top_k by proximity (0: all of them) in ascending (proximity, row) order.  The reference
+ * orders them with np.argsort's default sort, whose order among equal proximities depends
+ * on numpy's sort implementation; here it is the stable one (ties by ascending row).
+ * aggregation RFX_IMPUTE_MEAN or RFX_IMPUTE_MEDIAN.  rfx_impute_round(...) equals
+ * rfx_impute_round_ex(..., -1, RFX_IMPUTE_MEAN, out_host). */
+int rfx_impute_round_ex(void* ctx, const float* xc_host, const uint8_t* miss_host,
+                        const uint8_t* is_cat_host, int n, int p, const int* cells_host,
+                        int ncells, int top_k, int aggregation, float* out_host);
 
 /* ---- Low-rank proximity (use_qlora=True, quant_mode="int8") --------------------------
  * Replaces LowRankProximityMatrix (include/rf_proximity_lowrank.hpp:27-439,

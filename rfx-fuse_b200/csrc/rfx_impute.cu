@@ -1,5 +1,5 @@
-// Proximity-weighted imputation round (the loop body of rfx_impute_proximity,
-// python/rfx_impute.py:730-775, aggregation 'mean', top_k None), bit for bit.
+// Proximity imputation round (the loop body of rfx_impute_proximity,
+// python/rfx_impute.py:730-775), bit for bit, for every aggregation and top_k.
 //
 // For a missing cell (i, j) the reference takes the finishprox'd proximity row i as float32,
 // zeroes the row's own entry and the rows missing in column j, keeps the rows with positive
@@ -12,6 +12,15 @@
 // share its proximity row, so each warp takes one row and reads that row once; per cell it
 // compacts the selected (p, x) pairs into its scratch in index order, the lanes sum the
 // leaves of the pairwise tree, and lane 0 combines them in the tree's order.
+//
+// top_k (rfx_impute.py:744-748): when more rows qualify, only the top_k by proximity are kept,
+// in ascending (proximity, row) order -- the stable order; the reference's np.argsort leaves
+// the order of equal proximities to numpy's sort implementation.  A radix select over the
+// proximity bits finds the k-th value, the rows above it and the last rows equal to it are
+// kept, and each kept pair is placed by counting the kept pairs before it.
+// median (rfx_impute.py:754-762): np.median of the values (the middle one, or the float32
+// mean of the two middle ones, both found by radix select); categorical: the value that
+// occurs most often (ascending values, first maximum).
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -132,6 +141,74 @@ __device__ float warp_pairwise(const F& f, int n, int2* leaves, float* leafsum, 
     return __shfl_sync(0xffffffffu, r, 0);
 }
 
+// Order-preserving key of a float (a larger float has a larger key; -0 counts as +0, so a
+// zero median is +0) and its inverse.
+__device__ __forceinline__ uint32_t fkey(float f) {
+    uint32_t u = __float_as_uint(f);
+    if ((u << 1) == 0u) u = 0u;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float fkey_inv(uint32_t k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// Key of rank r (0 = largest) among the keys of src[0, m) by one warp: four 8-bit radix
+// passes over the keys that share the digits found so far, with the warp's 256-bin
+// histogram in shared memory.  *above = keys strictly larger than the result.
+__device__ uint32_t warp_select_desc(const float* src, int m, int r, unsigned* hist, int lane,
+                                     int* above) {
+    uint32_t prefix = 0, mask = 0;
+    int need = r, ab = 0;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int b = lane; b < 256; b += 32) hist[b] = 0;
+        __syncwarp();
+        for (int q = lane; q < m; q += 32) {
+            const uint32_t k = fkey(src[q]);
+            if ((k & mask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1u);
+        }
+        __syncwarp();
+        // lane l holds bins 255 - 8l down to 248 - 8l; counts from the top
+        unsigned c[8], tot = 0;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            c[t] = hist[255 - 8 * lane - t];
+            tot += c[t];
+        }
+        unsigned incl = tot;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const unsigned excl = incl - tot;
+        const bool mine = excl <= (unsigned)need && (unsigned)need < incl;
+        const unsigned bal = __ballot_sync(0xffffffffu, mine);
+        int digit = 0;
+        unsigned before = 0;
+        if (mine) {
+            unsigned acc = excl;
+            for (int t = 0; t < 8; ++t) {
+                if ((unsigned)need < acc + c[t]) {
+                    digit = 255 - 8 * lane - t;
+                    before = acc;
+                    break;
+                }
+                acc += c[t];
+            }
+        }
+        const int owner = __ffs(bal) - 1;
+        digit = __shfl_sync(0xffffffffu, digit, owner);
+        before = __shfl_sync(0xffffffffu, before, owner);
+        need -= (int)before;
+        ab += (int)before;
+        prefix |= (uint32_t)digit << shift;
+        mask |= 255u << shift;
+        __syncwarp();
+    }
+    *above = ab;
+    return prefix;
+}
+
 }  // namespace
 
 // One warp per row that has missing cells (grid-stride over rows).  The warp first compacts
@@ -156,7 +233,11 @@ __global__ void __launch_bounds__(256, 4) k_impute(ImputeArgs a) {
     float* wbuf = rs + nn;                      // the cell's selection: weight, value
     float* vbuf = wbuf + nn;
     float* tbuf = vbuf + nn;                    // per-category subsequence
-    int2* leaves = reinterpret_cast<int2*>(tbuf + nn) + 1;  // [-1] carries the leaf count
+    float* selw = tbuf + nn;                    // the top_k selection in row order
+    float* selv = selw + nn;
+    int2* leaves = reinterpret_cast<int2*>(selv + nn) + 1;  // [-1] carries the leaf count
+    __shared__ unsigned s_hist[8][256];
+    unsigned* hist = s_hist[threadIdx.x >> 5];
     float* leafsum = reinterpret_cast<float*>(leaves + a.max_leaves + 1);
     const unsigned lt = (1u << lane) - 1u;
     for (int r = wid; r < a.nrows; r += nwarps) {
@@ -230,8 +311,55 @@ __global__ void __launch_bounds__(256, 4) k_impute(ImputeArgs a) {
                 atomicAdd(a.prof + 3, (unsigned long long)(clock64() - tp));
                 tp = clock64();
             }
+            if (mm > 0 && a.top_k >= 0 && mm > a.top_k) {
+                // the top kk by (proximity, row), placed in ascending order
+                const int kk = a.top_k == 0 ? mm : a.top_k;
+                int above;
+                const uint32_t K = warp_select_desc(wbuf, mm, kk - 1, hist, lane, &above);
+                int eqc = 0;
+                for (int q = lane; q < mm; q += 32) eqc += fkey(wbuf[q]) == K ? 1 : 0;
+                for (int o = 16; o > 0; o >>= 1) eqc += __shfl_xor_sync(0xffffffffu, eqc, o);
+                const int skip = eqc - (kk - above);  // the first rows equal to the k-th drop
+                int ms = 0, eqseen = 0;
+                for (int q0 = 0; q0 < mm; q0 += 32) {
+                    const int q = q0 + lane;
+                    const uint32_t key = q < mm ? fkey(wbuf[q]) : 0u;
+                    const bool eq = q < mm && key == K;
+                    const unsigned beq = __ballot_sync(0xffffffffu, eq);
+                    const bool keep = q < mm && (key > K || (eq && eqseen + __popc(beq & lt) >= skip));
+                    const unsigned bk = __ballot_sync(0xffffffffu, keep);
+                    if (keep) {
+                        selw[ms + __popc(bk & lt)] = wbuf[q];
+                        selv[ms + __popc(bk & lt)] = vbuf[q];
+                    }
+                    ms += __popc(bk);
+                    eqseen += __popc(beq);
+                }
+                __syncwarp();
+                for (int t = lane; t < kk; t += 32) {
+                    const float wt = selw[t];
+                    int rank = 0;
+                    for (int u = 0; u < kk; ++u) {
+                        const float wu = selw[u];
+                        rank += (wu < wt || (wu == wt && u < t)) ? 1 : 0;
+                    }
+                    wbuf[rank] = wt;
+                    vbuf[rank] = selv[t];
+                }
+                __syncwarp();
+                mm = kk;
+            }
             float result = __int_as_float(0x7fc00000);
-            if (mm > 0) {
+            if (mm > 0 && a.median && !a.is_cat[j]) {
+                int above;
+                if (mm & 1) {
+                    result = fkey_inv(warp_select_desc(vbuf, mm, (mm - 1) / 2, hist, lane, &above));
+                } else {
+                    const float hi = fkey_inv(warp_select_desc(vbuf, mm, mm / 2 - 1, hist, lane, &above));
+                    const float lo = fkey_inv(warp_select_desc(vbuf, mm, mm / 2, hist, lane, &above));
+                    result = (lo + hi) / 2.0f;
+                }
+            } else if (mm > 0) {
                 if (!a.is_cat[j]) {
                     const float tot = warp_pairwise(Plain{wbuf}, mm, leaves, leafsum, lane);
                     result = warp_pairwise(Scaled{wbuf, vbuf, tot}, mm, leaves, leafsum, lane, false);
@@ -259,7 +387,8 @@ __global__ void __launch_bounds__(256, 4) k_impute(ImputeArgs a) {
                             mc += __popc(bal);
                         }
                         __syncwarp();
-                        const float cntw = warp_pairwise(Plain{tbuf}, mc, leaves, leafsum, lane);
+                        const float cntw = a.median ? (float)mc
+                                                    : warp_pairwise(Plain{tbuf}, mc, leaves, leafsum, lane);
                         if (first || cntw > best) {
                             best = cntw;
                             best_v = nxt;

@@ -20,19 +20,22 @@ struct ImputeArgs {
     const int* row_cells;    // [nrows + 1] cells of rows[r]: [row_cells[r], row_cells[r + 1])
     int nrows;
     float* out;              // [ncells] new value, NaN = unchanged
-    float* scratch;          // per warp: 5 n floats, then leaves and leaf sums
+    float* scratch;          // per warp: 7 n floats, then leaves and leaf sums
     long long scratch_stride;
     int max_leaves;
+    int top_k;               // >= 0: only the top_k neighbours by proximity (0: all, reordered);
+                             // -1: all in row order
+    int median;              // 1: median / most frequent value, 0: proximity-weighted mean / mode
     unsigned long long* prof;  // optional counters (RFX_IMPUTE_PROF), null = off
 };
 
 // floats of one n-long scratch buffer (a multiple of 8, so the next one starts on 32 bytes)
 __host__ __device__ inline int impute_row_floats(int n) { return (n + 7) / 8 * 8; }
 
-// floats of scratch one warp needs for n rows: five n-long buffers, the leaf list (int2, one
+// floats of scratch one warp needs for n rows: seven n-long buffers, the leaf list (int2, one
 // extra slot for the count) and the leaf sums
 inline long long impute_scratch_floats(int n, int max_leaves) {
-    long long f = 5LL * impute_row_floats(n) + 2LL * (max_leaves + 2) + max_leaves + 2;
+    long long f = 7LL * impute_row_floats(n) + 2LL * (max_leaves + 2) + max_leaves + 2;
     return (f + 7) / 8 * 8;
 }
 

@@ -14,7 +14,17 @@ extern "C" {
 int rfx_impute_round(void* ctx, const float* xc_host, const uint8_t* miss_host,
                      const uint8_t* is_cat_host, int n, int p, const int* cells_host, int ncells,
                      float* out_host) {
+    return rfx_impute_round_ex(ctx, xc_host, miss_host, is_cat_host, n, p, cells_host, ncells, -1,
+                               RFX_IMPUTE_MEAN, out_host);
+}
+
+int rfx_impute_round_ex(void* ctx, const float* xc_host, const uint8_t* miss_host,
+                        const uint8_t* is_cat_host, int n, int p, const int* cells_host,
+                        int ncells, int top_k, int aggregation, float* out_host) {
     return guarded([&] {
+        require(top_k >= -1, RFX_ERR_ARG, "top_k must be -1 (none) or >= 0");
+        require(aggregation == RFX_IMPUTE_MEAN || aggregation == RFX_IMPUTE_MEDIAN, RFX_ERR_ARG,
+                "unknown aggregation");
         Ctx& c = *as_ctx(ctx);
         require(c.loaded && c.prox, RFX_ERR_STATE, "dense proximity counts are required (fit with compute_proximity)");
         require(n == c.R, RFX_ERR_ARG, "n must equal the proximity rows of the fit");
@@ -93,6 +103,8 @@ int rfx_impute_round(void* ctx, const float* xc_host, const uint8_t* miss_host,
             a.scratch = scratch;
             a.scratch_stride = stride;
             a.max_leaves = max_leaves;
+            a.top_k = top_k;
+            a.median = aggregation == RFX_IMPUTE_MEDIAN ? 1 : 0;
             a.prof = prof;
             const int grid = std::min(blocks, (a.nrows + 7) / 8);
             rfx::k_impute<<<grid, 256, 0, st>>>(a);

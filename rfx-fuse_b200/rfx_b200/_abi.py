@@ -70,7 +70,7 @@ SYMBOLS = (
     "rfx_set_profiling", "rfx_get_stats", "rfx_reset_stats", "rfx_sync",
     "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk", "rfx_lowrank_product",
     "rfx_prox_apply", "rfx_lowrank_set_factors", "rfx_load_forest", "rfx_predict",
-    "rfx_lowrank_topk_part", "rfx_impute_round", "rfx_leaf_assignments", "rfx_leaf_index",
+    "rfx_lowrank_topk_part", "rfx_impute_round", "rfx_impute_round_ex", "rfx_leaf_assignments", "rfx_leaf_index",
     "rfx_leaf_top_k_similar", "rfx_leaf_proximity", "rfx_predict_leaves",
     "rfx_predict_top_k_similar", "rfx_leaf_select_anchors", "rfx_leaf_outlier_scores",
     "rfx_rank_scores_desc", "rfx_predict_outlier_scores",
@@ -141,6 +141,8 @@ def load_library(path: str = LIB_PATH):
     L.rfx_lowrank_set_factors.argtypes = [vp, C.POINTER(C.c_int8), _pf, C.c_int, C.c_int]
     L.rfx_load_forest.argtypes = [vp, C.POINTER(Forest)]
     L.rfx_impute_round.argtypes = [vp, _pf, _pu8, _pu8, C.c_int, C.c_int, _pi, C.c_int, _pf]
+    L.rfx_impute_round_ex.argtypes = [vp, _pf, _pu8, _pu8, C.c_int, C.c_int, _pi, C.c_int,
+                                      C.c_int, C.c_int, _pf]
     L.rfx_lowrank_topk_part.argtypes = [vp, C.c_int, C.c_int, C.c_int, _pi, _pi, _pf,
                                         C.POINTER(C.c_int)]
     L.rfx_predict.argtypes = [vp, _pf, C.c_int, C.c_int, _pi, _pf, _pf]
@@ -163,7 +165,8 @@ def load_library(path: str = LIB_PATH):
                  "rfx_sync", "rfx_lowrank_build", "rfx_lowrank_factors", "rfx_lowrank_topk",
                  "rfx_lowrank_product", "rfx_prox_apply", "rfx_lowrank_set_factors",
                  "rfx_load_forest", "rfx_predict", "rfx_lowrank_topk_part",
-                 "rfx_impute_round", "rfx_leaf_assignments", "rfx_leaf_index",
+                 "rfx_impute_round", "rfx_impute_round_ex", "rfx_leaf_assignments",
+                 "rfx_leaf_index",
                  "rfx_leaf_top_k_similar", "rfx_leaf_proximity", "rfx_predict_leaves",
                  "rfx_predict_top_k_similar", "rfx_leaf_select_anchors",
                  "rfx_leaf_outlier_scores", "rfx_rank_scores_desc",
@@ -412,18 +415,24 @@ class Context:
         return out
 
     # ---- imputation ----
-    def impute_round(self, xc: np.ndarray, miss: np.ndarray, is_cat: np.ndarray, cells: np.ndarray):
+    def impute_round(self, xc: np.ndarray, miss: np.ndarray, is_cat: np.ndarray, cells: np.ndarray,
+                     top_k=None, aggregation="mean"):
         """New values of `cells` ([m, 2] (row, column), sorted by row) from this context's
-        proximity; NaN = keep.  xc / miss are [p][n] (column-major)."""
+        proximity; NaN = keep.  xc / miss are [p][n] (column-major).  top_k None or >= 0;
+        aggregation 'mean' / 'weighted_mean' / 'median'."""
+        agg = {"mean": 0, "weighted_mean": 0, "median": 1}.get(aggregation)
+        if agg is None:
+            raise ValueError(f"Unknown aggregation: {aggregation}")
         xc = np.ascontiguousarray(xc, np.float32)
         miss = np.ascontiguousarray(miss, np.uint8)
         is_cat = np.ascontiguousarray(is_cat, np.uint8)
         cells = np.ascontiguousarray(cells, np.int32)
         p, n = xc.shape
         out = np.zeros(cells.shape[0], np.float32)
-        check(self._lib.rfx_impute_round(self.handle, ptr(xc, _pf), ptr(miss, _pu8),
-                                         ptr(is_cat, _pu8), n, p, ptr(cells, _pi),
-                                         cells.shape[0], ptr(out, _pf)))
+        check(self._lib.rfx_impute_round_ex(self.handle, ptr(xc, _pf), ptr(miss, _pu8),
+                                            ptr(is_cat, _pu8), n, p, ptr(cells, _pi),
+                                            cells.shape[0], -1 if top_k is None else int(top_k),
+                                            agg, ptr(out, _pf)))
         return out
 
     # ---- low-rank proximity ----

@@ -3,10 +3,11 @@
 
 Each iteration fits an unsupervised forest on the current matrix (proximity over the real
 rows), then fills every originally-missing cell from the finished proximity row
-(rfx_impute_round: proximity-weighted mean for continuous columns, proximity-weighted mode
-for categorical ones, numpy's summation order kept), and stops early when the summed change
-falls below 1e-6.  Supports the reference's default aggregation ('mean' / 'weighted_mean'
-with top_k None).
+(rfx_impute_round_ex: proximity-weighted mean for continuous columns, proximity-weighted mode
+for categorical ones, numpy's summation order kept; or with aggregation 'median' the median
+and the most frequent value; with top_k only the top_k rows by proximity), and stops early
+when the summed change falls below 1e-6.  top_k keeps equal proximities in row order (the
+reference's np.argsort leaves their order to numpy's sort implementation).
 """
 from __future__ import annotations
 
@@ -119,8 +120,10 @@ def rfx_impute_proximity(X, ntree=100, n_iterations=5, use_gpu=True, categorical
     iseed = seed if seed is not None else iseed
     show_progress = verbose if verbose is not None else show_progress
     maxcat = max_categorical_unique if max_categorical_unique is not None else maxcat
-    if top_k is not None or aggregation not in ("mean", "weighted_mean"):
-        raise NotImplementedError("the device fill implements aggregation 'mean' with top_k None")
+    if aggregation not in ("mean", "weighted_mean", "median"):
+        raise ValueError(f"Unknown aggregation: {aggregation}")
+    if top_k is not None and int(top_k) < 0:
+        raise ValueError("top_k must be None or >= 0")
     X, auto_cat, encoders = _encode(X)
     n, p = X.shape
     missing = np.isnan(X)
@@ -150,7 +153,8 @@ def rfx_impute_proximity(X, ntree=100, n_iterations=5, use_gpu=True, categorical
         model = RandomForestUnsupervised(prox_rows=n, device=device, **kw)
         model.fit(Xi)
         t1 = time.perf_counter()
-        new = model._context().impute_round(np.ascontiguousarray(Xi.T), miss_cm, cat_u8, cells)
+        new = model._context().impute_round(np.ascontiguousarray(Xi.T), miss_cm, cat_u8, cells,
+                                            top_k, aggregation)
         timing.append((t1 - t0, time.perf_counter() - t1))
         # apply, and the reference's change sum (float32 under numpy 2 scalar rules) in its
         # visiting order: columns ascending, rows ascending
@@ -170,3 +174,13 @@ def rfx_impute_proximity(X, ntree=100, n_iterations=5, use_gpu=True, categorical
             "method": "proximity", "top_k": top_k, "aggregation": aggregation,
             "encoders": encoders, "timing_fit_fill_s": timing}
     return Xi, info
+
+
+def rfx_impute_topk_mean(X, k=10, **kwargs):
+    """Mean of the k rows most similar by proximity (python/rfx_impute.py:798-800)."""
+    return rfx_impute_proximity(X, top_k=k, aggregation="mean", **kwargs)
+
+
+def rfx_impute_topk_median(X, k=10, **kwargs):
+    """Median of the k rows most similar by proximity (python/rfx_impute.py:803-805)."""
+    return rfx_impute_proximity(X, top_k=k, aggregation="median", **kwargs)

@@ -123,7 +123,7 @@ def impute_data(n=400, seed=61):
     return X
 
 
-def impute_golden():
+def impute_golden(aggregation="mean"):
     """The reference's rfx_impute_proximity (python/rfx_impute.py:596-793) on impute_data()."""
     sys.path.insert(0, oracle.ref_dir())
     tree = oracle.reference_tree()
@@ -134,7 +134,7 @@ def impute_golden():
     ri = importlib.import_module("rfx_impute")
     X = impute_data()
     Xo, info = ri.rfx_impute_proximity(X.copy(), ntree=25, n_iterations=3, use_gpu=False,
-                                       iseed=42, minndsize=1)
+                                       iseed=42, minndsize=1, aggregation=aggregation)
     return {"X": X, "X_imputed": np.asarray(Xo, np.float32),
             "n_iterations": np.int32(info["n_iterations"])}
 
@@ -243,6 +243,7 @@ def main():
     save_gz(u, os.path.join(HERE, "unsup_model.rfx.gz"))
     out["unsup_model"] = {"X": Xu}
     out["impute"] = impute_golden()
+    out["impute_median"] = impute_golden("median")
     for name, d in out.items():
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **d)
     np.savez_compressed(os.path.join(HERE, "bootstrap.npz"), **boot)
@@ -254,5 +255,8 @@ if __name__ == "__main__":
     if len(sys.argv) > 1 and sys.argv[1] == "leaves":  # only the leaf-query fixtures
         for name, d in leaves_golden().items():
             np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **d)
+    elif len(sys.argv) > 1 and sys.argv[1] == "impute":  # only the imputation fixtures
+        for agg, name in (("mean", "impute"), ("median", "impute_median")):
+            np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **impute_golden(agg))
     else:
         main()

@@ -19,6 +19,17 @@ def test_impute_matches_reference_golden():
     assert np.array_equal(Xo.view(np.uint32), g["X_imputed"].view(np.uint32))
 
 
+def test_impute_median_matches_reference_golden():
+    """aggregation='median' (np.median; categorical: most frequent value), top_k None."""
+    import rfx_b200
+    g = np.load(os.path.join(GOLD, "impute_median.npz"))
+    Xo, info = rfx_b200.rfx_impute_proximity(g["X"].copy(), ntree=25, n_iterations=3,
+                                             use_gpu=False, iseed=42, minndsize=1,
+                                             aggregation="median")
+    assert info["n_iterations"] == int(g["n_iterations"])
+    assert np.array_equal(Xo.view(np.uint32), g["X_imputed"].view(np.uint32))
+
+
 def _numpy_fill(prox, X, missing, cat, cells):
     """The reference's fill of the given cells (python/rfx_impute.py:733-771, 'mean')."""
     out = np.full(len(cells), np.nan, np.float32)
@@ -65,3 +76,44 @@ def test_impute_round_vs_numpy_large_rows():
                                       cat.astype(np.uint8), cells)
     want = _numpy_fill(prox, Xf, missing, cat, cells)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@pytest.mark.parametrize("top_k,aggregation", [(None, "median"), (0, "mean"), (1, "mean"),
+                                               (7, "mean"), (7, "median"), (64, "median"),
+                                               (200, "mean"), (10, "weighted_mean")])
+def test_impute_round_top_k_and_median_vs_oracle(top_k, aggregation):
+    """top_k / median fill of 3000-row neighbour lists against the CPU restatement (stable
+    order among equal proximities), bit for bit; proximities here are heavily tied (40
+    trees), so the tie rule at the top_k cut is exercised."""
+    import rfx_b200
+    from oracle.impute_fill import fill
+    rng = np.random.default_rng(8)
+    n, p = 3000, 6
+    X = rng.normal(size=(n, p)).astype(np.float32)
+    X[:, 4] = rng.normal(size=n).astype(np.float32).round(1)  # repeated values
+    X[:, 5] = rng.integers(0, 5, n)
+    missing = rng.random((n, p)) < 0.1
+    Xf = X.copy()
+    Xf[missing] = 0.5
+    cat = np.array([0, 0, 0, 0, 0, 1], bool)
+    est = rfx_b200.RandomForestUnsupervised(nsample=n, ntree=40, mtry=2, minndsize=5,
+                                            compute_importance=False, prox_rows=n)
+    est.fit(Xf)
+    prox = est.get_proximity_matrix()
+    jj, ii = np.nonzero(missing.T)
+    sel = np.arange(len(ii))[:: max(1, len(ii) // 300)]
+    cells = np.stack([ii[sel], jj[sel]], axis=1).astype(np.int32)
+    cells = cells[np.lexsort((cells[:, 1], cells[:, 0]))]
+    got = est._context().impute_round(np.ascontiguousarray(Xf.T), missing.T.astype(np.uint8),
+                                      cat.astype(np.uint8), cells, top_k, aggregation)
+    want = fill(prox, Xf, missing, cat, cells, top_k, aggregation)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_impute_top_k_wrappers_run():
+    import rfx_b200
+    g = np.load(os.path.join(GOLD, "impute.npz"))
+    for f in (rfx_b200.rfx_impute_topk_mean, rfx_b200.rfx_impute_topk_median):
+        Xo, info = f(g["X"].copy(), k=5, ntree=10, n_iterations=1, iseed=3, minndsize=1)
+        assert not np.isnan(Xo).any() and info["top_k"] == 5
