@@ -15,10 +15,26 @@ constexpr int kLrK = 64;               // stored factor width (rank <= 64, zero 
 // product / top-k kernel geometry
 constexpr int kTkRows = 128;    // rows of a CTA (MMA M)
 constexpr int kTkCols = 256;    // columns of a tile (MMA N)
-constexpr int kTkStages = 3;    // column-tile ring
+constexpr int kTkStages = 2;    // column-tile ring
 constexpr int kTkSlots = 64;    // heap entries per row (k <= 64)
+constexpr int kTkBuf = 48;      // candidate buffer entries per row
 constexpr int kTkThreads = 192; // warp 0 loads, warp 1 issues MMAs, warps 2-5 read out
-constexpr int kTkSmem = 16384 + kTkStages * 32768 + kTkSlots * kTkRows * 8 + 128 + 4096 + 16384 + 1024;
+constexpr int kTkScr = 4 * 32 * 33 * 4;  // per read-out warp: a 32 x 32 chunk, rows padded to 33
+
+// Shared-memory layout of the product kernel for k neighbours: row tile, column-tile ring,
+// heaps [k][128], candidate buffers [kTkBuf][128] (values, then original ids), the read-out
+// warps' chunk transposes, then barriers and the staged column scales and ids of two tiles.
+struct TkLayout {
+    int heap, buf, scr, misc, bytes;
+};
+__host__ __device__ constexpr TkLayout tk_layout(int k) {
+    return TkLayout{16384 + kTkStages * 32768,
+                    16384 + kTkStages * 32768 + k * kTkRows * 8,
+                    16384 + kTkStages * 32768 + k * kTkRows * 8 + kTkBuf * kTkRows * 8,
+                    16384 + kTkStages * 32768 + k * kTkRows * 8 + kTkBuf * kTkRows * 8 + kTkScr,
+                    16384 + kTkStages * 32768 + k * kTkRows * 8 + kTkBuf * kTkRows * 8 + kTkScr +
+                        4352 + 1024};
+}
 
 struct TopkArgs {
     int R;              // valid rows (= valid columns)

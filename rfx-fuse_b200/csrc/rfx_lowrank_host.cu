@@ -221,9 +221,10 @@ void run_product(Ctx& c, int r0, int r1, int k, int* oi, float* ov, float* dense
         RFX_CUDA(cudaMemsetAsync(prof, 0, 128, st));
         a.prof = prof;
     }
-    set_smem((const void*)rfx::k_topk_tc, rfx::kTkSmem);
+    const int smem = rfx::tk_layout(k).bytes;
+    set_smem((const void*)rfx::k_topk_tc, smem);
     if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev0, st));
-    rfx::k_topk_tc<<<grid, rfx::kTkThreads, rfx::kTkSmem, st>>>(tm, a);
+    rfx::k_topk_tc<<<grid, rfx::kTkThreads, smem, st>>>(tm, a);
     RFX_LAUNCH("k_topk_tc");
     if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev1, st));
     c.launches += 1;
@@ -242,11 +243,11 @@ void run_product(Ctx& c, int r0, int r1, int k, int* oi, float* ov, float* dense
         unsigned long long hp[16] = {};
         RFX_CUDA(cudaMemcpy(hp, prof, 128, cudaMemcpyDeviceToHost));
         std::fprintf(stderr,
-                     "[rfx topk] rows=%d chunks=%llu scanned=%llu pushes=%llu compactions=%llu "
+                     "[rfx topk] rows=%d chunks=%llu scanned=%llu pushes=%llu flushes=%llu "
                      "polls: readout=%llu mma=%llu load=%llu  cycles: readout wait=%llu "
-                     "readout total=%llu mma wait-acc=%llu mma wait-load=%llu load wait-free=%llu\n",
+                     "readout total=%llu mma wait-acc=%llu mma wait-load=%llu load wait-free=%llu tmem=%llu filter=%llu scan=%llu\n",
                      r1 - r0, hp[0], hp[1], hp[2], hp[3], hp[4], hp[5], hp[6], hp[7], hp[8], hp[9],
-                     hp[10], hp[11]);
+                     hp[10], hp[11], hp[12], hp[13], hp[14]);
     }
 }
 

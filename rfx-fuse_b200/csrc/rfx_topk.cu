@@ -9,7 +9,7 @@
 // so the strongest candidates come first and each row's k-th value rises at once.
 // CTA = 128 rows (the MMA's M), sweeping the column tiles of 256 (N) in stored order:
 //   warp 0      one thread issues TMA loads: the CTA's 128x64 row tile once, then the
-//               256x64 column tiles through a 3-stage ring (128-byte swizzle, K-major);
+//               256x64 column tiles through a 2-stage ring (128-byte swizzle, K-major);
 //   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators) and one thread
 //               issues 4 x tcgen05.mma (K = 16 each) per tile, committing to the ring's
 //               "empty" barrier and to the accumulator's "full" barrier;
@@ -19,10 +19,16 @@
 //               memory (each thread loads two for the next tile while it works on this one).
 //               A chunk of 32 columns is scanned only when max_j(acc_ij * s_j) * s_i reaches
 //               the row's current k-th value less a 1e-6 relative margin (the exact value
-//               rounds the same three factors in another order); survivors that beat the
-//               bar enter the row's heap of the best k in shared memory.  A row is final once n_i * n_(next tile's first
-//               column) is below its k-th value; when all 128 rows are final the CTA lowers
-//               its stop limit and the three roles end their sweeps.
+//               rounds the same three factors in another order).  Scanned values that beat
+//               the bar are appended to the row's candidate buffer; the warp moves its 32
+//               buffers into the rows' heaps of the best k together, so most lanes work in
+//               each heap step (a stream in no particular order replaces the k-th entry about
+//               k ln(N / k) times, and single-lane pushes cost a whole warp each).  Every
+//               eighth tile, after such a flush, a row is final once n_i * n_(next tile's
+//               first column) is below its k-th value; when all 128 rows are final the CTA
+//               lowers its stop limit and the three roles end their sweeps.
+// The single-thread producer and MMA roles sleep inside mbarrier.try_wait (suspend-time
+// hint), so their waits do not take issue slots from the read-out warps.
 // The bar carries the k-th entry's column id, so ties are broken by the original index
 // whatever the sweep order, and the result is the exact top-k under the total order.
 //
@@ -39,6 +45,8 @@ namespace rfx {
 namespace {
 
 constexpr unsigned long long kWaitNs = 1000000000ull;
+// A sleeping waiter stays in try_wait until the phase completes or this many nanoseconds pass.
+constexpr uint32_t kSuspendNs = 2000;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -50,15 +58,26 @@ __device__ __forceinline__ unsigned long long now_ns() {
     return t;
 }
 
+template <bool kSleep>
 __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
+    if (kSleep) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity), "r"(kSuspendNs)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}\n"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+    }
     return ok != 0;
 }
 
@@ -67,27 +86,27 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 // kWaitStop once step `it` is at or beyond the CTA's stop limit (limit may be null).
 constexpr int kWaitFail = 0, kWaitOk = 1, kWaitStop = 2;
 
+template <bool kSleep = true>
 __device__ int mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
                          unsigned long long* polls = nullptr, volatile int* limit = nullptr,
                          int it = 0) {
     const unsigned long long t0 = now_ns();
     for (uint32_t spin = 1;; ++spin) {
         if (polls) ++*polls;
-        if (mbar_try(bar, parity)) return kWaitOk;
-        if ((spin & 63u) == 0) {
-            if (limit && it >= *limit) return kWaitStop;
-            if (abort && *abort) return kWaitFail;
-            if (now_ns() - t0 > kWaitNs) return kWaitFail;
-        }
+        if (mbar_try<kSleep>(bar, parity)) return kWaitOk;
+        if (limit && it >= *limit) return kWaitStop;
+        if (abort && *abort) return kWaitFail;
+        if ((spin & 15u) == 0 && now_ns() - t0 > kWaitNs) return kWaitFail;
     }
 }
 
 // mbar_wait that also adds the cycles it spent to *cyc.
+template <bool kSleep = true>
 __device__ __forceinline__ int mbar_wait_t(uint32_t bar, uint32_t parity, volatile int* abort,
                                            unsigned long long* polls, unsigned long long* cyc,
                                            volatile int* limit = nullptr, int it = 0) {
     const long long t0 = clock64();
-    const int r = mbar_wait(bar, parity, abort, polls, limit, it);
+    const int r = mbar_wait<kSleep>(bar, parity, abort, polls, limit, it);
     *cyc += (unsigned long long)(clock64() - t0);
     return r;
 }
@@ -193,10 +212,8 @@ __device__ __forceinline__ bool better(float va, int ja, float vb, int jb) {
 
 constexpr int kHeapDepth = 6;  // levels below the root of a heap of <= 64 entries
 
-// Insert (val, col) into a heap of n < k entries.  (Out of line, like heap_replace_root: the
-// read-out calls them from many unrolled sites, and inlined copies overflow the
-// instruction cache.)
-__device__ __noinline__ void heap_insert(float* v, int* j, int n, float val, int col) {
+// Insert (val, col) into a heap of n < k entries.
+__device__ __forceinline__ void heap_insert(float* v, int* j, int n, float val, int col) {
     int i = n;
 #pragma unroll
     for (int l = 0; l < kHeapDepth; ++l) {
@@ -212,7 +229,7 @@ __device__ __noinline__ void heap_insert(float* v, int* j, int n, float val, int
 }
 
 // Replace the root (worst) of a full heap of n entries by (val, col) and restore the order.
-__device__ __noinline__ void heap_replace_root(float* v, int* j, int n, float val, int col) {
+__device__ __forceinline__ void heap_replace_root(float* v, int* j, int n, float val, int col) {
     int i = 0;
 #pragma unroll
     for (int l = 0; l < kHeapDepth; ++l) {
@@ -229,33 +246,46 @@ __device__ __noinline__ void heap_replace_root(float* v, int* j, int n, float va
     j[i * kTkRows] = col;
 }
 
+// Largest of three floats (the three-input max.f32 of sm_100).
+__device__ __forceinline__ float fmax3(float x, float y, float z) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(x), "f"(y), "f"(z));
+    return d;
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(kTkThreads, 1)
 k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
     extern __shared__ uint8_t smem_raw[];
-    uint8_t* sm = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    // 1024-byte aligned base, indexed from the shared array so accesses stay shared-space
+    uint8_t* sm = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int k = a.k;
+    const TkLayout lay = tk_layout(k);
     uint8_t* sA = sm;
     uint8_t* sB = sm + 16384;
-    float* cand_v = (float*)(sm + 16384 + kTkStages * 32768);
-    int* cand_j = (int*)(sm + 16384 + kTkStages * 32768 + kTkSlots * kTkRows * 4);
-    uint64_t* bars = (uint64_t*)(sm + 16384 + kTkStages * 32768 + kTkSlots * kTkRows * 8);
-    // bars: full[0..2], empty[3..5], acc_full[6..7], acc_empty[8..9], a_full[10],
-    // sready[11..12] (the tile's column scales and row ids are in sc[b] / sid[b])
-    uint32_t* tmem_slot = (uint32_t*)(bars + 13);
+    float* heap_v = (float*)(sm + lay.heap);                  // [k][128]
+    int* heap_j = (int*)(sm + lay.heap + k * kTkRows * 4);    // [k][128]
+    float* buf_v = (float*)(sm + lay.buf);                    // [kTkBuf][128]
+    int* buf_j = (int*)(sm + lay.buf + kTkBuf * kTkRows * 4); // [kTkBuf][128]
+    float* scr_all = (float*)(sm + lay.scr);                 // [4 warps][32][33]
+    uint64_t* bars = (uint64_t*)(sm + lay.misc);
+    // bars: full[0..1], empty[2..3], acc_full[4..5], acc_empty[6..7], a_full[8],
+    // sready[9..10] (the tile's column scales and ids are in sc[b] / sid[b])
+    uint32_t* tmem_slot = (uint32_t*)(bars + 11);
     volatile int* abort = (volatile int*)(tmem_slot + 1);
     volatile int* limit = (volatile int*)(tmem_slot + 2);  // column tiles the CTA still needs
     int* ndone = (int*)(tmem_slot + 3);                     // read-out warps whose rows are final
-    float* sc = (float*)((uint8_t*)bars + 128);   // [2][256] column scales of a tile
-    float* scratch = (float*)((uint8_t*)bars + 128 + 4096);  // [32][128] values of a chunk
-    int* sid = (int*)((uint8_t*)bars + 128 + 2048);  // [2][256] original ids of its columns
+    float* sc = (float*)((uint8_t*)bars + 256);             // [2][256] column scales of a tile
+    int* sid = (int*)((uint8_t*)bars + 256 + 2048);         // [2][256] original ids of its columns
     const uint32_t bar0 = smem_u32(bars);
     auto full = [&](int s) { return bar0 + 8u * s; };
-    auto empty = [&](int s) { return bar0 + 8u * (3 + s); };
-    auto accf = [&](int b) { return bar0 + 8u * (6 + b); };
-    auto acce = [&](int b) { return bar0 + 8u * (8 + b); };
-    const uint32_t afull = bar0 + 80u;
-    auto sready = [&](int b) { return bar0 + 8u * (11 + b); };
+    auto empty = [&](int s) { return bar0 + 8u * (kTkStages + s); };
+    auto accf = [&](int b) { return bar0 + 8u * (4 + b); };
+    auto acce = [&](int b) { return bar0 + 8u * (6 + b); };
+    const uint32_t afull = bar0 + 64u;
+    auto sready = [&](int b) { return bar0 + 8u * (9 + b); };
+    const float kNegInf = -__int_as_float(0x7f800000);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // first position (row of the stored factor order) of this CTA's 128 rows
@@ -377,18 +407,50 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
         // columns stored by n_j descending; 1e-5 covers the roundings of P and of n
         const float ni = a.norm && pos < a.R ? __ldg(a.norm + pos) * 1.00001f : 0.0f;
         bool warp_final = false;
-        const int k = a.k;
-        float* cv = cand_v + rl;
-        int* cj = cand_j + rl;
-        float* scr = scratch + rl;
-        int cnt = 0;                                  // heap entries
-        float theta = -__int_as_float(0x7f800000);    // bar: the root once the heap is full
+        float* cv = heap_v + rl;
+        int* cj = heap_j + rl;
+        float* bv = buf_v + rl;
+        int* bj = buf_j + rl;
+        float* scr = scr_all + (warp & 3) * (32 * 33);
+        const unsigned lt = (1u << lane) - 1u;
+        int cnt = 0;                  // heap entries
+        int nb = 0;                   // buffered candidates
+        float theta = kNegInf;        // bar: the root once the heap is full
         int theta_j = 0x7fffffff;
         const uint32_t lane_addr = (uint32_t)(32 * (warp & 3)) << 16;
         bool ok = true;
-        unsigned long long n_test = 0, n_scan = 0, n_push = 0, polls = 0;
-        unsigned long long cyc_wait = 0;
+        unsigned long long n_test = 0, n_scan = 0, n_push = 0, polls = 0, n_flush = 0;
+        unsigned long long cyc_wait = 0, cyc_tm = 0, cyc_f = 0, cyc_s = 0;
+        const bool timing = a.prof != nullptr;  // per-warp cycle split when counters are on
         const long long cyc0 = clock64();
+        // Candidates that beat the bar are appended to the row's buffer; the warp moves its 32
+        // buffers into the heaps together (most lanes busy at once, rather than one lane per
+        // push), when a buffer may not hold another chunk and before each finality check.
+        auto flush = [&]() {
+            const int nmax = __reduce_max_sync(0xffffffffu, nb);
+            ++n_flush;
+            for (int s = 0; s < nmax; ++s) {
+                if (s < nb) {
+                    const float val = bv[s * kTkRows];
+                    const int col = bj[s * kTkRows];
+                    if (better(val, col, theta, theta_j)) {  // the bar may have risen since
+                        ++n_push;
+                        if (cnt < k) {
+                            heap_insert(cv, cj, cnt, val, col);
+                            ++cnt;
+                        } else {
+                            heap_replace_root(cv, cj, cnt, val, col);
+                        }
+                        if (cnt == k) {
+                            theta = cv[0];
+                            theta_j = cj[0];
+                        }
+                    }
+                }
+            }
+            nb = 0;
+            __syncwarp();
+        };
         // column scales and ids of a tile: each thread stages two of the 256 (loaded one tile
         // ahead, stored once the tile's reads of the other buffer are done)
         auto fetch = [&](int it, float2& s2, int2& i2) {
@@ -408,28 +470,29 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
         for (int it = 0; it < ntiles; ++it) {
             const int b = it & 1;
             if (it + 1 < ntiles) fetch(it + 1, nxt_s, nxt_i);
-            // (a stop limit at or below this tile means every row of the CTA is final)
-            int w = mbar_wait_t(sready(b), (uint32_t)(it >> 1) & 1u, abort, &polls, &cyc_wait, limit, it);
-            if (w == kWaitOk && *(volatile int*)ndone == 4) {  // every row is final: stop the sweep
-                atomicMin((int*)limit, it);
-                break;
-            }
-            if (w == kWaitOk)
-                w = mbar_wait_t(accf(b), (uint32_t)(it >> 1) & 1u, abort, &polls, &cyc_wait, limit, it);
-            if (w == kWaitStop) break;
-            if (w == kWaitFail) {
+            int w = mbar_wait_t<false>(sready(b), (uint32_t)(it >> 1) & 1u, abort, &polls, &cyc_wait, limit, it);
+            // one decision per warp (the TMEM loads below are warp-collective)
+            if (__any_sync(0xffffffffu, w == kWaitFail)) {
                 ok = false;
                 break;
             }
-            __syncwarp();
+            if (__any_sync(0xffffffffu, w == kWaitStop)) break;
+            if (__any_sync(0xffffffffu, *(volatile int*)ndone == 4)) {  // every row is final
+                atomicMin((int*)limit, it);
+                break;
+            }
+            w = mbar_wait_t<false>(accf(b), (uint32_t)(it >> 1) & 1u, abort, &polls, &cyc_wait, limit, it);
+            if (__any_sync(0xffffffffu, w == kWaitFail)) {
+                ok = false;
+                break;
+            }
+            if (__any_sync(0xffffffffu, w == kWaitStop)) break;
             tc_fence_after();
             const float* scb = sc + b * kTkCols;
             const int* idb = sid + b * kTkCols;
-            // a column can only beat the bar if its product with the row scale, taken in the
-            // other order (two roundings either way), reaches the bar less a 1e-6 margin
-            const float theta_lo = theta - fabsf(theta) * 1e-6f;
 #pragma unroll 1
             for (int h = 0; h < 2; ++h) {  // 128 columns per TMEM wait
+                long long t0 = timing ? clock64() : 0;
                 uint32_t r[4][32];
                 __syncwarp();
 #pragma unroll
@@ -441,6 +504,11 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
                 if (h == 1) {
                     tc_fence_before();
                     mbar_arrive(acce(b));
+                }
+                if (timing) {
+                    const long long t1 = clock64();
+                    cyc_tm += t1 - t0;
+                    t0 = t1;
                 }
                 if (k == 0) {
                     if (valid) {
@@ -457,73 +525,78 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
                     }
                     continue;
                 }
+                // max_j acc_j s_j of each 32-column chunk (four independent chains), then
+                // times s_i: the exact value rounds the same three factors in another order,
+                // so the test keeps a 1e-6 relative margin
+                float m[4];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const float4* s4 = reinterpret_cast<const float4*>(scb + 128 * h + 32 * c);
-                    float m[16];
+                for (int c = 0; c < 4; ++c) m[c] = kNegInf;
 #pragma unroll
-                    for (int e4 = 0; e4 < 4; ++e4) {
-                        const float4 lo = s4[e4], hi = s4[e4 + 4];
-                        const float sl[4] = {lo.x, lo.y, lo.z, lo.w};
-                        const float sh[4] = {hi.x, hi.y, hi.z, hi.w};
+                for (int e4 = 0; e4 < 8; ++e4) {
 #pragma unroll
-                        for (int u = 0; u < 4; ++u)
-                            m[4 * e4 + u] = fmaxf(__uint_as_float(r[c][4 * e4 + u]) * sl[u],
-                                                  __uint_as_float(r[c][16 + 4 * e4 + u]) * sh[u]);
-                    }
-#pragma unroll
-                    for (int w = 8; w > 0; w >>= 1)
-#pragma unroll
-                        for (int e = 0; e < w; ++e) m[e] = fmaxf(m[e], m[e + w]);
-                    ++n_test;
-                    if (!(valid && m[0] * si >= theta_lo)) continue;
-                    ++n_scan;
-                    // exact values of the chunk into this thread's scratch column, and the
-                    // mask of those that beat the bar; then one push site walks the mask
-                    const int* idc = idb + 128 * h + 32 * c;
-                    const int4* i4 = reinterpret_cast<const int4*>(idc);
-                    uint32_t mask = 0;
-#pragma unroll
-                    for (int e4 = 0; e4 < 8; ++e4) {
-                        const float4 sj = s4[e4];
-                        const int4 jj = i4[e4];
-                        const float sjv[4] = {sj.x, sj.y, sj.z, sj.w};
-                        const int jv[4] = {jj.x, jj.y, jj.z, jj.w};
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int e = 4 * e4 + u;
-                            const float val = (__uint_as_float(r[c][e]) * si) * sjv[u];
-                            scr[e * kTkRows] = val;
-                            const bool pass = better(val, jv[u], theta, theta_j) && jv[u] != row &&
-                                              jv[u] < a.R;
-                            mask |= (pass ? 1u : 0u) << e;
-                        }
-                    }
-                    while (mask) {
-                        const int e = __ffs(mask) - 1;
-                        mask &= mask - 1;
-                        const float val = scr[e * kTkRows];
-                        const int col = idc[e];
-                        if (!better(val, col, theta, theta_j)) continue;  // the bar rose meanwhile
-                        ++n_push;
-                        if (cnt < k) {
-                            heap_insert(cv, cj, cnt, val, col);
-                            ++cnt;
-                        } else {
-                            heap_replace_root(cv, cj, cnt, val, col);
-                        }
-                        if (cnt == k) {
-                            theta = cv[0];
-                            theta_j = cj[0];
-                        }
+                    for (int c = 0; c < 4; ++c) {
+                        const float4 sj = reinterpret_cast<const float4*>(scb + 128 * h + 32 * c)[e4];
+                        m[c] = fmax3(m[c], __uint_as_float(r[c][4 * e4]) * sj.x,
+                                     __uint_as_float(r[c][4 * e4 + 1]) * sj.y);
+                        m[c] = fmax3(m[c], __uint_as_float(r[c][4 * e4 + 2]) * sj.z,
+                                     __uint_as_float(r[c][4 * e4 + 3]) * sj.w);
                     }
                 }
+                n_test += 4;
+                const float bar_lo = theta - fabsf(theta) * 1e-6f;
+                uint32_t passes = 0;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) passes |= (valid && m[c] * si >= bar_lo ? 1u : 0u) << c;
+                if (timing) {
+                    const long long t1 = clock64();
+                    cyc_f += t1 - t0;
+                    t0 = t1;
+                }
+                if (!__any_sync(0xffffffffu, passes != 0)) continue;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const bool pass = (passes >> c) & 1u;
+                    if (!__any_sync(0xffffffffu, pass)) continue;
+                    if (__any_sync(0xffffffffu, nb > kTkBuf - 32)) flush();  // room for a chunk
+                    // the passing rows' 32 accumulators go through the warp's transpose, and
+                    // the whole warp tests one row's 32 columns at a time (lane = column)
+                    if (pass) {
+                        ++n_scan;
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) scr[lane * 33 + e] = __uint_as_float(r[c][e]);
+                    }
+                    __syncwarp();
+                    const float sj = scb[128 * h + 32 * c + lane];
+                    const int jj = idb[128 * h + 32 * c + lane];
+                    uint32_t todo = __ballot_sync(0xffffffffu, pass);
+                    while (todo) {
+                        const int L = __ffs(todo) - 1;
+                        todo &= todo - 1;
+                        const float sL = __shfl_sync(0xffffffffu, si, L);
+                        const float thL = __shfl_sync(0xffffffffu, theta, L);
+                        const int thjL = __shfl_sync(0xffffffffu, theta_j, L);
+                        const int rowL = __shfl_sync(0xffffffffu, row, L);
+                        const int nbL = __shfl_sync(0xffffffffu, nb, L);
+                        const float val = (scr[L * 33 + lane] * sL) * sj;
+                        const bool take = better(val, jj, thL, thjL) && jj != rowL && jj < a.R;
+                        const unsigned bal = __ballot_sync(0xffffffffu, take);
+                        if (take) {
+                            const int slot = (nbL + __popc(bal & lt)) * kTkRows + (rl - lane + L);
+                            buf_v[slot] = val;
+                            buf_j[slot] = jj;
+                        }
+                        if (lane == L) nb += __popc(bal);
+                    }
+                    __syncwarp();
+                }
+                if (timing) cyc_s += clock64() - t0;
             }
-            // a row is final once no later column can beat its k-th value
-            if (k > 0 && a.norm && !warp_final && it + 1 < ntiles) {
-                const float nb = __ldg(a.norm + (it + 1) * kTkCols);
-                const bool fin = !valid || ni * nb < theta;
-                __syncwarp();
+            // a row is final once no later column can beat its k-th value (checked every
+            // eighth tile, after the buffers are moved into the heaps)
+            if (k > 0 && a.norm && !warp_final && it + 1 < ntiles && (it & 7) == 7) {
+                flush();
+                const float nb1 = __ldg(a.norm + (it + 1) * kTkCols);
+                const bool fin = !valid || ni * nb1 < theta;
                 if (__all_sync(0xffffffffu, fin)) {
                     warp_final = true;
                     if (lane == 0) atomicAdd(ndone, 1);
@@ -531,13 +604,18 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
             }
             if (it + 1 < ntiles) stage(b ^ 1, nxt_s, nxt_i);
         }
+        if (k > 0) flush();
         if (a.prof) {
             atomicAdd(a.prof + 0, n_test);
             atomicAdd(a.prof + 1, n_scan);
             atomicAdd(a.prof + 2, n_push);
+            atomicAdd(a.prof + 3, n_flush);
             atomicAdd(a.prof + 4, polls);
             atomicAdd(a.prof + 7, cyc_wait);
             atomicAdd(a.prof + 8, (unsigned long long)(clock64() - cyc0));
+            atomicAdd(a.prof + 12, cyc_tm);
+            atomicAdd(a.prof + 13, cyc_f);
+            atomicAdd(a.prof + 14, cyc_s);
         }
         if (!ok) {
             if (!*abort) atomicExch(a.err, 3);
