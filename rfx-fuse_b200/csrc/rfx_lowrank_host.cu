@@ -243,11 +243,11 @@ void run_product(Ctx& c, int r0, int r1, int k, int* oi, float* ov, float* dense
         unsigned long long hp[16] = {};
         RFX_CUDA(cudaMemcpy(hp, prof, 128, cudaMemcpyDeviceToHost));
         std::fprintf(stderr,
-                     "[rfx topk] rows=%d chunks=%llu scanned=%llu pushes=%llu flushes=%llu "
+                     "[rfx topk] rows=%d chunks=%llu scanned=%llu pushes=%llu finality-cycles=%llu "
                      "polls: readout=%llu mma=%llu load=%llu  cycles: readout wait=%llu "
-                     "readout total=%llu mma wait-acc=%llu mma wait-load=%llu load wait-free=%llu tmem=%llu filter=%llu scan=%llu\n",
+                     "readout total=%llu mma wait-acc=%llu mma wait-load=%llu load wait-free=%llu tmem=%llu filter=%llu scan=%llu stage=%llu\n",
                      r1 - r0, hp[0], hp[1], hp[2], hp[3], hp[4], hp[5], hp[6], hp[7], hp[8], hp[9],
-                     hp[10], hp[11], hp[12], hp[13], hp[14]);
+                     hp[10], hp[11], hp[12], hp[13], hp[14], hp[15]);
     }
 }
 

@@ -24,7 +24,7 @@
 //               buffers into the rows' heaps of the best k together, so most lanes work in
 //               each heap step (a stream in no particular order replaces the k-th entry about
 //               k ln(N / k) times, and single-lane pushes cost a whole warp each).  Every
-//               eighth tile, after such a flush, a row is final once n_i * n_(next tile's
+//               fourth tile, after such a flush, a row is final once n_i * n_(next tile's
 //               first column) is below its k-th value; when all 128 rows are final the CTA
 //               lowers its stop limit and the three roles end their sweeps.
 // The single-thread producer and MMA roles sleep inside mbarrier.try_wait (suspend-time
@@ -47,6 +47,10 @@ namespace {
 constexpr unsigned long long kWaitNs = 1000000000ull;
 // A sleeping waiter stays in try_wait until the phase completes or this many nanoseconds pass.
 constexpr uint32_t kSuspendNs = 2000;
+#ifndef RFX_TK_CHECK
+#define RFX_TK_CHECK 4
+#endif
+constexpr int kTkCheck = RFX_TK_CHECK;  // tiles between flush + finality checks
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -202,7 +206,7 @@ __device__ __forceinline__ void tmem_pin32(uint32_t* r) {
                    "+r"(r[30]), "+r"(r[31]));
 }
 
-// The best k of one row are kept as a binary heap in shared memory whose root is the
+// The best k of one row are kept as a 4-ary heap in shared memory whose root is the
 // worst kept entry (the bar a new column must beat).  Entry s of the row sits at
 // v[s * kTkRows], j[s * kTkRows] (slot-major: lanes never share a bank).  Sift-up and
 // sift-down run a fixed number of predicated steps, so lanes of a warp stay converged.
@@ -210,14 +214,15 @@ __device__ __forceinline__ bool better(float va, int ja, float vb, int jb) {
     return va > vb || (va == vb && ja < jb);
 }
 
-constexpr int kHeapDepth = 6;  // levels below the root of a heap of <= 64 entries
+constexpr int kHeapDepth = 3;  // levels below the root of a 4-ary heap of <= 64 entries
+                               // (1 + 4 + 16 + 64 slots); a node's 4 children load together
 
 // Insert (val, col) into a heap of n < k entries.
 __device__ __forceinline__ void heap_insert(float* v, int* j, int n, float val, int col) {
     int i = n;
 #pragma unroll
     for (int l = 0; l < kHeapDepth; ++l) {
-        const int p = (i - 1) >> 1;
+        const int p = (i - 1) >> 2;
         if (i > 0 && better(v[p * kTkRows], j[p * kTkRows], val, col)) {  // parent is better:
             v[i * kTkRows] = v[p * kTkRows];                               // the new entry rises
             j[i * kTkRows] = j[p * kTkRows];
@@ -233,13 +238,24 @@ __device__ __forceinline__ void heap_replace_root(float* v, int* j, int n, float
     int i = 0;
 #pragma unroll
     for (int l = 0; l < kHeapDepth; ++l) {
-        const int c0 = 2 * i + 1, c1 = c0 + 1;
-        int c = c0;
-        if (c1 < n && better(v[c0 * kTkRows], j[c0 * kTkRows], v[c1 * kTkRows], j[c1 * kTkRows])) c = c1;
-        if (c0 < n && better(val, col, v[c * kTkRows], j[c * kTkRows])) {  // worse child rises
-            v[i * kTkRows] = v[c * kTkRows];
-            j[i * kTkRows] = j[c * kTkRows];
-            i = c;
+        const int c0 = 4 * i + 1;
+        float cv[4];
+        int cj[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const bool in = c0 + u < n;
+            cv[u] = in ? v[(c0 + u) * kTkRows] : __int_as_float(0x7f800000);
+            cj[u] = in ? j[(c0 + u) * kTkRows] : 0x7fffffff;
+        }
+        // the worst child (absent children rank as +inf, never the worst)
+        int w = 0;
+#pragma unroll
+        for (int u = 1; u < 4; ++u)
+            if (better(cv[w], cj[w], cv[u], cj[u])) w = u;
+        if (c0 < n && better(val, col, cv[w], cj[w])) {  // the worst child rises
+            v[i * kTkRows] = cv[w];
+            j[i * kTkRows] = cj[w];
+            i = c0 + w;
         }
     }
     v[i * kTkRows] = val;
@@ -250,6 +266,20 @@ __device__ __forceinline__ void heap_replace_root(float* v, int* j, int n, float
 __device__ __forceinline__ float fmax3(float x, float y, float z) {
     float d;
     asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(x), "f"(y), "f"(z));
+    return d;
+}
+
+// Two fp32 products in one packed instruction (mul.rn.f32x2 of sm_100; each lane of the pair
+// rounds like a scalar multiply).
+__device__ __forceinline__ float2 fmul2(float x0, float x1, float y0, float y1) {
+    float2 d;
+    asm("{\n\t.reg .b64 a, b, c;\n\t"
+        "mov.b64 a, {%2, %3};\n\t"
+        "mov.b64 b, {%4, %5};\n\t"
+        "mul.rn.f32x2 c, a, b;\n\t"
+        "mov.b64 {%0, %1}, c;\n\t}\n"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(x0), "f"(x1), "f"(y0), "f"(y1));
     return d;
 }
 
@@ -420,7 +450,7 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
         const uint32_t lane_addr = (uint32_t)(32 * (warp & 3)) << 16;
         bool ok = true;
         unsigned long long n_test = 0, n_scan = 0, n_push = 0, polls = 0, n_flush = 0;
-        unsigned long long cyc_wait = 0, cyc_tm = 0, cyc_f = 0, cyc_s = 0;
+        unsigned long long cyc_wait = 0, cyc_tm = 0, cyc_f = 0, cyc_s = 0, cyc_fin = 0, cyc_stage = 0;
         const bool timing = a.prof != nullptr;  // per-warp cycle split when counters are on
         const long long cyc0 = clock64();
         // Candidates that beat the bar are appended to the row's buffer; the warp moves its 32
@@ -536,10 +566,12 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
 #pragma unroll
                     for (int c = 0; c < 4; ++c) {
                         const float4 sj = reinterpret_cast<const float4*>(scb + 128 * h + 32 * c)[e4];
-                        m[c] = fmax3(m[c], __uint_as_float(r[c][4 * e4]) * sj.x,
-                                     __uint_as_float(r[c][4 * e4 + 1]) * sj.y);
-                        m[c] = fmax3(m[c], __uint_as_float(r[c][4 * e4 + 2]) * sj.z,
-                                     __uint_as_float(r[c][4 * e4 + 3]) * sj.w);
+                        const float2 p01 = fmul2(__uint_as_float(r[c][4 * e4]),
+                                                 __uint_as_float(r[c][4 * e4 + 1]), sj.x, sj.y);
+                        const float2 p23 = fmul2(__uint_as_float(r[c][4 * e4 + 2]),
+                                                 __uint_as_float(r[c][4 * e4 + 3]), sj.z, sj.w);
+                        m[c] = fmax3(m[c], p01.x, p01.y);
+                        m[c] = fmax3(m[c], p23.x, p23.y);
                     }
                 }
                 n_test += 4;
@@ -592,8 +624,9 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
                 if (timing) cyc_s += clock64() - t0;
             }
             // a row is final once no later column can beat its k-th value (checked every
-            // eighth tile, after the buffers are moved into the heaps)
-            if (k > 0 && a.norm && !warp_final && it + 1 < ntiles && (it & 7) == 7) {
+            // kTkCheck-th tile, after the buffers are moved into the heaps)
+            long long tf = timing ? clock64() : 0;
+            if (k > 0 && a.norm && !warp_final && it + 1 < ntiles && (it % kTkCheck) == kTkCheck - 1) {
                 flush();
                 const float nb1 = __ldg(a.norm + (it + 1) * kTkCols);
                 const bool fin = !valid || ni * nb1 < theta;
@@ -602,20 +635,27 @@ k_topk_tc(const __grid_constant__ CUtensorMap tm, TopkArgs a) {
                     if (lane == 0) atomicAdd(ndone, 1);
                 }
             }
+            if (timing) {
+                const long long t1 = clock64();
+                cyc_fin += t1 - tf;
+                tf = t1;
+            }
             if (it + 1 < ntiles) stage(b ^ 1, nxt_s, nxt_i);
+            if (timing) cyc_stage += clock64() - tf;
         }
         if (k > 0) flush();
         if (a.prof) {
             atomicAdd(a.prof + 0, n_test);
             atomicAdd(a.prof + 1, n_scan);
             atomicAdd(a.prof + 2, n_push);
-            atomicAdd(a.prof + 3, n_flush);
             atomicAdd(a.prof + 4, polls);
             atomicAdd(a.prof + 7, cyc_wait);
             atomicAdd(a.prof + 8, (unsigned long long)(clock64() - cyc0));
             atomicAdd(a.prof + 12, cyc_tm);
             atomicAdd(a.prof + 13, cyc_f);
             atomicAdd(a.prof + 14, cyc_s);
+            atomicAdd(a.prof + 3, cyc_fin);   // (replaces the flush count)
+            atomicAdd(a.prof + 15, cyc_stage);
         }
         if (!ok) {
             if (!*abort) atomicExch(a.err, 3);
