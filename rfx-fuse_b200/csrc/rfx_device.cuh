@@ -13,18 +13,23 @@ constexpr int kBins = 256;        // histogram bins (uint8 codes)
 constexpr uint32_t kFull = 0xffffffffu;
 constexpr unsigned long long kNoKey = ~0ull;
 constexpr int kBigSegment = 2048;  // segments above this are partitioned by a whole block
-constexpr int kSmallNode = 64;     // nodes up to this size go to the per-node small kernels
-// k_hist_lane (regression nodes of at most kSmallNode rows, one lane per drawn feature)
-constexpr int kLaneTile = 68;      // staged bins per lane (17 words: lanes in distinct banks)
+constexpr int kSmallNode = 64;     // classification nodes up to this size go to k_hist_small
+// k_hist_lane (regression nodes of at most kLaneNode rows, one lane per drawn feature), in
+// two instantiations: nodes of at most kLaneSmall rows (smaller shared-memory footprint, more
+// warps per SM) and the rest of the small list up to kLaneNode rows.
+constexpr int kLaneNode = 128;
+constexpr int kLaneSmall = 64;
 constexpr int kLaneSlots = 8;      // nodes per warp at most
-// shared memory of one k_hist_lane warp taking `slots` nodes
-__host__ __device__ __forceinline__ int lane_bytes(int slots) {
-    return kSmallNode * 32 * 9 + 2 * 1024 + 32 * kLaneTile + slots * kSmallNode * 8 + kLaneSlots * 4;
+// staged bins per lane for nodes of `node` rows (an odd number of words: lanes in distinct banks)
+__host__ __device__ constexpr int lane_tile(int node) { return node + 4; }
+// shared memory of one k_hist_lane warp taking `slots` nodes of at most `node` rows
+__host__ __device__ constexpr int lane_bytes(int node, int slots) {
+    return node * 32 * 9 + 2 * 1024 + 32 * lane_tile(node) + slots * node * 8 + kLaneSlots * 4;
 }
-// Rows of the largest node the small kernels search (the rest go to k_hist_warp); 0 when
-// regression draws more than 32 features (k_hist_lane needs a lane per draw).
+// Rows of the largest node the small kernels search (the rest go to the block-per-node
+// kernels); 0 when regression draws more than 32 features (k_hist_lane needs a lane per draw).
 __host__ __device__ __forceinline__ int small_node_limit(int nclass, int mtry) {
-    return (nclass == 1 && mtry > 32) ? 0 : kSmallNode;
+    return nclass == 1 ? (mtry > 32 ? 0 : kLaneNode) : kSmallNode;
 }
 
 // ------------------------------------------------------------------------------------
@@ -144,6 +149,7 @@ struct Batch {
     int M;            // maxnode
     int mtry;
     int minsplit;     // rows needed to search a node
+    int lane_split;   // 1: the small list's task records are split by size for k_hist_lane
     int tree0;        // global id of tree 0 of the batch
     int iseed, boot_seed;
     int* nin;         // [T][N]
@@ -167,8 +173,10 @@ struct Batch {
     int* srch;        // [T][M] searched nodes of the level, in node order
     int* srch_cnt;    // [T]
     int* srch_off;    // [T+1]
-    int* counters;    // [8]: 0 level total, 1 searched total, 2 next-level total, 4 big searched,
-                      //      5 big partitions, 6 small searched
+    int* counters;    // [32]: 0 level total, 1 searched total, 2 next-level total, 3 pipeline
+                      //      timeouts, 4 big searched, 5 big partitions, 6 small searched,
+                      //      7 levels with nodes, 8-9 hist_bytes, 10-11 prox_pairs, 12-19 diag,
+                      //      20 / 21 small-list records of at most / above kLaneSmall rows
     unsigned long long* hist_bytes;  // algorithmic bytes read by k_hist (sum of c_v*(mtry+L))
     unsigned long long* prox_pairs;  // proximity pair updates counted by k_prox
     unsigned long long* diag;        // [4] optional histogram diagnostics (nullptr: off): exact
@@ -179,6 +187,8 @@ struct Batch {
     int4* big_rec;    // flat over the level's big searched nodes: {tree, node, start, rows}
     int4* sml_rec;    // the same for the small searched nodes
     int* srch_sml;    // [T][M] searched nodes of at most small_node_limit rows; total in counters[6]
+                      // (task records: nodes of at most kLaneSmall rows first, counters[20]
+                      // of them)
     int* srch_sml_cnt;  // [T]
     int* srch_sml_off;  // [T+1]
     long long* part_big;  // split nodes (t*M + node) with segments above kBigSegment; count in counters[5]

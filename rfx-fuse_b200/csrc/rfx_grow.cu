@@ -65,6 +65,8 @@ __global__ void __launch_bounds__(1024) k_level_begin(Batch B, int level) {
     if (threadIdx.x == 0) {
         B.lvl_off[B.T] = carry;
         B.counters[0] = carry;
+        B.counters[20] = 0;
+        B.counters[21] = 0;
         if (carry > 0) B.counters[7] = level + 1;  // levels that had nodes
         B.counters[2] = 0;
         B.counters[5] = 0;
@@ -73,7 +75,7 @@ __global__ void __launch_bounds__(1024) k_level_begin(Batch B, int level) {
 
 // ---------------------------------------------------------------------------------------
 // Node evaluation (classification: one warp per node of the level; regression: one lane
-// per node of at most kLaneNode rows, one warp per larger node): member count, class
+// per node of at most kEvalLaneNode rows, one warp per larger node): member count, class
 // counts and majority, or the serial float sums of y; the size, purity and variance tests that
 // decide whether the node is searched (src/rf_growtree.cpp:700-774); crit0 (:783-795).
 // Nodes that are not searched become terminal here.
@@ -114,7 +116,7 @@ __device__ __forceinline__ void node_finalize(const Batch& B, size_t m, int c, i
 }
 
 // Regression nodes up to this many rows are summed by one lane (32 nodes per warp).
-constexpr int kLaneNode = 64;
+constexpr int kEvalLaneNode = 64;
 
 __global__ void __launch_bounds__(256) k_node_eval(Data D, Batch B, int cur) {
     __shared__ int ccount[8][kMaxClass];
@@ -137,7 +139,7 @@ __global__ void __launch_bounds__(256) k_node_eval(Data D, Batch B, int cur) {
                 start = B.nd_start[m];
                 c = B.nd_cnt[m];
             }
-            const bool mine = lane < G && w < total && c <= kLaneNode;
+            const bool mine = lane < G && w < total && c <= kEvalLaneNode;
             if (mine) {
                 const int* seg = B.seg[cur] + (size_t)t * D.N + start;
                 float ts = 0.0f, ts2 = 0.0f;
@@ -312,6 +314,9 @@ __global__ void __launch_bounds__(1024) k_srch_scan(Batch B) {
 
 // Flat task records of the level's big and small searched nodes (one block per tree), so
 // that the histogram kernels find a task's tree, node, segment start and size with one load.
+// True when the small list feeds k_hist_lane (regression): its records are split by size.
+__device__ __forceinline__ bool lane_split_list(const Batch& B) { return B.lane_split != 0; }
+
 __global__ void __launch_bounds__(256) k_task_records(Batch B) {
     const int t = blockIdx.x;
     const size_t base = (size_t)t * B.M;
@@ -320,8 +325,16 @@ __global__ void __launch_bounds__(256) k_task_records(Batch B) {
         const bool big = i < nb;
         const int node = big ? B.srch_big[base + i] : B.srch_sml[base + (i - nb)];
         const int4 r = make_int4(t, node, B.nd_start[base + node], B.nd_cnt[base + node]);
-        if (big) B.big_rec[B.srch_big_off[t] + i] = r;
-        else B.sml_rec[B.srch_sml_off[t] + (i - nb)] = r;
+        if (big) {
+            B.big_rec[B.srch_big_off[t] + i] = r;
+        } else if (lane_split_list(B)) {
+            // regression small list: nodes of at most kLaneSmall rows from the front, the
+            // others from the back (two k_hist_lane instantiations take the two ranges)
+            if (r.w <= kLaneSmall) B.sml_rec[atomicAdd(&B.counters[20], 1)] = r;
+            else B.sml_rec[B.counters[6] - 1 - atomicAdd(&B.counters[21], 1)] = r;
+        } else {
+            B.sml_rec[B.srch_sml_off[t] + (i - nb)] = r;
+        }
     }
 }
 

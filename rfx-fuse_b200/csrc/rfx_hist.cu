@@ -3,10 +3,10 @@
 // (src/rf_growtree.cpp:820-836, :929-955), for every searched node of a level at once.
 //
 // Three kernels share the work by node size:
-//   k_hist_warp   nodes above kSmallNode rows: one block per (node, group of up to 16
+//   k_hist_warp   nodes above the small-node limit: one block per (node, group of up to 16
 //                 draws), one warp per drawn feature streaming the node's rows 32 at a time
 //                 (bins and targets gathered from the packed rows, no block barriers);
-//   k_hist_lane   regression nodes up to kSmallNode rows: one LANE per (node, drawn
+//   k_hist_lane   regression nodes up to kLaneNode rows: one LANE per (node, drawn
 //                 feature), several nodes per warp, the node's rows staged in shared memory
 //                 once and every lane running its feature's histogram serially;
 //   k_hist_small  classification nodes up to kSmallNode rows: one warp per node.
@@ -459,7 +459,7 @@ __device__ __forceinline__ void hist_warp(const Data& D, const Batch& B, int cur
 }
 
 // ---------------------------------------------------------------------------------------
-// k_hist_pipe: regression nodes above kSmallNode rows, warp-specialised.  A block takes one
+// k_hist_pipe: regression nodes above kLaneNode rows, warp-specialised.  A block takes one
 // searched node and up to `warps` of its draws.  Warp 0 (producer) streams the node's packed
 // rows into a ring of kPipeBufs chunks of `ch` rows in shared memory (16-byte cp.async; row
 // stride rs + 16 bytes, the 16-byte multiple that spreads 32 consecutive rows over the most
@@ -820,7 +820,7 @@ __global__ void __launch_bounds__(512, 1) k_hist_warp_class(Data D, Batch B, int
 }
 
 // ---------------------------------------------------------------------------------------
-// k_hist_lane: regression nodes of at most kSmallNode rows.  A warp takes `slots` nodes of
+// k_hist_lane: regression nodes of at most kLaneNode rows.  A warp takes `slots` nodes of
 // the level's small list; lane = slot * mtry + draw.  The nodes' rows (drawn bins and
 // targets) are staged in shared memory by the whole warp, then every lane builds its draw's
 // histogram as a list of the non-empty bins (a 256-bit set gives each bin its list index),
@@ -828,16 +828,16 @@ __global__ void __launch_bounds__(512, 1) k_hist_warp_class(Data D, Batch B, int
 //
 // Filter.  With the exact chain values L, R (left/right sums), the reference's MSE times
 // the node size is P - G + d, where P = L2 + R2 is within 2m u T2 of T2 = sum of the node's
-// squared targets (m <= kSmallNode list entries), G = L^2/cl + R^2/cr, and |d| <= 16.1 u T2
+// squared targets (m <= kLaneNode list entries), G = L^2/cl + R^2/cr, and |d| <= 16.1 u T2
 // (rounding of the float formula; G <= P).  The approximation G_h (hardware reciprocals) is
-// within 5.1 u T2 of G.  So the reference's choice has G_h >= max G_h - 2 (2 kSmallNode + 22) u T2
-// over all draws of the node; only those entries get the exact criterion (the window below
-// is that bound times 1.25).
+// within 5.1 u T2 of G.  So the reference's choice has G_h >= max G_h - 2 (2 kLaneNode + 22) u T2
+// over all draws of the node; only those entries get the exact criterion (kLaneWin is that
+// bound times 1.25, rounded up).
 //
 // Per-warp shared memory (lane_bytes(slots)):
-//   LS float2[kSmallNode][32] (bin sum, sum of squares) | LK u8[kSmallNode][32] (counts) |
+//   LS float2[kLaneNode][32] (bin sum, sum of squares) | LK u8[kLaneNode][32] (counts) |
 //   BM u32[8][32] (bin sets) | BS u32[8][32] (list index of each set word) |
-//   TL u8[32][kLaneTile] (bins, lane-major) | TG float2[slots][kSmallNode] (targets) |
+//   TL u8[32][kLaneTile] (bins, lane-major) | TG float2[slots][kLaneNode] (targets) |
 //   UM u32[kLaneSlots] (ordered max G_h per node)
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ float rcp_approx(float x) {
@@ -846,22 +846,29 @@ __device__ __forceinline__ float rcp_approx(float x) {
     return r;
 }
 
-__global__ void __launch_bounds__(32) k_hist_lane(Data D, Batch B, int cur, int slots) {
+// NODE: the largest node of the instantiation; part 0 takes the task records [0,
+// counters[20]) (nodes of at most kLaneSmall rows), part 1 the rest of the small list.
+template <int NODE>
+__device__ __forceinline__ void hist_lane(const Data& D, const Batch& B, int cur, int slots, int part) {
+    constexpr int kLaneTile = lane_tile(NODE);
+    constexpr int kLaneH = NODE / 32;  // rows per lane when staging a node
+    constexpr float kLaneWin = (float)((5 * (2 * NODE + 22) + 1) / 2 + 8) * 0x1p-24f;
     extern __shared__ __align__(16) uint8_t smem[];
     const int lane = threadIdx.x;
     float2* LS = reinterpret_cast<float2*>(smem);
-    uint8_t* LK = smem + kSmallNode * 32 * 8;
-    uint32_t* BM = reinterpret_cast<uint32_t*>(LK + kSmallNode * 32);
+    uint8_t* LK = smem + NODE * 32 * 8;
+    uint32_t* BM = reinterpret_cast<uint32_t*>(LK + NODE * 32);
     uint32_t* BS = BM + 256;
     uint8_t* TL = reinterpret_cast<uint8_t*>(BS + 256);
     float2* TG = reinterpret_cast<float2*>(TL + 32 * kLaneTile);
-    unsigned* UM = reinterpret_cast<unsigned*>(TG + slots * kSmallNode);
+    unsigned* UM = reinterpret_cast<unsigned*>(TG + slots * NODE);
     const int mtry = B.mtry, rs = D.rs, ro = D.ro;
-    const int total = B.counters[6];
+    const int first = part == 0 ? 0 : B.counters[20];
+    const int total = part == 0 ? B.counters[20] : B.counters[6];
     const int slot = lane / mtry, d = lane - slot * mtry;
     const bool lane_on = slot < slots;
     const uint8_t* tl = TL + lane * kLaneTile;
-    for (int g0 = blockIdx.x * slots; g0 < total; g0 += gridDim.x * slots) {
+    for (int g0 = first + blockIdx.x * slots; g0 < total; g0 += gridDim.x * slots) {
         int my_t = 0, my_node = 0, my_c = 0, my_start = 0;
         if (lane < slots && g0 + lane < total) {
             const int4 rec = B.sml_rec[g0 + lane];  // {tree, node, start, rows}
@@ -873,17 +880,19 @@ __global__ void __launch_bounds__(32) k_hist_lane(Data D, Batch B, int cur, int 
         if (lane < slots) UM[lane] = 0u;
         // ---- stage: lanes take rows, every drawn feature's bin and the target (row ids of
         // all slots first, so that their loads are in flight together)
-        int rid[2 * kLaneSlots];
+        int rid[kLaneH * kLaneSlots];
 #pragma unroll
         for (int s = 0; s < kLaneSlots; ++s) {
-            rid[2 * s] = rid[2 * s + 1] = -1;
+#pragma unroll
+            for (int h = 0; h < kLaneH; ++h) rid[kLaneH * s + h] = -1;
             if (s < slots) {
                 const int c = __shfl_sync(kFull, my_c, s);
                 const int t = __shfl_sync(kFull, my_t, s);
                 const int start = __shfl_sync(kFull, my_start, s);
                 const int* seg = B.seg[cur] + (size_t)t * D.N + start;
-                if (lane < c) rid[2 * s] = __ldg(seg + lane);
-                if (lane + 32 < c) rid[2 * s + 1] = __ldg(seg + lane + 32);
+#pragma unroll
+                for (int h = 0; h < kLaneH; ++h)
+                    if (lane + 32 * h < c) rid[kLaneH * s + h] = __ldg(seg + lane + 32 * h);
             }
         }
 #pragma unroll
@@ -897,12 +906,12 @@ __global__ void __launch_bounds__(32) k_hist_lane(Data D, Batch B, int cur, int 
             if (lane == 0 && B.hist_bytes)
                 atomicAdd(B.hist_bytes, (unsigned long long)c * (unsigned long long)(mtry + 4));
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
+            for (int h = 0; h < kLaneH; ++h) {
                 if (h * 32 >= c) break;
                 const int i = h * 32 + lane;
-                const bool ok = rid[2 * s + h] >= 0;
-                const uint8_t* row = D.rows + (ok ? (size_t)rid[2 * s + h] * rs : 0);
-                if (ok) TG[s * kSmallNode + i] = __ldg(reinterpret_cast<const float2*>(row + ro));
+                const bool ok = rid[kLaneH * s + h] >= 0;
+                const uint8_t* row = D.rows + (ok ? (size_t)rid[kLaneH * s + h] * rs : 0);
+                if (ok) TG[s * NODE + i] = __ldg(reinterpret_cast<const float2*>(row + ro));
                 uint8_t* dst = TL + (s * mtry) * kLaneTile + i;
                 for (int dd = 0; dd < mtry; ++dd) {
                     const int fd = __shfl_sync(kFull, fl, dd);
@@ -916,7 +925,7 @@ __global__ void __launch_bounds__(32) k_hist_lane(Data D, Batch B, int cur, int 
         const int c = lane_on ? cs : 0;
         const int t = __shfl_sync(kFull, my_t, sl);
         const int node = __shfl_sync(kFull, my_node, sl);
-        const float2* tg = TG + sl * kSmallNode;
+        const float2* tg = TG + sl * NODE;
         // ---- bin set and list indices
 #pragma unroll
         for (int q = 0; q < 8; ++q) BM[q * 32 + lane] = 0u;
@@ -1002,7 +1011,7 @@ __global__ void __launch_bounds__(32) k_hist_lane(Data D, Batch B, int cur, int 
         if (lane_on && gmax >= 0.0f) atomicMax(&UM[slot], ord_of(gmax));
         __syncwarp();
         const unsigned um = lane_on ? UM[slot] : 0u;
-        const float thr = um ? float_of(um) - 0x1.8p-16f * tot2 : 0.0f;
+        const float thr = um ? float_of(um) - kLaneWin * tot2 : 0.0f;
         if (um != 0u && gmax >= thr) {
             float L = 0.0f, R = tot, L2 = 0.0f, R2 = tot2;
             int kc = 0;
@@ -1030,6 +1039,13 @@ __global__ void __launch_bounds__(32) k_hist_lane(Data D, Batch B, int cur, int 
         }
         __syncwarp();
     }
+}
+
+__global__ void __launch_bounds__(32) k_hist_lane(Data D, Batch B, int cur, int slots) {
+    hist_lane<kLaneSmall>(D, B, cur, slots, 0);
+}
+__global__ void __launch_bounds__(32) k_hist_lane_mid(Data D, Batch B, int cur, int slots) {
+    hist_lane<kLaneNode>(D, B, cur, slots, 1);
 }
 
 // ---------------------------------------------------------------------------------------

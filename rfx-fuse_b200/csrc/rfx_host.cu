@@ -139,6 +139,7 @@ void alloc_batch(Ctx& c, int Tcap) {
     B.M = c.M;
     B.mtry = c.prm.mtry;
     B.minsplit = c.task == RFX_TASK_REGRESSION ? 2 * c.prm.minndsize : c.prm.minndsize;
+    B.lane_split = c.task == RFX_TASK_REGRESSION && c.prm.mtry <= 32 ? 1 : 0;
     B.iseed = c.prm.iseed;
     B.boot_seed = c.prm.boot_seed;
     c.Tcap = Tcap;
@@ -340,7 +341,8 @@ struct HistCfg {
     rfx::HistArgs a;
     int threads, smem, grid;
     int small_warp_bytes, small_smem, small_grid;  // k_hist_small (classification)
-    int lane_slots, lane_grid, lane_bytes;         // k_hist_lane (regression)
+    int lane_slots, lane_grid, lane_bytes;         // k_hist_lane (regression, <= kLaneSmall rows)
+    int mid_grid = 0, mid_bytes = 0;               // k_hist_lane_mid (up to kLaneNode rows)
     rfx::PipeArgs pa;                              // k_hist_pipe (regression)
     int pipe_threads = 0, pipe_smem = 0, pipe_grid = 0;
 };
@@ -403,11 +405,16 @@ HistCfg hist_cfg(Ctx& c) {
         h.small_grid = c.sm_count * std::max(1, per_sm);
     } else if (mtry <= 32) {
         h.lane_slots = std::min(rfx::kLaneSlots, 32 / mtry);
-        h.lane_bytes = rfx::lane_bytes(h.lane_slots);
+        h.lane_bytes = rfx::lane_bytes(rfx::kLaneSmall, h.lane_slots);
         RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist_lane, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       h.lane_bytes));
         RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist_lane, 32, h.lane_bytes));
         h.lane_grid = c.sm_count * std::max(1, per_sm);
+        h.mid_bytes = rfx::lane_bytes(rfx::kLaneNode, h.lane_slots);
+        RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist_lane_mid, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      h.mid_bytes));
+        RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist_lane_mid, 32, h.mid_bytes));
+        h.mid_grid = c.sm_count * std::max(1, per_sm);
     }
     return h;
 }
@@ -569,8 +576,10 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
                 rfx::k_hist_pipe<<<hc.pipe_grid, hc.pipe_threads, hc.pipe_smem, st>>>(D, B, cl, hc.pa);
             else
                 rfx::k_hist_warp_regr<<<hc.grid, hc.threads, hc.smem, st>>>(D, B, cl, hc.a);
-                if (hc.lane_grid > 0)
+                if (hc.lane_grid > 0) {
                     rfx::k_hist_lane<<<hc.lane_grid, 32, hc.lane_bytes, st>>>(D, B, cl, hc.lane_slots);
+                    rfx::k_hist_lane_mid<<<hc.mid_grid, 32, hc.mid_bytes, st>>>(D, B, cl, hc.lane_slots);
+                }
             } else {
                 rfx::k_hist_warp_class<<<hc.grid, hc.threads, hc.smem, st>>>(D, B, cl, hc.a);
                 rfx::k_hist_small<<<hc.small_grid, 256, hc.small_smem, st>>>(D, B, cl, hc.small_warp_bytes);
@@ -580,7 +589,7 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
             rfx::k_partition<<<gw, 256, 0, st>>>(D, B, cl);
             rfx::k_partition_big<<<c.sm_count * 2, 256, 0, st>>>(D, B, cl);
             RFX_LAUNCH("level kernels");
-            c.launches += 10;
+            c.launches += 8 + (c.nclass != 1 ? 2 : (hc.lane_grid > 0 ? 3 : 1));
         }
         RFX_CUDA(cudaMemcpyAsync(c.h_counters, B.counters, c.level_log ? 80 : 32, cudaMemcpyDeviceToHost, st));
         RFX_CUDA(cudaStreamSynchronize(st));
