@@ -473,10 +473,13 @@ __device__ __forceinline__ void hist_warp(const Data& D, const Batch& B, int cur
 // access each.  Every wait is bounded (about one second); on expiry the block records
 // counters[3] and returns after its own copies have landed.
 //
-// Shared memory: mbarriers full[kPipeBufs], empty[kPipeBufs], cons | umin[2] | ring
+// Shared memory: mbarriers full[kPipeBufs], empty[kPipeBufs] | umin[kPipeBounds] | ring
 // [kPipeBufs][ch][rs + 16] | per consumer HE float4[256] | BL u8[256] | CF u8[256].
 // ---------------------------------------------------------------------------------------
 constexpr int kPipeBufs = 4;
+// Slots of the per-node bound (the consumers of one block are at most kPipeBufs chunks, so
+// at most 4 tasks, apart).
+constexpr int kPipeBounds = 8;
 constexpr int kPipeDraw = 256 * 16 + 512;  // shared memory per consumer warp
 constexpr unsigned long long kPipeWaitNs = 1000000000ull;
 
@@ -522,8 +525,7 @@ __global__ void __launch_bounds__(544, 2) k_hist_pipe(Data D, Batch B, int cur, 
     extern __shared__ __align__(16) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kPipeBufs;
-    uint64_t* cons = empty + kPipeBufs;  // the consumers' per-node barrier
-    unsigned* s_umin = reinterpret_cast<unsigned*>(smem + 96);
+    unsigned* s_umin = reinterpret_cast<unsigned*>(smem + 96);  // [kPipeBounds]
     uint8_t* ring = smem + 128;
     const int ch = a.ch, RS = a.rstride, W = a.warps;
     uint8_t* dbase = ring + (size_t)kPipeBufs * ch * RS;
@@ -534,8 +536,7 @@ __global__ void __launch_bounds__(544, 2) k_hist_pipe(Data D, Batch B, int cur, 
             pipe_init(&full[b], 32);
             pipe_init(&empty[b], W);
         }
-        pipe_init(cons, W);
-        s_umin[0] = s_umin[1] = 0xffffffffu;
+        for (int k = 0; k < kPipeBounds; ++k) s_umin[k] = 0xffffffffu;
     }
     __syncthreads();
     const int total = B.counters[4] * a.groups;
@@ -624,7 +625,10 @@ __global__ void __launch_bounds__(544, 2) k_hist_pipe(Data D, Batch B, int cur, 
         const int mv = grp * W + cw;
         const bool active = mv < B.mtry;
         const int f = active ? fcur : 0;
-        unsigned* umin = &s_umin[it & 1];
+        unsigned* umin = &s_umin[it % kPipeBounds];
+        // the slot of task it + kPipeBounds / 2 starts empty: no consumer is that far ahead
+        // of consumer 0, nor still on the task that used it before
+        if (cw == 0 && lane == 0) s_umin[(it + kPipeBounds / 2) % kPipeBounds] = 0xffffffffu;
         if (cw == 0 && lane == 0 && grp == 0 && B.hist_bytes)
             atomicAdd(B.hist_bytes, (unsigned long long)c * (unsigned long long)(B.mtry + 4));
         for (int k = lane; k < 256; k += 32) HE[k] = make_float4(0.0f, 0.0f, 0.0f, tag0);
@@ -676,6 +680,7 @@ __global__ void __launch_bounds__(544, 2) k_hist_pipe(Data D, Batch B, int cur, 
         float lo[8];
         int binq[8];
         int nm = 0;
+        unsigned own = 0xffffffffu;
         if (active) {
             {
                 int k = 0;
@@ -752,17 +757,15 @@ __global__ void __launch_bounds__(544, 2) k_hist_pipe(Data D, Batch B, int cur, 
             }
             hmin = warp_min_f(hmin);
             if (lane == 0 && hmin < __int_as_float(0x7f800000)) atomicMin(umin, ord_of(hmin));
+            own = hmin < __int_as_float(0x7f800000) ? ord_of(hmin) : 0xffffffffu;
         }
-        // every consumer's bound is in umin (a bounded wait, so that no warp can hang here)
+        // The threshold: this draw's bound and the smallest bound the node's other draws have
+        // posted so far (each is an upper bound of the node's best criterion, so the best
+        // split stays a candidate of its own draw whatever the others have posted).  No
+        // consumer waits for the others.
         __syncwarp();
-        if (lane == 0) pipe_arrive(cons);
-        if (!pipe_wait(cons, (unsigned)(it & 1))) {
-            atomicExch(&B.counters[3], 1);
-            return;
-        }
-        if (cw == 0 && lane == 0) s_umin[(it + 1) & 1] = 0xffffffffu;
         if (!active) continue;
-        const unsigned uo = *umin;
+        const unsigned uo = min(own, __shfl_sync(kFull, *reinterpret_cast<volatile unsigned*>(umin), 0));
         if (uo == 0xffffffffu) continue;
         const float thr = float_of(uo);
         bool any = false;
@@ -777,29 +780,59 @@ __global__ void __launch_bounds__(544, 2) k_hist_pipe(Data D, Batch B, int cur, 
         bmax = __reduce_max_sync(kFull, (unsigned)(bmax + 1)) - 1;
         __syncwarp();
         if (lane == 0) {
-            // the reference's serial chains over the non-empty bins (empty bins add +0)
+            // the reference's serial chains over the non-empty bins (empty bins add +0); the
+            // entries of 4 bins are loaded ahead of their additions (the order of the float
+            // additions is unchanged)
             float tot = 0.0f, tot2 = 0.0f;
-            for (int j = 0; j < nm; ++j) {
-                const float4 h = HE[BL[j]];
-                tot += h.x;
-                tot2 += h.y;
+            for (int j0 = 0; j0 < nm; j0 += 4) {
+                float hx[4], hy[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const float4 h = j0 + u < nm ? HE[BL[j0 + u]] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    hx[u] = h.x;
+                    hy[u] = h.y;
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    if (j0 + u < nm) {
+                        tot += hx[u];
+                        tot2 += hy[u];
+                    }
+                }
             }
             float L = 0.0f, R = tot, L2 = 0.0f, R2 = tot2;
             int kc = 0;
             unsigned long long best = kNoKey;
-            for (int j = 0; j < nm; ++j) {
-                const int bb = BL[j];
-                if (bb > bmax) break;
-                const float4 h = HE[bb];
-                kc += (int)h.z;
-                L += h.x;
-                R -= h.x;
-                L2 += h.y;
-                R2 -= h.y;
-                if (CF[bb]) {
-                    best = min(best, regr_key(L, R, L2, R2, kc, c, ((uint32_t)mv << 8) | (uint32_t)bb));
-                    if (B.diag) atomicAdd(&B.diag[0], 1ull);
+            const int jend = nm;  // entries past bmax are skipped below
+            for (int j0 = 0; j0 < jend; j0 += 4) {
+                int bq[4];
+                float hx[4], hy[4], hz[4];
+                bool cf[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    bq[u] = j0 + u < nm ? (int)BL[j0 + u] : 256;
+                    const bool in = bq[u] <= bmax;
+                    const float4 h = in ? HE[bq[u]] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                    hx[u] = h.x;
+                    hy[u] = h.y;
+                    hz[u] = h.z;
+                    cf[u] = in && CF[bq[u]];
                 }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    if (bq[u] <= bmax) {
+                        kc += (int)hz[u];
+                        L += hx[u];
+                        R -= hx[u];
+                        L2 += hy[u];
+                        R2 -= hy[u];
+                        if (cf[u]) {
+                            best = min(best, regr_key(L, R, L2, R2, kc, c, ((uint32_t)mv << 8) | (uint32_t)bq[u]));
+                            if (B.diag) atomicAdd(&B.diag[0], 1ull);
+                        }
+                    }
+                }
+                if (bq[3] >= bmax) break;  // bins ascend: nothing after bmax
             }
             if (best != kNoKey) atomicMin(&B.nd_key[m], best);
         }

@@ -603,11 +603,12 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
                 c.hist_ms += ms;
                 c.hist_launches += 1;
                 if (c.level_log)
-                    std::fprintf(stderr, "[rfx] tree0=%d level=%d nodes=%d searched=%d big=%d small=%d next=%d hist_ms=%.3f exact=%llu rounds=%llu steps=%llu\n",
+                    std::fprintf(stderr, "[rfx] tree0=%d level=%d nodes=%d searched=%d big=%d small=%d next=%d hist_ms=%.3f exact=%llu rounds=%llu steps=%llu d3=%llu\n",
                                  tree0, lv0 + k, c.h_counters[0], c.h_counters[1], c.h_counters[4], c.h_counters[6], c.h_counters[2], ms,
                                  *reinterpret_cast<unsigned long long*>(c.h_counters + 12),
                                  *reinterpret_cast<unsigned long long*>(c.h_counters + 14),
-                                 *reinterpret_cast<unsigned long long*>(c.h_counters + 16));
+                                 *reinterpret_cast<unsigned long long*>(c.h_counters + 16),
+                                 *reinterpret_cast<unsigned long long*>(c.h_counters + 18));
             }
         }
         if (c.h_counters[2] == 0) {
