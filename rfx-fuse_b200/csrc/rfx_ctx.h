@@ -5,6 +5,7 @@
 
 #include <algorithm>
 #include <map>
+#include <mutex>
 #include <cstdint>
 #include <cstdlib>
 #include <stdexcept>
@@ -57,22 +58,81 @@ int guarded(F&& f) {
 }
 
 // Device buffer that only grows.
+// Device blocks released by destroyed contexts, per device, for the next contexts of the
+// process (a fit through the estimator API makes a new context each time; cudaMalloc and
+// the synchronising cudaFree of its buffers would otherwise recur on every fit).  A block is
+// cached only after its context's stream has drained.  An allocation takes the smallest
+// cached block of at least its size and at most twice it; when cudaMalloc runs out of
+// memory, the device's cached blocks are freed and the allocation retried.
+struct BlockCache {
+    std::mutex mu;
+    std::map<int, std::multimap<size_t, void*>> free;  // device -> (size, block)
+};
+inline BlockCache& block_cache() {
+    static BlockCache* c = new BlockCache;  // never destroyed: exit-time order does not matter
+    return *c;
+}
+inline void* cache_take(int dev, size_t bytes, size_t* got) {
+    BlockCache& bc = block_cache();
+    std::lock_guard<std::mutex> lock(bc.mu);
+    auto& m = bc.free[dev];
+    auto it = m.lower_bound(bytes);
+    if (it == m.end() || it->first > 2 * bytes) return nullptr;
+    void* p = it->second;
+    *got = it->first;
+    m.erase(it);
+    return p;
+}
+inline void cache_put(int dev, void* p, size_t bytes) {
+    BlockCache& bc = block_cache();
+    std::lock_guard<std::mutex> lock(bc.mu);
+    bc.free[dev].emplace(bytes, p);
+}
+inline void cache_flush(int dev) {
+    BlockCache& bc = block_cache();
+    std::lock_guard<std::mutex> lock(bc.mu);
+    for (auto& kv : bc.free[dev]) cudaFree(kv.second);
+    bc.free[dev].clear();
+}
+
 struct DBuf {
     void* p = nullptr;
     size_t cap = 0;
     void* get(size_t bytes) {
         if (bytes == 0) bytes = 16;
         if (bytes > cap) {
-            if (p) cudaFree(p);
+            if (p) cudaFree(p);  // synchronising: the context's queued work may still use it
             p = nullptr;
             cap = 0;
-            RFX_CUDA(cudaMalloc(&p, bytes));
+            int dev = 0;
+            RFX_CUDA(cudaGetDevice(&dev));
+            size_t got = 0;
+            if (void* q = cache_take(dev, bytes, &got)) {
+                p = q;
+                cap = got;
+                return p;
+            }
+            cudaError_t e = cudaMalloc(&p, bytes);
+            if (e == cudaErrorMemoryAllocation) {
+                cudaGetLastError();
+                cache_flush(dev);
+                e = cudaMalloc(&p, bytes);
+            }
+            if (e != cudaSuccess)
+                throw RfxError(e == cudaErrorMemoryAllocation ? RFX_ERR_OOM : RFX_ERR_CUDA,
+                               std::string("cudaMalloc: ") + cudaGetErrorString(e));
             cap = bytes;
         }
         return p;
     }
     void release() {
         if (p) cudaFree(p);
+        p = nullptr;
+        cap = 0;
+    }
+    // Hand the block to the process's cache (the owner's stream has drained).
+    void retire(int dev) {
+        if (p) cache_put(dev, p, cap);
         p = nullptr;
         cap = 0;
     }
@@ -185,8 +245,11 @@ struct Ctx {
                        &lr_err, &lr_out_i, &lr_out_v, &ts_status, &ts_bestvar, &ts_xbest, &ts_treemap,
                        &ts_nodeclass, &ts_nnode, &ts_nodepred, &ts_tnodewt};
         cudaSetDevice(device);
-        if (st) cudaStreamSynchronize(st);
-        for (DBuf* b : all) b->release();
+        const bool drained = !st || cudaStreamSynchronize(st) == cudaSuccess;
+        for (DBuf* b : all) {
+            if (drained) b->retire(device);
+            else b->release();
+        }
         if (h_counters) cudaFreeHost(h_counters);
         for (int b = 0; b < 2; ++b) {
             if (ev_stage[b]) cudaEventDestroy(ev_stage[b]);
