@@ -62,12 +62,14 @@ WORKLOAD = ("config[1]: regression n=200000 p=50 U(-1,1), ntree=500 forest, mtry
             "no proximity, maxnode=32001")
 
 
-# DRAM bytes (read + write) of one k_hist_pipe launch of a 250-tree level, measured once with
-# ncu (dram__bytes_read.sum + dram__bytes_write.sum; levels 0 and 9: 146.8 MB and 149.1 MB)
-# and carried here as a constant; the capture is summarised under profiles/.
-HIST_TRAFFIC_BYTES = 147.9e6
-HIST_TRAFFIC_SOURCE = ("ncu capture of k_hist_pipe, levels 0 and 9 of a 250-tree batch "
-                       "(146.8 MB, 149.1 MB per launch), constant")
+# DRAM bytes (read + write) of the histogram kernels per tree level (the unit the bench's
+# histogram time and algorithmic bytes are counted in), measured once with ncu over every
+# histogram launch of a 250-tree batch and carried here as a constant; the capture is
+# summarised under profiles/.
+HIST_TRAFFIC_BYTES = 179.6e6
+HIST_TRAFFIC_SOURCE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of every histogram "
+                       "launch (k_hist_pipe, k_hist_lane, k_hist_lane_mid) of a 250-tree batch: "
+                       "3232 MB over its 18 levels, per level, constant")
 
 
 def make_data(n, p, seed=20261201 + 1):
