@@ -368,8 +368,8 @@ def run_config1(args):
                          if world > 1 else "rfx_b200.RandomForestRegressor(ntree=500).fit(X, y)")
                         + " + get_oob_error()"},
         "gpu_launches": int(st["kernel_launches"]),
-        "roofline": {"bound": "hbm", "kernel": "histogram search (k_hist_warp + k_hist_lane, "
-                                                "one tree level)",
+        "roofline": {"bound": "hbm", "kernel": "histogram search (k_hist_pipe + k_hist_lane_mid "
+                                                "+ k_hist_lane, one tree level)",
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": (achieved / peak) if achieved else None,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
