@@ -15,10 +15,11 @@ constexpr unsigned long long kNoKey = ~0ull;
 constexpr int kBigSegment = 2048;  // segments above this are partitioned by a whole block
 constexpr int kSmallNode = 64;     // classification nodes up to this size go to k_hist_small
 // k_hist_lane (regression nodes of at most kLaneNode rows, one lane per drawn feature), in
-// two instantiations: nodes of at most kLaneSmall rows (smaller shared-memory footprint, more
-// warps per SM) and the rest of the small list up to kLaneNode rows.
+// three instantiations by node size (at most kLaneTiny, kLaneSmall, kLaneNode rows): the
+// smaller the nodes, the smaller the shared memory of a warp and the more warps per SM.
 constexpr int kLaneNode = 128;
 constexpr int kLaneSmall = 64;
+constexpr int kLaneTiny = 32;
 constexpr int kLaneSlots = 8;      // nodes per warp at most
 // staged bins per lane for nodes of `node` rows (an odd number of words: lanes in distinct banks)
 __host__ __device__ constexpr int lane_tile(int node) { return node + 4; }
@@ -176,7 +177,8 @@ struct Batch {
     int* counters;    // [32]: 0 level total, 1 searched total, 2 next-level total, 3 pipeline
                       //      timeouts, 4 big searched, 5 big partitions, 6 small searched,
                       //      7 levels with nodes, 8-9 hist_bytes, 10-11 prox_pairs, 12-19 diag,
-                      //      20 / 21 small-list records of at most / above kLaneSmall rows
+                      //      20 / 21 / 22 small-list records of at most kLaneTiny / above
+                      //      kLaneSmall / in between rows
     unsigned long long* hist_bytes;  // algorithmic bytes read by k_hist (sum of c_v*(mtry+L))
     unsigned long long* prox_pairs;  // proximity pair updates counted by k_prox
     unsigned long long* diag;        // [4] optional histogram diagnostics (nullptr: off): exact
@@ -186,9 +188,10 @@ struct Batch {
     int* srch_big_off;  // [T+1]
     int4* big_rec;    // flat over the level's big searched nodes: {tree, node, start, rows}
     int4* sml_rec;    // the same for the small searched nodes
+    int4* sml2_rec;   // regression: the small searched nodes of kLaneTiny+1..kLaneSmall rows
     int* srch_sml;    // [T][M] searched nodes of at most small_node_limit rows; total in counters[6]
-                      // (task records: nodes of at most kLaneSmall rows first, counters[20]
-                      // of them)
+                      // (regression task records: nodes of at most kLaneTiny rows first,
+                      // counters[20] of them, nodes above kLaneSmall rows last, counters[21])
     int* srch_sml_cnt;  // [T]
     int* srch_sml_off;  // [T+1]
     long long* part_big;  // split nodes (t*M + node) with segments above kBigSegment; count in counters[5]

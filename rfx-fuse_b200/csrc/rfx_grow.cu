@@ -67,6 +67,7 @@ __global__ void __launch_bounds__(1024) k_level_begin(Batch B, int level) {
         B.counters[0] = carry;
         B.counters[20] = 0;
         B.counters[21] = 0;
+        B.counters[22] = 0;
         if (carry > 0) B.counters[7] = level + 1;  // levels that had nodes
         B.counters[2] = 0;
         B.counters[5] = 0;
@@ -328,9 +329,11 @@ __global__ void __launch_bounds__(256) k_task_records(Batch B) {
         if (big) {
             B.big_rec[B.srch_big_off[t] + i] = r;
         } else if (lane_split_list(B)) {
-            // regression small list: nodes of at most kLaneSmall rows from the front, the
-            // others from the back (two k_hist_lane instantiations take the two ranges)
-            if (r.w <= kLaneSmall) B.sml_rec[atomicAdd(&B.counters[20], 1)] = r;
+            // regression small list, by size for the three k_hist_lane instantiations: nodes
+            // of at most kLaneTiny rows from the front of sml_rec, those above kLaneSmall
+            // from its back, the others in sml2_rec
+            if (r.w <= kLaneTiny) B.sml_rec[atomicAdd(&B.counters[20], 1)] = r;
+            else if (r.w <= kLaneSmall) B.sml2_rec[atomicAdd(&B.counters[22], 1)] = r;
             else B.sml_rec[B.counters[6] - 1 - atomicAdd(&B.counters[21], 1)] = r;
         } else {
             B.sml_rec[B.srch_sml_off[t] + (i - nb)] = r;

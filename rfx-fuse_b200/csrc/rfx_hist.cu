@@ -879,8 +879,9 @@ __device__ __forceinline__ float rcp_approx(float x) {
     return r;
 }
 
-// NODE: the largest node of the instantiation; part 0 takes the task records [0,
-// counters[20]) (nodes of at most kLaneSmall rows), part 1 the rest of the small list.
+// NODE: the largest node of the instantiation; part 0 takes sml_rec [0, counters[20]) (nodes
+// of at most kLaneTiny rows), part 1 sml2_rec [0, counters[22]) (up to kLaneSmall rows),
+// part 2 the last counters[21] records of sml_rec (up to kLaneNode rows).
 template <int NODE>
 __device__ __forceinline__ void hist_lane(const Data& D, const Batch& B, int cur, int slots, int part) {
     constexpr int kLaneTile = lane_tile(NODE);
@@ -896,15 +897,16 @@ __device__ __forceinline__ void hist_lane(const Data& D, const Batch& B, int cur
     float2* TG = reinterpret_cast<float2*>(TL + 32 * kLaneTile);
     unsigned* UM = reinterpret_cast<unsigned*>(TG + slots * NODE);
     const int mtry = B.mtry, rs = D.rs, ro = D.ro;
-    const int first = part == 0 ? 0 : B.counters[20];
-    const int total = part == 0 ? B.counters[20] : B.counters[6];
+    const int4* recs = part == 1 ? B.sml2_rec : B.sml_rec;
+    const int first = part == 2 ? B.counters[6] - B.counters[21] : 0;
+    const int total = part == 0 ? B.counters[20] : part == 1 ? B.counters[22] : B.counters[6];
     const int slot = lane / mtry, d = lane - slot * mtry;
     const bool lane_on = slot < slots;
     const uint8_t* tl = TL + lane * kLaneTile;
     for (int g0 = first + blockIdx.x * slots; g0 < total; g0 += gridDim.x * slots) {
         int my_t = 0, my_node = 0, my_c = 0, my_start = 0;
         if (lane < slots && g0 + lane < total) {
-            const int4 rec = B.sml_rec[g0 + lane];  // {tree, node, start, rows}
+            const int4 rec = recs[g0 + lane];  // {tree, node, start, rows}
             my_t = rec.x;
             my_node = rec.y;
             my_start = rec.z;
@@ -1074,11 +1076,14 @@ __device__ __forceinline__ void hist_lane(const Data& D, const Batch& B, int cur
     }
 }
 
+__global__ void __launch_bounds__(32) k_hist_lane_tiny(Data D, Batch B, int cur, int slots) {
+    hist_lane<kLaneTiny>(D, B, cur, slots, 0);
+}
 __global__ void __launch_bounds__(32) k_hist_lane(Data D, Batch B, int cur, int slots) {
-    hist_lane<kLaneSmall>(D, B, cur, slots, 0);
+    hist_lane<kLaneSmall>(D, B, cur, slots, 1);
 }
 __global__ void __launch_bounds__(32) k_hist_lane_mid(Data D, Batch B, int cur, int slots) {
-    hist_lane<kLaneNode>(D, B, cur, slots, 1);
+    hist_lane<kLaneNode>(D, B, cur, slots, 2);
 }
 
 // ---------------------------------------------------------------------------------------

@@ -113,6 +113,7 @@ void alloc_batch(Ctx& c, int Tcap) {
     B.srch_sml = (int*)c.b_srchsml.get(T * M * 4);
     B.big_rec = (int4*)c.b_bigrec.get(T * M * 16);
     B.sml_rec = (int4*)c.b_smlrec.get(T * M * 16);
+    B.sml2_rec = (int4*)c.b_sml2rec.get(T * M * 16);
     B.part_big = (long long*)c.b_partbig.get(T * (N / rfx::kBigSegment + 2) * 8);
     B.srch = (int*)c.b_srch.get(T * M * 4);
     B.srch_cnt = (int*)c.b_srchcnt.get(T * 12);
@@ -343,6 +344,7 @@ struct HistCfg {
     int small_warp_bytes, small_smem, small_grid;  // k_hist_small (classification)
     int lane_slots, lane_grid, lane_bytes;         // k_hist_lane (regression, <= kLaneSmall rows)
     int mid_grid = 0, mid_bytes = 0;               // k_hist_lane_mid (up to kLaneNode rows)
+    int tiny_grid = 0, tiny_bytes = 0;             // k_hist_lane_tiny (up to kLaneTiny rows)
     rfx::PipeArgs pa;                              // k_hist_pipe (regression)
     int pipe_threads = 0, pipe_smem = 0, pipe_grid = 0;
 };
@@ -415,6 +417,11 @@ HistCfg hist_cfg(Ctx& c) {
                                       h.mid_bytes));
         RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist_lane_mid, 32, h.mid_bytes));
         h.mid_grid = c.sm_count * std::max(1, per_sm);
+        h.tiny_bytes = rfx::lane_bytes(rfx::kLaneTiny, h.lane_slots);
+        RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist_lane_tiny, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      h.tiny_bytes));
+        RFX_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rfx::k_hist_lane_tiny, 32, h.tiny_bytes));
+        h.tiny_grid = c.sm_count * std::max(1, per_sm);
     }
     return h;
 }
@@ -577,6 +584,7 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
             else
                 rfx::k_hist_warp_regr<<<hc.grid, hc.threads, hc.smem, st>>>(D, B, cl, hc.a);
                 if (hc.lane_grid > 0) {
+                    rfx::k_hist_lane_tiny<<<hc.tiny_grid, 32, hc.tiny_bytes, st>>>(D, B, cl, hc.lane_slots);
                     rfx::k_hist_lane<<<hc.lane_grid, 32, hc.lane_bytes, st>>>(D, B, cl, hc.lane_slots);
                     rfx::k_hist_lane_mid<<<hc.mid_grid, 32, hc.mid_bytes, st>>>(D, B, cl, hc.lane_slots);
                 }
@@ -589,7 +597,7 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
             rfx::k_partition<<<gw, 256, 0, st>>>(D, B, cl);
             rfx::k_partition_big<<<c.sm_count * 2, 256, 0, st>>>(D, B, cl);
             RFX_LAUNCH("level kernels");
-            c.launches += 8 + (c.nclass != 1 ? 2 : (hc.lane_grid > 0 ? 3 : 1));
+            c.launches += 8 + (c.nclass != 1 ? 2 : (hc.lane_grid > 0 ? 4 : 1));
         }
         RFX_CUDA(cudaMemcpyAsync(c.h_counters, B.counters, c.level_log ? 80 : 32, cudaMemcpyDeviceToHost, st));
         RFX_CUDA(cudaStreamSynchronize(st));

@@ -32,6 +32,7 @@ __global__ void k_hist_warp_class(Data D, Batch B, int cur, HistArgs a);
 __global__ void k_hist_pipe(Data D, Batch B, int cur, PipeArgs a);
 __global__ void k_hist_lane(Data D, Batch B, int cur, int slots);
 __global__ void k_hist_lane_mid(Data D, Batch B, int cur, int slots);
+__global__ void k_hist_lane_tiny(Data D, Batch B, int cur, int slots);
 __global__ void k_hist_small(Data D, Batch B, int cur, int warp_bytes);
 
 // rfx_post.cu
