@@ -200,7 +200,7 @@ struct Batch {
     uint8_t* used;    // [T][p]
     int* right;       // [T] correct OOB votes (classification importance)
     int* rightimp;    // [T][p]
-    float* d2;        // [T][N][p] regression importance squared errors per OOB rank
+    float* d2;        // [T][p][N] regression importance squared errors per OOB rank
     float* d0;        // [T][N]
     float* rr;        // [T][p]
     float* rsum;      // [T][p + 1] regression importance: row-order error sums

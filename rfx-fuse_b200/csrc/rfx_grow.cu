@@ -182,10 +182,19 @@ __global__ void __launch_bounds__(256) k_node_eval(Data D, Batch B, int cur) {
 #pragma unroll
                     for (int q = 0; q < U; ++q) {
                         const int k = min(32, cb - (b0 + q * 32));
-                        for (int j = 0; j < k; ++j) {
-                            const float x = __shfl_sync(kFull, v[q], j);
-                            ts += x * 1.0f;
-                            ts2 += x * x * 1.0f;
+                        if (k == 32) {  // unrolled: the shuffles issue ahead of the chain
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) {
+                                const float x = __shfl_sync(kFull, v[q], j);
+                                ts += x * 1.0f;
+                                ts2 += x * x * 1.0f;
+                            }
+                        } else {
+                            for (int j = 0; j < k; ++j) {
+                                const float x = __shfl_sync(kFull, v[q], j);
+                                ts += x * 1.0f;
+                                ts2 += x * x * 1.0f;
+                            }
                         }
                     }
                 }

@@ -639,7 +639,7 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
             rfx::k_imp_class_rr<<<T, 256, 0, st>>>(D, B);
         } else {
             rfx::k_imp_regr<<<rg, 256, 0, st>>>(D, B);
-            const size_t warps = (size_t)T * ((p + 1 + 31) / 32);
+            const size_t warps = (size_t)T * (p + 1);
             rfx::k_imp_regr_sum<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(D, B);
             rfx::k_imp_regr_rr<<<T, 256, 0, st>>>(D, B);
         }

@@ -170,8 +170,8 @@ __global__ void k_imp_class_rr(Data D, Batch B) {
 
 // Regression importance, squared errors (cpu_varimp_regression, src/rf_varimp.cpp:477-597):
 // d0[j] for the unpermuted prediction, d2[j][k] with feature k permuted, per OOB rank j.
-// The squared errors of OOB rank j of tree t into out[0, p).
-__device__ void imp_regr_row(const Data& D, const Batch& B, int t, int j, float* out) {
+// The squared errors of OOB rank j of tree t into out[k * os], k in [0, p).
+__device__ void imp_regr_row(const Data& D, const Batch& B, int t, int j, float* out, size_t os) {
     const size_t mo = (size_t)t * B.M;
     const int *st = B.status + mo, *bv = B.bestvar + mo, *tm = B.treemap + 2 * mo;
     const float *xb = B.xbest + mo, *np = B.nodepred + mo;
@@ -188,7 +188,7 @@ __device__ void imp_regr_row(const Data& D, const Batch& B, int t, int j, float*
     // only the nodes testing k can turn the walk, so one pass down the row's path checks, at
     // every node, the permuted value of the node's feature (unless that feature's walk has
     // already left the path) and walks the tree from where a permuted walk leaves it.
-    for (int k = 0; k < D.p; ++k) out[k] = dd;
+    for (int k = 0; k < D.p; ++k) out[k * os] = dd;
     bool deep = D.has_cat != 0 || D.p > 64;
     if (!deep) {
         constexpr int kMaxPath = 48;
@@ -220,7 +220,7 @@ __device__ void imp_regr_row(const Data& D, const Batch& B, int t, int j, float*
                         }
                     }
                     const float dk = pk - y;
-                    out[f] = 1.0f * dk * dk;
+                    out[f * os] = 1.0f * dk * dk;
                 }
             }
             ++depth;
@@ -234,7 +234,7 @@ __device__ void imp_regr_row(const Data& D, const Batch& B, int t, int j, float*
                 const float dk = np[kt] - y;
                 const float e = 1.0f * dk * dk;
                 for (int k = 0; k < D.p; ++k)
-                    if ((stay >> k) & 1ull) out[k] = e;
+                    if ((stay >> k) & 1ull) out[k * os] = e;
             } else {
                 deep = true;
             }
@@ -243,47 +243,53 @@ __device__ void imp_regr_row(const Data& D, const Batch& B, int t, int j, float*
     if (deep) {
         for (int k = 0; k < D.p; ++k) {
             const float dk = walk_perm_regr(D, st, bv, xb, tm, np, nn, row, prow, k) - y;
-            out[k] = 1.0f * dk * dk;
+            out[k * os] = 1.0f * dk * dk;
         }
     }
 }
 
-// One thread per OOB rank, rows written straight to d2 (the walks, not the stores, bound
-// this kernel: staging the block's rows in shared memory measured slower).
+// One thread per OOB rank; d2 is feature-major, so a warp's stores of one feature are
+// consecutive ranks.
 __global__ void __launch_bounds__(256) k_imp_regr(Data D, Batch B) {
     const int t = blockIdx.y;
     const int j = blockIdx.x * blockDim.x + threadIdx.x;
     if (j >= B.noob[t]) return;
-    imp_regr_row(D, B, t, j, B.d2 + ((size_t)t * D.N + j) * D.p);
+    imp_regr_row(D, B, t, j, B.d2 + (size_t)t * D.p * D.N + j, (size_t)D.N);
 }
 
 // Serial sums over the OOB rows in row order (the reference's loop order).  One warp per
-// (tree, 32 columns): lane k keeps column k's running sum (k < p: the permuted errors of
-// feature k, k == p: the unpermuted errors) and reads one row of 32 consecutive floats per
-// step, 32 rows in flight.  rsum[t][k] = the sums.
+// (tree, column k): k < p the permuted errors of feature k, k == p the unpermuted errors.
+// The warp loads 8 x 32 consecutive ranks at a time (coalesced) and every lane runs the
+// same serial chain over them through shuffles.  rsum[t][k] = the sums.
 __global__ void __launch_bounds__(256) k_imp_regr_sum(Data D, Batch B) {
-    constexpr int U = 32;
+    constexpr int U = 8;
     const int p = D.p, P1 = D.p + 1;
-    const int nch = (P1 + 31) / 32;
     const int g = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
-    if (g >= B.T * nch) return;
-    const int t = g / nch, k = (g - t * nch) * 32 + lane;
-    if (k > p) return;
+    if (g >= B.T * P1) return;
+    const int t = g / P1, k = g - t * P1;
     const int noob = B.noob[t];
-    const float* src = k < p ? B.d2 + (size_t)t * D.N * p + k : B.d0 + (size_t)t * D.N;
-    const size_t stride = k < p ? (size_t)p : 1;
+    const float* src = k < p ? B.d2 + ((size_t)t * p + k) * D.N : B.d0 + (size_t)t * D.N;
     float s = 0.0f;
-    int j = 0;
-    for (; j + U <= noob; j += U) {
+    for (int b0 = 0; b0 < noob; b0 += 32 * U) {
         float x[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) x[u] = src[(size_t)(j + u) * stride];
+        for (int q = 0; q < U; ++q) {
+            const int i = b0 + q * 32 + lane;
+            x[q] = i < noob ? src[i] : 0.0f;
+        }
 #pragma unroll
-        for (int u = 0; u < U; ++u) s += x[u];
+        for (int q = 0; q < U; ++q) {
+            const int n = min(32, noob - (b0 + q * 32));
+            if (n == 32) {
+#pragma unroll
+                for (int e = 0; e < 32; ++e) s += __shfl_sync(kFull, x[q], e);
+            } else {
+                for (int e = 0; e < n; ++e) s += __shfl_sync(kFull, x[q], e);
+            }
+        }
     }
-    for (; j < noob; ++j) s += src[(size_t)j * stride];
-    B.rsum[(size_t)t * P1 + k] = s;
+    if (lane == 0) B.rsum[(size_t)t * P1 + k] = s;
 }
 
 // rr = mse_perm - mse_orig per (tree, feature), 0 for a tree without OOB rows.
