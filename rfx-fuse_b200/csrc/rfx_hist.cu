@@ -542,10 +542,10 @@ __global__ void __launch_bounds__(544, 2) k_hist_pipe(Data D, Batch B, int cur, 
     const int total = B.counters[4] * a.groups;
     long long g = 0;  // chunk counter, identical sequence in every warp
     if (warp == 0) {
-        // ---- producer: lane l copies rows l and l + 32 of each chunk (16-byte pieces); the
-        // next chunk's row ids are loaded while the current chunk's copies are issued
-        // one flat sequence of chunks over the block's tasks; the next chunk's row ids (the
-        // next task's first chunk at a task's end) load while this chunk's copies issue
+        // ---- producer: lane l copies rows l and l + 32 of each chunk (16-byte pieces), in
+        // one flat sequence of chunks over the block's tasks.  The row ids of the chunk three
+        // ahead load while this chunk's copies issue (and the record of the task after the
+        // furthest one is loaded a task ahead), so the copies never wait on an id load.
         auto rec_of = [&](int task) {
             return task < total ? B.big_rec[task / a.groups] : make_int4(0, 0, 0, 0);
         };
@@ -555,20 +555,35 @@ __global__ void __launch_bounds__(544, 2) k_hist_pipe(Data D, Batch B, int cur, 
             q0 = lane < n ? __ldg(seg + lane) : -1;
             q1 = lane + 32 < n ? __ldg(seg + 32 + lane) : -1;
         };
-        int task = blockIdx.x, c0 = 0;
-        int4 rec = rec_of(task);
-        int r0 = -1, r1 = -1;
-        if (task < total) ids(rec, 0, r0, r1);
-        while (task < total) {
-            int ntask = task, nc0 = c0 + ch;
-            int4 nrec = rec;
-            if (nc0 >= rec.w) {
-                ntask = task + gridDim.x;
-                nc0 = 0;
-                nrec = rec_of(ntask);
+        // chunk positions: (task, first row, record); `after` = record of the task that
+        // follows the furthest position's task
+        int t0 = blockIdx.x, c00 = 0;
+        int4 rc0 = rec_of(t0);
+        int4 after = rec_of(t0 + (int)gridDim.x);
+        auto advance = [&](int& t, int& c, int4& r) {
+            c += ch;
+            if (c >= r.w) {
+                t += gridDim.x;
+                c = 0;
+                r = after;
+                after = rec_of(t + (int)gridDim.x);
             }
-            int q0 = -1, q1 = -1;
-            if (ntask < total) ids(nrec, nc0, q0, q1);
+        };
+        int t1 = t0, c1 = c00, t2, c2;
+        int4 rc1 = rc0, rc2;
+        int r0 = -1, r1 = -1, q0 = -1, q1 = -1, s0 = -1, s1 = -1;
+        if (t0 < total) ids(rc0, 0, r0, r1);
+        advance(t1, c1, rc1);
+        if (t1 < total) ids(rc1, c1, q0, q1);
+        t2 = t1; c2 = c1; rc2 = rc1;
+        advance(t2, c2, rc2);
+        if (t2 < total) ids(rc2, c2, s0, s1);
+        while (t0 < total) {
+            int t3 = t2, c3 = c2;
+            int4 rc3 = rc2;
+            advance(t3, c3, rc3);
+            int u0 = -1, u1 = -1;
+            if (t3 < total) ids(rc3, c3, u0, u1);
             const int b = (int)(g % kPipeBufs);
             const long long u = g / kPipeBufs;
             if (u > 0 && !pipe_wait(&empty[b], (unsigned)((u - 1) & 1))) {
@@ -588,11 +603,12 @@ __global__ void __launch_bounds__(544, 2) k_hist_pipe(Data D, Batch B, int cur, 
             }
             pipe_arrive_on_copies(&full[b]);
             ++g;
-            task = ntask;
-            c0 = nc0;
-            rec = nrec;
-            r0 = q0;
-            r1 = q1;
+            t0 = t1; t1 = t2; t2 = t3;
+            c1 = c2; c2 = c3;
+            rc1 = rc2; rc2 = rc3;
+            r0 = q0; r1 = q1;
+            q0 = s0; q1 = s1;
+            s0 = u0; s1 = u1;
         }
         pipe_wait_copies();
         return;
