@@ -21,6 +21,9 @@ constexpr int kLaneNode = 128;
 constexpr int kLaneSmall = 64;
 constexpr int kLaneTiny = 32;
 constexpr int kLaneSlots = 8;      // nodes per warp at most
+// k_hist_pipe: chunks in the shared-memory ring; bytes before the ring (mbarriers, bounds)
+constexpr int kPipeBufs = 6;
+constexpr int kPipeHead = 256;
 // staged bins per lane for nodes of `node` rows (an odd number of words: lanes in distinct banks)
 __host__ __device__ constexpr int lane_tile(int node) { return node + 4; }
 // shared memory of one k_hist_lane warp taking `slots` nodes of at most `node` rows

@@ -476,10 +476,11 @@ __device__ __forceinline__ void hist_warp(const Data& D, const Batch& B, int cur
 // Shared memory: mbarriers full[kPipeBufs], empty[kPipeBufs] | umin[kPipeBounds] | ring
 // [kPipeBufs][ch][rs + 16] | per consumer HE float4[256] | BL u8[256] | CF u8[256].
 // ---------------------------------------------------------------------------------------
-constexpr int kPipeBufs = 4;
 // Slots of the per-node bound (the consumers of one block are at most kPipeBufs chunks, so
-// at most 4 tasks, apart).
-constexpr int kPipeBounds = 8;
+// at most kPipeBufs tasks, apart).
+constexpr int kPipeBounds = 16;
+static_assert(kPipeBounds / 2 >= kPipeBufs, "bound slots must cover the consumers' skew");
+static_assert(16 * kPipeBufs + 4 * kPipeBounds <= kPipeHead, "k_hist_pipe header");
 constexpr int kPipeDraw = 256 * 16 + 512;  // shared memory per consumer warp
 constexpr unsigned long long kPipeWaitNs = 1000000000ull;
 
@@ -525,8 +526,8 @@ __global__ void __launch_bounds__(544, 2) k_hist_pipe(Data D, Batch B, int cur, 
     extern __shared__ __align__(16) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kPipeBufs;
-    unsigned* s_umin = reinterpret_cast<unsigned*>(smem + 96);  // [kPipeBounds]
-    uint8_t* ring = smem + 128;
+    unsigned* s_umin = reinterpret_cast<unsigned*>(smem + 16 * kPipeBufs);  // [kPipeBounds]
+    uint8_t* ring = smem + kPipeHead;
     const int ch = a.ch, RS = a.rstride, W = a.warps;
     uint8_t* dbase = ring + (size_t)kPipeBufs * ch * RS;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -384,7 +384,7 @@ HistCfg hist_cfg(Ctx& c) {
         h.pa.ch = 64;
         h.pa.rstride = c.D.rs + 16;
         h.pipe_threads = 32 * (h.pa.warps + 1);
-        h.pipe_smem = 128 + 4 * h.pa.ch * h.pa.rstride + h.pa.warps * (256 * 16 + 512);
+        h.pipe_smem = rfx::kPipeHead + rfx::kPipeBufs * h.pa.ch * h.pa.rstride + h.pa.warps * (256 * 16 + 512);
         if (h.pipe_smem <= 220 * 1024) {
             RFX_CUDA(cudaFuncSetAttribute(rfx::k_hist_pipe, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           h.pipe_smem));
