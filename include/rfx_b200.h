@@ -106,6 +106,15 @@ const char* rfx_last_error(void);
 int rfx_abi_version(void);
 int rfx_device_count(void);
 
+/* Device memory of destroyed contexts is kept in a process-wide cache per device and reused
+ * by the next contexts (each estimator fit makes a new context).  No counterpart in the
+ * reference, whose CPU path allocates host memory per fit.  rfx_cached_bytes reports the
+ * bytes cached for `device` (-1: all devices); rfx_empty_cache frees them (another library
+ * in the process that needs the memory calls it first).  Contexts alive keep their own
+ * buffers either way. */
+long long rfx_cached_bytes(int device);
+int rfx_empty_cache(int device);
+
 /* Context bound to CUDA device `device`; NULL on failure (see rfx_last_error). */
 void* rfx_create(int device);
 void rfx_destroy(void* ctx);

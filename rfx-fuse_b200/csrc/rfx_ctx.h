@@ -94,6 +94,33 @@ inline void cache_flush(int dev) {
     for (auto& kv : bc.free[dev]) cudaFree(kv.second);
     bc.free[dev].clear();
 }
+// Bytes cached for `dev` (-1: every device).
+inline long long cache_bytes(int dev) {
+    BlockCache& bc = block_cache();
+    std::lock_guard<std::mutex> lock(bc.mu);
+    long long n = 0;
+    for (auto& d : bc.free)
+        if (dev < 0 || d.first == dev)
+            for (auto& kv : d.second) n += (long long)kv.first;
+    return n;
+}
+// Free the blocks cached for `dev` (-1: every device), each with its device current.
+inline void cache_empty(int dev) {
+    BlockCache& bc = block_cache();
+    std::lock_guard<std::mutex> lock(bc.mu);
+    bool any = false;
+    for (auto& d : bc.free) any = any || ((dev < 0 || d.first == dev) && !d.second.empty());
+    if (!any) return;
+    int prev = 0;
+    RFX_CUDA(cudaGetDevice(&prev));
+    for (auto& d : bc.free) {
+        if (dev >= 0 && d.first != dev) continue;
+        RFX_CUDA(cudaSetDevice(d.first));
+        for (auto& kv : d.second) RFX_CUDA(cudaFree(kv.second));
+        d.second.clear();
+    }
+    RFX_CUDA(cudaSetDevice(prev));
+}
 
 struct DBuf {
     void* p = nullptr;

@@ -757,6 +757,12 @@ int rfx_device_count(void) {
     return n;
 }
 
+long long rfx_cached_bytes(int device) { return cache_bytes(device); }
+
+int rfx_empty_cache(int device) {
+    return guarded([&] { cache_empty(device); });
+}
+
 void* rfx_create(int device) {
     Ctx* c = nullptr;
     const int rc = guarded([&] {

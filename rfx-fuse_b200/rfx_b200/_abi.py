@@ -62,7 +62,8 @@ class Stats(C.Structure):
 
 
 SYMBOLS = (
-    "rfx_last_error", "rfx_abi_version", "rfx_device_count", "rfx_create", "rfx_destroy",
+    "rfx_last_error", "rfx_abi_version", "rfx_device_count", "rfx_cached_bytes", "rfx_empty_cache",
+    "rfx_create", "rfx_destroy",
     "rfx_load", "rfx_grow", "rfx_results", "rfx_fit", "rfx_set_prox_buffer",
     "rfx_get_prox_buffer", "rfx_get_vote_buffers", "rfx_prox_finish", "rfx_prox_dense",
     "rfx_prox_finish_packed", "rfx_reset_forest", "rfx_set_progress", "rfx_get_trees",
@@ -107,6 +108,9 @@ def load_library(path: str = LIB_PATH):
     L.rfx_last_error.restype = C.c_char_p
     L.rfx_abi_version.restype = C.c_int
     L.rfx_device_count.restype = C.c_int
+    L.rfx_cached_bytes.restype = C.c_longlong
+    L.rfx_cached_bytes.argtypes = [C.c_int]
+    L.rfx_empty_cache.argtypes = [C.c_int]
     L.rfx_create.restype = vp
     L.rfx_create.argtypes = [C.c_int]
     L.rfx_destroy.argtypes = [vp]
@@ -189,6 +193,18 @@ def check(rc: int) -> None:
 
 def ptr(a, t):
     return None if a is None else a.ctypes.data_as(t)
+
+
+def cached_bytes(device: int = -1) -> int:
+    """Bytes of device memory the library keeps from destroyed contexts for reuse (device -1:
+    every device)."""
+    return int(load_library().rfx_cached_bytes(int(device)))
+
+
+def empty_cache(device: int = -1) -> None:
+    """Free the device memory kept from destroyed contexts (device -1: every device), e.g.
+    before another library in the process allocates."""
+    check(load_library().rfx_empty_cache(int(device)))
 
 
 class Context:

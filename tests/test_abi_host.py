@@ -39,6 +39,13 @@ def test_abi_version_and_no_device_here_is_reported():
     assert lib.rfx_device_count() >= 0
 
 
+def test_block_cache_is_empty_without_contexts():
+    # nothing has been cached in a process that made no device context; emptying is a no-op
+    assert rfx_b200.cached_bytes() == 0
+    rfx_b200.empty_cache()
+    assert rfx_b200.cached_bytes(0) == 0
+
+
 def test_create_on_missing_device_fails_cleanly():
     lib = rfx_b200.load_library()
     h = lib.rfx_create(10_000)
