@@ -328,7 +328,7 @@ void load(Ctx& c, const rfx_fit_params* prm, const rfx_inputs* in) {
     size_t free_b = 0, total_b = 0;
     RFX_CUDA(cudaMemGetInfo(&free_b, &total_b));
     const size_t budget = std::min<size_t>(free_b / 2, (size_t)32 << 30);
-    int Tcap = P.batch_trees > 0 ? P.batch_trees : 256;
+    int Tcap = P.batch_trees > 0 ? P.batch_trees : 512;
     Tcap = (int)std::max<size_t>(1, std::min<size_t>((size_t)Tcap, budget / per_tree));
     Tcap = std::min(Tcap, 4096);
     alloc_batch(c, Tcap);
