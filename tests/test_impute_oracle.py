@@ -67,3 +67,14 @@ def test_fill_restatement_reproduces_reference(top_k, aggregation):
     got = _loop(ri, R, X.copy(), top_k, aggregation, None)
     assert np.array_equal(np.asarray(got, np.float32).view(np.uint32),
                           np.asarray(want, np.float32).view(np.uint32))
+
+
+def test_imputation_rejects_bad_aggregation_and_top_k():
+    """Argument checks run before any device work (python/rfx_impute.py raises ValueError
+    for an unknown aggregation)."""
+    import rfx_b200
+    X = np.array([[1.0, np.nan], [2.0, 3.0], [np.nan, 4.0]], np.float32)
+    with pytest.raises(ValueError):
+        rfx_b200.rfx_impute_proximity(X, aggregation="mode")
+    with pytest.raises(ValueError):
+        rfx_b200.rfx_impute_proximity(X, top_k=-1)
