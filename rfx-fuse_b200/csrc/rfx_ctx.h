@@ -253,7 +253,7 @@ struct Ctx {
     DBuf b_nin, b_seg0, b_seg1, b_ninbag, b_oob, b_noob, b_mt, b_mtpos, b_status, b_bestvar,
         b_xbest, b_treemap, b_nodeclass, b_nodepred, b_tnodewt, b_ndstart, b_ndcnt, b_ndbuf,
         b_ndflag, b_ndcrit0, b_ndmaj, b_ndsum, b_ndkey, b_feat, b_lvl, b_srch, b_srchcnt,
-        b_srchoff, b_srchsml, b_bigrec, b_smlrec, b_sml2rec, b_counters, b_oobleaf, b_used, b_right, b_rightimp, b_d2, b_d0, b_rr, b_rsum, b_srchbig, b_partbig, b_pcode, b_pocnt, b_ppairs;
+        b_srchoff, b_srchsml, b_bigrec, b_smlrec, b_sml2rec, b_counters, b_oobleaf, b_used, b_right, b_rightimp, b_d2, b_d0, b_impnode, b_rr, b_rsum, b_srchbig, b_partbig, b_pcode, b_pocnt, b_ppairs;
 
     ~Ctx() {
         DBuf* all[] = {&xc, &rows, &edges, &nb, &kind, &cat, &lab, &yreg, &yv, &perm, &ks, &cumw,
@@ -263,7 +263,7 @@ struct Ctx {
                        &b_xbest, &b_treemap, &b_nodeclass, &b_nodepred, &b_tnodewt, &b_ndstart,
                        &b_ndcnt, &b_ndbuf, &b_ndflag, &b_ndcrit0, &b_ndmaj, &b_ndsum, &b_ndkey,
                        &b_feat, &b_lvl, &b_srch, &b_srchcnt, &b_srchoff, &b_srchsml, &b_bigrec, &b_smlrec, &b_sml2rec, &b_counters,
-                       &b_oobleaf, &b_used, &b_right, &b_rightimp, &b_d2, &b_d0, &b_rr, &b_rsum, &b_srchbig, &b_partbig, &b_pcode, &b_pocnt, &b_ppairs,
+                       &b_oobleaf, &b_used, &b_right, &b_rightimp, &b_d2, &b_d0, &b_impnode, &b_rr, &b_rsum, &b_srchbig, &b_partbig, &b_pcode, &b_pocnt, &b_ppairs,
                        &lr_code, &lr_order, &lr_goff, &lr_ngroups, &lr_tmp, &lr_X, &lr_Z,
                        &lr_CZ, &lr_Y, &lr_ls, &lr_part, &lr_small, &lr_A, &lr_q, &lr_qb, &lr_s, &lr_qbp, &lr_sp, &lr_perm, &lr_blocks, &lr_np, &lr_norm, &lr_ids, &lr_keys, &lr_order_s, &lr_cub, &f_nodes, &f_root, &f_cat, &f_cw, &p_X,
                        &p_xc, &p_vote, &p_val, &p_cls, &p_proba, &p_pred, &i_x, &i_miss, &i_cat,

@@ -166,6 +166,9 @@ struct Batch {
     // tree arrays (reference layout)
     int* status; int* bestvar; float* xbest; int* treemap; int* nodeclass;
     float* nodepred; float* tnodewt;
+    int4* imp_node;   // [T][M] regression importance: a node in one 16-byte record
+                      //   {status << 24 | split feature, threshold (terminal: prediction), left,
+                      //   right}, or nullptr
     // node work arrays
     int* nd_start; int* nd_cnt; uint8_t* nd_buf; uint8_t* nd_flag;
     float* nd_crit0; int* nd_maj; float* nd_sum;

@@ -132,9 +132,11 @@ void alloc_batch(Ctx& c, int Tcap) {
     if (c.task == RFX_TASK_REGRESSION && c.prm.compute_importance) {
         B.d2 = (float*)c.b_d2.get(T * N * p * 4);
         B.d0 = (float*)c.b_d0.get(T * N * 4);
+        B.imp_node = (int4*)c.b_impnode.get(T * M * 16);
     } else {
         B.d2 = nullptr;
         B.d0 = nullptr;
+        B.imp_node = nullptr;
     }
     B.tree_oob = nullptr;
     B.M = c.M;
@@ -638,6 +640,7 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
             rfx::k_imp_class<<<rg, 256, 0, st>>>(D, B);
             rfx::k_imp_class_rr<<<T, 256, 0, st>>>(D, B);
         } else {
+            rfx::k_imp_pack<<<dim3((unsigned)((M + 255) / 256), (unsigned)T), 256, 0, st>>>(B);
             rfx::k_imp_regr<<<rg, 256, 0, st>>>(D, B);
             const size_t warps = (size_t)T * (p + 1);
             rfx::k_imp_regr_sum<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(D, B);
@@ -645,7 +648,7 @@ void grow_batch(Ctx& c, int tree0, int T, rfx_trees* out, int out_off) {
         }
         rfx::k_imp_fold<<<1, 256, 0, st>>>(D, B, (float*)c.avimp.p, (float*)c.sqsd.p);
         RFX_LAUNCH("importance kernels");
-        c.launches += c.nclass > 1 ? 4 : 5;
+        c.launches += c.nclass > 1 ? 4 : 6;
     }
     if (c.prm.compute_proximity && c.prox) {
         if (c.profiling) RFX_CUDA(cudaEventRecord(c.ev0, st));

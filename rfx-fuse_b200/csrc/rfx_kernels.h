@@ -43,6 +43,7 @@ __global__ void k_imp_used(Data D, Batch B);
 __global__ void k_imp_class(Data D, Batch B);
 __global__ void k_imp_class_rr(Data D, Batch B);
 __global__ void k_imp_regr(Data D, Batch B);
+__global__ void k_imp_pack(Batch B);
 __global__ void k_imp_regr_sum(Data D, Batch B);
 __global__ void k_imp_regr_rr(Data D, Batch B);
 __global__ void k_imp_fold(Data D, Batch B, float* avimp, float* sqsd);

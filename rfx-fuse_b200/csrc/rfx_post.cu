@@ -171,12 +171,35 @@ __global__ void k_imp_class_rr(Data D, Batch B) {
 // Regression importance, squared errors (cpu_varimp_regression, src/rf_varimp.cpp:477-597):
 // d0[j] for the unpermuted prediction, d2[j][k] with feature k permuted, per OOB rank j.
 // The squared errors of OOB rank j of tree t into out[k * os], k in [0, p).
+// The walks read a node as one 16-byte record (B.imp_node, written by k_imp_pack).
+__device__ __forceinline__ int pk_status(const int4& n) { return (int)(int8_t)((unsigned)n.x >> 24); }
+__device__ __forceinline__ int pk_feature(const int4& n) { return n.x & 0xFFFFFF; }
+
+__device__ __forceinline__ float walk_perm_regr_pk(const Data& D, const int4* nd, int nnode,
+                                                   int row, int prow, int mr) {
+    int kt = 0;
+    for (int k = 0; k < nnode; ++k) {
+        const int4 n = nd[kt];
+        if (pk_status(n) == -1) return __int_as_float(n.y);
+        const int m = pk_feature(n);
+        if (m >= D.p) break;
+        const float v = D.xc[(size_t)m * D.N + (m == mr ? prow : row)];
+        if (D.cat[m] <= 2) kt = v <= __int_as_float(n.y) ? n.z : n.w;
+        else {
+            const int j = (int)(v + 0.5f);
+            if (j >= 0 && j < D.maxcat) kt = n.w;
+            else break;
+        }
+        if (kt < 0 || kt >= nnode) break;
+    }
+    return 0.0f;
+}
+
 __device__ void imp_regr_row(const Data& D, const Batch& B, int t, int j, float* out, size_t os) {
-    const size_t mo = (size_t)t * B.M;
-    const int *st = B.status + mo, *bv = B.bestvar + mo, *tm = B.treemap + 2 * mo;
-    const float *xb = B.xbest + mo, *np = B.nodepred + mo;
+    const int4* nd = B.imp_node + (size_t)t * B.M;
     const int row = B.oob[(size_t)t * D.N + j];
-    const float pred = np[B.oob_leaf[(size_t)t * D.N + row]];
+    // (nodepred itself: a walk that did not end on a terminal node reports the root)
+    const float pred = B.nodepred[(size_t)t * B.M + B.oob_leaf[(size_t)t * D.N + row]];
     const float y = D.yreg[row];
     const float d = pred - y;
     const float dd = 1.0f * d * d;
@@ -194,13 +217,14 @@ __device__ void imp_regr_row(const Data& D, const Batch& B, int t, int j, float*
         constexpr int kMaxPath = 48;
         unsigned long long tested = 0, left = 0;  // features on the path / walks that left it
         int kt = 0, steps = 0, depth = 0;
-        while (st[kt] == 1 && steps < 1000) {
+        int4 n = nd[0];
+        while (pk_status(n) == 1 && steps < 1000) {
             ++steps;
             if (depth == kMaxPath) { deep = true; break; }
-            const int f = bv[kt];
-            if (f < 0 || f >= D.p) { deep = true; break; }
-            const float th = xb[kt];
-            const int l = tm[2 * kt], r = tm[2 * kt + 1];
+            const int f = pk_feature(n);
+            if (f >= D.p) { deep = true; break; }
+            const float th = __int_as_float(n.y);
+            const int l = n.z, r = n.w;
             const int nx = D.xc[(size_t)f * D.N + row] <= th ? l : r;
             tested |= 1ull << f;
             if (!((left >> f) & 1ull)) {
@@ -212,10 +236,11 @@ __device__ void imp_regr_row(const Data& D, const Batch& B, int t, int j, float*
                     float pk = 0.0f;
                     if (pk_kt >= 0 && pk_kt < nn) {
                         for (int k = depth + 1; k < nn; ++k) {
-                            if (st[pk_kt] == -1) { pk = np[pk_kt]; break; }
-                            const int m = bv[pk_kt];
+                            const int4 q = nd[pk_kt];
+                            if (pk_status(q) == -1) { pk = __int_as_float(q.y); break; }
+                            const int m = pk_feature(q);
                             const float v = D.xc[(size_t)m * D.N + (m == f ? prow : row)];
-                            pk_kt = v <= xb[pk_kt] ? tm[2 * pk_kt] : tm[2 * pk_kt + 1];
+                            pk_kt = v <= __int_as_float(q.y) ? q.z : q.w;
                             if (pk_kt < 0 || pk_kt >= nn) break;
                         }
                     }
@@ -225,13 +250,14 @@ __device__ void imp_regr_row(const Data& D, const Batch& B, int t, int j, float*
             }
             ++depth;
             kt = nx;
-            if (st[kt] != 1) break;
+            n = nd[kt];
+            if (pk_status(n) != 1) break;
         }
         // walks that never left the path end at the row's own terminal node
         const unsigned long long stay = tested & ~left;
         if (!deep && stay) {
-            if (kt >= 0 && kt < nn && st[kt] == -1) {
-                const float dk = np[kt] - y;
+            if (kt >= 0 && kt < nn && pk_status(n) == -1) {
+                const float dk = __int_as_float(n.y) - y;
                 const float e = 1.0f * dk * dk;
                 for (int k = 0; k < D.p; ++k)
                     if ((stay >> k) & 1ull) out[k * os] = e;
@@ -242,10 +268,22 @@ __device__ void imp_regr_row(const Data& D, const Batch& B, int t, int j, float*
     }
     if (deep) {
         for (int k = 0; k < D.p; ++k) {
-            const float dk = walk_perm_regr(D, st, bv, xb, tm, np, nn, row, prow, k) - y;
+            const float dk = walk_perm_regr_pk(D, nd, nn, row, prow, k) - y;
             out[k * os] = 1.0f * dk * dk;
         }
     }
+}
+
+// The batch's nodes as 16-byte records for the regression importance walks.  grid (M/256, T).
+__global__ void k_imp_pack(Batch B) {
+    const int t = blockIdx.y;
+    const int k = blockIdx.x * blockDim.x + threadIdx.x;
+    if (k >= B.M) return;
+    const size_t m = (size_t)t * B.M + k;
+    const int st = B.status[m];
+    const float v = st == -1 ? B.nodepred[m] : B.xbest[m];
+    B.imp_node[m] = make_int4((int)(((unsigned)st & 0xFFu) << 24 | ((unsigned)B.bestvar[m] & 0xFFFFFFu)),
+                              __float_as_int(v), B.treemap[2 * m], B.treemap[2 * m + 1]);
 }
 
 // One thread per OOB rank; d2 is feature-major, so a warp's stores of one feature are
